@@ -1,0 +1,124 @@
+"""The CPU oracle against the reference's own outputs (tests/golden/, made by tests/golden/make_golden.py from the
+reference checkout). These pin the restatement before it is used to check the CUDA path."""
+import pytest
+import torch
+
+from oracle import credit, eggroll, gpt
+
+
+def _check_weights(w, sums):
+    for name, (s, a, head) in sums.items():
+        assert torch.equal(w[name].flatten()[:8], head), name
+        assert abs(float(w[name].double().sum()) - s) <= 1e-9 * max(1.0, abs(a)), name
+        assert abs(float(w[name].double().abs().sum()) - a) <= 1e-9 * max(1.0, a), name
+
+
+def test_param_order_and_count():
+    names = [n for n, _ in gpt.param_shapes()]
+    assert len(names) == 60 and names[:3] == ['resid_lambdas', 'x0_lambdas', 'transformer.wte.weight']
+    assert gpt.param_count() == 37_749_776
+
+
+def test_init_matches_reference_constructor(golden):
+    _check_weights(gpt.init_weights(0), golden('gpt_forward.pt')['weights'])
+
+
+def test_init_matches_reference_make_model(golden):
+    _check_weights(gpt.init_weights(0, eggroll=True), golden('population_T256.pt')['weights'])
+
+
+def test_zipf_tokens_match_fixture(golden):
+    g = golden('gpt_forward.pt')
+    assert torch.equal(gpt.zipf_tokens(4, 2049, seed=0), g['tokens'].long())
+
+
+@pytest.mark.parametrize('rows', [1])
+def test_forward_fp32_matches_reference(golden, rows):
+    """Config 1 (one of its four rows, to keep the CPU suite short): the oracle's dense-attention forward against the
+    reference's flex-attention forward, fp32, per-token CE."""
+    g = golden('gpt_forward.pt')
+    tokens = g['tokens'].long()[:rows]
+    ce = gpt.forward(gpt.init_weights(0), tokens[:, :-1], tokens[:, 1:], loss_reduction='none').view(rows, -1)
+    torch.testing.assert_close(ce, g['ce'][:rows], rtol=1e-5, atol=1e-5)
+
+
+def _population_case(g):
+    buf = eggroll.make_buffer(g['noise_size'], seed=0)
+    assert torch.equal(buf[:16], g['buffer_head'])
+    assert abs(float(buf.double().sum()) - float(g['buffer_sum'])) < 1e-6
+    shapes = gpt.param_shapes()
+    offs = eggroll.offsets(shapes, g['pairs'], step=1, n_noise=g['noise_size'])
+    for name in offs:
+        assert torch.equal(offs[name], g['offsets'][name]), name
+    nz = eggroll.noise(buf, offs, g['directions'], shapes)
+    for name, ref in g['gathered'].items():
+        got = nz[name]
+        if isinstance(ref, tuple):
+            assert all(torch.equal(x[:, :4], y) for x, y in zip(got, ref)), name
+        else:
+            assert torch.equal(got[:, :4], ref), name
+    sign = torch.tensor([g['sigma'], -g['sigma']]).repeat(g['pairs'])
+    tokens = g['tokens'].long()
+    return nz, sign, tokens[:-1], tokens[1:]
+
+
+def test_noise_map_bit_exact(golden):
+    _population_case(golden('population_T256.pt'))
+
+
+@pytest.mark.parametrize('length', [256, 2048])
+def test_population_loss_fp32(golden, length):
+    g = golden(f'population_T{length}.pt')
+    nz, sign, idx, tgt = _population_case(g)
+    w = gpt.init_weights(0, eggroll=True)
+    got = eggroll.population_loss(w, nz, sign, idx, tgt)
+    torch.testing.assert_close(got, g['loss_fp32'], rtol=2e-6, atol=0)
+
+
+def test_population_loss_autocast(golden):
+    """The oracle's bf16 rounding points against the reference run under CPU bf16 autocast."""
+    g = golden('population_T256.pt')
+    nz, sign, idx, tgt = _population_case(g)
+    w = gpt.init_weights(0, eggroll=True)
+    got = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
+    torch.testing.assert_close(got, g['loss_autocast'], rtol=2e-5, atol=0)
+
+
+def test_member_layout_and_update(golden):
+    """One Eggroll.step: losses -> fitness -> seed-rebuilt gradient, against the reference step's gradients."""
+    g = golden('eggroll_step.pt')
+    pairs, rows, length, n = g['pairs'], g['rows'], g['length'], g['noise_size']
+    shapes = gpt.param_shapes()
+    members, per_seq, per_rank, directions, positive, row = eggroll.member_layout(pairs, rows)
+    assert (members, per_seq, per_rank) == (2 * pairs, 2 * pairs // rows, 2 * pairs)
+    buf = eggroll.make_buffer(n, seed=0)
+    offs = eggroll.offsets(shapes, pairs, step=g['step'], n_noise=n)
+    w = gpt.init_weights(0, eggroll=True)
+    tokens = g['tokens'].long()
+    losses = []
+    chunk = 2 * g['chunk']
+    for start in range(0, members, chunk):
+        sel = torch.arange(start, start + chunk)
+        nz = eggroll.noise(buf, offs, directions[sel], shapes)
+        sign = torch.where(positive[sel], eggroll.SIGMA, -eggroll.SIGMA)
+        r = int(row[start])
+        losses.append(eggroll.population_loss(w, nz, sign, tokens[r, :-1], tokens[r, 1:]))
+    losses = torch.cat(losses)
+    assert abs(float(losses.mean()) - g['mean_loss']) < 1e-5
+    weight, count = eggroll.fitness_weights(losses, pairs)
+    grads = eggroll.rebuild_update(buf, offs, weight, count, shapes)
+    for name, ref in g['grad_small'].items():
+        torch.testing.assert_close(grads[name], ref, rtol=1e-4, atol=1e-6)
+    for name, ref in g['grad_corner'].items():
+        torch.testing.assert_close(grads[name][:8, :8], ref, rtol=1e-4, atol=1e-6)
+
+
+def test_implicit_key_context_matches_reference_kernel(golden):
+    g = golden('implicit_key_context.pt')
+    gen = torch.Generator().manual_seed(g['seed'])
+    q, k, v, hub = (torch.randn(g['rows'], g['length'], 64, generator=gen) / 8 for _ in range(4))
+    hub = hub * 8
+    for window, (lse, center) in g['out'].items():
+        got_lse, got_center = credit.implicit_key_context(q, k, v, hub, window)
+        torch.testing.assert_close(got_lse.float(), lse, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(got_center.float(), center, rtol=1e-4, atol=1e-5)
