@@ -1,0 +1,133 @@
+/* noise_b200 — C ABI of the B200 (sm_100a) hot path of Noise's forward-only training.
+ *
+ * Every pointer is a device pointer unless stated; every entry point enqueues work on `stream` (a cudaStream_t,
+ * NULL = legacy default stream), performs no allocation, no host synchronisation and no host read of device data,
+ * and returns NOISE_OK or a NOISE_ERR_* status for arguments it rejects before launching anything. Scratch memory
+ * is caller-owned (`workspace`); its first NOISE_STATUS_BYTES hold a device status word that kernels set when a
+ * bounded wait gives up (read it with noise_read_status after synchronising).
+ *
+ * The reference is pure Python (PyTorch + Triton/Gluon JIT kernels), so these functions replace Python entry points;
+ * each declaration names the reference function it stands in for (path:line inside the reference project).
+ */
+#ifndef NOISE_B200_H
+#define NOISE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NOISE_OK 0
+#define NOISE_ERR_SHAPE 1       /* unsupported size (e.g. T not a multiple of 128, members < 1) */
+#define NOISE_ERR_ALIGN 2       /* a pointer or stride violates the 16-byte TMA / vector alignment rule */
+#define NOISE_ERR_WORKSPACE 3   /* workspace NULL or smaller than the *_workspace_bytes query */
+#define NOISE_ERR_ARGUMENT 4    /* NULL required pointer or bad enum value */
+#define NOISE_ERR_CUDA 5        /* a CUDA runtime/driver call failed (launch, tensor-map encode, attributes) */
+#define NOISE_ERR_DEVICE 6      /* not an sm_100 device */
+
+#define NOISE_STATUS_BYTES 256
+
+/* Device status word values (noise_read_status). */
+#define NOISE_DEVICE_OK 0
+#define NOISE_DEVICE_TIMEOUT 1     /* a bounded mbarrier/flag wait gave up; outputs are invalid */
+
+/* Model dimensions of the fixed GPT (reference utils/model.py:34-43). */
+#define NOISE_N_LAYER 8
+#define NOISE_N_HEAD 8
+#define NOISE_HEAD_DIM 64
+#define NOISE_N_EMBD 512
+#define NOISE_VOCAB 4096
+#define NOISE_N_PARAMS 60
+
+/* Index of each parameter in the reference's GPT.named_parameters() order (60 tensors):
+ * 0 resid_lambdas, 1 x0_lambdas, 2 transformer.wte.weight, then per block i the attn.c_q, attn.c_k, attn.c_v,
+ * attn.c_proj, [attn.ve_gate on odd blocks], mlp.c_fc, mlp.c_proj weights, then 55 lm_head.weight and
+ * 56..59 value_embeds.{1,3,5,7}.weight. noise_param_index() returns the index of block i's tensor `which`. */
+enum noise_block_param {
+  NOISE_P_CQ = 0, NOISE_P_CK = 1, NOISE_P_CV = 2, NOISE_P_CPROJ = 3, NOISE_P_VEGATE = 4, NOISE_P_CFC = 5,
+  NOISE_P_MPROJ = 6, NOISE_P_VE = 7
+};
+int noise_param_index(int block, int which);
+#define NOISE_PARAM_RESID 0
+#define NOISE_PARAM_X0 1
+#define NOISE_PARAM_WTE 2
+#define NOISE_PARAM_HEAD 55
+
+/* Rank-1 perturbation slices of one parameter for m members (reference eggroll.py:122-128). Member j's out-side
+ * vector a_j starts at a + off[j] and its in-side vector b_j at b + off[j] (fp32). For the EGGROLL buffer,
+ * a = buffer, b = buffer + out and off[j] = offsets[param][direction_j]; for materialised per-member tensors
+ * a [m, out] / b [m, in], pass off = NULL and the strides instead: a_j = a + j * a_stride, b_j = b + j * b_stride.
+ * 1-D parameters (the mixing scalars) use a only: eps_j = a + off[j] (or a + j * a_stride). */
+typedef struct {
+  const float* a;
+  const float* b;
+  const int64_t* off;
+  int64_t a_stride;
+  int64_t b_stride;
+} noise_slice_t;
+
+/* The model's weights as the CUDA path consumes them: matrices packed to bf16 once per update (noise_pack_bf16),
+ * embeddings and mixing scalars fp32 (EGGROLL keeps them fp32, eggroll.py:50-52), RoPE tables bf16
+ * [>= T, 32] (utils/model.py:177-183). */
+typedef struct {
+  const void* wqkv[NOISE_N_LAYER];   /* bf16 [1536, 512]: rows 0..511 c_q, 512..1023 c_k, 1024..1535 c_v */
+  const void* wproj[NOISE_N_LAYER];  /* bf16 [512, 512] attn.c_proj */
+  const void* wfc[NOISE_N_LAYER];    /* bf16 [2048, 512] mlp.c_fc */
+  const void* wmproj[NOISE_N_LAYER]; /* bf16 [512, 2048] mlp.c_proj */
+  const float* wgate[NOISE_N_LAYER]; /* fp32 [8, 32] attn.ve_gate on odd blocks, NULL on even blocks */
+  const void* whead;                 /* bf16 [4096, 512] lm_head */
+  const float* wte;                  /* fp32 [4096, 512] */
+  const float* ve[NOISE_N_LAYER];    /* fp32 [4096, 512] value_embeds on odd blocks, NULL on even blocks */
+  const float* resid_lambdas;        /* fp32 [8] */
+  const float* x0_lambdas;           /* fp32 [8] */
+  const void* cos;                   /* bf16 [>= T, 32] */
+  const void* sin;                   /* bf16 [>= T, 32] */
+} noise_gpt_t;
+
+#define NOISE_REDUCTION_MEAN 0
+#define NOISE_REDUCTION_SUM 1
+
+/* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
+size_t noise_population_workspace_bytes(int members, int tokens);
+
+/* Per-member cross-entropy of m rank-1-perturbed copies of the GPT on one shared token row.
+ * Replaces eggroll.population_loss (archive/10M/train/val/eggroll.py:66-103) and the lowrank/lowrank_embed
+ * helpers it calls (:56-63); the perturbed weights are never materialised: every linear layer is a tcgen05 GEMM
+ * whose epilogue adds sign_j (x . b_j) a_j.
+ *   noise[NOISE_N_PARAMS]: host array of slices in named_parameters order; sign[m] fp32 (+-sigma);
+ *   idx[T], targets[T] int64 token ids; losses[m] fp32 out (mean or sum over T per `reduction`).
+ * Requirements: T % 128 == 0, 128 <= T <= 2048, members >= 1. */
+int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
+                          const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
+                          float* losses, void* workspace, size_t workspace_bytes, void* stream);
+
+/* D[m, n] (fp32, row-major) = A[m, k] . B[n, k]^T for bf16 row-major A and B, on the persistent tcgen05/TMA GEMM
+ * that every linear layer of noise_population_loss runs on, with a plain store epilogue. Stands in for the cuBLAS
+ * GEMM autocast issues for `x @ weight.t()` (eggroll.py:58; utils/model.py:83-85). m % 128 == 0, n % 256 == 0,
+ * k % 64 == 0; `workspace` holds at least NOISE_STATUS_BYTES (the device status word). */
+int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace, void* stream);
+
+/* fp32 -> bf16 (round to nearest even) of n values; both pointers 16-byte aligned, n % 8 == 0.
+ * Replaces autocast's per-call weight casts inside the reference's linears (eggroll.py:58 under
+ * torch.autocast, eggroll.py:144). */
+int noise_pack_bf16(const float* src, void* dst, int64_t n, void* stream);
+
+/* Copy the device status word at the head of `workspace` to *status (synchronises `stream`). */
+int noise_read_status(const void* workspace, int* status, void* stream);
+
+/* Clear the device status word (enqueued on `stream`). */
+int noise_clear_status(void* workspace, void* stream);
+
+/* Human-readable name of a NOISE_ERR_* status. */
+const char* noise_status_string(int status);
+
+/* Number of kernels the most recent successful noise_population_loss call on this thread enqueued. */
+int noise_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NOISE_B200_H */

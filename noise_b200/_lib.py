@@ -1,0 +1,107 @@
+"""ctypes binding of the C ABI in include/noise_b200.h (the in-tree libnoise_b200.so).
+
+There is no fallback: if the library is missing or fails to load, every op raises. Device pointers are passed as
+integers (``tensor.data_ptr()``), streams as the raw ``cudaStream_t`` of the current PyTorch stream.
+"""
+import ctypes
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / 'libnoise_b200.so'
+
+N_LAYER, N_HEAD, HEAD_DIM, N_EMBD, VOCAB, N_PARAMS = 8, 8, 64, 512, 4096, 60
+REDUCTION = {'mean': 0, 'sum': 1}
+STATUS_BYTES = 256
+
+
+class Slice(ctypes.Structure):
+    """noise_slice_t."""
+    _fields_ = [('a', ctypes.c_void_p), ('b', ctypes.c_void_p), ('off', ctypes.c_void_p),
+                ('a_stride', ctypes.c_int64), ('b_stride', ctypes.c_int64)]
+
+
+class GPT(ctypes.Structure):
+    """noise_gpt_t."""
+    _fields_ = [('wqkv', ctypes.c_void_p * N_LAYER), ('wproj', ctypes.c_void_p * N_LAYER),
+                ('wfc', ctypes.c_void_p * N_LAYER), ('wmproj', ctypes.c_void_p * N_LAYER),
+                ('wgate', ctypes.c_void_p * N_LAYER), ('whead', ctypes.c_void_p), ('wte', ctypes.c_void_p),
+                ('ve', ctypes.c_void_p * N_LAYER), ('resid_lambdas', ctypes.c_void_p),
+                ('x0_lambdas', ctypes.c_void_p), ('cos', ctypes.c_void_p), ('sin', ctypes.c_void_p)]
+
+
+class NoiseError(RuntimeError):
+    pass
+
+
+_lib = None
+
+# (name, restype, argtypes) of every exported entry point; tests check each one is present.
+SIGNATURES = [
+    ('noise_param_index', ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    ('noise_population_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_population_loss', ctypes.c_int,
+     [ctypes.POINTER(GPT), ctypes.POINTER(Slice), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_gemm_bf16_tn', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+      ctypes.c_void_p]),
+    ('noise_pack_bf16', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
+    ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
+    ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),
+    ('noise_last_launch_count', ctypes.c_int, []),
+]
+
+
+def lib():
+    """The loaded library (raises NoiseError when it is missing: there is no CPU path)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise NoiseError(f'{LIB_PATH} is missing: build it with `python -m noise_b200.build`')
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, res, args in SIGNATURES:
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def check(status, what):
+    if status != 0:
+        raise NoiseError(f'{what}: {lib().noise_status_string(status).decode()} (status {status})')
+
+
+def stream_handle(device=None):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if not t.is_cuda:
+            raise NoiseError('noise_b200 ops run on CUDA tensors only (no CPU fallback)')
+
+
+def read_status(workspace):
+    """Device status word at the head of a workspace (synchronises the current stream)."""
+    out = ctypes.c_int(0)
+    check(lib().noise_read_status(workspace.data_ptr(), ctypes.byref(out), stream_handle(workspace.device)),
+          'noise_read_status')
+    return out.value
+
+
+def launches():
+    return lib().noise_last_launch_count()
+
+
+def gemm_bf16_tn(a, b):
+    """fp32 a @ b.T for bf16 a [m, k], b [n, k] on the tcgen05 GEMM core (m % 128, n % 256, k % 64 == 0)."""
+    require_cuda(a, b)
+    a, b = a.contiguous(), b.contiguous()
+    out = torch.empty((a.shape[0], b.shape[0]), dtype=torch.float32, device=a.device)
+    ws = torch.empty(STATUS_BYTES, dtype=torch.uint8, device=a.device)
+    check(lib().noise_gemm_bf16_tn(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.shape[0], b.shape[0], a.shape[1],
+                                   ws.data_ptr(), stream_handle(a.device)), 'noise_gemm_bf16_tn')
+    out._noise_workspace = ws
+    return out

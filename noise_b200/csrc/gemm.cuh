@@ -1,0 +1,204 @@
+// Persistent, warp-specialised bf16 "TN" GEMM for sm_100a: D[M, N] = A[M, K] . B[N, K]^T with both operands
+// K-major in HBM (activations row-major, nn.Linear weights [out, in]), fp32 accumulation in tensor memory, and a
+// fused per-row epilogue supplied as a functor.
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      one lane issues TMA tile loads (128-byte swizzle) into a STAGES-deep shared-memory ring;
+//   warp 1      allocates 2 x BN TMEM columns (double-buffered accumulator); one lane issues tcgen05.mma
+//               (M = 128, N = BN, K = 16 per instruction) and tcgen05.commit to release ring slots / publish tiles;
+//   warps 2..5  epilogue: warp w reads TMEM lane quarter (w % 4), i.e. one output row per thread, in column chunks
+//               (tcgen05.ld 32x32b), and hands them to the functor; then frees the accumulator buffer.
+// Schedule: CTA c owns row blocks c, c + grid, ...; for each it walks all N tiles in order, so an epilogue can carry
+// per-row state (a running log-sum-exp, a partial dot product) across the N tiles of its row.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "ptx.cuh"
+
+namespace noise {
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN, int STAGES>
+struct GemmLayout {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFFSET + 8 * (2 * STAGES + 5) + 16 + 1024;  // + 1024 alignment slack
+  static constexpr int TMEM_COLS = 2 * BN;
+  static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tcgen05 M=128 needs N in [16, 256], N % 16 == 0");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation must be a power of two");
+};
+
+// Epilogue functor contract (all methods run on the thread that owns `row`):
+//   static constexpr int CH;                          columns per TMEM load (16, 32 or 64)
+//   void row_begin(int row);                          before the first N tile of the row block
+//   void chunk(int row, int col, const float* v);     v[0..CH) = D[row, col .. col + CH)
+//   void tile_end(int row, int n_tile);               after the last chunk of a tile
+//   void row_end(int row);                            after the last N tile
+template <int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        int m_tiles, int n_tiles, int k_blocks, Epi epi, int* status) {
+  using L = GemmLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int mb = blockIdx.x; mb < m_tiles && ok; mb += gridDim.x)
+        for (int nb = 0; nb < n_tiles && ok; ++nb)
+          for (int kb = 0; kb < k_blocks; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, status)) {
+              ok = false;
+              break;
+            }
+            uint8_t* a = smem + stage * L::STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
+            tma_load_2d(a, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
+            tma_load_2d(a + L::A_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+      // Drain: the last min(issued, STAGES) loads must have landed before the CTA may exit.
+      for (int i = 0; i < STAGES && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = STAGES - 1;
+          phase ^= 1u;
+        }
+        mbar_wait(&full[stage], phase, status);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int t = 0;
+      bool ok = true;
+      for (int mb = blockIdx.x; mb < m_tiles && ok; mb += gridDim.x)
+        for (int nb = 0; nb < n_tiles && ok; ++nb, ++t) {
+          const int buf = t & 1;
+          const uint32_t use = static_cast<uint32_t>(t >> 1);
+          if (!mbar_wait(&acce[buf], (use & 1u) ^ 1u, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
+          for (int kb = 0; kb < k_blocks; ++kb) {
+            if (!mbar_wait(&full[stage], phase, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a = smem_u32(smem + stage * L::STAGE_BYTES);
+            const uint64_t ad = sdesc_kmajor_sw128(a), bd = sdesc_kmajor_sw128(a + L::A_BYTES);
+#pragma unroll
+            for (int k = 0; k < GEMM_BK / 16; ++k)  // +32 bytes along K = +2 in the 16-byte address field
+              tc_mma(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0);
+            tc_commit(&empty[stage]);
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+          }
+          if (ok) tc_commit(&accf[buf]);
+        }
+      // Drain every MMA this thread issued before TMEM is freed.
+      tc_commit(drain);
+      mbar_wait(drain, 0, status);
+    }
+  } else {
+    Epi e = epi;  // per-thread copy: the functor may carry per-row state
+    const int quarter = warp & 3;
+    const int r_in = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    int t = 0;
+    bool ok = true;
+    for (int mb = blockIdx.x; mb < m_tiles && ok; mb += gridDim.x) {
+      const int row = mb * GEMM_BM + r_in;
+      e.row_begin(row);
+      for (int nb = 0; nb < n_tiles; ++nb, ++t) {
+        const int buf = t & 1;
+        const uint32_t use = static_cast<uint32_t>(t >> 1);
+        ok = mbar_wait(&accf[buf], use & 1u, status);
+        tc_fence_after();
+        if (ok) {
+          const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += Epi::CH) {
+            float v[Epi::CH];
+            if constexpr (Epi::CH == 64) {
+              tmem_ld32(base + c, v);
+              tmem_ld32(base + c + 32, v + 32);
+            } else if constexpr (Epi::CH == 32) {
+              tmem_ld32(base + c, v);
+            } else {
+              tmem_ld16(base + c, v);
+            }
+            tc_wait_ld();
+            e.chunk(row, nb * BN + c, v);
+          }
+          e.tile_end(row, nb);
+        }
+        tc_fence_before();
+        mbar_arrive(&acce[buf]);
+        if (!ok) break;
+      }
+      if (ok) e.row_end(row);
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
+}  // namespace noise

@@ -1,0 +1,983 @@
+// Population-perturbed forward of Noise's fixed GPT on sm_100a.
+//
+// Replaces eggroll.population_loss (reference archive/10M/train/val/eggroll.py:66-103): m members, each the GPT
+// of utils/model.py with every matrix and embedding perturbed by sign_j a_j b_j^T and every mixing scalar by
+// sign_j eps_j, all evaluated on one shared token row. Rows of every activation are (member, token) pairs,
+// row r = j * T + t, so a 128-row GEMM tile belongs to one member (T % 128 == 0).
+//
+// Per block (8 blocks), 6 kernels:
+//   norm_kernel<BLOCK>   mixing resid x + x0l x0 (x0 recomputed from wte + rank-1 term), RMS norm -> bf16 h,
+//                        rank-1 dot products h.b for q, k, v, the value-embedding gate
+//   GEMM + EpiQKV        h [M,512] x Wqkv^T [512,1536]; epilogue adds sign (h.b) a, RoPE + RMS norm of q and k,
+//                        gated value embedding of v; writes q, k, v bf16 [m, H, T, 64]
+//   attention_kernel     windowed causal softmax(q k^T / 8) v (mma.sync), writes y bf16 [M,512] and the per-head
+//                        partial dots y.b of the c_proj perturbation
+//   GEMM + EpiResid      x += y Wproj^T + sign (y.b) a
+//   norm_kernel<MID>     RMS norm -> bf16 h, h.b of c_fc
+//   GEMM + EpiFC         relu(h Wfc^T + sign (h.b) a)^2 -> bf16 hidden [M,2048], partial dots hidden.b of mlp.c_proj
+//   GEMM + EpiResid      x += hidden Wmproj^T + sign (hidden.b) a
+// then norm_kernel<FINAL> and GEMM + EpiHeadCE (LM head, softcap 15 tanh(z/15), cross-entropy against the target,
+// logits never leave the SM) and member_reduce_kernel (per-member mean or sum).
+//
+// Rounding follows the reference under torch.autocast('cuda', bfloat16): every matmul takes bf16 operands and
+// returns bf16; the rank-1 correction sign bf16(x.b) a and the residual stream stay fp32.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "noise_b200.h"
+#include "ptx.cuh"
+
+namespace noise {
+
+constexpr int D = NOISE_N_EMBD;  // 512
+constexpr int H = NOISE_N_HEAD;  // 8
+constexpr int HD = NOISE_HEAD_DIM;  // 64
+constexpr int F = 4 * NOISE_N_EMBD;  // 2048
+constexpr int V = NOISE_VOCAB;  // 4096
+constexpr float RMS_EPS = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm(eps=None) on fp32
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr int GEMM_BN = 256;
+constexpr int GEMM_STAGES = 4;
+
+struct Slice {
+  const float* a;
+  const float* b;
+  const int64_t* off;
+  int64_t as, bs;
+  __device__ __forceinline__ const float* A(int j) const { return a + (off ? off[j] : j * as); }
+  __device__ __forceinline__ const float* B(int j) const { return b + (off ? off[j] : j * bs); }
+};
+
+static Slice to_slice(const noise_slice_t& s) { return Slice{s.a, s.b, s.off, s.a_stride, s.b_stride}; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Norm / mixing kernel: one warp per row, lane l holds columns 4 l + 128 i + {0..3}, i = 0..3.
+// ---------------------------------------------------------------------------------------------------------------
+enum NormMode { NORM_BLOCK = 0, NORM_MID = 1, NORM_FINAL = 2 };
+
+struct NormArgs {
+  int layer, T, M;
+  const int64_t* idx;
+  const float* sign;
+  float* x;            // residual stream [M, 512] fp32
+  __nv_bfloat16* h;    // out [M, 512] bf16
+  float* svec;         // out [M, 4]: BLOCK (s_q, s_k, s_v, s_gate); MID s_fc; FINAL s_head (slot 0)
+  float* gate;         // out [M, 8] (BLOCK, value-embedding layers)
+  const float* wte;
+  Slice n_wte, n_resid, n_x0;
+  const float* resid_l;
+  const float* x0_l;
+  Slice nb0, nb1, nb2;  // b sources of the dot products (BLOCK: c_q, c_k, c_v; MID: c_fc; FINAL: lm_head)
+  const float* wgate;  // [8, 32] fp32 or NULL
+  Slice n_gate;
+};
+
+__device__ __forceinline__ float dot_bf16_row(const float (&hb)[16], const float* b, int lane) {
+  // b is a noise slice at an arbitrary buffer offset: 4-byte aligned only, so scalar loads
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc += hb[4 * i + c] * bf16_round(b[4 * lane + 128 * i + c]);
+  return bf16_round(warp_sum(acc));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(256) norm_kernel(NormArgs p) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= p.M) return;
+  const int r = warp, j = r / p.T, t = r - j * p.T;
+  const float sg = p.sign[j];
+  float x[16];
+  float* xrow = p.x + static_cast<int64_t>(r) * D;
+
+  if (MODE == NORM_BLOCK) {
+    // x0 = norm(wte[idx] + sign a[idx] b), eggroll.py:61-63, 74
+    const int64_t tok = p.idx[t];
+    const float* w = p.wte + tok * D;
+    const float* bw = p.n_wte.B(j);
+    const float sa = sg * p.n_wte.A(j)[tok];
+    float x0[16], ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * i);
+      const float* bp = bw + 4 * lane + 128 * i;  // noise slice: scalar loads
+      x0[4 * i + 0] = wv.x + sa * bp[0];
+      x0[4 * i + 1] = wv.y + sa * bp[1];
+      x0[4 * i + 2] = wv.z + sa * bp[2];
+      x0[4 * i + 3] = wv.w + sa * bp[3];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ss += x0[i] * x0[i];
+    const float inv0 = rsqrtf(warp_sum(ss) / D + RMS_EPS);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x0[i] *= inv0;
+    // mixing, eggroll.py:77-79
+    const float resid = p.resid_l[p.layer] + sg * p.n_resid.A(j)[p.layer];
+    const float mix = p.x0_l[p.layer] + sg * p.n_x0.A(j)[p.layer];
+    if (p.layer == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = resid * x0[i] + mix * x0[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 xv = *reinterpret_cast<const float4*>(xrow + 4 * lane + 128 * i);
+        x[4 * i + 0] = resid * xv.x + mix * x0[4 * i + 0];
+        x[4 * i + 1] = resid * xv.y + mix * x0[4 * i + 1];
+        x[4 * i + 2] = resid * xv.z + mix * x0[4 * i + 2];
+        x[4 * i + 3] = resid * xv.w + mix * x0[4 * i + 3];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4*>(xrow + 4 * lane + 128 * i) =
+          make_float4(x[4 * i + 0], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 xv = *reinterpret_cast<const float4*>(xrow + 4 * lane + 128 * i);
+      x[4 * i + 0] = xv.x;
+      x[4 * i + 1] = xv.y;
+      x[4 * i + 2] = xv.z;
+      x[4 * i + 3] = xv.w;
+    }
+  }
+
+  // h = norm(x) in fp32, rounded to bf16 as autocast feeds it to the matmuls
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) ss += x[i] * x[i];
+  const float inv = rsqrtf(warp_sum(ss) / D + RMS_EPS);
+  float hb[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) hb[i] = bf16_round(x[i] * inv);
+  __nv_bfloat16* hrow = p.h + static_cast<int64_t>(r) * D;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint2 pk;
+    pk.x = pack_bf16x2(hb[4 * i + 0], hb[4 * i + 1]);
+    pk.y = pack_bf16x2(hb[4 * i + 2], hb[4 * i + 3]);
+    *reinterpret_cast<uint2*>(hrow + 4 * lane + 128 * i) = pk;
+  }
+
+  float* sv = p.svec + static_cast<int64_t>(r) * 4;
+  if (MODE == NORM_BLOCK) {
+    const float sq = dot_bf16_row(hb, p.nb0.B(j), lane);
+    const float sk = dot_bf16_row(hb, p.nb1.B(j), lane);
+    const float svv = dot_bf16_row(hb, p.nb2.B(j), lane);
+    float sgate = 0.f;
+    if (p.wgate) {
+      // value-embedding gate 2 sigmoid(lowrank(h[:32], W_g, a, b)), eggroll.py:88; h[:32] lives in lanes 0..7 (i = 0)
+      const float* bg = p.n_gate.B(j);
+      const float* ag = p.n_gate.A(j);
+      float part = 0.f;
+      if (lane < 8) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) part += hb[c] * bf16_round(bg[4 * lane + c]);
+      }
+      sgate = bf16_round(warp_sum(part));
+      float gsel = 0.f;
+#pragma unroll
+      for (int hh = 0; hh < H; ++hh) {
+        float z = 0.f;
+        if (lane < 8) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) z += hb[c] * bf16_round(p.wgate[hh * 32 + 4 * lane + c]);
+        }
+        z = bf16_round(warp_sum(z)) + sg * sgate * ag[hh];
+        const float g = 2.f / (1.f + __expf(-z));
+        if (lane == hh) gsel = g;
+      }
+      if (lane < H) p.gate[static_cast<int64_t>(r) * H + lane] = gsel;
+    }
+    if (lane == 0) *reinterpret_cast<float4*>(sv) = make_float4(sq, sk, svv, sgate);
+  } else {
+    const float s0 = dot_bf16_row(hb, p.nb0.B(j), lane);
+    if (lane == 0) sv[0] = s0;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// GEMM epilogues
+// ---------------------------------------------------------------------------------------------------------------
+
+// q, k: + sign (h.b) a, RoPE (utils/model.py:55-58), RMS norm over the head; v: + sign (h.b) a + gate ve
+// (eggroll.py:82-90). Writes bf16 [m, H, T, 64].
+struct EpiQKV {
+  static constexpr int CH = 64;
+  int T;
+  const float* sign;
+  const float* svec;
+  const float* gate;  // NULL on blocks without value embeddings
+  const int64_t* idx;
+  const __nv_bfloat16* cosb;
+  const __nv_bfloat16* sinb;
+  const float* vew;  // value-embedding table [4096, 512] fp32 or NULL
+  Slice nq, nk, nv, nve;
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  int j, t;
+  float sg;
+
+  __device__ __forceinline__ void row_begin(int row) {
+    j = row / T;
+    t = row - j * T;
+    sg = sign[j];
+  }
+  __device__ __forceinline__ void tile_end(int, int) {}
+  __device__ __forceinline__ void row_end(int) {}
+  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+    const int sec = col / D, hh = (col % D) / HD;
+    const float coef = sg * svec[static_cast<int64_t>(row) * 4 + sec];
+    const float* a = (sec == 0 ? nq.A(j) : sec == 1 ? nk.A(j) : nv.A(j)) + (col % D);
+    float val[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) val[d] = bf16_round(acc[d]) + coef * a[d];  // a: noise slice, scalar loads
+    __nv_bfloat16* dst;
+    if (sec < 2) {
+      const __nv_bfloat16* cr = cosb + static_cast<int64_t>(t) * (HD / 2);
+      const __nv_bfloat16* sr = sinb + static_cast<int64_t>(t) * (HD / 2);
+      float ss = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD / 2; ++d) {
+        const float c = __bfloat162float(cr[d]), s = __bfloat162float(sr[d]);
+        const float x1 = val[d], x2 = val[d + HD / 2];
+        const float o1 = x1 * c + x2 * s;
+        const float o2 = x1 * -s + x2 * c;
+        val[d] = o1;
+        val[d + HD / 2] = o2;
+        ss += o1 * o1 + o2 * o2;
+      }
+      const float inv = rsqrtf(ss / HD + RMS_EPS);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) val[d] *= inv;
+      dst = sec == 0 ? q : k;
+    } else {
+      if (gate) {
+        const float g = gate[static_cast<int64_t>(row) * H + hh];
+        const int64_t tok = idx[t];
+        const float* ver = vew + tok * D + hh * HD;
+        const float sa = sg * nve.A(j)[tok];
+        const float* bve = nve.B(j) + hh * HD;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) val[d] = val[d] + g * (ver[d] + sa * bve[d]);
+      }
+      dst = v;
+    }
+    uint4* out = reinterpret_cast<uint4*>(dst + ((static_cast<int64_t>(j) * H + hh) * T + t) * HD);
+#pragma unroll
+    for (int d = 0; d < HD; d += 8) {
+      uint4 pk;
+      pk.x = pack_bf16x2(val[d + 0], val[d + 1]);
+      pk.y = pack_bf16x2(val[d + 2], val[d + 3]);
+      pk.z = pack_bf16x2(val[d + 4], val[d + 5]);
+      pk.w = pack_bf16x2(val[d + 6], val[d + 7]);
+      out[d / 8] = pk;
+    }
+  }
+};
+
+// x += bf16(acc) + sign bf16(sum of the row's partial dots) a  (c_proj and mlp.c_proj, eggroll.py:92-93).
+struct EpiResid {
+  static constexpr int CH = 32;
+  int T, nparts;
+  const float* sign;
+  const float* parts;  // [M, nparts] partial dots of the input row with this linear's b
+  Slice n;
+  float* x;
+  int j;
+  float coef;
+  const float* a;
+
+  __device__ __forceinline__ void row_begin(int row) {
+    j = row / T;
+    const float* pr = parts + static_cast<int64_t>(row) * nparts;
+    float s = 0.f;
+    for (int i = 0; i < nparts; ++i) s += pr[i];
+    coef = sign[j] * bf16_round(s);
+    a = n.A(j);
+  }
+  __device__ __forceinline__ void tile_end(int, int) {}
+  __device__ __forceinline__ void row_end(int) {}
+  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D + col);
+    const float* ar = a + col;  // noise slice: scalar loads
+#pragma unroll
+    for (int i = 0; i < CH / 4; ++i) {
+      float4 xv = xr[i];
+      xv.x += bf16_round(acc[4 * i + 0]) + coef * ar[4 * i + 0];
+      xv.y += bf16_round(acc[4 * i + 1]) + coef * ar[4 * i + 1];
+      xv.z += bf16_round(acc[4 * i + 2]) + coef * ar[4 * i + 2];
+      xv.w += bf16_round(acc[4 * i + 3]) + coef * ar[4 * i + 3];
+      xr[i] = xv;
+    }
+  }
+};
+
+// hidden = bf16(relu(bf16(acc) + sign bf16(h.b_fc) a_fc)^2), and per N tile the partial dot hidden.b_mproj
+// (the next linear's rank-1 input dot), eggroll.py:93.
+struct EpiFC {
+  static constexpr int CH = 32;
+  int T;
+  const float* sign;
+  const float* svec;
+  Slice nfc, nmp;
+  __nv_bfloat16* hidden;
+  float* pdot;  // [M, F / GEMM_BN]
+  int j;
+  float coef, pd;
+  const float* a;
+  const float* b;
+
+  __device__ __forceinline__ void row_begin(int row) {
+    j = row / T;
+    coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
+    a = nfc.A(j);
+    b = nmp.B(j);
+    pd = 0.f;
+  }
+  __device__ __forceinline__ void tile_end(int row, int nb) {
+    pdot[static_cast<int64_t>(row) * (F / GEMM_BN) + nb] = pd;
+    pd = 0.f;
+  }
+  __device__ __forceinline__ void row_end(int) {}
+  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+    uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row) * F + col);
+#pragma unroll
+    for (int i = 0; i < CH; i += 8) {
+      float r[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float u = bf16_round(acc[i + e]) + coef * a[col + i + e];
+        const float rl = fmaxf(u, 0.f);
+        r[e] = bf16_round(rl * rl);
+        pd += r[e] * bf16_round(b[col + i + e]);
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(r[0], r[1]);
+      pk.y = pack_bf16x2(r[2], r[3]);
+      pk.z = pack_bf16x2(r[4], r[5]);
+      pk.w = pack_bf16x2(r[6], r[7]);
+      out[i / 8] = pk;
+    }
+  }
+};
+
+// LM head: z = bf16(acc) + sign bf16(h.b) a; c = 15 tanh(z / 15); per row the cross-entropy
+// log sum_v exp(c_v) - c_target (eggroll.py:96-102). Since c <= 15, exp(c - 15) never overflows, so the
+// log-sum-exp needs no running maximum. tanh(y) = 1 - 2 / (exp(2|y|) + 1) keeps the absolute error ~1e-7.
+struct EpiHeadCE {
+  static constexpr int CH = 32;
+  int T;
+  const float* sign;
+  const float* svec;
+  const int64_t* targets;
+  Slice n;
+  float* ce;  // [M]
+  int j;
+  int64_t tgt;
+  float coef, sum, zt;
+  const float* a;
+
+  __device__ __forceinline__ void row_begin(int row) {
+    j = row / T;
+    const int t = row - j * T;
+    tgt = targets[t];
+    coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
+    a = n.A(j);
+    sum = 0.f;
+    zt = 0.f;
+  }
+  __device__ __forceinline__ void tile_end(int, int) {}
+  __device__ __forceinline__ void row_end(int row) { ce[row] = 15.f + logf(sum) - zt; }
+  __device__ __forceinline__ void chunk(int, int col, const float* acc) {
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const float z = bf16_round(acc[i]) + coef * a[col + i];
+      const float y = fabsf(z) * (1.f / 15.f);
+      const float th = 1.f - 2.f * rcp_approx(ex2_approx(2.f * LOG2E * y) + 1.f);
+      const float c = copysignf(15.f * th, z);
+      sum += ex2_approx((c - 15.f) * LOG2E);
+      if (col + i == tgt) zt = c;
+    }
+  }
+};
+
+// Plain fp32 store of the accumulator: D[row, col] = acc (the tcgen05 core without any fused arithmetic).
+struct EpiStore {
+  static constexpr int CH = 32;
+  float* d;
+  int ldd;
+  __device__ __forceinline__ void row_begin(int) {}
+  __device__ __forceinline__ void tile_end(int, int) {}
+  __device__ __forceinline__ void row_end(int) {}
+  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+    float4* out = reinterpret_cast<float4*>(d + static_cast<int64_t>(row) * ldd + col);
+#pragma unroll
+    for (int i = 0; i < CH / 4; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+  }
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// Windowed causal attention (mma.sync m16n8k16 bf16, FA2-style online softmax).
+// q, k, v: bf16 [m*H, T, 64]; key s visible to query t iff 0 <= t - s <= window (utils/model.py:17-21).
+// Writes y bf16 [M, 512] (row j*T + t, columns h*64 + d) and ydot[row, h] = sum_d bf16(y) bf16(b_cproj).
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int ATT_BQ = 64, ATT_BK = 64;
+
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  __nv_bfloat16* y;
+  float* ydot;
+  int T, window;
+  Slice nproj;  // c_proj noise (b used)
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][64] bf16 tile
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void load_tile_async(uint32_t sbase, const __nv_bfloat16* g, int tid) {
+  // 64 rows x 128 B = 512 16-byte chunks, 128 threads x 4
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = tid + 128 * i;
+    const int row = c >> 3, ch = c & 7;
+    cp_async16(sbase + swz(row, ch), g + row * 64 + ch * 8);
+  }
+}
+
+__global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
+  __shared__ __align__(128) uint8_t smem[ATT_BQ * 128 + 4 * ATT_BK * 128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_qt = p.T / ATT_BQ;
+  const int qt = n_qt - 1 - blockIdx.x;  // heaviest tiles first
+  const int bh = blockIdx.y;             // member * H + head
+  const int j = bh / H, hh = bh - j * H;
+  const int q0 = qt * ATT_BQ;
+  const int64_t base = static_cast<int64_t>(bh) * p.T * HD;
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK[2] = {sQ + ATT_BQ * 128, sQ + ATT_BQ * 128 + ATT_BK * 128};
+  const uint32_t sV[2] = {sQ + ATT_BQ * 128 + 2 * ATT_BK * 128, sQ + ATT_BQ * 128 + 3 * ATT_BK * 128};
+
+  const int lo = q0 - p.window > 0 ? (q0 - p.window) / ATT_BK : 0;  // window % 64 == 0
+  const int hi = q0 / ATT_BK;
+
+  load_tile_async(sQ, p.q + base + static_cast<int64_t>(q0) * HD, tid);
+  load_tile_async(sK[0], p.k + base + static_cast<int64_t>(lo) * ATT_BK * HD, tid);
+  load_tile_async(sV[0], p.v + base + static_cast<int64_t>(lo) * ATT_BK * HD, tid);
+  cp_async_commit();
+
+  float o[8][4];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  uint32_t qf[4][4];
+  const float sl2 = 0.125f * LOG2E;
+  const int r_lo = warp * 16 + (lane >> 2);  // this thread's rows within the q tile: r_lo, r_lo + 8
+
+  for (int kt = lo; kt <= hi; ++kt) {
+    const int buf = (kt - lo) & 1;
+    if (kt < hi) {
+      load_tile_async(sK[buf ^ 1], p.k + base + static_cast<int64_t>(kt + 1) * ATT_BK * HD, tid);
+      load_tile_async(sV[buf ^ 1], p.v + base + static_cast<int64_t>(kt + 1) * ATT_BK * HD, tid);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (kt == lo) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int row = warp * 16 + (lane & 15), ch = kk * 2 + (lane >> 4);
+        ldsm_x4(sQ + swz(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      }
+    }
+    // S = Q K^T: 16 rows x 64 keys per warp
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of 8-key tiles
+        const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int ch = kk * 2 + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(sK[buf] + swz(key, ch), b0, b1, b2, b3);
+        mma_bf16(s[2 * np], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+        mma_bf16(s[2 * np + 1], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b2, b3);
+      }
+    }
+    // masks: diagonal tile (key <= query) and the window's first tile (query - key <= window)
+    const bool diag = kt == hi, edge = (q0 - p.window > 0) && kt == lo;
+    if (diag || edge) {
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int rq = r_lo + ((e >> 1) << 3);
+          const int key = n * 8 + ((lane & 3) << 1) + (e & 1);
+          const int tq = q0 + rq, sk = kt * ATT_BK + key;
+          if (sk > tq || tq - sk > p.window) s[n][e] = -INFINITY;
+        }
+    }
+    // online softmax (base 2)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) mx = fmaxf(mx, fmaxf(s[n][2 * hr], s[n][2 * hr + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mnew = fmaxf(mrow[hr], mx);
+      const float msafe = mnew == -INFINITY ? 0.f : mnew;
+      const float scale = ex2_approx((mrow[hr] - msafe) * sl2);
+      mrow[hr] = mnew;
+      float rs = 0.f;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        s[n][2 * hr] = ex2_approx((s[n][2 * hr] - msafe) * sl2);
+        s[n][2 * hr + 1] = ex2_approx((s[n][2 * hr + 1] - msafe) * sl2);
+        rs += s[n][2 * hr] + s[n][2 * hr + 1];
+        o[n][2 * hr] *= scale;
+        o[n][2 * hr + 1] *= scale;
+      }
+      lrow[hr] = lrow[hr] * scale + rs;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {  // 16 keys per step
+      const uint32_t a0 = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      const uint32_t a1 = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      const uint32_t a2 = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      const uint32_t a3 = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of 8-dim tiles
+        const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int ch = np * 2 + (lane >> 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(sV[buf] + swz(key, ch), b0, b1, b2, b3);
+        mma_bf16(o[2 * np], a0, a1, a2, a3, b0, b1);
+        mma_bf16(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+
+  // epilogue: normalise, bf16, y and the c_proj rank-1 partial dot
+  float lsum[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    float l = lrow[hr];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    lsum[hr] = 1.f / l;
+  }
+  const float* bproj = p.nproj.B(j) + hh * HD;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int tq = q0 + r_lo + hr * 8;
+    const int64_t row = static_cast<int64_t>(j) * p.T + tq;
+    __nv_bfloat16* yr = p.y + row * D + hh * HD;
+    float dp = 0.f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const int d = n * 8 + ((lane & 3) << 1);
+      const float y0 = bf16_round(o[n][2 * hr] * lsum[hr]);
+      const float y1 = bf16_round(o[n][2 * hr + 1] * lsum[hr]);
+      *reinterpret_cast<uint32_t*>(yr + d) = pack_bf16x2(y0, y1);
+      dp += y0 * bf16_round(bproj[d]) + y1 * bf16_round(bproj[d + 1]);
+    }
+    dp += __shfl_xor_sync(0xffffffffu, dp, 1);
+    dp += __shfl_xor_sync(0xffffffffu, dp, 2);
+    if ((lane & 3) == 0) p.ydot[row * H + hh] = dp;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Per-member reduction of the per-row cross-entropy (fixed order: deterministic).
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) member_reduce_kernel(const float* ce, int T, float scale, float* out) {
+  __shared__ float part[8];
+  const int j = blockIdx.x;
+  float s = 0.f;
+  for (int t = threadIdx.x; t < T; t += 256) s += ce[static_cast<int64_t>(j) * T + t];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < 8; ++w) tot += part[w];
+    out[j] = tot * scale;
+  }
+}
+
+__global__ void pack_bf16_kernel(const float4* __restrict__ src, uint2* __restrict__ dst, int64_t n4) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = src[i];
+    dst[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
+}
+
+__global__ void clear_status_kernel(int* status) { *status = 0; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 row-major [outer, inner] tensor, box [box_outer, 64] with 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return NOISE_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(GEMM_BK), box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+static thread_local int g_launches = 0;
+
+template <class Epi>
+static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi& epi, int* status, cudaStream_t s) {
+  using L = GemmLayout<GEMM_BN, GEMM_STAGES>;
+  if (M % GEMM_BM || N % GEMM_BN || K % GEMM_BK) return NOISE_ERR_SHAPE;
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, A, K, M, GEMM_BM);
+  if (rc) return rc;
+  rc = make_map(&mb, B, K, N, GEMM_BN);
+  if (rc) return rc;
+  auto kern = gemm_bf16_tn_kernel<GEMM_BN, GEMM_STAGES, Epi>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+    return NOISE_ERR_CUDA;
+  const int m_tiles = M / GEMM_BM;
+  int sms = sm_count();
+  if (sms <= 0) return NOISE_ERR_CUDA;
+  const int grid = m_tiles < sms ? m_tiles : sms;
+  kern<<<grid, GEMM_THREADS, L::SMEM_BYTES, s>>>(ma, mb, m_tiles, N / GEMM_BN, K / GEMM_BK, epi, status);
+  ++g_launches;
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+struct Workspace {
+  int* status;
+  float* x;
+  __nv_bfloat16 *h, *q, *k, *v, *y, *hidden;
+  float *svec, *gate, *ydot, *pdot, *ce;
+  size_t bytes;
+};
+
+static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+static Workspace carve(void* ws, int64_t M) {
+  Workspace w{};
+  size_t off = NOISE_STATUS_BYTES;
+  auto take = [&](size_t n) {
+    void* p = ws ? static_cast<uint8_t*>(ws) + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  w.status = static_cast<int*>(ws);
+  w.x = static_cast<float*>(take(M * D * 4));
+  w.h = static_cast<__nv_bfloat16*>(take(M * D * 2));
+  w.q = static_cast<__nv_bfloat16*>(take(M * D * 2));
+  w.k = static_cast<__nv_bfloat16*>(take(M * D * 2));
+  w.v = static_cast<__nv_bfloat16*>(take(M * D * 2));
+  w.y = static_cast<__nv_bfloat16*>(take(M * D * 2));
+  w.hidden = static_cast<__nv_bfloat16*>(take(M * F * 2));
+  w.svec = static_cast<float*>(take(M * 4 * 4));
+  w.gate = static_cast<float*>(take(M * H * 4));
+  w.ydot = static_cast<float*>(take(M * H * 4));
+  w.pdot = static_cast<float*>(take(M * (F / GEMM_BN) * 4));
+  w.ce = static_cast<float*>(take(M * 4));
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace noise
+
+using namespace noise;
+
+extern "C" {
+
+int noise_param_index(int block, int which) {
+  if (block < 0 || block >= NOISE_N_LAYER) return -1;
+  if (which == NOISE_P_VE) return (block & 1) ? 56 + block / 2 : -1;
+  if (which == NOISE_P_VEGATE && !(block & 1)) return -1;
+  int idx = 3;  // first block tensor
+  for (int b = 0; b < block; ++b) idx += (b & 1) ? 7 : 6;
+  static const int even[7] = {0, 1, 2, 3, -1, 4, 5};
+  static const int odd[7] = {0, 1, 2, 3, 4, 5, 6};
+  const int k = (block & 1) ? odd[which] : even[which];
+  return k < 0 ? -1 : idx + k;
+}
+
+size_t noise_population_workspace_bytes(int members, int tokens) {
+  if (members < 1 || tokens < 1) return 0;
+  return carve(nullptr, static_cast<int64_t>(members) * tokens).bytes;
+}
+
+int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, const float* sign, const int64_t* idx,
+                          const int64_t* targets, int members, int tokens, int reduction, float* losses,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model || !nz || !sign || !idx || !targets || !losses) return NOISE_ERR_ARGUMENT;
+  if (reduction != NOISE_REDUCTION_MEAN && reduction != NOISE_REDUCTION_SUM) return NOISE_ERR_ARGUMENT;
+  if (members < 1 || tokens < GEMM_BM || tokens > 2048 || tokens % GEMM_BM) return NOISE_ERR_SHAPE;
+  const int64_t M = static_cast<int64_t>(members) * tokens;
+  if (M > (int64_t(1) << 31) / F) return NOISE_ERR_SHAPE;
+  const Workspace w = carve(workspace, M);
+  if (!workspace || workspace_bytes < w.bytes) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  for (int l = 0; l < NOISE_N_LAYER; ++l) {
+    if (!model->wqkv[l] || !model->wproj[l] || !model->wfc[l] || !model->wmproj[l]) return NOISE_ERR_ARGUMENT;
+    if ((l & 1) && (!model->wgate[l] || !model->ve[l])) return NOISE_ERR_ARGUMENT;
+  }
+  if (!model->whead || !model->wte || !model->resid_lambdas || !model->x0_lambdas || !model->cos || !model->sin)
+    return NOISE_ERR_ARGUMENT;
+  int dev = 0, major = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return NOISE_ERR_DEVICE;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int T = tokens, Mi = static_cast<int>(M);
+  g_launches = 0;
+  int rc;
+  if (cudaMemsetAsync(w.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  const int norm_blocks = static_cast<int>((M * 32 + 255) / 256);
+
+  for (int l = 0; l < NOISE_N_LAYER; ++l) {
+    const bool ve = l & 1;
+    NormArgs na{};
+    na.layer = l;
+    na.T = T;
+    na.M = Mi;
+    na.idx = idx;
+    na.sign = sign;
+    na.x = w.x;
+    na.h = w.h;
+    na.svec = w.svec;
+    na.gate = w.gate;
+    na.wte = model->wte;
+    na.n_wte = to_slice(nz[NOISE_PARAM_WTE]);
+    na.n_resid = to_slice(nz[NOISE_PARAM_RESID]);
+    na.n_x0 = to_slice(nz[NOISE_PARAM_X0]);
+    na.resid_l = model->resid_lambdas;
+    na.x0_l = model->x0_lambdas;
+    na.nb0 = to_slice(nz[noise_param_index(l, NOISE_P_CQ)]);
+    na.nb1 = to_slice(nz[noise_param_index(l, NOISE_P_CK)]);
+    na.nb2 = to_slice(nz[noise_param_index(l, NOISE_P_CV)]);
+    na.wgate = ve ? model->wgate[l] : nullptr;
+    if (ve) na.n_gate = to_slice(nz[noise_param_index(l, NOISE_P_VEGATE)]);
+    norm_kernel<NORM_BLOCK><<<norm_blocks, 256, 0, s>>>(na);
+    ++g_launches;
+
+    EpiQKV eq{};
+    eq.T = T;
+    eq.sign = sign;
+    eq.svec = w.svec;
+    eq.gate = ve ? w.gate : nullptr;
+    eq.idx = idx;
+    eq.cosb = static_cast<const __nv_bfloat16*>(model->cos);
+    eq.sinb = static_cast<const __nv_bfloat16*>(model->sin);
+    eq.vew = ve ? model->ve[l] : nullptr;
+    eq.nq = na.nb0;
+    eq.nk = na.nb1;
+    eq.nv = na.nb2;
+    if (ve) eq.nve = to_slice(nz[noise_param_index(l, NOISE_P_VE)]);
+    eq.q = w.q;
+    eq.k = w.k;
+    eq.v = w.v;
+    if ((rc = run_gemm(w.h, Mi, D, model->wqkv[l], 3 * D, eq, w.status, s))) return rc;
+
+    AttnArgs aa{};
+    aa.q = w.q;
+    aa.k = w.k;
+    aa.v = w.v;
+    aa.y = w.y;
+    aa.ydot = w.ydot;
+    aa.T = T;
+    aa.window = (l % 4 == 3 || l == NOISE_N_LAYER - 1) ? 2048 : 1024;  // SSSL, last block L
+    aa.nproj = to_slice(nz[noise_param_index(l, NOISE_P_CPROJ)]);
+    attention_kernel<<<dim3(T / ATT_BQ, members * H), 128, 0, s>>>(aa);
+    ++g_launches;
+
+    EpiResid er{};
+    er.T = T;
+    er.nparts = H;
+    er.sign = sign;
+    er.parts = w.ydot;
+    er.n = aa.nproj;
+    er.x = w.x;
+    if ((rc = run_gemm(w.y, Mi, D, model->wproj[l], D, er, w.status, s))) return rc;
+
+    NormArgs nm = na;
+    nm.nb0 = to_slice(nz[noise_param_index(l, NOISE_P_CFC)]);
+    norm_kernel<NORM_MID><<<norm_blocks, 256, 0, s>>>(nm);
+    ++g_launches;
+
+    EpiFC ef{};
+    ef.T = T;
+    ef.sign = sign;
+    ef.svec = w.svec;
+    ef.nfc = nm.nb0;
+    ef.nmp = to_slice(nz[noise_param_index(l, NOISE_P_MPROJ)]);
+    ef.hidden = w.hidden;
+    ef.pdot = w.pdot;
+    if ((rc = run_gemm(w.h, Mi, D, model->wfc[l], F, ef, w.status, s))) return rc;
+
+    EpiResid em{};
+    em.T = T;
+    em.nparts = F / GEMM_BN;
+    em.sign = sign;
+    em.parts = w.pdot;
+    em.n = ef.nmp;
+    em.x = w.x;
+    if ((rc = run_gemm(w.hidden, Mi, F, model->wmproj[l], D, em, w.status, s))) return rc;
+  }
+
+  NormArgs nf{};
+  nf.T = T;
+  nf.M = Mi;
+  nf.idx = idx;
+  nf.sign = sign;
+  nf.x = w.x;
+  nf.h = w.h;
+  nf.svec = w.svec;
+  nf.nb0 = to_slice(nz[NOISE_PARAM_HEAD]);
+  norm_kernel<NORM_FINAL><<<norm_blocks, 256, 0, s>>>(nf);
+  ++g_launches;
+
+  EpiHeadCE eh{};
+  eh.T = T;
+  eh.sign = sign;
+  eh.svec = w.svec;
+  eh.targets = targets;
+  eh.n = nf.nb0;
+  eh.ce = w.ce;
+  if ((rc = run_gemm(w.h, Mi, D, model->whead, V, eh, w.status, s))) return rc;
+
+  member_reduce_kernel<<<members, 256, 0, s>>>(w.ce, T, reduction == NOISE_REDUCTION_MEAN ? 1.f / T : 1.f, losses);
+  ++g_launches;
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace,
+                       void* stream) {
+  if (!a || !b || !d || !workspace) return NOISE_ERR_ARGUMENT;
+  if (m <= 0 || n <= 0 || k <= 0 || m % GEMM_BM || n % GEMM_BN || k % GEMM_BK) return NOISE_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(d) & 15) return NOISE_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  g_launches = 0;
+  EpiStore e{d, n};
+  return run_gemm(a, m, k, b, n, e, static_cast<int*>(workspace), s);
+}
+
+int noise_pack_bf16(const float* src, void* dst, int64_t n, void* stream) {
+  if (!src || !dst || n < 0) return NOISE_ERR_ARGUMENT;
+  if (n % 8 || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return NOISE_ERR_ALIGN;
+  if (n == 0) return NOISE_OK;
+  const int64_t n4 = n / 4;
+  int blocks = static_cast<int>((n4 + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  pack_bf16_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<const float4*>(src),
+                                                                           static_cast<uint2*>(dst), n4);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_read_status(const void* workspace, int* status, void* stream) {
+  if (!workspace || !status) return NOISE_ERR_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(status, workspace, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return NOISE_ERR_CUDA;
+  return cudaStreamSynchronize(s) == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_clear_status(void* workspace, void* stream) {
+  if (!workspace) return NOISE_ERR_ARGUMENT;
+  clear_status_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int*>(workspace));
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+const char* noise_status_string(int status) {
+  switch (status) {
+    case NOISE_OK: return "ok";
+    case NOISE_ERR_SHAPE: return "unsupported shape";
+    case NOISE_ERR_ALIGN: return "misaligned pointer or stride";
+    case NOISE_ERR_WORKSPACE: return "workspace missing or too small";
+    case NOISE_ERR_ARGUMENT: return "invalid argument";
+    case NOISE_ERR_CUDA: return "CUDA call failed";
+    case NOISE_ERR_DEVICE: return "not an sm_100 device";
+    default: return "unknown status";
+  }
+}
+
+int noise_last_launch_count(void) { return g_launches; }
+
+}  // extern "C"

@@ -1,0 +1,208 @@
+"""Drop-in population-perturbed forward (the hot path of EGGROLL, reference archive/10M/train/val/eggroll.py).
+
+``population_loss(model, p, noise, sign, idx, targets)`` has the reference's signature and meaning
+(eggroll.py:66-103): the cross-entropy of m rank-1-perturbed copies of the fixed GPT on one token row, one value per
+member, computed as under ``torch.autocast('cuda', torch.bfloat16)``. The work runs in libnoise_b200.so
+(tcgen05 GEMMs with the rank-1 term fused into their epilogues, windowed attention, LM head fused with the softcap and
+cross-entropy); this module only packs the weights, describes the noise slices and calls the C ABI.
+
+``population_loss_offsets`` is the same forward fed straight from EGGROLL's fixed noise buffer and per-step offsets
+(eggroll.py:114-128): member j of parameter P reads buffer[offsets[P, direction_j] : ... + out + in] in place, so the
+reference's ``noise()`` gather and ``repeat_interleave`` copies (eggroll.py:141-142) disappear.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+N_LAYER, N_HEAD, HEAD_DIM, N_EMBD, VOCAB = 8, 8, 64, 512, 4096
+WINDOWS = [1024, 1024, 1024, 2048, 1024, 1024, 1024, 2048]
+
+
+def has_ve(i):
+    return i % 2 == (N_LAYER - 1) % 2
+
+
+def param_shapes():
+    """(name, shape) in the reference GPT's named_parameters() order (utils/model.py:123-147)."""
+    out = [('resid_lambdas', (N_LAYER,)), ('x0_lambdas', (N_LAYER,)), ('transformer.wte.weight', (VOCAB, N_EMBD))]
+    for i in range(N_LAYER):
+        pre = f'transformer.h.{i}.'
+        out += [(pre + f'attn.{n}.weight', (N_EMBD, N_EMBD)) for n in ('c_q', 'c_k', 'c_v', 'c_proj')]
+        if has_ve(i):
+            out.append((pre + 'attn.ve_gate.weight', (N_HEAD, 32)))
+        out += [(pre + 'mlp.c_fc.weight', (4 * N_EMBD, N_EMBD)), (pre + 'mlp.c_proj.weight', (N_EMBD, 4 * N_EMBD))]
+    out.append(('lm_head.weight', (VOCAB, N_EMBD)))
+    out += [(f'value_embeds.{i}.weight', (VOCAB, N_EMBD)) for i in range(N_LAYER) if has_ve(i)]
+    return out
+
+
+PARAMS = param_shapes()
+NAMES = [n for n, _ in PARAMS]
+INDEX = {n: i for i, n in enumerate(NAMES)}
+
+
+def rotary_tables(length, device, base=10000):
+    """bf16 cos, sin [length, 32] as utils/model.py:177-183 computes them on ``device``."""
+    inv_freq = 1.0 / base ** (torch.arange(0, HEAD_DIM, 2, dtype=torch.float32, device=device) / HEAD_DIM)
+    t = torch.arange(length, dtype=torch.float32, device=device)
+    freqs = torch.outer(t, inv_freq)
+    return freqs.cos().bfloat16().contiguous(), freqs.sin().bfloat16().contiguous()
+
+
+class PackedGPT:
+    """The weights as the C ABI consumes them (noise_gpt_t): matrices packed to bf16 once, embeddings fp32.
+
+    ``refresh()`` re-packs only when a source tensor changed (new storage or an in-place update)."""
+
+    def __init__(self, params, device=None, cos=None, sin=None):
+        self.params = params
+        self.device = torch.device(device) if device is not None else params['lm_head.weight'].device
+        self._key = None
+        self._cos, self._sin = cos, sin
+        self.refresh()
+
+    def _source_key(self):
+        return tuple((t.data_ptr(), t._version) for t in (self.params[n] for n in NAMES))
+
+    def _pack(self, dst, src):
+        src = src.detach().float().contiguous()
+        _lib.check(_lib.lib().noise_pack_bf16(src.data_ptr(), dst.data_ptr(), src.numel(),
+                                              _lib.stream_handle(self.device)), 'noise_pack_bf16')
+
+    def refresh(self):
+        key = self._source_key()
+        if key == self._key:
+            return self
+        p, dev = self.params, self.device
+        for t in p.values():
+            _lib.require_cuda(t)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.wqkv, self.wproj, self.wfc, self.wmproj, self.wgate, self.ve = [], [], [], [], [], []
+        for i in range(N_LAYER):
+            pre = f'transformer.h.{i}.'
+            qkv = torch.empty((3 * N_EMBD, N_EMBD), **bf)
+            for k, n in enumerate(('c_q', 'c_k', 'c_v')):
+                self._pack(qkv[k * N_EMBD:(k + 1) * N_EMBD], p[pre + f'attn.{n}.weight'])
+            proj = torch.empty((N_EMBD, N_EMBD), **bf)
+            self._pack(proj, p[pre + 'attn.c_proj.weight'])
+            fc = torch.empty((4 * N_EMBD, N_EMBD), **bf)
+            self._pack(fc, p[pre + 'mlp.c_fc.weight'])
+            mproj = torch.empty((N_EMBD, 4 * N_EMBD), **bf)
+            self._pack(mproj, p[pre + 'mlp.c_proj.weight'])
+            self.wqkv.append(qkv)
+            self.wproj.append(proj)
+            self.wfc.append(fc)
+            self.wmproj.append(mproj)
+            self.wgate.append(p[pre + 'attn.ve_gate.weight'].detach().float().contiguous() if has_ve(i) else None)
+            self.ve.append(p[f'value_embeds.{i}.weight'].detach().float().contiguous() if has_ve(i) else None)
+        self.whead = torch.empty((VOCAB, N_EMBD), **bf)
+        self._pack(self.whead, p['lm_head.weight'])
+        self.wte = p['transformer.wte.weight'].detach().float().contiguous()
+        self.resid = p['resid_lambdas'].detach().float().contiguous()
+        self.x0 = p['x0_lambdas'].detach().float().contiguous()
+        if self._cos is None:
+            self._cos, self._sin = rotary_tables(2048, dev)
+        s = _lib.GPT()
+        for i in range(N_LAYER):
+            s.wqkv[i], s.wproj[i] = self.wqkv[i].data_ptr(), self.wproj[i].data_ptr()
+            s.wfc[i], s.wmproj[i] = self.wfc[i].data_ptr(), self.wmproj[i].data_ptr()
+            s.wgate[i] = self.wgate[i].data_ptr() if self.wgate[i] is not None else None
+            s.ve[i] = self.ve[i].data_ptr() if self.ve[i] is not None else None
+        s.whead, s.wte = self.whead.data_ptr(), self.wte.data_ptr()
+        s.resid_lambdas, s.x0_lambdas = self.resid.data_ptr(), self.x0.data_ptr()
+        s.cos, s.sin = self._cos.data_ptr(), self._sin.data_ptr()
+        self.struct = s
+        self._key = key
+        return self
+
+
+_packed = {}
+
+
+def _packed_for(model, p):
+    key = id(p)
+    cached = _packed.get(key)
+    if cached is None or cached.params is not p:
+        cos = sin = None
+        if model is not None and hasattr(model, 'cos'):
+            cos = model.cos.reshape(-1, HEAD_DIM // 2)[:2048].contiguous()
+            sin = model.sin.reshape(-1, HEAD_DIM // 2)[:2048].contiguous()
+        _packed.clear()
+        cached = _packed[key] = PackedGPT(p, cos=cos, sin=sin)
+    return cached.refresh()
+
+
+def _run(packed, slices, keep, sign, idx, targets, reduction):
+    dev = packed.device
+    sign = sign.detach().float().contiguous()
+    idx = idx.detach().long().contiguous()
+    targets = targets.detach().long().contiguous()
+    _lib.require_cuda(sign, idx, targets)
+    m, length = sign.shape[0], idx.shape[0]
+    if targets.shape[0] != length:
+        raise ValueError('idx and targets must have the same length')
+    L = _lib.lib()
+    nbytes = L.noise_population_workspace_bytes(m, length)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    losses = torch.empty(m, dtype=torch.float32, device=dev)
+    arr = (_lib.Slice * len(NAMES))(*slices)
+    rc = L.noise_population_loss(ctypes.byref(packed.struct), arr, sign.data_ptr(), idx.data_ptr(),
+                                 targets.data_ptr(), m, length, _lib.REDUCTION[reduction], losses.data_ptr(),
+                                 ws.data_ptr(), nbytes, _lib.stream_handle(dev))
+    _lib.check(rc, 'noise_population_loss')
+    losses._noise_workspace = ws  # keeps the scratch (and its status word) alive with the result
+    del keep
+    return losses
+
+
+def population_loss(model, p, noise, sign, idx, targets, reduction='mean'):
+    """Mean (or summed) cross-entropy [m] of m perturbed models on one sequence (eggroll.py:66-103).
+
+    model: the reference GPT module (its RoPE tables are used when present) or None; p: parameter name -> tensor;
+    noise: name -> (a [m, out], b [m, in]) for matrices and embeddings, eps [m, numel] for the mixing scalars;
+    sign [m] (+-sigma); idx, targets [T] int64 with T % 128 == 0."""
+    packed = _packed_for(model, p)
+    slices, keep = [], []
+    for name in NAMES:
+        v = noise[name]
+        if isinstance(v, (tuple, list)):
+            a, b = (t.detach().float() for t in v)
+            if a.stride(-1) != 1 or b.stride(-1) != 1:
+                a, b = a.contiguous(), b.contiguous()
+            _lib.require_cuda(a, b)
+            keep += [a, b]
+            slices.append(_lib.Slice(a.data_ptr(), b.data_ptr(), None, a.stride(0), b.stride(0)))
+        else:
+            e = v.detach().float()
+            if e.stride(-1) != 1:
+                e = e.contiguous()
+            _lib.require_cuda(e)
+            keep.append(e)
+            slices.append(_lib.Slice(e.data_ptr(), e.data_ptr(), None, e.stride(0), e.stride(0)))
+    return _run(packed, slices, keep, sign, idx, targets, reduction)
+
+
+def member_offsets(offsets, directions):
+    """int64 [60, m]: offsets [60, pairs] (one row per parameter, named_parameters order) gathered at the members'
+    directions."""
+    return offsets.index_select(1, directions.to(offsets.device)).contiguous()
+
+
+def population_loss_offsets(packed, buffer, member_off, sign, idx, targets, reduction='mean'):
+    """population_loss with every member's (a, b) read in place from the fixed noise buffer: member j of parameter P
+    uses a = buffer[off : off + out], b = buffer[off + out : off + out + in] with off = member_off[P, j]
+    (eggroll.py:122-128). member_off: int64 [60, m] device tensor (``member_offsets``)."""
+    packed = packed.refresh()
+    _lib.require_cuda(buffer, member_off)
+    if buffer.dtype != torch.float32 or member_off.dtype != torch.int64 or member_off.shape[0] != len(NAMES):
+        raise ValueError('buffer must be fp32 and member_off int64 [60, m]')
+    member_off = member_off.contiguous()
+    base = buffer.data_ptr()
+    slices = []
+    for k, (name, shape) in enumerate(PARAMS):
+        off = member_off[k].data_ptr()
+        out = shape[0] if len(shape) == 2 else 0
+        slices.append(_lib.Slice(base, base + 4 * out, off, 0, 0))
+    return _run(packed, slices, [member_off, buffer], sign, idx, targets, reduction)

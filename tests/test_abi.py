@@ -1,0 +1,79 @@
+"""The C ABI without a GPU: the library loads, exports every entry point include/noise_b200.h declares, and rejects
+bad arguments before touching the device."""
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / 'include' / 'noise_b200.h'
+
+
+def declared():
+    text = HEADER.read_text()
+    text = re.sub(r'/\*.*?\*/', '', text, flags=re.S)
+    return sorted(set(re.findall(r'\b(noise_[a-z0-9_]+)\s*\(', text)))
+
+
+@pytest.fixture(scope='module')
+def L():
+    from noise_b200 import _lib
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(L):
+    names = declared()
+    assert 'noise_population_loss' in names
+    for name in names:
+        assert hasattr(L, name), name
+
+
+def test_bindings_cover_header():
+    from noise_b200 import _lib
+    assert sorted(n for n, _, _ in _lib.SIGNATURES) == declared()
+
+
+def test_param_index_matches_named_parameters(L):
+    from noise_b200.population import INDEX, N_LAYER, has_ve
+    kinds = {0: 'attn.c_q', 1: 'attn.c_k', 2: 'attn.c_v', 3: 'attn.c_proj', 4: 'attn.ve_gate', 5: 'mlp.c_fc',
+             6: 'mlp.c_proj'}
+    for block in range(N_LAYER):
+        for which, kind in kinds.items():
+            got = L.noise_param_index(block, which)
+            name = f'transformer.h.{block}.{kind}.weight'
+            assert got == INDEX.get(name, -1), (block, kind)
+        assert L.noise_param_index(block, 7) == (INDEX[f'value_embeds.{block}.weight'] if has_ve(block) else -1)
+    assert INDEX['lm_head.weight'] == 55 and INDEX['transformer.wte.weight'] == 2
+
+
+def test_param_order_matches_oracle():
+    from noise_b200.population import PARAMS
+    from oracle import gpt
+    assert PARAMS == gpt.param_shapes()
+
+
+def test_workspace_size(L):
+    small = L.noise_population_workspace_bytes(1, 128)
+    big = L.noise_population_workspace_bytes(4, 2048)
+    assert 0 < small < big
+    assert L.noise_population_workspace_bytes(0, 128) == 0
+
+
+def test_rejects_bad_shapes_before_launch(L):
+    from noise_b200 import _lib
+    gpt = _lib.GPT()
+    slices = (_lib.Slice * 60)()
+    fake = 256  # never dereferenced: validation fails first
+    args = (ctypes.byref(gpt), slices, fake, fake, fake)
+    assert L.noise_population_loss(*args, 4, 100, 0, fake, fake, 1 << 30, None) == 1   # T % 128
+    assert L.noise_population_loss(*args, 4, 4096, 0, fake, fake, 1 << 30, None) == 1  # T > 2048
+    assert L.noise_population_loss(*args, 0, 128, 0, fake, fake, 1 << 30, None) == 1   # no members
+    assert L.noise_population_loss(*args, 4, 128, 7, fake, fake, 1 << 30, None) == 4   # reduction
+    assert L.noise_population_loss(*args, 4, 128, 0, fake, fake, 16, None) == 3        # workspace too small
+    assert L.noise_status_string(3) == b'workspace missing or too small'
+
+
+def test_product_path_has_no_oracle_import():
+    for path in (ROOT / 'noise_b200').rglob('*.py'):
+        assert 'oracle' not in path.read_text(), path

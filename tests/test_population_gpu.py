@@ -1,0 +1,106 @@
+"""Parity of the CUDA population-perturbed forward with the CPU oracle (bf16 autocast rounding points) and with the
+reference's own outputs (tests/golden/population_T*.pt).
+
+Tolerance: per-member mean cross-entropy within 2e-3 relative of the oracle. The CUDA path rounds q, k, v to bf16
+before attention where the reference attends in fp32; everything else follows the autocast rounding points."""
+import pytest
+import torch
+
+from oracle import eggroll, gpt
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
+RTOL = 2e-3
+
+
+def _case(members, length, seed=0, n_noise=2 ** 20, pairs=None):
+    pairs = pairs or members // 2
+    shapes = gpt.param_shapes()
+    w = gpt.init_weights(0, eggroll=True)
+    buf = eggroll.make_buffer(n_noise, seed=0)
+    offs = eggroll.offsets(shapes, pairs, step=seed + 1, n_noise=n_noise)
+    directions = torch.arange(members) // 2 % pairs
+    nz = eggroll.noise(buf, offs, directions, shapes)
+    sign = torch.where(torch.arange(members) % 2 == 0, eggroll.SIGMA, -eggroll.SIGMA)
+    tokens = gpt.zipf_tokens(1, length + 1, seed=seed + 1)[0]
+    return w, buf, offs, directions, nz, sign, tokens[:-1], tokens[1:]
+
+
+def _to(d):
+    return {k: (tuple(t.to(DEV) for t in v) if isinstance(v, tuple) else v.to(DEV)) for k, v in d.items()}
+
+
+def _gpu(w, nz, sign, idx, tgt, reduction='mean'):
+    import noise_b200
+    out = noise_b200.population_loss(None, _to(w), _to(nz), sign.to(DEV), idx.to(DEV), tgt.to(DEV), reduction)
+    torch.cuda.synchronize()
+    assert noise_b200._lib.read_status(out._noise_workspace) == 0
+    return out.cpu()
+
+
+@pytest.mark.parametrize('members,length', [(4, 128), (4, 256), (2, 1024)])
+def test_matches_oracle_autocast(members, length):
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(members, length)
+    ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
+    got = _gpu(w, nz, sign, idx, tgt)
+    torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
+
+
+def test_full_length_window_matches_oracle():
+    """T = 2048: the S layers' 1024-token window binds."""
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(2, 2048)
+    ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
+    torch.testing.assert_close(_gpu(w, nz, sign, idx, tgt), ref, rtol=RTOL, atol=0)
+
+
+@pytest.mark.parametrize('length', [256, 2048])
+def test_matches_reference_golden(golden, length):
+    """Against the reference's own population_loss outputs (fp32 CPU run and CPU bf16 autocast run)."""
+    g = golden(f'population_T{length}.pt')
+    shapes = gpt.param_shapes()
+    w = gpt.init_weights(0, eggroll=True)
+    buf = eggroll.make_buffer(g['noise_size'], seed=0)
+    nz = eggroll.noise(buf, g['offsets'], g['directions'], shapes)
+    sign = torch.tensor([g['sigma'], -g['sigma']]).repeat(g['pairs'])
+    tokens = g['tokens'].long()
+    got = _gpu(w, nz, sign, tokens[:-1], tokens[1:])
+    torch.testing.assert_close(got, g['loss_autocast'], rtol=RTOL, atol=0)
+    torch.testing.assert_close(got, g['loss_fp32'], rtol=RTOL, atol=0)
+
+
+def test_sum_reduction_is_mean_times_length():
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(2, 256)
+    mean = _gpu(w, nz, sign, idx, tgt, 'mean')
+    total = _gpu(w, nz, sign, idx, tgt, 'sum')
+    torch.testing.assert_close(total, mean * 256, rtol=1e-5, atol=0)
+
+
+def test_offsets_path_is_bit_identical_to_materialised_noise():
+    import noise_b200
+    from noise_b200.population import PackedGPT, member_offsets
+    members, length = 6, 256
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(members, length, pairs=3)
+    dict_path = _gpu(w, nz, sign, idx, tgt)
+    packed = PackedGPT({k: v.to(DEV) for k, v in w.items()})
+    table = torch.stack([offs[n] for n, _ in gpt.param_shapes()]).to(DEV)
+    got = noise_b200.population_loss_offsets(packed, buf.to(DEV), member_offsets(table, directions.to(DEV)),
+                                             sign.to(DEV), idx.to(DEV), tgt.to(DEV)).cpu()
+    assert torch.equal(got, dict_path)
+
+
+def test_members_are_independent():
+    """A member's loss does not depend on which other members share the launch (row-independent kernels)."""
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(4, 256)
+    full = _gpu(w, nz, sign, idx, tgt)
+    sub = {k: (tuple(t[2:] for t in v) if isinstance(v, tuple) else v[2:]) for k, v in nz.items()}
+    part = _gpu(w, sub, sign[2:], idx, tgt)
+    assert torch.equal(full[2:], part)
+
+
+def test_antithetic_fitness_tracks_oracle():
+    """The fitness l(-) - l(+) that drives the update agrees with the oracle's in sign and size."""
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(16, 256, pairs=8)
+    ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
+    got = _gpu(w, nz, sign, idx, tgt)
+    fr, fg = ref[1::2] - ref[0::2], got[1::2] - got[0::2]
+    assert torch.corrcoef(torch.stack([fr, fg]))[0, 1] > 0.95
