@@ -1,0 +1,309 @@
+"""Benchmark of the population-perturbed forward (BASELINE config 2 per GPU).
+
+One step = one population evaluation on every rank: 512 antithetic members (256 pairs, sigma 1e-3) of the fixed
+37.7M GPT (random init of utils/model.py's architecture, EGGROLL's make_model), each member scoring 8 rows x 2048
+synthetic Zipf(1.1) tokens (summed cross-entropy = its fitness), the rank-1 noise read in place from EGGROLL's
+2**28-value N(0, 1) buffer at the step's offsets, then the NCCL all-gather of the fitness vector (N > 1). Ranks hold
+disjoint members of one population of 512 N (weak scaling). The unit of work is a population forward: one member
+over one 2048-token row (BASELINE.md's "population forwards/s").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
+fp32, all host threads) on a bounded sample of the same workload, rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = 'train tokens/sec at pop 24k on 1/2/4/8 B200; population forwards/sec/GPU'
+UNIT = 'population forwards/s (one member x one 2048-token row, all GPUs)'
+MEMBERS, ROWS, T, SIGMA = 512, 8, 2048, 1e-3
+FLOP_PER_MEMBER_TOKEN = 68.3e6  # algorithmic forward FLOPs per member-token (linears + attention)
+CPU_SAMPLE_MEMBERS, CPU_SAMPLE_T = 2, 2048
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=5)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    return ap.parse_args()
+
+
+def zipf_rows(rows, length, seed):
+    p = torch.arange(1, 4097, dtype=torch.float64) ** -1.1
+    g = torch.Generator().manual_seed(seed)
+    return torch.multinomial((p / p.sum()).float(), rows * length, replacement=True, generator=g).view(rows, length)
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# window attention pair counts (for the algorithmic FLOPs of the attention kernel)
+# ------------------------------------------------------------------------------------------------------------------
+def visible_pairs(length, window):
+    return sum(min(t, window) + 1 for t in range(length))
+
+
+WINDOWS = [1024, 1024, 1024, 2048, 1024, 1024, 1024, 2048]
+
+
+def kernel_work(kind, members, length):
+    """(algorithmic FLOPs, algorithmic HBM bytes) of ONE launch of a kernel kind on members x length rows."""
+    M = members * length
+    gemm = {'gemm_qkv': (512, 1536), 'gemm_cproj': (512, 512), 'gemm_cfc': (512, 2048), 'gemm_mproj': (2048, 512),
+            'gemm_head_ce': (512, 4096)}
+    if kind in gemm:
+        k, n = gemm[kind]
+        return 2.0 * M * n * k, None
+    if kind == 'attention':
+        pairs = sum(visible_pairs(length, w) for w in WINDOWS) / len(WINDOWS)
+        return 4.0 * 64 * pairs * members * 8, None
+    return None, None
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) of this GPU while the timed region runs."""
+
+    def __init__(self, device):
+        self.samples, self.proc = [], None
+        try:
+            ident = 'GPU-' + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            ident = str(device.index)
+        q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+             'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+             'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={q}', '--format=csv,noheader,nounits',
+                                          '-lms', '200', '-i', ident], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        sm, mx, reasons = [], [], set()
+        for s in self.samples:
+            try:
+                sm.append(float(s[1]))
+                mx.append(float(s[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, s[5:9]):
+                if val.lower().startswith('active'):
+                    reasons.add(name)
+        load = [c for c in sm if mx and c > 0.3 * max(mx)] or sm
+        return {'sm_mhz': statistics.median(load) if load else None, 'sm_max_mhz': max(mx) if mx else None,
+                'reasons': sorted(reasons), 'samples': len(self.samples)}
+
+
+def cpu_reference_sample(threads):
+    """Seconds for the oracle restatement of eggroll.population_loss (fp32, CPU) on CPU_SAMPLE_MEMBERS members x
+    CPU_SAMPLE_T tokens."""
+    from oracle import eggroll as oe, gpt as og  # the CPU baseline leg only
+    torch.set_num_threads(threads)
+    w = og.init_weights(0, eggroll=True)
+    buf = oe.make_buffer(2 ** 20, seed=0)
+    shapes = og.param_shapes()
+    offs = oe.offsets(shapes, 1, step=1, n_noise=2 ** 20)
+    nz = oe.noise(buf, offs, torch.tensor([0, 0]), shapes)
+    sign = torch.tensor([SIGMA, -SIGMA])
+    tok = zipf_rows(1, CPU_SAMPLE_T + 1, seed=0)[0]
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        oe.population_loss(w, nz, sign, tok[:-1], tok[1:], reduction='sum')
+    return time.perf_counter() - t0
+
+
+def run_reference(a):
+    rank = int(os.environ.get('RANK', 0))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048  # population forwards per sample
+    for _ in range(a.warmup):
+        cpu_reference_sample(threads)
+    times = [cpu_reference_sample(threads) for _ in range(a.steps)]
+    value = per * len(times) / sum(times)
+    sample = (f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of the fp32 population forward per step '
+              f'(oracle restatement of eggroll.population_loss, dense attention)')
+    print(json.dumps({
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': a.gpus, 'steps': a.steps,
+        'warmup': a.warmup, 'ms_per_step': 1e3 * sum(times) / len(times), 'higher_is_better': True,
+        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': 'population forward, BASELINE config 2 shape, bounded CPU sample',
+                   'members_per_step': CPU_SAMPLE_MEMBERS, 'seq_len': CPU_SAMPLE_T},
+        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }), flush=True)
+
+
+def run_ours(a):
+    import noise_b200
+    from noise_b200 import _lib
+    from noise_b200.eggroll import Population, make_params
+
+    rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=300))
+    dist = world > 1
+
+    params = make_params(device, seed=0)
+    pairs = MEMBERS // 2 * world
+    pop = Population(params, pairs, sigma=SIGMA, seed=0, rank=rank, world=world)
+    host_rows = [zipf_rows(ROWS, T + 1, seed=1000 * s + 7).pin_memory() for s in range(2)]
+    dev_rows = [r.to(device) for r in host_rows]
+    torch.cuda.synchronize()
+
+    def step(i, tokens):
+        _, fit = pop.evaluate(tokens, step=i + 1, rows_per_member=ROWS, reduction='sum')
+        return fit
+
+    for i in range(a.warmup):
+        step(i, dev_rows[i % 2])
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+
+    # device-resident timed region
+    clocks = Clocks(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with _lib.LaunchProfile() as prof:
+        e0.record()
+        for i in range(a.steps):
+            step(a.warmup + i, dev_rows[i % 2])
+            launches += pop.launches
+        e1.record()
+        torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+
+    # end-to-end: host token rows -> device, evaluate, fitness -> host, every step
+    fit_host = torch.empty(MEMBERS * world, pin_memory=True)
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(a.steps):
+        tokens = host_rows[i % 2].to(device, non_blocking=True)
+        fit = step(a.warmup + a.steps + i, tokens)
+        fit_host.copy_(fit, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    f1.record()
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    if dist:
+        t = torch.tensor([ms, ms_e2e], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+
+    work = MEMBERS * ROWS * world * a.steps  # population forwards (member x 2048-token row) in the timed region
+    value = work / (ms / 1e3)
+    e2e_value = work / (ms_e2e / 1e3)
+
+    # roofline of the dominant kernel kind (CUDA-event times of every launch in the timed region)
+    kinds = {}
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    tf_peak = peaks.get('bf16_tflops_sustained', 1400.0)
+    traffic_file = ROOT / 'profiles' / 'traffic_per_row.json'
+    traffic = json.loads(traffic_file.read_text()) if traffic_file.exists() else {}
+    total = sum(prof.ms.values())
+    for k, kms in prof.ms.items():
+        n = prof.count[k]
+        flops, _ = kernel_work(k, pop.chunk, T)
+        per = kms / n
+        kinds[k] = {'launches': n, 'ms_per_launch': round(per, 4), 'share': round(kms / total, 4)}
+        if flops:
+            kinds[k]['tflops'] = round(flops / (per / 1e3) / 1e12, 1)
+    dom = max(prof.ms, key=prof.ms.get)
+    flops, _ = kernel_work(dom, pop.chunk, T)
+    per_launch_s = prof.ms[dom] / prof.count[dom] / 1e3
+    tr = traffic.get(dom)
+    roofline = {
+        'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1), 'peak': tf_peak,
+        'unit': 'TFLOP/s', 'frac': round(flops / per_launch_s / 1e12 / tf_peak, 4),
+        'peak_source': 'MEASURED_PEAKS.json bf16_tflops_sustained (of measured)' if peaks else 'fallback',
+        'traffic': (tr * pop.chunk * T if tr is not None else None),
+        'algorithmic_flops_per_launch': flops,
+        'step': {'achieved': round(MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12, 1),
+                 'frac': round(MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12 / tf_peak, 4)},
+    }
+
+    line = {
+        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
+        'ms_per_step': ms / a.steps, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'bf16',
+        'data': 'synthetic: Zipf(1.1) token rows over vocab 4096; random-init weights of the utils/model.py GPT '
+                '(EGGROLL make_model); EGGROLL 2**28 N(0,1) noise buffer',
+        'config': {'workload': 'BASELINE config 2 per GPU: population forward of 512 antithetic members x 8 rows x '
+                               '2048 tokens (summed-CE fitness), NCCL all-gather of fitness',
+                   'members_per_gpu': MEMBERS, 'rows_per_member': ROWS, 'seq_len': T, 'sigma': SIGMA,
+                   'member_tokens_per_s': value * T, 'train_tokens_per_step': ROWS * T,
+                   'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}'},
+        'roofline': roofline, 'kernels': kinds, 'clocks': clk,
+        'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': ROWS * (T + 1) * 8,
+                'd2h_bytes_per_step': MEMBERS * world * 4},
+        'gpu_launches': launches,
+    }
+    if rank == 0 and world == 1:
+        threads = os.cpu_count() or 1
+        secs = [cpu_reference_sample(threads) for _ in range(2)]
+        cv = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(secs)
+        line['cpu_baseline'] = {'value': cv, 'unit': UNIT, 'cores': threads, 'kind': 'port',
+                                'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens, fp32 oracle '
+                                          f'restatement of eggroll.population_loss, median of 2'}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    a = args_()
+    if a.impl == 'reference':
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == '__main__':
+    main()

@@ -126,6 +126,16 @@ const char* noise_status_string(int status);
 /* Number of kernels the most recent successful noise_population_loss call on this thread enqueued. */
 int noise_last_launch_count(void);
 
+/* Per-launch timing with CUDA events (no counterpart in the reference, which times whole updates with CUDA events,
+ * train/speedrun/run.py:4262-4263). After noise_profile_start(capacity), every launch of noise_population_loss /
+ * noise_gemm_bf16_tn on this thread records an event pair around itself on its stream (up to `capacity` launches).
+ * noise_profile_stop synchronises on the recorded events, adds the elapsed milliseconds per kernel kind into
+ * kind_ms[k] / kind_count[k] (k < nkinds; kinds: 0 norm+mix, 1 QKV GEMM, 2 attention, 3 c_proj GEMM, 4 mid norm,
+ * 5 c_fc GEMM, 6 mlp.c_proj GEMM, 7 final norm, 8 LM-head+CE GEMM, 9 member reduce, 10 plain GEMM), frees the
+ * events and turns timing off (kind_ms / kind_count may be NULL to discard). */
+int noise_profile_start(int capacity);
+int noise_profile_stop(float* kind_ms, int* kind_count, int nkinds);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,6 +51,9 @@ SIGNATURES = [
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),
     ('noise_last_launch_count', ctypes.c_int, []),
+    ('noise_profile_start', ctypes.c_int, [ctypes.c_int]),
+    ('noise_profile_stop', ctypes.c_int,
+     [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
 ]
 
 
@@ -105,3 +108,27 @@ def gemm_bf16_tn(a, b):
                                    ws.data_ptr(), stream_handle(a.device)), 'noise_gemm_bf16_tn')
     out._noise_workspace = ws
     return out
+
+
+KINDS = ['norm_mix', 'gemm_qkv', 'attention', 'gemm_cproj', 'norm_mid', 'gemm_cfc', 'gemm_mproj', 'norm_final',
+         'gemm_head_ce', 'member_reduce', 'gemm_plain']
+
+
+class LaunchProfile:
+    """Context manager: per-kernel-kind CUDA-event times of the launches made inside it (this thread).
+    After exit, ``.ms[kind]`` and ``.count[kind]`` hold the summed milliseconds and launch counts."""
+
+    def __init__(self, capacity=100000):
+        self.capacity, self.ms, self.count = capacity, {}, {}
+
+    def __enter__(self):
+        check(lib().noise_profile_start(self.capacity), 'noise_profile_start')
+        return self
+
+    def __exit__(self, *exc):
+        n = len(KINDS)
+        ms, cnt = (ctypes.c_float * n)(), (ctypes.c_int * n)()
+        check(lib().noise_profile_stop(ms, cnt, n), 'noise_profile_stop')
+        self.ms = {k: ms[i] for i, k in enumerate(KINDS) if cnt[i]}
+        self.count = {k: cnt[i] for i, k in enumerate(KINDS) if cnt[i]}
+        return False

@@ -2,12 +2,13 @@
 // K-major in HBM (activations row-major, nn.Linear weights [out, in]), fp32 accumulation in tensor memory, and a
 // fused per-row epilogue supplied as a functor.
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (320 threads, one CTA per SM):
 //   warp 0      one lane issues TMA tile loads (128-byte swizzle) into a STAGES-deep shared-memory ring;
 //   warp 1      allocates 2 x BN TMEM columns (double-buffered accumulator); one lane issues tcgen05.mma
 //               (M = 128, N = BN, K = 16 per instruction) and tcgen05.commit to release ring slots / publish tiles;
-//   warps 2..5  epilogue: warp w reads TMEM lane quarter (w % 4), i.e. one output row per thread, in column chunks
-//               (tcgen05.ld 32x32b), and hands them to the functor; then frees the accumulator buffer.
+//   warps 2..9  epilogue: warp w reads TMEM lane quarter (w % 4), i.e. one output row per thread; the two warps of a
+//               quarter split the tile's columns into halves (part 0 / 1). Column chunks come from tcgen05.ld 32x32b
+//               and go to the functor; then the accumulator buffer is released.
 // Schedule: CTA c owns row blocks c, c + grid, ...; for each it walks all N tiles in order, so an epilogue can carry
 // per-row state (a running log-sum-exp, a partial dot product) across the N tiles of its row.
 #pragma once
@@ -20,7 +21,8 @@ namespace noise {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
 template <int BN, int STAGES>
 struct GemmLayout {
@@ -34,12 +36,12 @@ struct GemmLayout {
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation must be a power of two");
 };
 
-// Epilogue functor contract (all methods run on the thread that owns `row`):
+// Epilogue functor contract (all methods run on a thread that owns `row` and column half `part` of every tile):
 //   static constexpr int CH;                          columns per TMEM load (16, 32 or 64)
-//   void row_begin(int row);                          before the first N tile of the row block
-//   void chunk(int row, int col, const float* v);     v[0..CH) = D[row, col .. col + CH)
-//   void tile_end(int row, int n_tile);               after the last chunk of a tile
-//   void row_end(int row);                            after the last N tile
+//   void row_begin(int row, int part);                before the first N tile of the row block
+//   void chunk(int row, int col, float* v);           v[0..CH) = D[row, col .. col + CH) (may be modified in place)
+//   void tile_end(int row, int n_tile, int part);     after the last chunk of the thread's half of a tile
+//   void row_end(int row, int part);                  after the last N tile
 template <int BN, int STAGES, class Epi>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -62,7 +64,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 128);
+      mbar_init(&acce[b], 32 * GEMM_EPI_WARPS);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -155,22 +157,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     Epi e = epi;  // per-thread copy: the functor may carry per-row state
     const int quarter = warp & 3;
+    const int part = (warp - 2) >> 2;  // column half of every tile this warp handles
     const int r_in = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr int HALF = BN / 2;
+    static_assert(HALF % Epi::CH == 0, "epilogue chunk must divide half a tile");
     int t = 0;
     bool ok = true;
     for (int mb = blockIdx.x; mb < m_tiles && ok; mb += gridDim.x) {
       const int row = mb * GEMM_BM + r_in;
-      e.row_begin(row);
+      e.row_begin(row, part);
       for (int nb = 0; nb < n_tiles; ++nb, ++t) {
         const int buf = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
         ok = mbar_wait(&accf[buf], use & 1u, status);
         tc_fence_after();
         if (ok) {
-          const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN);
+          const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN + part * HALF);
 #pragma unroll 1
-          for (int c = 0; c < BN; c += Epi::CH) {
+          for (int c = 0; c < HALF; c += Epi::CH) {
             float v[Epi::CH];
             if constexpr (Epi::CH == 64) {
               tmem_ld32(base + c, v);
@@ -181,15 +186,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               tmem_ld16(base + c, v);
             }
             tc_wait_ld();
-            e.chunk(row, nb * BN + c, v);
+            e.chunk(row, nb * BN + part * HALF + c, v);
           }
-          e.tile_end(row, nb);
+          e.tile_end(row, nb, part);
         }
         tc_fence_before();
         mbar_arrive(&acce[buf]);
         if (!ok) break;
       }
-      if (ok) e.row_end(row);
+      if (ok) e.row_end(row, part);
     }
   }
   __syncwarp();

@@ -228,34 +228,41 @@ struct EpiQKV {
   int j, t;
   float sg;
 
-  __device__ __forceinline__ void row_begin(int row) {
+  __device__ __forceinline__ void row_begin(int row, int) {
     j = row / T;
     t = row - j * T;
     sg = sign[j];
   }
-  __device__ __forceinline__ void tile_end(int, int) {}
-  __device__ __forceinline__ void row_end(int) {}
-  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+  __device__ __forceinline__ void tile_end(int, int, int) {}
+  __device__ __forceinline__ void row_end(int, int) {}
+  __device__ __forceinline__ void chunk(int row, int col, float* val) {
     const int sec = col / D, hh = (col % D) / HD;
     const float coef = sg * svec[static_cast<int64_t>(row) * 4 + sec];
-    const float* a = (sec == 0 ? nq.A(j) : sec == 1 ? nk.A(j) : nv.A(j)) + (col % D);
-    float val[HD];
+    const float* __restrict__ a = (sec == 0 ? nq.A(j) : sec == 1 ? nk.A(j) : nv.A(j)) + (col % D);
 #pragma unroll
-    for (int d = 0; d < HD; ++d) val[d] = bf16_round(acc[d]) + coef * a[d];  // a: noise slice, scalar loads
+    for (int d = 0; d < HD; ++d) val[d] = bf16_round(val[d]) + coef * a[d];  // a: noise slice, scalar loads
     __nv_bfloat16* dst;
     if (sec < 2) {
-      const __nv_bfloat16* cr = cosb + static_cast<int64_t>(t) * (HD / 2);
-      const __nv_bfloat16* sr = sinb + static_cast<int64_t>(t) * (HD / 2);
+      const uint4* cr = reinterpret_cast<const uint4*>(cosb + static_cast<int64_t>(t) * (HD / 2));
+      const uint4* sr = reinterpret_cast<const uint4*>(sinb + static_cast<int64_t>(t) * (HD / 2));
       float ss = 0.f;
 #pragma unroll
-      for (int d = 0; d < HD / 2; ++d) {
-        const float c = __bfloat162float(cr[d]), s = __bfloat162float(sr[d]);
-        const float x1 = val[d], x2 = val[d + HD / 2];
-        const float o1 = x1 * c + x2 * s;
-        const float o2 = x1 * -s + x2 * c;
-        val[d] = o1;
-        val[d + HD / 2] = o2;
-        ss += o1 * o1 + o2 * o2;
+      for (int g = 0; g < 4; ++g) {  // 8 rotary pairs per 16-byte load of the bf16 tables
+        const uint4 cv = cr[g], sv = sr[g];
+        const __nv_bfloat162* c2 = reinterpret_cast<const __nv_bfloat162*>(&cv);
+        const __nv_bfloat162* s2 = reinterpret_cast<const __nv_bfloat162*>(&sv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int d = 8 * g + e;
+          const float c = e & 1 ? __high2float(c2[e >> 1]) : __low2float(c2[e >> 1]);
+          const float s = e & 1 ? __high2float(s2[e >> 1]) : __low2float(s2[e >> 1]);
+          const float x1 = val[d], x2 = val[d + HD / 2];
+          const float o1 = x1 * c + x2 * s;
+          const float o2 = x1 * -s + x2 * c;
+          val[d] = o1;
+          val[d + HD / 2] = o2;
+          ss += o1 * o1 + o2 * o2;
+        }
       }
       const float inv = rsqrtf(ss / HD + RMS_EPS);
 #pragma unroll
@@ -265,11 +272,17 @@ struct EpiQKV {
       if (gate) {
         const float g = gate[static_cast<int64_t>(row) * H + hh];
         const int64_t tok = idx[t];
-        const float* ver = vew + tok * D + hh * HD;
+        const float4* ver = reinterpret_cast<const float4*>(vew + tok * D + hh * HD);
         const float sa = sg * nve.A(j)[tok];
-        const float* bve = nve.B(j) + hh * HD;
+        const float* __restrict__ bve = nve.B(j) + hh * HD;
 #pragma unroll
-        for (int d = 0; d < HD; ++d) val[d] = val[d] + g * (ver[d] + sa * bve[d]);
+        for (int d4 = 0; d4 < HD / 4; ++d4) {
+          const float4 w4 = ver[d4];
+          val[4 * d4 + 0] += g * (w4.x + sa * bve[4 * d4 + 0]);
+          val[4 * d4 + 1] += g * (w4.y + sa * bve[4 * d4 + 1]);
+          val[4 * d4 + 2] += g * (w4.z + sa * bve[4 * d4 + 2]);
+          val[4 * d4 + 3] += g * (w4.w + sa * bve[4 * d4 + 3]);
+        }
       }
       dst = v;
     }
@@ -294,32 +307,37 @@ struct EpiResid {
   const float* parts;  // [M, nparts] partial dots of the input row with this linear's b
   Slice n;
   float* x;
-  int j;
   float coef;
   const float* a;
 
-  __device__ __forceinline__ void row_begin(int row) {
-    j = row / T;
+  __device__ __forceinline__ void row_begin(int row, int) {
+    const int j = row / T;
     const float* pr = parts + static_cast<int64_t>(row) * nparts;
     float s = 0.f;
     for (int i = 0; i < nparts; ++i) s += pr[i];
     coef = sign[j] * bf16_round(s);
     a = n.A(j);
   }
-  __device__ __forceinline__ void tile_end(int, int) {}
-  __device__ __forceinline__ void row_end(int) {}
-  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
-    float4* xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D + col);
-    const float* ar = a + col;  // noise slice: scalar loads
+  __device__ __forceinline__ void tile_end(int, int, int) {}
+  __device__ __forceinline__ void row_end(int, int) {}
+  __device__ __forceinline__ void chunk(int row, int col, float* acc) {
+    float4* __restrict__ xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D + col);
+    const float* __restrict__ ar = a + col;  // noise slice: scalar loads
+    float4 xv[CH / 4];
+    float av[CH];
+#pragma unroll
+    for (int i = 0; i < CH / 4; ++i) xv[i] = xr[i];  // every load issued before any store
+#pragma unroll
+    for (int i = 0; i < CH; ++i) av[i] = __ldg(ar + i);
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) {
-      float4 xv = xr[i];
-      xv.x += bf16_round(acc[4 * i + 0]) + coef * ar[4 * i + 0];
-      xv.y += bf16_round(acc[4 * i + 1]) + coef * ar[4 * i + 1];
-      xv.z += bf16_round(acc[4 * i + 2]) + coef * ar[4 * i + 2];
-      xv.w += bf16_round(acc[4 * i + 3]) + coef * ar[4 * i + 3];
-      xr[i] = xv;
+      xv[i].x += bf16_round(acc[4 * i + 0]) + coef * av[4 * i + 0];
+      xv[i].y += bf16_round(acc[4 * i + 1]) + coef * av[4 * i + 1];
+      xv[i].z += bf16_round(acc[4 * i + 2]) + coef * av[4 * i + 2];
+      xv[i].w += bf16_round(acc[4 * i + 3]) + coef * av[4 * i + 3];
     }
+#pragma unroll
+    for (int i = 0; i < CH / 4; ++i) xr[i] = xv[i];
   }
 };
 
@@ -327,40 +345,42 @@ struct EpiResid {
 // (the next linear's rank-1 input dot), eggroll.py:93.
 struct EpiFC {
   static constexpr int CH = 32;
+  static constexpr int NPARTS = 2 * (F / GEMM_BN);  // per row: one partial dot per (N tile, column half)
   int T;
   const float* sign;
   const float* svec;
   Slice nfc, nmp;
   __nv_bfloat16* hidden;
-  float* pdot;  // [M, F / GEMM_BN]
-  int j;
+  float* pdot;  // [M, NPARTS]
   float coef, pd;
   const float* a;
   const float* b;
 
-  __device__ __forceinline__ void row_begin(int row) {
-    j = row / T;
+  __device__ __forceinline__ void row_begin(int row, int) {
+    const int j = row / T;
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
     a = nfc.A(j);
     b = nmp.B(j);
     pd = 0.f;
   }
-  __device__ __forceinline__ void tile_end(int row, int nb) {
-    pdot[static_cast<int64_t>(row) * (F / GEMM_BN) + nb] = pd;
+  __device__ __forceinline__ void tile_end(int row, int nb, int part) {
+    pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] = pd;
     pd = 0.f;
   }
-  __device__ __forceinline__ void row_end(int) {}
-  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+  __device__ __forceinline__ void row_end(int, int) {}
+  __device__ __forceinline__ void chunk(int row, int col, float* acc) {
     uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row) * F + col);
+    const float* __restrict__ ap = a + col;
+    const float* __restrict__ bp = b + col;
 #pragma unroll
     for (int i = 0; i < CH; i += 8) {
       float r[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float u = bf16_round(acc[i + e]) + coef * a[col + i + e];
+        const float u = bf16_round(acc[i + e]) + coef * __ldg(ap + i + e);
         const float rl = fmaxf(u, 0.f);
         r[e] = bf16_round(rl * rl);
-        pd += r[e] * bf16_round(b[col + i + e]);
+        pd += r[e] * bf16_round(__ldg(bp + i + e));
       }
       uint4 pk;
       pk.x = pack_bf16x2(r[0], r[1]);
@@ -382,27 +402,26 @@ struct EpiHeadCE {
   const float* svec;
   const int64_t* targets;
   Slice n;
-  float* ce;  // [M]
-  int j;
+  float2* ce2;  // [M, 2]: per column half, (sum exp(c - 15), c_target or 0)
   int64_t tgt;
   float coef, sum, zt;
   const float* a;
 
-  __device__ __forceinline__ void row_begin(int row) {
-    j = row / T;
-    const int t = row - j * T;
-    tgt = targets[t];
+  __device__ __forceinline__ void row_begin(int row, int) {
+    const int j = row / T;
+    tgt = targets[row - j * T];
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
     a = n.A(j);
     sum = 0.f;
     zt = 0.f;
   }
-  __device__ __forceinline__ void tile_end(int, int) {}
-  __device__ __forceinline__ void row_end(int row) { ce[row] = 15.f + logf(sum) - zt; }
-  __device__ __forceinline__ void chunk(int, int col, const float* acc) {
+  __device__ __forceinline__ void tile_end(int, int, int) {}
+  __device__ __forceinline__ void row_end(int row, int part) { ce2[static_cast<int64_t>(row) * 2 + part] = make_float2(sum, zt); }
+  __device__ __forceinline__ void chunk(int, int col, float* acc) {
+    const float* __restrict__ ap = a + col;
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const float z = bf16_round(acc[i]) + coef * a[col + i];
+      const float z = bf16_round(acc[i]) + coef * __ldg(ap + i);
       const float y = fabsf(z) * (1.f / 15.f);
       const float th = 1.f - 2.f * rcp_approx(ex2_approx(2.f * LOG2E * y) + 1.f);
       const float c = copysignf(15.f * th, z);
@@ -417,10 +436,10 @@ struct EpiStore {
   static constexpr int CH = 32;
   float* d;
   int ldd;
-  __device__ __forceinline__ void row_begin(int) {}
-  __device__ __forceinline__ void tile_end(int, int) {}
-  __device__ __forceinline__ void row_end(int) {}
-  __device__ __forceinline__ void chunk(int row, int col, const float* acc) {
+  __device__ __forceinline__ void row_begin(int, int) {}
+  __device__ __forceinline__ void tile_end(int, int, int) {}
+  __device__ __forceinline__ void row_end(int, int) {}
+  __device__ __forceinline__ void chunk(int row, int col, float* acc) {
     float4* out = reinterpret_cast<float4*>(d + static_cast<int64_t>(row) * ldd + col);
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
@@ -638,11 +657,14 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
 // ---------------------------------------------------------------------------------------------------------------
 // Per-member reduction of the per-row cross-entropy (fixed order: deterministic).
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) member_reduce_kernel(const float* ce, int T, float scale, float* out) {
+__global__ void __launch_bounds__(256) member_reduce_kernel(const float4* ce2, int T, float scale, float* out) {
   __shared__ float part[8];
   const int j = blockIdx.x;
   float s = 0.f;
-  for (int t = threadIdx.x; t < T; t += 256) s += ce[static_cast<int64_t>(j) * T + t];
+  for (int t = threadIdx.x; t < T; t += 256) {
+    const float4 c = ce2[static_cast<int64_t>(j) * T + t];  // (sum, c_target) of both column halves
+    s += 15.f + logf(c.x + c.z) - (c.y + c.w);
+  }
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
   __syncthreads();
@@ -702,9 +724,35 @@ static int sm_count() {
 }
 
 static thread_local int g_launches = 0;
+// Optional per-launch timing (noise_profile_start/stop): an event pair around every launch, labelled by kind.
+enum LaunchKind {
+  K_NORM_BLOCK, K_GEMM_QKV, K_ATTENTION, K_GEMM_PROJ, K_NORM_MID, K_GEMM_FC, K_GEMM_MPROJ, K_NORM_FINAL,
+  K_GEMM_HEAD, K_REDUCE, K_GEMM_PLAIN, K_KINDS
+};
+struct Profiler {
+  bool on = false;
+  int capacity = 0, used = 0;
+  cudaEvent_t* ev = nullptr;
+  int* kind = nullptr;
+};
+static thread_local Profiler g_prof;
+static thread_local int g_kind = 0;
+
+static inline void launch_begin(cudaStream_t s, int kind) {
+  g_kind = kind;
+  if (g_prof.on && g_prof.used < g_prof.capacity) cudaEventRecord(g_prof.ev[2 * g_prof.used], s);
+}
+static inline void launch_end(cudaStream_t s) {
+  if (g_prof.on && g_prof.used < g_prof.capacity) {
+    cudaEventRecord(g_prof.ev[2 * g_prof.used + 1], s);
+    g_prof.kind[g_prof.used++] = g_kind;
+  }
+  ++g_launches;
+}
 
 template <class Epi>
-static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi& epi, int* status, cudaStream_t s) {
+static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi& epi, int* status, cudaStream_t s,
+                    int kind) {
   using L = GemmLayout<GEMM_BN, GEMM_STAGES>;
   if (M % GEMM_BM || N % GEMM_BN || K % GEMM_BK) return NOISE_ERR_SHAPE;
   CUtensorMap ma, mb;
@@ -719,8 +767,9 @@ static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi
   int sms = sm_count();
   if (sms <= 0) return NOISE_ERR_CUDA;
   const int grid = m_tiles < sms ? m_tiles : sms;
+  launch_begin(s, kind);
   kern<<<grid, GEMM_THREADS, L::SMEM_BYTES, s>>>(ma, mb, m_tiles, N / GEMM_BN, K / GEMM_BK, epi, status);
-  ++g_launches;
+  launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
@@ -728,7 +777,8 @@ struct Workspace {
   int* status;
   float* x;
   __nv_bfloat16 *h, *q, *k, *v, *y, *hidden;
-  float *svec, *gate, *ydot, *pdot, *ce;
+  float *svec, *gate, *ydot, *pdot;
+  float2* ce2;
   size_t bytes;
 };
 
@@ -753,8 +803,8 @@ static Workspace carve(void* ws, int64_t M) {
   w.svec = static_cast<float*>(take(M * 4 * 4));
   w.gate = static_cast<float*>(take(M * H * 4));
   w.ydot = static_cast<float*>(take(M * H * 4));
-  w.pdot = static_cast<float*>(take(M * (F / GEMM_BN) * 4));
-  w.ce = static_cast<float*>(take(M * 4));
+  w.pdot = static_cast<float*>(take(M * EpiFC::NPARTS * 4));
+  w.ce2 = static_cast<float2*>(take(M * 2 * 8));
   w.bytes = off;
   return w;
 }
@@ -834,8 +884,9 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     na.nb2 = to_slice(nz[noise_param_index(l, NOISE_P_CV)]);
     na.wgate = ve ? model->wgate[l] : nullptr;
     if (ve) na.n_gate = to_slice(nz[noise_param_index(l, NOISE_P_VEGATE)]);
+    launch_begin(s, K_NORM_BLOCK);
     norm_kernel<NORM_BLOCK><<<norm_blocks, 256, 0, s>>>(na);
-    ++g_launches;
+    launch_end(s);
 
     EpiQKV eq{};
     eq.T = T;
@@ -853,7 +904,7 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     eq.q = w.q;
     eq.k = w.k;
     eq.v = w.v;
-    if ((rc = run_gemm(w.h, Mi, D, model->wqkv[l], 3 * D, eq, w.status, s))) return rc;
+    if ((rc = run_gemm(w.h, Mi, D, model->wqkv[l], 3 * D, eq, w.status, s, K_GEMM_QKV))) return rc;
 
     AttnArgs aa{};
     aa.q = w.q;
@@ -864,8 +915,9 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     aa.T = T;
     aa.window = (l % 4 == 3 || l == NOISE_N_LAYER - 1) ? 2048 : 1024;  // SSSL, last block L
     aa.nproj = to_slice(nz[noise_param_index(l, NOISE_P_CPROJ)]);
+    launch_begin(s, K_ATTENTION);
     attention_kernel<<<dim3(T / ATT_BQ, members * H), 128, 0, s>>>(aa);
-    ++g_launches;
+    launch_end(s);
 
     EpiResid er{};
     er.T = T;
@@ -874,12 +926,13 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     er.parts = w.ydot;
     er.n = aa.nproj;
     er.x = w.x;
-    if ((rc = run_gemm(w.y, Mi, D, model->wproj[l], D, er, w.status, s))) return rc;
+    if ((rc = run_gemm(w.y, Mi, D, model->wproj[l], D, er, w.status, s, K_GEMM_PROJ))) return rc;
 
     NormArgs nm = na;
     nm.nb0 = to_slice(nz[noise_param_index(l, NOISE_P_CFC)]);
+    launch_begin(s, K_NORM_MID);
     norm_kernel<NORM_MID><<<norm_blocks, 256, 0, s>>>(nm);
-    ++g_launches;
+    launch_end(s);
 
     EpiFC ef{};
     ef.T = T;
@@ -889,16 +942,16 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     ef.nmp = to_slice(nz[noise_param_index(l, NOISE_P_MPROJ)]);
     ef.hidden = w.hidden;
     ef.pdot = w.pdot;
-    if ((rc = run_gemm(w.h, Mi, D, model->wfc[l], F, ef, w.status, s))) return rc;
+    if ((rc = run_gemm(w.h, Mi, D, model->wfc[l], F, ef, w.status, s, K_GEMM_FC))) return rc;
 
     EpiResid em{};
     em.T = T;
-    em.nparts = F / GEMM_BN;
+    em.nparts = EpiFC::NPARTS;
     em.sign = sign;
     em.parts = w.pdot;
     em.n = ef.nmp;
     em.x = w.x;
-    if ((rc = run_gemm(w.hidden, Mi, F, model->wmproj[l], D, em, w.status, s))) return rc;
+    if ((rc = run_gemm(w.hidden, Mi, F, model->wmproj[l], D, em, w.status, s, K_GEMM_MPROJ))) return rc;
   }
 
   NormArgs nf{};
@@ -910,8 +963,9 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
   nf.h = w.h;
   nf.svec = w.svec;
   nf.nb0 = to_slice(nz[NOISE_PARAM_HEAD]);
+  launch_begin(s, K_NORM_FINAL);
   norm_kernel<NORM_FINAL><<<norm_blocks, 256, 0, s>>>(nf);
-  ++g_launches;
+  launch_end(s);
 
   EpiHeadCE eh{};
   eh.T = T;
@@ -919,11 +973,13 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
   eh.svec = w.svec;
   eh.targets = targets;
   eh.n = nf.nb0;
-  eh.ce = w.ce;
-  if ((rc = run_gemm(w.h, Mi, D, model->whead, V, eh, w.status, s))) return rc;
+  eh.ce2 = w.ce2;
+  if ((rc = run_gemm(w.h, Mi, D, model->whead, V, eh, w.status, s, K_GEMM_HEAD))) return rc;
 
-  member_reduce_kernel<<<members, 256, 0, s>>>(w.ce, T, reduction == NOISE_REDUCTION_MEAN ? 1.f / T : 1.f, losses);
-  ++g_launches;
+  launch_begin(s, K_REDUCE);
+  member_reduce_kernel<<<members, 256, 0, s>>>(reinterpret_cast<const float4*>(w.ce2), T,
+                                               reduction == NOISE_REDUCTION_MEAN ? 1.f / T : 1.f, losses);
+  launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
@@ -936,7 +992,7 @@ int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int
   if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
   g_launches = 0;
   EpiStore e{d, n};
-  return run_gemm(a, m, k, b, n, e, static_cast<int*>(workspace), s);
+  return run_gemm(a, m, k, b, n, e, static_cast<int*>(workspace), s, K_GEMM_PLAIN);
 }
 
 int noise_pack_bf16(const float* src, void* dst, int64_t n, void* stream) {
@@ -979,5 +1035,47 @@ const char* noise_status_string(int status) {
 }
 
 int noise_last_launch_count(void) { return g_launches; }
+
+int noise_profile_start(int capacity) {
+  if (capacity < 1) return NOISE_ERR_ARGUMENT;
+  noise_profile_stop(nullptr, nullptr, 0);
+  g_prof.ev = new cudaEvent_t[2 * capacity];
+  g_prof.kind = new int[capacity];
+  for (int i = 0; i < 2 * capacity; ++i) {
+    if (cudaEventCreate(&g_prof.ev[i]) != cudaSuccess) {
+      g_prof.capacity = i / 2;
+      noise_profile_stop(nullptr, nullptr, 0);
+      return NOISE_ERR_CUDA;
+    }
+  }
+  g_prof.capacity = capacity;
+  g_prof.used = 0;
+  g_prof.on = true;
+  return NOISE_OK;
+}
+
+int noise_profile_stop(float* kind_ms, int* kind_count, int nkinds) {
+  int rc = NOISE_OK;
+  if (kind_ms && kind_count) {
+    for (int k = 0; k < nkinds; ++k) kind_ms[k] = 0.f, kind_count[k] = 0;
+    for (int i = 0; i < g_prof.used; ++i) {
+      float ms = 0.f;
+      if (cudaEventSynchronize(g_prof.ev[2 * i + 1]) != cudaSuccess ||
+          cudaEventElapsedTime(&ms, g_prof.ev[2 * i], g_prof.ev[2 * i + 1]) != cudaSuccess) {
+        rc = NOISE_ERR_CUDA;
+        break;
+      }
+      const int k = g_prof.kind[i];
+      if (k < nkinds) kind_ms[k] += ms, kind_count[k] += 1;
+    }
+  }
+  if (g_prof.ev) {
+    for (int i = 0; i < 2 * g_prof.capacity; ++i) cudaEventDestroy(g_prof.ev[i]);
+    delete[] g_prof.ev;
+    delete[] g_prof.kind;
+  }
+  g_prof = Profiler{};
+  return rc;
+}
 
 }  // extern "C"
