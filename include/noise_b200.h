@@ -26,6 +26,7 @@ extern "C" {
 #define NOISE_ERR_ARGUMENT 4    /* NULL required pointer or bad enum value */
 #define NOISE_ERR_CUDA 5        /* a CUDA runtime/driver call failed (launch, tensor-map encode, attributes) */
 #define NOISE_ERR_DEVICE 6      /* not an sm_100 device */
+#define NOISE_ERR_TOO_LARGE 7   /* size beyond the static scratch of noise_population_loss_noalloc */
 
 #define NOISE_STATUS_BYTES 256
 
@@ -102,6 +103,25 @@ size_t noise_population_workspace_bytes(int members, int tokens);
 int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
                           const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
                           float* losses, void* workspace, size_t workspace_bytes, void* stream);
+
+/* No counterpart in the reference: noise_population_loss for callers that cannot allocate device memory — a host
+ * that embeds this library without a CUDA allocator of its own (a C/FFI caller that must not call cudaMalloc, which
+ * synchronises the device, on its hot path), or one whose memory pool is fully reserved by the time it evaluates.
+ * Same arguments and results as noise_population_loss minus the workspace: the scratch is a file-scope
+ * __device__ array of NOISE_STATIC_SCRATCH_BYTES that every GPU which loads the library holds until exit, so
+ * members * tokens is limited to what fits in it (noise_population_workspace_bytes(members, tokens) <=
+ * NOISE_STATIC_SCRATCH_BYTES, about 4,400 rows, e.g. 2 members x 2048 tokens); larger sizes return
+ * NOISE_ERR_TOO_LARGE before anything is launched. Nothing is allocated: no cudaMalloc/cudaFree, no allocating
+ * library routine. The first call on a device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture. All calls share the one array and it
+ * keeps the last call's contents (the status word is cleared at the start of each call): calls that overlap on the
+ * GPU (concurrent streams, or threads sharing a device) race on it, so serialise them. The device status word is the
+ * array's first int and is not readable through noise_read_status (it has no host-visible workspace pointer). */
+#define NOISE_STATIC_SCRATCH_BYTES (48u << 20)
+#define NOISE_STATIC_MAX_DEVICES 64
+int noise_population_loss_noalloc(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
+                                  const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
+                                  float* losses, void* stream);
 
 /* D[m, n] (fp32, row-major) = A[m, k] . B[n, k]^T for bf16 row-major A and B, on the persistent tcgen05/TMA GEMM
  * that every linear layer of noise_population_loss runs on, with a plain store epilogue. Stands in for the cuBLAS

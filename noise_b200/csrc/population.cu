@@ -983,6 +983,41 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// No-allocation variant of noise_population_loss. Its scratch is this file-scope device array, which every GPU that
+// loads the library holds until the process exits. In host code `g_static_scratch` is only a host-side stand-in
+// for the symbol, never a device address: its device address is looked up once per device with
+// cudaGetSymbolAddress (with that device current) and only that address reaches the kernels.
+// ---------------------------------------------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_static_scratch[NOISE_STATIC_SCRATCH_BYTES];
+static void* g_static_scratch_addr[NOISE_STATIC_MAX_DEVICES];
+static std::mutex g_static_scratch_mutex;
+
+int noise_population_loss_noalloc(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
+                                  const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
+                                  float* losses, void* stream) {
+  const size_t need = noise_population_workspace_bytes(members, tokens);
+  if (need == 0) return NOISE_ERR_SHAPE;
+  if (need > NOISE_STATIC_SCRATCH_BYTES) return NOISE_ERR_TOO_LARGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (dev < 0 || dev >= NOISE_STATIC_MAX_DEVICES) return NOISE_ERR_DEVICE;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+    if (!g_static_scratch_addr[dev]) {  // first call on this device: resolve the array's device address
+      void* addr = nullptr;
+      if (cudaGetSymbolAddress(&addr, g_static_scratch) != cudaSuccess || !addr) return NOISE_ERR_CUDA;
+      g_static_scratch_addr[dev] = addr;
+    }
+    scratch = g_static_scratch_addr[dev];
+  }
+  // The status word at the head of the scratch is cleared by noise_population_loss itself; every other buffer is
+  // fully written before it is read, so stale contents of an earlier call never leak into this one.
+  return noise_population_loss(model, noise, sign, idx, targets, members, tokens, reduction, losses, scratch,
+                               NOISE_STATIC_SCRATCH_BYTES, stream);
+}
+
 int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace,
                        void* stream) {
   if (!a || !b || !d || !workspace) return NOISE_ERR_ARGUMENT;
@@ -1030,6 +1065,7 @@ const char* noise_status_string(int status) {
     case NOISE_ERR_ARGUMENT: return "invalid argument";
     case NOISE_ERR_CUDA: return "CUDA call failed";
     case NOISE_ERR_DEVICE: return "not an sm_100 device";
+    case NOISE_ERR_TOO_LARGE: return "members x tokens exceed the static scratch of the no-allocation entry point";
     default: return "unknown status";
   }
 }

@@ -206,3 +206,27 @@ def population_loss_offsets(packed, buffer, member_off, sign, idx, targets, redu
         out = shape[0] if len(shape) == 2 else 0
         slices.append(_lib.Slice(base, base + 4 * out, off, 0, 0))
     return _run(packed, slices, [member_off, buffer], sign, idx, targets, reduction)
+
+
+def population_loss_offsets_noalloc(packed, buffer, member_off, sign, idx, targets, reduction='mean'):
+    """``population_loss_offsets`` through ``noise_population_loss_noalloc``: for callers that cannot allocate device
+    memory, the C entry point takes no workspace and runs in the library's static device scratch (48 MiB per GPU:
+    members x tokens up to about 4,400 rows). Only the returned loss vector is allocated here, by torch. Calls that
+    overlap on the GPU race on the shared scratch."""
+    packed = packed.refresh()
+    _lib.require_cuda(buffer, member_off)
+    member_off = member_off.contiguous()
+    sign = sign.detach().float().contiguous()
+    idx = idx.detach().long().contiguous()
+    targets = targets.detach().long().contiguous()
+    base = buffer.data_ptr()
+    slices = [_lib.Slice(base, base + 4 * (shape[0] if len(shape) == 2 else 0), member_off[k].data_ptr(), 0, 0)
+              for k, (name, shape) in enumerate(PARAMS)]
+    m, length = sign.shape[0], idx.shape[0]
+    losses = torch.empty(m, dtype=torch.float32, device=packed.device)
+    arr = (_lib.Slice * len(NAMES))(*slices)
+    rc = _lib.lib().noise_population_loss_noalloc(ctypes.byref(packed.struct), arr, sign.data_ptr(), idx.data_ptr(),
+                                                  targets.data_ptr(), m, length, _lib.REDUCTION[reduction],
+                                                  losses.data_ptr(), _lib.stream_handle(packed.device))
+    _lib.check(rc, 'noise_population_loss_noalloc')
+    return losses
