@@ -7,7 +7,9 @@ never runs this script, it only reads the committed ``*.pt`` files. Reference fi
 - ``archive/10M/train/val/eggroll.py``: make_model, lowrank, lowrank_embed, population_loss, Eggroll.offsets/noise
   and one Eggroll.step (member layout, fitness, seed-rebuilt gradient).
 - ``train/speedrun/moment_kernels.py``: _implicit_key_context under TRITON_INTERPRET=1 (its dots are fp32 tf32 dots,
-  which the interpreter evaluates in fp32).
+  which the interpreter evaluates in fp32), then every credit kernel (lse/center on bf16 inputs, value pass, key
+  scan, query moments, key moments) under the interpreter with its bf16 dot and bf16 rounding fixed
+  (patch_triton_interpreter: a fix of the tool's arithmetic; the reference kernels run unmodified).
 
 Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is switched to the eager
 ``flex_attention`` (same function, no compilation). The noise buffer is shrunk from 2**28 to 2**20 values
@@ -24,6 +26,8 @@ os.environ.setdefault('TRITON_INTERPRET', '1')  # read when triton is first impo
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+from credit_inputs import credit_inputs  # noqa: E402
 SMALL_NOISE = 2 ** 20
 
 
@@ -140,6 +144,111 @@ def golden_implicit(root):
     print('implicit_key_context: ok')
 
 
+def patch_triton_interpreter():
+    """Make the Triton interpreter compute what the GPU computes (a fix of the tool, not of the reference kernels).
+
+    The interpreter stores bf16 tensors as raw uint16 bits. Its tl.dot multiplies those bits as integers, and its
+    fp32 -> bf16 cast truncates, where the hardware rounds to nearest even. Patched: bf16 dot operands are widened to
+    fp32 before the numpy matmul (bf16 products are exact in fp32; accumulation is fp32 as on the tensor cores) and
+    fp32 <-> bf16 casts go through torch's round-to-nearest-even conversion."""
+    import numpy as np
+    import triton.language as tl
+    from triton.runtime import interpreter as ti
+
+    def widen(h):
+        if h.dtype.scalar != tl.bfloat16:
+            return h
+        return ti.TensorHandle((h.data.astype(np.uint32) << 16).view(np.float32), tl.float32)
+
+    def narrow(data):
+        t = torch.from_numpy(np.ascontiguousarray(data, dtype=np.float32))
+        return t.bfloat16().view(torch.int16).numpy().view(np.uint16).reshape(np.shape(data))
+
+    dot = ti.InterpreterBuilder.create_dot
+    cast = ti.InterpreterBuilder.cast_impl
+    fp_to_fp = ti.InterpreterBuilder.create_fp_to_fp
+
+    def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
+        return dot(self, widen(a), widen(b), d, input_precision, max_num_imprecise_acc)
+
+    def cast_impl(self, src, dst_type):
+        s, d = src.dtype.scalar, dst_type.scalar
+        if s == tl.float32 and d == tl.bfloat16:
+            return ti.TensorHandle(narrow(src.data), d)
+        if s == tl.bfloat16 and d == tl.float32:
+            return ti.TensorHandle(widen(src).data, d)
+        return cast(self, src, dst_type)
+
+    def create_fp_to_fp(self, src, dst_type, rounding_mode):
+        if src.dtype.scalar in (tl.float32, tl.bfloat16) and dst_type.scalar in (tl.float32, tl.bfloat16):
+            return cast_impl(self, src, dst_type)
+        return fp_to_fp(self, src, dst_type, rounding_mode)
+
+    ti.InterpreterBuilder.create_dot = create_dot
+    ti.InterpreterBuilder.cast_impl = cast_impl
+    ti.InterpreterBuilder.create_fp_to_fp = create_fp_to_fp
+
+
+def interpreter_libdevice():
+    """numpy float32 versions of the libdevice functions the credit kernels call (log1p, expm1, rsqrt); the interpreter
+    has no libdevice of its own. Installed as the interpreted module's ``libdevice`` global."""
+    import types
+
+    import numpy as np
+    import triton.language as tl
+    from triton.runtime import interpreter as ti
+
+    def unary(fn):
+        def f(x, *args, **kwargs):
+            data = fn(np.asarray(x.handle.data, dtype=np.float32)).astype(np.float32)
+            return tl.core.tensor(ti.TensorHandle(data, x.handle.dtype.scalar), x.type)
+        return f
+
+    return types.SimpleNamespace(log1p=unary(np.log1p), expm1=unary(np.expm1),
+                                 rsqrt=unary(lambda v: np.float32(1.0) / np.sqrt(v)))
+
+
+def golden_credit(root, rows=2, t=256):
+    """Every credit kernel of the reference (moment_kernels.py) on Cut-like inputs, through the patched interpreter:
+    implicit_key_context (bf16 inputs), the value pass, the key scan (with and without the value credit), query
+    moments and the identity phase's key moments. Inputs are regenerated by credit_inputs(rows, t, seed)."""
+    patch_triton_interpreter()
+    spec = importlib.util.spec_from_file_location('ref_moments_patched', root / 'train/speedrun/moment_kernels.py')
+    mk = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mk)
+    mk.libdevice = interpreter_libdevice()
+    x = credit_inputs(rows, t)
+    b16 = lambda z: z.bfloat16().contiguous()
+    q16, k16, v16, h16 = b16(x['qp']), b16(x['kp']), b16(x['values']), b16(x['hub'])
+    out = {}
+    for window in (128, t):
+        lse, center = mk._implicit_key_context(q16, k16, v16, h16, window, edges=True)
+        raw_value = mk._value_pass(q16, k16, lse, x['hub'], window)
+        key = mk._key_scan(x['qp'], x['kp'], x['k_raw'], lse, x['values'], x['hub'], center, x['cos'], x['sin'],
+                           window, 0.003, False)[0]
+        key_v, raw_v = mk._key_scan(x['qp'], x['kp'], x['k_raw'], lse, x['values'], x['hub'], center, x['cos'],
+                                    x['sin'], window, 0.003, True)
+        sq = x['q_raw'].square().sum(-1)
+        steps = 0.01 * (sq / 64).sqrt().clamp(min=1e-6)
+        qs = torch.empty(1, rows, t, 64, dtype=torch.bfloat16)
+        mk._moment_query_scores(q16, k16, v16, h16, x['q_raw'].unsqueeze(0).contiguous(), sq, x['kp'], x['cos'],
+                                x['sin'], lse, center, steps, qs, 4, window)
+        out[window] = dict(lse=lse.clone(), center=center.clone(), raw_value=raw_value.clone(), key=key.clone(),
+                           key_v=key_v.clone(), raw_v=raw_v.clone(), query=qs[0].float().clone(), sq=sq, steps=steps)
+    # identity phase: full causal key moments (receivers s >= t), lse / hub_out of the full causal context
+    lse, center = mk._implicit_key_context(q16, k16, v16, h16, t, edges=True)
+    sqk = x['k_raw'].square().sum(-1)
+    stepsk = 0.01 * (sqk / 64).sqrt().clamp(min=1e-6)
+    ko = torch.empty(1, rows, t, 64)
+    kv = torch.empty(1, rows, t, 64)
+    mk._moment_key_scores(q16, k16, v16, h16, x['k_raw'].unsqueeze(0).contiguous(), sqk, x['qp'], x['cos'], x['sin'],
+                          lse, center, stepsk, ko, kv, 2)
+    out['keys'] = dict(lse=lse.clone(), center=center.clone(), sq=sqk, steps=stepsk, out=ko[0].clone(),
+                       values=kv[0].clone())
+    torch.save(dict(rows=rows, length=t, seed=7, out=out), HERE / 'credit_kernels.pt')
+    print('credit kernels: ok')
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -150,6 +259,7 @@ def main():
     golden_population(eggroll, length=2048)
     golden_step(eggroll)
     golden_implicit(root)
+    golden_credit(root)
 
 
 if __name__ == '__main__':

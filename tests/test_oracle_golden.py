@@ -122,3 +122,46 @@ def test_implicit_key_context_matches_reference_kernel(golden):
         got_lse, got_center = credit.implicit_key_context(q, k, v, hub, window)
         torch.testing.assert_close(got_lse.float(), lse, rtol=1e-5, atol=1e-5)
         torch.testing.assert_close(got_center.float(), center, rtol=1e-4, atol=1e-5)
+
+
+def _credit_case(golden):
+    import sys
+    from conftest import GOLDEN
+    sys.path.insert(0, str(GOLDEN))
+    from credit_inputs import credit_inputs
+    g = golden('credit_kernels.pt')
+    x = credit_inputs(g['rows'], g['length'], g['seed'])
+    b16 = {k: x[k].bfloat16().double() for k in ('qp', 'kp', 'values', 'hub')}
+    return g, x, b16
+
+
+def _rel(a, r):
+    return ((a.double() - r.double()).abs().max() / r.double().abs().max()).item()
+
+
+@pytest.mark.parametrize('window', [128, 256])
+def test_credit_oracle_matches_reference_kernels(golden, window):
+    """The dense credit restatements (bf16 operand rounding emulated) against the reference Triton kernels run under
+    the interpreter (its bf16 dot and rounding fixed, tests/golden/make_golden.py)."""
+    g, x, b = _credit_case(golden)
+    o = g['out'][window]
+    lse, center = credit.implicit_key_context(b['qp'], b['kp'], b['values'], b['hub'], window)
+    assert _rel(lse, o['lse']) < 1e-6 and _rel(center, o['center']) < 1e-6
+    vp = credit.value_pass(b['qp'], b['kp'], o['lse'], x['hub'], window, emulate=True)
+    assert _rel(vp, o['raw_value']) < 1e-4
+    key = credit.key_scan(x['qp'], x['kp'], x['k_raw'], o['lse'], x['values'], x['hub'], o['center'], x['cos'],
+                          x['sin'], window, 0.003, emulate=True)
+    assert _rel(key, o['key']) < 1e-3
+    assert torch.equal(o['key_v'], o['key'])
+    qs = credit.moment_query_scores(b['qp'], b['kp'], b['values'], b['hub'], x['q_raw'], o['sq'], x['kp'], x['cos'],
+                                    x['sin'], o['lse'], o['center'], o['steps'], window, emulate=True)
+    qs = qs.float().bfloat16().float()  # the reference stores bf16
+    assert (qs != o['query']).float().mean() < 0.01 and _rel(qs, o['query']) < 1e-3
+
+
+def test_key_moment_oracle_matches_reference_kernel(golden):
+    g, x, b = _credit_case(golden)
+    o = g['out']['keys']
+    out, values = credit.moment_key_scores(b['qp'], b['kp'], b['values'], b['hub'], x['k_raw'], o['sq'], x['qp'],
+                                           x['cos'], x['sin'], o['lse'], o['center'], o['steps'], emulate=True)
+    assert _rel(out, o['out']) < 1e-4 and _rel(values, o['values']) < 1e-4
