@@ -90,6 +90,64 @@ typedef struct {
 #define NOISE_REDUCTION_MEAN 0
 #define NOISE_REDUCTION_SUM 1
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Credit-readout kernels (reference train/speedrun/moment_kernels.py). Rows are (layer, head, sequence) slices of
+ * one attention map, [rows, T, 64]; receiver/query s and key t interact iff 0 <= s - t <= window. T % 64 == 0.
+ * ------------------------------------------------------------------------------------------------------------- */
+#define NOISE_DTYPE_F32 0
+#define NOISE_DTYPE_BF16 1
+
+/* A [rows, T, 64] view: element (row, t, c) at data + L * layer_stride + (row % heads) * 64 + t * token_stride + c,
+ * L = row / heads, or layer_map[row / heads] when layer_map (int32, device) is set. The reference's stacked layout is
+ * heads = 1, layer_stride = T * 64, token_stride = 64; its "by token" (layers, T, heads * 64) views
+ * (moment_kernels.py:66-74) are heads = H, layer_stride = stride(0), token_stride = stride(1). 16-byte aligned. */
+typedef struct {
+  void* data;
+  int64_t layer_stride;
+  int64_t token_stride;
+  int heads;
+  const int32_t* layer_map;
+} noise_rows_t;
+
+/* lse[row, s] = logsumexp_t q_s.k_t / 8 and center[row, s] = sum_t p(s, t) (hub_s . v_t) over the window; q, k,
+ * values, hub contiguous [rows, T, 64] of `dtype` (fp32 operands use tf32 dots, as the reference's PREC = 'tf32').
+ * Replaces moment_kernels.implicit_key_context_edges (moment_kernels.py:137-194); window % 64 == 0. */
+int noise_implicit_key_context(const void* q, const void* k, const void* values, const void* hub, int dtype, int rows,
+                               int tokens, int window, float* lse, float* center, void* stream);
+
+/* out[row, t] = sum_{s: 0 <= s - t <= window} exp(q_s.k_t / 8 - lse_s) source[row, s] (64 channels), the
+ * probabilities rounded to bf16 and the fp32 source split into bf16 hi + lo, fp32 accumulation. Replaces
+ * moment_kernels._value_pass / _value_credit_kernel (moment_kernels.py:612-717) and value_gluon.value_pass_gluon:
+ * raw_value_credits(_by_token), terminal_value_credits(_into). q, k contiguous [rows, T, 64] of `dtype`. */
+int noise_value_pass(const void* q, const void* k, int dtype, const float* lse, const noise_rows_t* source,
+                     const noise_rows_t* out, int rows, int tokens, int window, void* stream);
+
+/* Key credits: per key t and raw key coordinate d, the degree-2 moment response of the receivers' softmax to a finite
+ * step sigma * rms(k_raw[t]) of k_raw[t, d] through RoPE and the RMS norm (moment_kernels.py:467-607; key_gluon.py);
+ * with value_out (data != NULL) also the raw value credit sum_s p hub_s. All inputs fp32 contiguous; cos / sin
+ * [T, 32]; key_out / value_out fp32 views. */
+int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const float* lse, const float* values,
+                   const float* hub, const float* center, const float* cos, const float* sin, int rows, int tokens,
+                   int window, float sigma, const noise_rows_t* key_out, const noise_rows_t* value_out, void* stream);
+
+/* The identity phase's key credits and value sums (moment_kernels._moment_keys_kernel, :370-462): receivers s >= t
+ * (full causal), q, k, v, hub bf16 [rows, T, 64]; raw (the keys' raw coordinates), side (the queries' fp32 pair
+ * feature source) fp32 [rows, T, 64]; sq, steps (keys'), lse, hub_out (receivers') [rows, T]; out, values_out fp32
+ * views. */
+int noise_moment_key_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
+                            const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
+                            const float* hub_out, const float* steps, int rows, int tokens, const noise_rows_t* out,
+                            const noise_rows_t* values_out, void* stream);
+
+/* Query credits: per query s and raw query coordinate d, zn / (1 + zd) / steps_s from the numerator / denominator
+ * moments of its own softmax (moment_kernels._moment_queries_kernel, :197-365), rounded to bf16 (stored as bf16 or
+ * as fp32 per out_dtype). q, k, v, hub bf16 [rows, T, 64]; raw (queries' raw coordinates), side (the keys' fp32 pair
+ * feature source, kp at the reference's call site) fp32 [rows, T, 64]; sq, steps, lse, hub_out [rows, T]. */
+int noise_moment_query_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
+                              const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
+                              const float* hub_out, const float* steps, int rows, int tokens, int window,
+                              const noise_rows_t* out, int out_dtype, void* stream);
+
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);
 

@@ -33,6 +33,7 @@
 #include "gemm.cuh"
 #include "noise_b200.h"
 #include "ptx.cuh"
+#include "warp_mma.cuh"
 
 namespace noise {
 
@@ -463,38 +464,6 @@ struct AttnArgs {
   Slice nproj;  // c_proj noise (b used)
 };
 
-__device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in a [64][64] bf16 tile
-  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 __device__ __forceinline__ void load_tile_async(uint32_t sbase, const __nv_bfloat16* g, int tid) {
   // 64 rows x 128 B = 512 16-byte chunks, 128 threads x 4
 #pragma unroll
@@ -518,7 +487,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
   const uint32_t sK[2] = {sQ + ATT_BQ * 128, sQ + ATT_BQ * 128 + ATT_BK * 128};
   const uint32_t sV[2] = {sQ + ATT_BQ * 128 + 2 * ATT_BK * 128, sQ + ATT_BQ * 128 + 3 * ATT_BK * 128};
 
-  const int lo = q0 - p.window > 0 ? (q0 - p.window) / ATT_BK : 0;  // window % 64 == 0
+  const int lo = q0 - p.window >= 0 ? (q0 - p.window) / ATT_BK : 0;  // window % 64 == 0
   const int hi = q0 / ATT_BK;
 
   load_tile_async(sQ, p.q + base + static_cast<int64_t>(q0) * HD, tid);
@@ -569,7 +538,7 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
       }
     }
     // masks: diagonal tile (key <= query) and the window's first tile (query - key <= window)
-    const bool diag = kt == hi, edge = (q0 - p.window > 0) && kt == lo;
+    const bool diag = kt == hi, edge = (q0 - p.window >= 0) && kt == lo;
     if (diag || edge) {
 #pragma unroll
       for (int n = 0; n < 8; ++n)

@@ -1,0 +1,321 @@
+"""Drop-in credit-readout ops (reference train/speedrun/moment_kernels.py) on the sm_100a kernels of
+libnoise_b200.so.
+
+Same function names, arguments, shapes and results as the reference module; each is also registered as a
+``torch.library.custom_op`` (namespace ``noise_b200``) with a fake implementation, so they stay usable under
+``torch.compile`` and CUDA-graph capture (no host synchronisation, outputs from the caching allocator).
+``key_scan`` / ``value_pass`` have the signatures of the reference's ``KEY_IMPL`` / ``VALUE_IMPL`` plug-in seams
+(moment_kernels.py:642-650), so run.py:1678-1681 can install them in place of the Gluon kernels.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+F32, BF16 = 0, 1
+_DT = {torch.float32: F32, torch.bfloat16: BF16}
+
+
+def _rows(t, heads=1, layers=None):
+    """noise_rows_t of a [rows, T, 64] stacked view (heads = 1) or a (layers, T, heads * 64) by-token view."""
+    if t.stride(-1) != 1:
+        raise ValueError('credit views need a unit last stride')
+    m = _lib.Rows()
+    m.data = t.data_ptr()
+    m.layer_stride, m.token_stride = t.stride(0), t.stride(1)
+    m.heads = heads
+    m.layer_map = layers.data_ptr() if layers is not None else None
+    return m
+
+
+def _stream(t):
+    return _lib.stream_handle(t.device)
+
+
+def _c(t, dtype=None):
+    t = t.detach()
+    if dtype is not None and t.dtype != dtype:
+        t = t.to(dtype)
+    return t.contiguous()
+
+
+def _check(rc, what):
+    _lib.check(rc, what)
+
+
+def _rope(cos, sin):
+    return _c(cos, torch.float32), _c(sin, torch.float32)
+
+
+# --- lse and center -----------------------------------------------------------------------------------------------
+
+def implicit_key_context_edges_impl(q, k, values, hub, window):
+    h, t, _ = q.shape
+    dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    q, k, values, hub = (_c(z, dt) for z in (q, k, values, hub))
+    _lib.require_cuda(q)
+    lse = torch.empty((h, t), device=q.device, dtype=torch.float32)
+    center = torch.empty_like(lse)
+    _check(_lib.lib().noise_implicit_key_context(q.data_ptr(), k.data_ptr(), values.data_ptr(), hub.data_ptr(),
+                                                 _DT[dt], h, t, window, lse.data_ptr(), center.data_ptr(),
+                                                 _stream(q)), 'noise_implicit_key_context')
+    return lse, center
+
+
+# --- value credits --------------------------------------------------------------------------------------------------
+
+def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, layers=None):
+    """sum_s p * source (moment_kernels._value_pass): source stacked (rows, T, C) or (in_heads > 1) by token
+    (rows // in_heads, T, in_heads * C); the output stacked or (out_heads > 1) by token, into ``out`` when given.
+    The signature of the reference's VALUE_IMPL plug-in."""
+    h, t, _ = q.shape
+    dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
+    q, k, lse = _c(q, dt), _c(k, dt), _c(lse, torch.float32)
+    _lib.require_cuda(q)
+    if source.dtype != torch.float32 or source.stride(-1) != 1:
+        source = source.float().contiguous()
+    channels = source.shape[-1] // in_heads
+    if channels != 64:
+        raise ValueError('the value pass runs 64 channels per head')
+    if out is None:
+        out = source.new_empty((h // out_heads, t, out_heads * channels), dtype=torch.float32)
+    src_rows = _rows(source, in_heads)
+    out_rows = _rows(out, out_heads, layers)
+    _check(_lib.lib().noise_value_pass(q.data_ptr(), k.data_ptr(), _DT[dt], lse.data_ptr(), ctypes.byref(src_rows),
+                                       ctypes.byref(out_rows), h, t, window, _stream(q)), 'noise_value_pass')
+    return out
+
+
+# --- key credits ----------------------------------------------------------------------------------------------------
+
+def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, with_values=False, out_heads=1, key=None,
+             layers=None):
+    """The key credits (and with_values the raw value credits), stacked (rows, T, D) or by token
+    (rows // out_heads, T, out_heads * D), into ``key`` when given (moment_kernels._key_scan). The signature of the
+    reference's KEY_IMPL plug-in; returns (key, raw_value) (raw_value is key when with_values is False)."""
+    h, t, d = k_raw.shape
+    qp, kp, k_raw, values, hub = (_c(z, torch.float32) for z in (qp, kp, k_raw, values, hub))
+    lse, center = _c(lse, torch.float32), _c(center, torch.float32)
+    cos, sin = _rope(cos, sin)
+    _lib.require_cuda(qp)
+    shape = (h // out_heads, t, out_heads * d)
+    key = qp.new_empty(shape) if key is None else key
+    raw_value = qp.new_empty(shape) if with_values else None
+    key_rows = _rows(key, out_heads, layers)
+    val_rows = _rows(raw_value, out_heads, layers) if with_values else _lib.Rows()
+    _check(_lib.lib().noise_key_scan(qp.data_ptr(), kp.data_ptr(), k_raw.data_ptr(), lse.data_ptr(), values.data_ptr(),
+                                     hub.data_ptr(), center.data_ptr(), cos.data_ptr(), sin.data_ptr(), h, t, window,
+                                     float(sigma), ctypes.byref(key_rows), ctypes.byref(val_rows), _stream(qp)),
+           'noise_key_scan')
+    k_out = key.view(h, t, d) if out_heads == 1 and layers is None else key
+    if not with_values:
+        return k_out, k_out
+    return k_out, raw_value.view(h, t, d) if out_heads == 1 else raw_value
+
+
+# --- query and key moments ------------------------------------------------------------------------------------------
+
+def _stacked_raw(raw, rows, t):
+    """The raw coordinates as contiguous fp32 [rows, T, 64] (the reference passes (1, rows, T, 64))."""
+    return raw.detach().float().reshape(rows, t, 64).contiguous()
+
+
+def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window=None, out_heads=0,
+                             layers=None):
+    rows, t, d = q.shape
+    if d != 64:
+        raise ValueError('head_dim 64 only (the reference asserts it)')
+    q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
+    raw = _stacked_raw(raw, rows, t)
+    side = _c(side, torch.float32)
+    sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
+    cos, sin = _rope(cos, sin)
+    window = t if window is None else min(window, t)
+    if out_heads:
+        target, heads, dt = out, out_heads, F32
+    else:  # the reference's (1, rows, T, D) bf16 output
+        target, heads = out[0], 1
+        dt = _DT[out.dtype]
+    o = _rows(target, heads, layers)
+    _check(_lib.lib().noise_moment_query_scores(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
+                                                raw.data_ptr(), sq.data_ptr(), side.data_ptr(), cos.data_ptr(),
+                                                sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(), steps.data_ptr(),
+                                                rows, t, window, ctypes.byref(o), dt, _stream(q)),
+           'noise_moment_query_scores')
+
+
+def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values):
+    rows, t, d = q.shape
+    q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
+    raw = _stacked_raw(raw, rows, t)
+    side = _c(side, torch.float32)
+    sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
+    cos, sin = _rope(cos, sin)
+    o, val = out.view(rows, t, d), values.view(rows, t, d)
+    if o.dtype != torch.float32 or o.stride(-1) != 1:
+        raise ValueError('out / values: fp32 [rows, T, 64] views')
+    ro, rv = _rows(o), _rows(val)
+    _check(_lib.lib().noise_moment_key_scores(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(), raw.data_ptr(),
+                                              sq.data_ptr(), side.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                              lse.data_ptr(), hub_out.data_ptr(), steps.data_ptr(), rows, t,
+                                              ctypes.byref(ro), ctypes.byref(rv), _stream(q)),
+           'noise_moment_key_scores')
+
+
+# --- the reference's custom ops (names as in moment_kernels.py:184-717) ---------------------------------------------
+
+@torch.library.custom_op('noise_b200::implicit_key_context_edges', mutates_args=())
+def implicit_key_context_edges(q: torch.Tensor, k: torch.Tensor, values: torch.Tensor, hub: torch.Tensor,
+                               window: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(lse, center) [rows, T] of the windowed softmax q k^T / 8 (moment_kernels.py:184-188)."""
+    return implicit_key_context_edges_impl(q, k, values, hub, window)
+
+
+@implicit_key_context_edges.register_fake
+def _(q, k, values, hub, window):
+    h, t, _ = q.shape
+    return q.new_empty((h, t), dtype=torch.float32), q.new_empty((h, t), dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::key_credits', mutates_args=())
+def key_credits(qp: torch.Tensor, kp: torch.Tensor, k_raw: torch.Tensor, lse: torch.Tensor, values: torch.Tensor,
+                hub: torch.Tensor, center: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, window: int,
+                sigma: float) -> torch.Tensor:
+    """batched_key_scores' key scan (moment_kernels.py:582-587)."""
+    return key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, False)[0]
+
+
+@key_credits.register_fake
+def _(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma):
+    return torch.empty_like(k_raw, dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::key_credits_into', mutates_args=('out',))
+def key_credits_into(qp: torch.Tensor, kp: torch.Tensor, k_raw: torch.Tensor, lse: torch.Tensor, values: torch.Tensor,
+                     hub: torch.Tensor, center: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, window: int,
+                     sigma: float, out: torch.Tensor, layers: torch.Tensor | None = None) -> None:
+    """key_credits_by_token into out, a (layers, T, heads * D) view with last stride 1 (moment_kernels.py:595-602)."""
+    key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, False, out.shape[-1] // k_raw.shape[-1],
+             out, layers)
+
+
+@key_credits_into.register_fake
+def _(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, out, layers=None):
+    return None
+
+
+@torch.library.custom_op('noise_b200::key_and_raw_value_credits', mutates_args=())
+def key_and_raw_value_credits(qp: torch.Tensor, kp: torch.Tensor, k_raw: torch.Tensor, lse: torch.Tensor,
+                              values: torch.Tensor, hub: torch.Tensor, center: torch.Tensor, cos: torch.Tensor,
+                              sin: torch.Tensor, window: int, sigma: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """The key scan with the raw value credit sum_s p hub in the same pass (moment_kernels.py:17)."""
+    key, raw = key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, True)
+    return key, raw
+
+
+@key_and_raw_value_credits.register_fake
+def _(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma):
+    return torch.empty_like(k_raw, dtype=torch.float32), torch.empty_like(k_raw, dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::raw_value_credits', mutates_args=())
+def raw_value_credits(q: torch.Tensor, k: torch.Tensor, lse: torch.Tensor, hub: torch.Tensor,
+                      window: int) -> torch.Tensor:
+    """sum_s p * hub for (heads, tokens, 64) inputs (moment_kernels.py:664-668)."""
+    return value_pass(q, k, lse, hub, window)
+
+
+@raw_value_credits.register_fake
+def _(q, k, lse, hub, window):
+    return torch.empty_like(hub, dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::terminal_value_credits', mutates_args=())
+def terminal_value_credits(q: torch.Tensor, k: torch.Tensor, lse: torch.Tensor, corrected: torch.Tensor,
+                           window: int) -> torch.Tensor:
+    """sum_s p * corrected (moment_kernels.py:676-680)."""
+    return value_pass(q, k, lse, corrected.contiguous(), window)
+
+
+@terminal_value_credits.register_fake
+def _(q, k, lse, corrected, window):
+    return torch.empty_like(corrected, dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::raw_value_credits_by_token', mutates_args=())
+def raw_value_credits_by_token(q: torch.Tensor, k: torch.Tensor, lse: torch.Tensor, hub: torch.Tensor, window: int,
+                               heads: int) -> torch.Tensor:
+    """raw_value_credits as (layers, T, heads * 64) (moment_kernels.py:693-698)."""
+    return value_pass(q, k, lse, hub, window, 1, heads)
+
+
+@raw_value_credits_by_token.register_fake
+def _(q, k, lse, hub, window, heads):
+    rows, t, d = hub.shape
+    return hub.new_empty((rows // heads, t, heads * d), dtype=torch.float32)
+
+
+@torch.library.custom_op('noise_b200::terminal_value_credits_into', mutates_args=('out',))
+def terminal_value_credits_into(q: torch.Tensor, k: torch.Tensor, lse: torch.Tensor, corrected: torch.Tensor,
+                                window: int, out: torch.Tensor, layers: torch.Tensor | None = None) -> None:
+    """terminal_value_credits_by_token into out (moment_kernels.py:706-712)."""
+    heads = corrected.shape[-1] // q.shape[-1]
+    value_pass(q, k, lse, corrected, window, heads, heads, out, layers)
+
+
+@terminal_value_credits_into.register_fake
+def _(q, k, lse, corrected, window, out, layers=None):
+    return None
+
+
+@torch.library.custom_op('noise_b200::moment_query_scores', mutates_args=('out',))
+def moment_query_scores(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, hub: torch.Tensor, raw: torch.Tensor,
+                        sq: torch.Tensor, side: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, lse: torch.Tensor,
+                        hub_out: torch.Tensor, steps: torch.Tensor, out: torch.Tensor, repeat: int,
+                        window: int | None = None) -> None:
+    """Query credits into the reference's (1, rows, T, D) bf16 out (moment_kernels.py:338-343)."""
+    if repeat != 4 or q.shape[-1] != 64:
+        raise ValueError('the reference call (repeat = head_dim // 16, head_dim 64)')
+    moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window)
+
+
+@moment_query_scores.register_fake
+def _(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, repeat, window=None):
+    return None
+
+
+@torch.library.custom_op('noise_b200::moment_query_scores_into', mutates_args=('out',))
+def moment_query_scores_into(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, hub: torch.Tensor, raw: torch.Tensor,
+                             sq: torch.Tensor, side: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                             lse: torch.Tensor, hub_out: torch.Tensor, steps: torch.Tensor, out: torch.Tensor,
+                             window: int | None = None, layers: torch.Tensor | None = None) -> None:
+    """Query credits by token into out, a (layers, T, heads * D) fp32 view (moment_kernels.py:351-360)."""
+    moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window,
+                             out.shape[-1] // q.shape[-1], layers)
+
+
+@moment_query_scores_into.register_fake
+def _(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window=None, layers=None):
+    return None
+
+
+@torch.library.custom_op('noise_b200::moment_key_scores', mutates_args=('out', 'values'))
+def moment_key_scores(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, hub: torch.Tensor, raw: torch.Tensor,
+                      sq: torch.Tensor, side: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, lse: torch.Tensor,
+                      hub_out: torch.Tensor, steps: torch.Tensor, out: torch.Tensor, values: torch.Tensor,
+                      repeat: int) -> None:
+    """The identity phase's key credits and value sums (moment_kernels.py:451-457); out / values fp32 with rows x T x
+    64 elements."""
+    if repeat != 2 or q.shape[-1] != 64:
+        raise ValueError("the identity phase's call (repeat = head_dim // 32, head_dim 64)")
+    moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values)
+
+
+@moment_key_scores.register_fake
+def _(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values, repeat):
+    return None
+
+
+KEY_IMPL = key_scan      # run.py:1678-1679 installs these in the reference module
+VALUE_IMPL = value_pass
