@@ -41,6 +41,7 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    ap.add_argument('--workload', default='population', choices=['population', 'credit'])
     return ap.parse_args()
 
 
@@ -297,10 +298,82 @@ def run_ours(a):
         torch.distributed.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# credit kernels in isolation
+# ------------------------------------------------------------------------------------------------------------------
+CREDIT_FLOP_PER_PAIR = {  # algorithmic FLOPs per visible (receiver, key) pair, one multiply-add = 2
+    'implicit_key_context': 256, 'value_pass': 384, 'key_scan': 704, 'moment_query_scores': 1152,
+    'moment_key_scores': 832}
+
+
+def run_credit(a):
+    """One line per window: every credit kernel on rows = 16 x 8 heads, T = 2048, d = 64 (q, k, v ~ N(0,1)/8, hub the
+    per-token error signal e[b, t] u_h with e ~ N(0, 1), u_h ~ N(0, 1)/8), CUDA-event timed over K launches after W
+    warm-ups; inputs (~0.5 GB) exceed L2."""
+    import noise_b200.moment_kernels as mk
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    g = torch.Generator(device).manual_seed(0)
+    B, H, t = 16, 8, 2048
+    rows = B * H
+    rn = lambda *s: torch.randn(*s, device=device, generator=g)
+    q, k, v = (rn(B, H, t, 64).div_(8).view(rows, t, 64) for _ in range(3))
+    e = rn(B, 1, t, 1)
+    u = rn(1, H, 1, 64) / 8
+    hub = (e * u).reshape(rows, t, 64).contiguous()
+    raw_q, raw_k = rn(rows, t, 64), rn(rows, t, 64)
+    inv = 1.0 / 10000 ** (torch.arange(0, 64, 2, dtype=torch.float32, device=device) / 64)
+    freqs = torch.outer(torch.arange(t, dtype=torch.float32, device=device), inv)
+    cos, sin = freqs.cos().bfloat16().float(), freqs.sin().bfloat16().float()
+    b16 = [z.bfloat16() for z in (q, k, v, hub)]
+    sq = raw_q.square().sum(-1)
+    steps = 0.01 * (sq / 64).sqrt().clamp(min=1e-6)
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    tf_peak = peaks.get('bf16_tflops', 1590.0)
+    for window in (2048, 1024):
+        pairs = rows * visible_pairs(t, window)
+        lse, center = mk.implicit_key_context_edges(*b16, window)
+        qs = torch.empty(1, rows, t, 64, dtype=torch.bfloat16, device=device)
+        ko, kv = torch.empty(1, rows, t, 64, device=device), torch.empty(1, rows, t, 64, device=device)
+        calls = {
+            'implicit_key_context': lambda: mk.implicit_key_context_edges(*b16, window),
+            'value_pass': lambda: mk.raw_value_credits(b16[0], b16[1], lse, hub, window),
+            'key_scan': lambda: mk.key_credits(q, k, raw_k, lse, v, hub, center, cos, sin, window, 0.003),
+            'moment_query_scores': lambda: mk.moment_query_scores(*b16, raw_q.unsqueeze(0), sq, k, cos, sin, lse,
+                                                                  center, steps, qs, 4, window),
+        }
+        if window >= t:
+            calls['moment_key_scores'] = lambda: mk.moment_key_scores(*b16, raw_k.unsqueeze(0), sq, q, cos, sin, lse,
+                                                                      center, steps, ko, kv, 2)
+        res = {}
+        for name, fn in calls.items():
+            for _ in range(a.warmup):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(a.steps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / a.steps
+            flops = CREDIT_FLOP_PER_PAIR[name] * pairs
+            res[name] = {'us': round(us, 1), 'tflops': round(flops / us / 1e6, 1),
+                         'frac_of_tensor_peak': round(flops / us / 1e6 / tf_peak, 4),
+                         'mufu_floor_us': round(pairs / (16 * 148 * 1.965e9) * 1e6, 1)}
+        print(json.dumps({'metric': 'credit-readout kernel time (BASELINE config 3)', 'unit': 'us per launch',
+                          'config': {'workload': 'credit kernels in isolation', 'B': B, 'H': H, 'T': t, 'd_head': 64,
+                                     'window': window, 'pairs': pairs},
+                          'peak': {'bf16_tflops': tf_peak, 'source': 'MEASURED_PEAKS.json bf16_tflops (burst)'},
+                          'kernels': res}), flush=True)
+
+
 def main():
     a = args_()
     if a.impl == 'reference':
         run_reference(a)
+    elif a.workload == 'credit':
+        run_credit(a)
     else:
         run_ours(a)
 
