@@ -1,0 +1,363 @@
+// Windowed causal attention on tcgen05 (sm_100a) for the population forward: softmax(q k^T / 8) v with key s
+// visible to query t iff 0 <= t - s <= window (reference utils/model.py:17-31, flex attention).
+//
+// q and k reach this kernel RMS-normalised per head (utils/model.py:94; EpiQKV), so |q|, |k| <= 8 (8.03 after bf16
+// rounding) and every logit q.k / 8 <= 8.03. Softmax is shift invariant, so the kernel uses the fixed offset 8 in place
+// of a running row maximum: p = exp(q.k / 8 - 8) <= 1.03 never overflows, there is no max pass and no rescaling of the
+// accumulator, and O = sum_j P_j V_j accumulates straight in tensor memory across key tiles.
+//
+// One CTA per (member x head, pair of 128-query tiles A = 2i, B = 2i + 1), 320 threads:
+//   warp 0      TMA: Q_A, Q_B once, then 128-key K / V tiles (the union of both tiles' key ranges) into a 3-stage
+//               ring (128-byte swizzle); both query tiles share every K / V load;
+//   warp 1      TMEM (512 columns: S_A, S_B 128 each, O_A, O_B 64 each) and one lane issuing, per key tile,
+//               S_w = Q_w K^T (M=128, N=128, K=64) for each tile w that sees it, then O_w += P_w V of the previous
+//               key tile (M=128, N=64, K=128; V an MN-major operand);
+//   warps 2..5  softmax group A, warps 6..9 group B: one query row per thread; S_w is read with one batched
+//               tcgen05.ld and released at once, P = exp2(s log2(e) / 8 - 8 log2(e)) goes as bf16 into 128-byte-
+//               swizzled shared memory (the A operand of the next O MMA), one in four exponentials on the FMA pipes
+//               (Cody-Waite split, cubic on [-1/2, 1/2], rel. error 7.5e-5) to offload the MUFU pipe; at the end
+//               y = O / l (bf16) and the per-head partial dot y . b of the c_proj rank-1 term.
+// Only the diagonal key tile and the window's first tile take the masked path.
+#pragma once
+#include <type_traits>
+
+#include "ptx.cuh"
+
+namespace noise {
+
+constexpr int TA_BQ = 128, TA_BK = 128, TA_STAGES = 3, TA_THREADS = 320;
+constexpr int TA_TILE = 128 * 128;  // bytes of one [128][64] bf16 tile
+constexpr int TA_Q = 0;             // Q_A, Q_B
+constexpr int TA_K = TA_Q + 2 * TA_TILE;
+constexpr int TA_V = TA_K + TA_STAGES * TA_TILE;
+constexpr int TA_P = TA_V + TA_STAGES * TA_TILE;  // P_A, P_B: 2 sub-tiles each (keys 0..63, 64..127)
+constexpr int TA_BAR = TA_P + 4 * TA_TILE;
+constexpr int TA_SMEM = TA_BAR + 256 + 1024;
+
+struct TAttnArgs {
+  int T, window;
+  int bh;            // member x head rows of q / k / v (each T tokens)
+  __nv_bfloat16* y;  // [M, 512]
+  float* ydot;       // [M, 8]
+  Slice nproj;       // c_proj noise: b used
+  int* status;
+};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Key-tile range [lo, hi] of query tile qt and whether its first tile is cut by the window.
+struct TileRange {
+  int lo, hi;
+  bool edge;
+};
+__device__ __forceinline__ TileRange tile_range(int qt, int window) {
+  const int q0 = qt * TA_BQ;
+  const bool edge = q0 - window >= 0;
+  return TileRange{edge ? (q0 - window) / TA_BK : 0, q0 / TA_BK, edge};
+}
+
+// 2^x for x <= 8.1 on the FMA pipes: x = j + f with j = rint(x), f in [-1/2, 1/2], 2^f by a cubic, 2^j by adding j
+// to the exponent field (x >= -126 here, so the result stays normal).
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: rint(x) in the low mantissa bits
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  float p = fmaf(0.05517161265015602f, f, 0.2426111400127411f);
+  p = fmaf(p, f, 0.6932610273361206f);
+  p = fmaf(p, f, 0.9999280571937561f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+__global__ void __launch_bounds__(TA_THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, TAttnArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TA_BAR);
+  uint64_t* q_full = bar;                    // Q_A / Q_B of the current item landed
+  uint64_t* q_empty = bar + 1;               // every S MMA of the current item done
+  uint64_t* kv_full = bar + 2;               // STAGES
+  uint64_t* kv_empty = kv_full + TA_STAGES;  // STAGES
+  uint64_t* s_full = kv_empty + TA_STAGES;   // per group
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* p_empty = p_full + 2;
+  uint64_t* o_full = p_empty + 2;            // per O buffer (items alternate): all MMAs of the item done
+  uint64_t* o_empty = o_full + 2;            // per O buffer: both groups read their O
+  uint64_t* drain = o_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = p.T / TA_BQ;
+  const int npairs = (nq + 1) / 2;
+  const int items = npairs * p.bh;
+
+  // work item w: pair pi (heaviest first, so every wave of CTAs takes equal-cost items) of head-row bh
+  struct Item {
+    int bh, qa, qb, lo, hi;
+    bool has_b;
+    TileRange ra, rb;
+  };
+  auto item = [&](int w) {
+    Item it;
+    const int pi = npairs - 1 - w / p.bh;
+    it.bh = w % p.bh;
+    it.qa = 2 * pi;
+    it.qb = 2 * pi + 1;
+    it.has_b = it.qb < nq;
+    it.ra = tile_range(it.qa, p.window);
+    it.rb = it.has_b ? tile_range(it.qb, p.window) : TileRange{it.ra.lo, it.ra.lo - 1, false};
+    it.lo = it.ra.lo;
+    it.hi = it.has_b ? it.rb.hi : it.ra.hi;
+    return it;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < TA_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 128);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&p_empty[b], 1);
+      mbar_init(&o_full[b], 1);
+      mbar_init(&o_empty[b], 256);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmq);
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t sbase = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int kv = 0, nitem = 0;  // K / V tiles issued, items started
+      bool ok = true;
+      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+        const Item it = item(w);
+        const int row0 = it.bh * p.T;
+        if (!mbar_wait(q_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status)) break;
+        mbar_arrive_expect_tx(q_full, (it.has_b ? 2 : 1) * TA_TILE);
+        tma_load_2d(smem + TA_Q, &tmq, q_full, 0, row0 + it.qa * TA_BQ);
+        if (it.has_b) tma_load_2d(smem + TA_Q + TA_TILE, &tmq, q_full, 0, row0 + it.qb * TA_BQ);
+        for (int kt = it.lo; kt <= it.hi; ++kt, ++kv) {
+          const int st = kv % TA_STAGES;
+          if (!mbar_wait(&kv_empty[st], (static_cast<uint32_t>(kv / TA_STAGES) & 1u) ^ 1u, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * TA_TILE);
+          tma_load_2d(smem + TA_K + st * TA_TILE, &tmk, &kv_full[st], 0, row0 + kt * TA_BK);
+          tma_load_2d(smem + TA_V + st * TA_TILE, &tmv, &kv_full[st], 0, row0 + kt * TA_BK);
+        }
+      }
+      // drain: the last Q load and the last STAGES K / V loads must land before the CTA exits
+      if (nitem > 0) mbar_wait(q_full, static_cast<uint32_t>(nitem - 1) & 1u, p.status);
+      for (int j = kv - 1; j >= 0 && j >= kv - TA_STAGES; --j)
+        mbar_wait(&kv_full[j % TA_STAGES], static_cast<uint32_t>(j / TA_STAGES) & 1u, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16(TA_BQ, TA_BK);
+      constexpr uint32_t idesc_pv = idesc_bf16(TA_BQ, 64, false, true);
+      int kv = 0, nitem = 0;
+      int s_count[2] = {0, 0}, pv_count[2] = {0, 0};
+      bool ok = true;
+      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+        const Item it = item(w);
+        const int ob = nitem & 1;
+        const TileRange rg[2] = {it.ra, it.rb};
+        auto sees = [&](int g, int kt) { return kt >= rg[g].lo && kt <= rg[g].hi; };
+        int first_pv[2] = {1, 1};  // the item's first O MMA overwrites the accumulator
+        auto issue_pv = [&](int g, int kt, int kvi) {  // O_g += P_g V of key tile kt (ring slot of tile kvi)
+          const int st = kvi % TA_STAGES;
+          if (!mbar_wait(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
+          tc_fence_after();
+          const uint32_t pbase = sbase + TA_P + g * 2 * TA_TILE;
+          const uint32_t vbase = sbase + TA_V + st * TA_TILE;
+#pragma unroll
+          for (int ks = 0; ks < TA_BK / 16; ++ks) {
+            const uint64_t ad = sdesc_kmajor_sw128(pbase + (ks >> 2) * TA_TILE) + 2u * (ks & 3);
+            const uint64_t bd = sdesc_mnmajor_sw128(vbase + ks * 2048, 16);
+            tc_mma(tmem + 256 + ob * 128 + g * 64, ad, bd, idesc_pv, !(first_pv[g] && ks == 0));
+          }
+          first_pv[g] = 0;
+          tc_commit(&p_empty[g]);
+          ++pv_count[g];
+          return true;
+        };
+        // the O buffer of this item must have been read by both groups (item nitem - 2)
+        if (!mbar_wait(&o_empty[ob], (static_cast<uint32_t>(nitem >> 1) & 1u) ^ 1u, p.status) ||
+            !mbar_wait(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+          ok = false;
+          break;
+        }
+        const int kv0 = kv;
+        for (int kt = it.lo; kt <= it.hi && ok; ++kt, ++kv) {
+          const int st = kv % TA_STAGES;
+          if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(kv / TA_STAGES) & 1u, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint64_t kd = sdesc_kmajor_sw128(sbase + TA_K + st * TA_TILE);
+          for (int g = 0; g < 2 && ok; ++g) {
+            if (!sees(g, kt)) continue;
+            if (!mbar_wait(&s_empty[g], (static_cast<uint32_t>(s_count[g]) & 1u) ^ 1u, p.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t qd = sdesc_kmajor_sw128(sbase + TA_Q + g * TA_TILE);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tc_mma(tmem + g * TA_BK, qd + 2u * k, kd + 2u * k, idesc_s, k > 0);
+            tc_commit(&s_full[g]);
+            ++s_count[g];
+          }
+          if (kt == it.hi && ok) tc_commit(q_empty);  // the item's last S MMAs read Q
+          if (kt > it.lo && ok) {  // O MMAs of the previous key tile, then release its ring slot
+            for (int g = 0; g < 2 && ok; ++g)
+              if (sees(g, kt - 1)) ok = issue_pv(g, kt - 1, kv - 1);
+            tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
+          }
+        }
+        if (ok) {
+          for (int g = 0; g < 2 && ok; ++g)
+            if (sees(g, it.hi)) ok = issue_pv(g, it.hi, kv0 + (it.hi - it.lo));
+          tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
+          tc_commit(&o_full[ob]);
+        }
+      }
+      tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
+      mbar_wait(drain, 0, p.status);
+    }
+  } else {
+    // softmax groups: warps 2..5 -> group A, 6..9 -> group B; thread = query row of the group's tile
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + g * TA_BK;
+    const uint32_t prow = sbase + TA_P + g * 2 * TA_TILE + r * 128;
+    constexpr float SL2 = 0.125f * 1.4426950408889634f;  // 1/8 in base 2
+    constexpr float OFF = 8.f * 1.4426950408889634f;     // the fixed offset 8 in base 2
+    int cnt = 0, nitem = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+      const Item it = item(w);
+      const int ob = nitem & 1;
+      const TileRange rg = g == 0 ? it.ra : it.rb;
+      const int tq = (g == 0 ? it.qa : it.qb) * TA_BQ + r;
+      const bool active = g == 0 || it.has_b;
+      float l = 0.f;
+      auto tile = [&](auto masked_tag, int kt) {
+        constexpr bool MASKED = decltype(masked_tag)::value;
+        float v[TA_BK];
+#pragma unroll
+        for (int c = 0; c < TA_BK; c += 32) tmem_ld32(s_addr + c, v + c);
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_empty[g]);  // S is in registers: the next S MMA may overwrite it
+        uint32_t pk[TA_BK / 2];
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < TA_BK; c += 8) {
+          float pe[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float x = fmaf(v[c + e], SL2, -OFF);
+            pe[e] = (e & 3) == 3 ? exp2_poly(x) : ex2_approx(x);
+            if constexpr (MASKED) {
+              const int key = kt * TA_BK + c + e;
+              if (key > tq || tq - key > p.window) pe[e] = 0.f;
+            }
+            rs += pe[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) pk[c / 2 + e] = pack_bf16x2(pe[2 * e], pe[2 * e + 1]);
+        }
+        // the P buffer is free once the previous O MMA of this group completed
+        if (!mbar_wait(&p_empty[g], (static_cast<uint32_t>(cnt) & 1u) ^ 1u, p.status)) return false;
+#pragma unroll
+        for (int c = 0; c < TA_BK; c += 8) {  // keys c .. c + 7: sub-tile c / 64, chunk (c % 64) / 8, 128-B swizzle
+          const int chunk = (c & 63) >> 3;
+          st_shared_v4(prow + (c >> 6) * TA_TILE + ((chunk ^ (r & 7)) << 4), pk[c / 2], pk[c / 2 + 1],
+                       pk[c / 2 + 2], pk[c / 2 + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&p_full[g]);
+        l += rs;
+        return true;
+      };
+      if (active) {
+        for (int kt = rg.lo; kt <= rg.hi && ok; ++kt, ++cnt) {
+          if (!mbar_wait(&s_full[g], static_cast<uint32_t>(cnt) & 1u, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const bool masked = kt == rg.hi || (rg.edge && kt == rg.lo);
+          ok = masked ? tile(std::true_type{}, kt) : tile(std::false_type{}, kt);
+        }
+      }
+      if (!ok || !mbar_wait(&o_full[ob], static_cast<uint32_t>(nitem >> 1) & 1u, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float o[64];
+      const uint32_t o_addr = tmem + lane_base + 256 + ob * 128 + g * 64;
+      tmem_ld32(o_addr, o);
+      tmem_ld32(o_addr + 32, o + 32);
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&o_empty[ob]);
+      if (active) {
+        const int j = it.bh / NOISE_N_HEAD, hh = it.bh % NOISE_N_HEAD;
+        const int64_t row = static_cast<int64_t>(j) * p.T + tq;
+        const float inv = 1.f / l;
+        const float* bproj = p.nproj.B(j) + hh * 64;
+        uint4* yr = reinterpret_cast<uint4*>(p.y + row * NOISE_N_EMBD + hh * 64);
+        float dp = 0.f;
+#pragma unroll
+        for (int d = 0; d < 64; d += 8) {
+          float yv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            yv[e] = bf16_round(o[d + e] * inv);
+            dp += yv[e] * bf16_round(bproj[d + e]);
+          }
+          yr[d / 8] = make_uint4(pack_bf16x2(yv[0], yv[1]), pack_bf16x2(yv[2], yv[3]), pack_bf16x2(yv[4], yv[5]),
+                                 pack_bf16x2(yv[6], yv[7]));
+        }
+        p.ydot[row * NOISE_N_HEAD + hh] = dp;
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace noise

@@ -24,12 +24,26 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 
+// Named barrier 1 over the epilogue warps, returning the AND of every thread's predicate.
+__device__ __forceinline__ bool epi_barrier_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(32 * GEMM_EPI_WARPS)
+      : "memory");
+  return r != 0;
+}
+
 template <int BN, int STAGES>
 struct GemmLayout {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr int B_BYTES = BN * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int SCRATCH_BYTES = 4 * 2 * BN;  // per accumulator buffer: two fp32 vectors of the tile's width
+  static constexpr int SCRATCH_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = SCRATCH_OFFSET + 2 * SCRATCH_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFFSET + 8 * (2 * STAGES + 5) + 16 + 1024;  // + 1024 alignment slack
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tcgen05 M=128 needs N in [16, 256], N % 16 == 0");
@@ -39,6 +53,10 @@ struct GemmLayout {
 // Epilogue functor contract (all methods run on a thread that owns `row` and column half `part` of every tile):
 //   static constexpr int CH;                          columns per TMEM load (16, 32 or 64)
 //   void row_begin(int row, int part);                before the first N tile of the row block
+//   void stage(int row0, int col0, float* s, int tid); before every tile, all 256 epilogue threads (tid 0..255):
+//                                                     may fill s[0 .. 2 BN) (16-byte aligned shared memory) with
+//                                                     per-tile vectors; the tile's chunks run after a barrier
+//   (chunk, tile_end and row_end may read the staged vectors through stage_ptr(), set by the kernel)
 //   void chunk(int row, int col, float* v);           v[0..CH) = D[row, col .. col + CH) (may be modified in place)
 //   void tile_end(int row, int n_tile, int part);     after the last chunk of the thread's half of a tile
 //   void row_end(int row, int part);                  after the last N tile
@@ -170,8 +188,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int nb = 0; nb < n_tiles; ++nb, ++t) {
         const int buf = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        ok = mbar_wait(&accf[buf], use & 1u, status);
+        const bool waited = mbar_wait(&accf[buf], use & 1u, status);
         tc_fence_after();
+        // per-tile shared vectors (double-buffered by accumulator buffer: the barrier of tile t + 1 orders every
+        // reader of tile t before the writers of tile t + 2). The barrier also ANDs every epilogue thread's wait
+        // result, so all of them leave the loop together when a bounded wait gives up.
+        float* scratch = reinterpret_cast<float*>(smem + L::SCRATCH_OFFSET + buf * L::SCRATCH_BYTES);
+        e.stage(mb * GEMM_BM, nb * BN, scratch, threadIdx.x - 64);
+        ok = epi_barrier_and(waited);
+        e.scratch = scratch;
         if (ok) {
           const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN + part * HALF);
 #pragma unroll 1

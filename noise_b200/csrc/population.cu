@@ -226,22 +226,36 @@ struct EpiQKV {
   __nv_bfloat16* q;
   __nv_bfloat16* k;
   __nv_bfloat16* v;
-  int j, t;
+  int j, t, col0;
   float sg;
+  float* scratch;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     j = row / T;
     t = row - j * T;
     sg = sign[j];
   }
+  // the tile's slice of a (q, k or v section) into shared memory
+  __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
+    col0 = c0;
+    const int jj = row0 / T, sec = c0 / D;
+    const float* a = (sec == 0 ? nq.A(jj) : sec == 1 ? nk.A(jj) : nv.A(jj)) + (c0 % D);
+    s[tid] = a[tid];
+  }
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* val) {
     const int sec = col / D, hh = (col % D) / HD;
     const float coef = sg * svec[static_cast<int64_t>(row) * 4 + sec];
-    const float* __restrict__ a = (sec == 0 ? nq.A(j) : sec == 1 ? nk.A(j) : nv.A(j)) + (col % D);
+    const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
 #pragma unroll
-    for (int d = 0; d < HD; ++d) val[d] = bf16_round(val[d]) + coef * a[d];  // a: noise slice, scalar loads
+    for (int d = 0; d < HD; d += 4) {
+      const float4 av = a4[d / 4];
+      val[d + 0] = bf16_round(val[d + 0]) + coef * av.x;
+      val[d + 1] = bf16_round(val[d + 1]) + coef * av.y;
+      val[d + 2] = bf16_round(val[d + 2]) + coef * av.z;
+      val[d + 3] = bf16_round(val[d + 3]) + coef * av.w;
+    }
     __nv_bfloat16* dst;
     if (sec < 2) {
       const uint4* cr = reinterpret_cast<const uint4*>(cosb + static_cast<int64_t>(t) * (HD / 2));
@@ -309,7 +323,8 @@ struct EpiResid {
   Slice n;
   float* x;
   float coef;
-  const float* a;
+  int col0;
+  float* scratch;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
@@ -317,25 +332,26 @@ struct EpiResid {
     float s = 0.f;
     for (int i = 0; i < nparts; ++i) s += pr[i];
     coef = sign[j] * bf16_round(s);
-    a = n.A(j);
+  }
+  __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
+    col0 = c0;
+    s[tid] = n.A(row0 / T)[c0 + tid];
   }
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
     float4* __restrict__ xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D + col);
-    const float* __restrict__ ar = a + col;  // noise slice: scalar loads
+    const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
     float4 xv[CH / 4];
-    float av[CH];
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) xv[i] = xr[i];  // every load issued before any store
 #pragma unroll
-    for (int i = 0; i < CH; ++i) av[i] = __ldg(ar + i);
-#pragma unroll
     for (int i = 0; i < CH / 4; ++i) {
-      xv[i].x += bf16_round(acc[4 * i + 0]) + coef * av[4 * i + 0];
-      xv[i].y += bf16_round(acc[4 * i + 1]) + coef * av[4 * i + 1];
-      xv[i].z += bf16_round(acc[4 * i + 2]) + coef * av[4 * i + 2];
-      xv[i].w += bf16_round(acc[4 * i + 3]) + coef * av[4 * i + 3];
+      const float4 av = a4[i];
+      xv[i].x += bf16_round(acc[4 * i + 0]) + coef * av.x;
+      xv[i].y += bf16_round(acc[4 * i + 1]) + coef * av.y;
+      xv[i].z += bf16_round(acc[4 * i + 2]) + coef * av.z;
+      xv[i].w += bf16_round(acc[4 * i + 3]) + coef * av.w;
     }
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) xr[i] = xv[i];
@@ -354,15 +370,20 @@ struct EpiFC {
   __nv_bfloat16* hidden;
   float* pdot;  // [M, NPARTS]
   float coef, pd;
-  const float* a;
-  const float* b;
+  int col0;
+  float* scratch;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
-    a = nfc.A(j);
-    b = nmp.B(j);
     pd = 0.f;
+  }
+  // the tile's slices of a_fc and of the bf16-rounded b of mlp.c_proj into shared memory
+  __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
+    col0 = c0;
+    const int j = row0 / T;
+    s[tid] = nfc.A(j)[c0 + tid];
+    s[GEMM_BN + tid] = bf16_round(nmp.B(j)[c0 + tid]);
   }
   __device__ __forceinline__ void tile_end(int row, int nb, int part) {
     pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] = pd;
@@ -371,17 +392,21 @@ struct EpiFC {
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
     uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row) * F + col);
-    const float* __restrict__ ap = a + col;
-    const float* __restrict__ bp = b + col;
+    const float* ap = scratch + (col - col0);
+    const float* bp = ap + GEMM_BN;
 #pragma unroll
     for (int i = 0; i < CH; i += 8) {
       float r[8];
+      const float4 a0 = *reinterpret_cast<const float4*>(ap + i), a1 = *reinterpret_cast<const float4*>(ap + i + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(bp + i), b1 = *reinterpret_cast<const float4*>(bp + i + 4);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float u = bf16_round(acc[i + e]) + coef * __ldg(ap + i + e);
+        const float u = bf16_round(acc[i + e]) + coef * av[e];
         const float rl = fmaxf(u, 0.f);
         r[e] = bf16_round(rl * rl);
-        pd += r[e] * bf16_round(__ldg(bp + i + e));
+        pd += r[e] * bv[e];
       }
       uint4 pk;
       pk.x = pack_bf16x2(r[0], r[1]);
@@ -406,23 +431,27 @@ struct EpiHeadCE {
   float2* ce2;  // [M, 2]: per column half, (sum exp(c - 15), c_target or 0)
   int64_t tgt;
   float coef, sum, zt;
-  const float* a;
+  int col0;
+  float* scratch;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
     tgt = targets[row - j * T];
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
-    a = n.A(j);
     sum = 0.f;
     zt = 0.f;
+  }
+  __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
+    col0 = c0;
+    s[tid] = n.A(row0 / T)[c0 + tid];
   }
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int row, int part) { ce2[static_cast<int64_t>(row) * 2 + part] = make_float2(sum, zt); }
   __device__ __forceinline__ void chunk(int, int col, float* acc) {
-    const float* __restrict__ ap = a + col;
+    const float* ap = scratch + (col - col0);
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const float z = bf16_round(acc[i]) + coef * __ldg(ap + i);
+      const float z = bf16_round(acc[i]) + coef * ap[i];
       const float y = fabsf(z) * (1.f / 15.f);
       const float th = 1.f - 2.f * rcp_approx(ex2_approx(2.f * LOG2E * y) + 1.f);
       const float c = copysignf(15.f * th, z);
@@ -437,6 +466,8 @@ struct EpiStore {
   static constexpr int CH = 32;
   float* d;
   int ldd;
+  float* scratch;
+  __device__ __forceinline__ void stage(int, int, float*, int) {}
   __device__ __forceinline__ void row_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
@@ -623,6 +654,10 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
   }
 }
 
+}  // namespace noise
+#include "attention_tc.cuh"
+namespace noise {
+
 // ---------------------------------------------------------------------------------------------------------------
 // Per-member reduction of the per-row cross-entropy (fixed order: deterministic).
 // ---------------------------------------------------------------------------------------------------------------
@@ -738,6 +773,27 @@ static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi
   const int grid = m_tiles < sms ? m_tiles : sms;
   launch_begin(s, kind);
   kern<<<grid, GEMM_THREADS, L::SMEM_BYTES, s>>>(ma, mb, m_tiles, N / GEMM_BN, K / GEMM_BK, epi, status);
+  launch_end(s);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+static int run_attention(const void* q, const void* k, const void* v, int M, int T, int members,
+                         const TAttnArgs& args, cudaStream_t s) {
+  CUtensorMap mq, mk, mv;
+  int rc;
+  const uint64_t rows = static_cast<uint64_t>(M) * H;  // q, k, v are head-major [members * H * T, 64]
+  if ((rc = make_map(&mq, q, HD, rows, TA_BQ)) || (rc = make_map(&mk, k, HD, rows, TA_BK)) ||
+      (rc = make_map(&mv, v, HD, rows, TA_BK)))
+    return rc;
+  if (cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
+    return NOISE_ERR_CUDA;
+  launch_begin(s, K_ATTENTION);
+  const int sms = sm_count();
+  if (sms <= 0) return NOISE_ERR_CUDA;
+  TAttnArgs a = args;
+  a.bh = members * H;
+  const int items = (T / TA_BQ + 1) / 2 * a.bh;
+  attention_tc_kernel<<<items < sms ? items : sms, TA_THREADS, TA_SMEM, s>>>(mq, mk, mv, a);
   launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
@@ -875,18 +931,14 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     eq.v = w.v;
     if ((rc = run_gemm(w.h, Mi, D, model->wqkv[l], 3 * D, eq, w.status, s, K_GEMM_QKV))) return rc;
 
-    AttnArgs aa{};
-    aa.q = w.q;
-    aa.k = w.k;
-    aa.v = w.v;
-    aa.y = w.y;
-    aa.ydot = w.ydot;
+    TAttnArgs aa{};
     aa.T = T;
     aa.window = (l % 4 == 3 || l == NOISE_N_LAYER - 1) ? 2048 : 1024;  // SSSL, last block L
+    aa.y = w.y;
+    aa.ydot = w.ydot;
     aa.nproj = to_slice(nz[noise_param_index(l, NOISE_P_CPROJ)]);
-    launch_begin(s, K_ATTENTION);
-    attention_kernel<<<dim3(T / ATT_BQ, members * H), 128, 0, s>>>(aa);
-    launch_end(s);
+    aa.status = w.status;
+    if ((rc = run_attention(w.q, w.k, w.v, Mi, T, members, aa, s))) return rc;
 
     EpiResid er{};
     er.T = T;

@@ -106,6 +106,22 @@ def init_weights(seed=0, constructed=True, eggroll=False, cuda_embeddings=False)
     return w
 
 
+def informative_weights(seed=0):
+    """EGGROLL's make_model weights with the parts that are inert at initialisation made active, for parity tests:
+    at init the LM head has std 1e-3, so every loss sits at ln 4096 whatever the body computes, and the value-embedding
+    gates are zero. Here the LM head is N(0, 2 / sqrt(512)) (logits of std ~2), the ve gates N(0, 0.5) and the mixing
+    scalars spread around their init, so per-member losses depend on every block."""
+    w = init_weights(seed, eggroll=True)
+    g = torch.Generator().manual_seed(10_000 + seed)
+    w['lm_head.weight'] = torch.randn(VOCAB, N_EMBD, generator=g) * (2 / N_EMBD ** 0.5)
+    for i in range(N_LAYER):
+        if has_ve(i):
+            w[f'transformer.h.{i}.attn.ve_gate.weight'] = torch.randn(N_HEAD, VE_GATE_CHANNELS, generator=g) * 0.5
+    w['resid_lambdas'] = 1 + 0.2 * torch.randn(N_LAYER, generator=g)
+    w['x0_lambdas'] = 0.1 + 0.2 * torch.randn(N_LAYER, generator=g)
+    return w
+
+
 def rotary(seq_len=ROTARY_LEN, head_dim=HEAD_DIM, base=10000):
     """bf16 cos, sin tables [seq_len, head_dim / 2] (model.py:177-183)."""
     inv_freq = 1.0 / base ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim)

@@ -1,8 +1,11 @@
 """Parity of the CUDA population-perturbed forward with the CPU oracle (bf16 autocast rounding points) and with the
 reference's own outputs (tests/golden/population_T*.pt).
 
-Tolerance: per-member mean cross-entropy within 2e-3 relative of the oracle. The CUDA path rounds q, k, v to bf16
-before attention where the reference attends in fp32; everything else follows the autocast rounding points."""
+The oracle comparisons use oracle.gpt.informative_weights: at EGGROLL's initialisation the LM head (std 1e-3) makes
+every loss ln 4096 whatever the body computes, which would hide errors anywhere before the head.
+Tolerances: per-member mean cross-entropy within RTOL relative of the oracle; the antithetic fitness l(-) - l(+)
+within FIT_TOL of the oracle's, relative to the fitness scale. The CUDA path rounds q, k, v to bf16 before attention
+where the reference attends in fp32; everything else follows the autocast rounding points."""
 import pytest
 import torch
 
@@ -10,13 +13,15 @@ from oracle import eggroll, gpt
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
-RTOL = 2e-3
+RTOL = 5e-4     # observed <= 2.2e-4; the reference's own autocast-vs-fp32 gap is 1.2-2.6e-4
+FIT_TOL = 0.12  # observed <= 8% of the fitness scale; the reference's own autocast-vs-fp32 gap is 1-4%
+GOLDEN_RTOL = 1e-4
 
 
 def _case(members, length, seed=0, n_noise=2 ** 20, pairs=None):
     pairs = pairs or members // 2
     shapes = gpt.param_shapes()
-    w = gpt.init_weights(0, eggroll=True)
+    w = gpt.informative_weights(0)
     buf = eggroll.make_buffer(n_noise, seed=0)
     offs = eggroll.offsets(shapes, pairs, step=seed + 1, n_noise=n_noise)
     directions = torch.arange(members) // 2 % pairs
@@ -38,19 +43,28 @@ def _gpu(w, nz, sign, idx, tgt, reduction='mean'):
     return out.cpu()
 
 
+def _check_fitness(got, ref):
+    fr, fg = ref[1::2] - ref[0::2], got[1::2] - got[0::2]
+    scale = fr.abs().max().item()
+    assert (fg - fr).abs().max().item() <= FIT_TOL * scale, (fg, fr)
+
+
 @pytest.mark.parametrize('members,length', [(4, 128), (4, 256), (2, 1024)])
 def test_matches_oracle_autocast(members, length):
     w, buf, offs, directions, nz, sign, idx, tgt = _case(members, length)
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
     got = _gpu(w, nz, sign, idx, tgt)
     torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
+    _check_fitness(got, ref)
 
 
 def test_full_length_window_matches_oracle():
     """T = 2048: the S layers' 1024-token window binds."""
     w, buf, offs, directions, nz, sign, idx, tgt = _case(2, 2048)
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
-    torch.testing.assert_close(_gpu(w, nz, sign, idx, tgt), ref, rtol=RTOL, atol=0)
+    got = _gpu(w, nz, sign, idx, tgt)
+    torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
+    _check_fitness(got, ref)
 
 
 @pytest.mark.parametrize('length', [256, 2048])
@@ -64,8 +78,8 @@ def test_matches_reference_golden(golden, length):
     sign = torch.tensor([g['sigma'], -g['sigma']]).repeat(g['pairs'])
     tokens = g['tokens'].long()
     got = _gpu(w, nz, sign, tokens[:-1], tokens[1:])
-    torch.testing.assert_close(got, g['loss_autocast'], rtol=RTOL, atol=0)
-    torch.testing.assert_close(got, g['loss_fp32'], rtol=RTOL, atol=0)
+    torch.testing.assert_close(got, g['loss_autocast'], rtol=GOLDEN_RTOL, atol=0)
+    torch.testing.assert_close(got, g['loss_fp32'], rtol=GOLDEN_RTOL, atol=0)
 
 
 def test_sum_reduction_is_mean_times_length():

@@ -12,7 +12,7 @@ import torch
 from oracle import eggroll, gpt
 
 pytestmark = pytest.mark.gpu
-RTOL = 2e-3  # the tolerance of tests/test_population_gpu.py
+RTOL = 5e-4  # the tolerance of tests/test_population_gpu.py
 
 
 def _case(members, length, seed, device):
@@ -32,7 +32,7 @@ def test_noalloc_matches_workspace_entry_point_twice_in_a_row():
     import noise_b200
     from noise_b200.population import PackedGPT, population_loss_offsets, population_loss_offsets_noalloc
     dev = torch.device('cuda', 0)
-    packed = PackedGPT({k: v.to(dev) for k, v in gpt.init_weights(0, eggroll=True).items()})
+    packed = PackedGPT({k: v.to(dev) for k, v in gpt.informative_weights(0).items()})
     for members, length, seed in [(2, 2048, 11), (4, 1024, 12)]:  # two calls in a row, different sizes and inputs
         buf, off, sign, idx, tgt = _case(members, length, seed, dev)
         got = population_loss_offsets_noalloc(packed, buf, off, sign, idx, tgt)
