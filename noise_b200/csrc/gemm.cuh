@@ -43,7 +43,9 @@ struct GemmLayout {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SCRATCH_BYTES = 4 * 2 * BN;  // per accumulator buffer: two fp32 vectors of the tile's width
   static constexpr int SCRATCH_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFFSET = SCRATCH_OFFSET + 2 * SCRATCH_BYTES;
+  static constexpr int STAGING_BYTES = 4096;         // per epilogue warp: one 32-row x 128-byte chunk
+  static constexpr int STAGING_OFFSET = SCRATCH_OFFSET + 2 * SCRATCH_BYTES;
+  static constexpr int BAR_OFFSET = STAGING_OFFSET + GEMM_EPI_WARPS * STAGING_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFFSET + 8 * (2 * STAGES + 5) + 16 + 1024;  // + 1024 alignment slack
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "tcgen05 M=128 needs N in [16, 256], N % 16 == 0");
@@ -56,7 +58,8 @@ struct GemmLayout {
 //   void stage(int row0, int col0, float* s, int tid); before every tile, all 256 epilogue threads (tid 0..255):
 //                                                     may fill s[0 .. 2 BN) (16-byte aligned shared memory) with
 //                                                     per-tile vectors; the tile's chunks run after a barrier
-//   (chunk, tile_end and row_end may read the staged vectors through stage_ptr(), set by the kernel)
+//   float* scratch; uint32_t stg;                     set by the kernel: the staged vectors of the current tile, and
+//                                                     the shared address of the warp's 4 KB staging tile
 //   void chunk(int row, int col, float* v);           v[0..CH) = D[row, col .. col + CH) (may be modified in place)
 //   void tile_end(int row, int n_tile, int part);     after the last chunk of the thread's half of a tile
 //   void row_end(int row, int part);                  after the last N tile
@@ -174,6 +177,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     Epi e = epi;  // per-thread copy: the functor may carry per-row state
+    // this warp's 32 x 128-byte staging tile (rows swizzled in 16-byte chunks: chunk c of row r at c ^ (r % 8)), for
+    // epilogues that turn a thread-per-row chunk into row-contiguous global accesses
+    e.stg = smem_u32(smem + L::STAGING_OFFSET + (warp - 2) * L::STAGING_BYTES);
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;  // column half of every tile this warp handles
     const int r_in = quarter * 32 + lane;

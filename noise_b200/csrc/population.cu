@@ -45,7 +45,7 @@ constexpr int V = NOISE_VOCAB;  // 4096
 constexpr float RMS_EPS = 1.1920928955078125e-07f;  // torch.finfo(float32).eps: F.rms_norm(eps=None) on fp32
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr int GEMM_BN = 256;
-constexpr int GEMM_STAGES = 4;
+constexpr int GEMM_STAGES = 3;
 
 struct Slice {
   const float* a;
@@ -209,6 +209,21 @@ __global__ void __launch_bounds__(256) norm_kernel(NormArgs p) {
 // ---------------------------------------------------------------------------------------------------------------
 // GEMM epilogues
 // ---------------------------------------------------------------------------------------------------------------
+// Warp staging tile: 32 rows x 128 bytes, 16-byte chunk c of row r stored at chunk c ^ (r % 8) (conflict-free both
+// when a thread writes its own row and when 8 lanes read one row). Rows of a warp's chunk are consecutive rows of the
+// GEMM output, so after staging, lane L handles chunk L % 8 of rows L / 8 + 4 i: every global access of the warp
+// covers 4 whole rows of 128 bytes (4 cache lines) instead of 32 lines.
+__device__ __forceinline__ uint32_t stg_addr(uint32_t stg, int r, int c) {
+  return stg + static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+  return v;
+}
 
 // q, k: + sign (h.b) a, RoPE (utils/model.py:55-58), RMS norm over the head; v: + sign (h.b) a + gate ve
 // (eggroll.py:82-90). Writes bf16 [m, H, T, 64].
@@ -229,6 +244,7 @@ struct EpiQKV {
   int j, t, col0;
   float sg;
   float* scratch;
+  uint32_t stg;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     j = row / T;
@@ -301,16 +317,21 @@ struct EpiQKV {
       }
       dst = v;
     }
-    uint4* out = reinterpret_cast<uint4*>(dst + ((static_cast<int64_t>(j) * H + hh) * T + t) * HD);
+    // this thread's head row (128 bytes) -> staging; then rows t0 .. t0 + 31 of the head, 4 per instruction
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-    for (int d = 0; d < HD; d += 8) {
-      uint4 pk;
-      pk.x = pack_bf16x2(val[d + 0], val[d + 1]);
-      pk.y = pack_bf16x2(val[d + 2], val[d + 3]);
-      pk.z = pack_bf16x2(val[d + 4], val[d + 5]);
-      pk.w = pack_bf16x2(val[d + 6], val[d + 7]);
-      out[d / 8] = pk;
+    for (int d = 0; d < HD; d += 8)
+      sts128(stg_addr(stg, lane, d / 8), make_uint4(pack_bf16x2(val[d], val[d + 1]), pack_bf16x2(val[d + 2], val[d + 3]),
+                                                   pack_bf16x2(val[d + 4], val[d + 5]), pack_bf16x2(val[d + 6], val[d + 7])));
+    __syncwarp();
+    uint4* out = reinterpret_cast<uint4*>(dst + ((static_cast<int64_t>(j) * H + hh) * T + (t - lane)) * HD);
+    const int c = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (lane >> 3) + 4 * i;
+      out[r * 8 + c] = lds128(stg_addr(stg, r, c));
     }
+    __syncwarp();
   }
 };
 
@@ -325,6 +346,7 @@ struct EpiResid {
   float coef;
   int col0;
   float* scratch;
+  uint32_t stg;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
@@ -340,28 +362,45 @@ struct EpiResid {
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
-    float4* __restrict__ xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row) * D + col);
+    // the linear's output for this thread's row (32 columns, 128 bytes) -> staging
     const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
-    float4 xv[CH / 4];
-#pragma unroll
-    for (int i = 0; i < CH / 4; ++i) xv[i] = xr[i];  // every load issued before any store
+    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) {
       const float4 av = a4[i];
-      xv[i].x += bf16_round(acc[4 * i + 0]) + coef * av.x;
-      xv[i].y += bf16_round(acc[4 * i + 1]) + coef * av.y;
-      xv[i].z += bf16_round(acc[4 * i + 2]) + coef * av.z;
-      xv[i].w += bf16_round(acc[4 * i + 3]) + coef * av.w;
+      float4 y;
+      y.x = bf16_round(acc[4 * i + 0]) + coef * av.x;
+      y.y = bf16_round(acc[4 * i + 1]) + coef * av.y;
+      y.z = bf16_round(acc[4 * i + 2]) + coef * av.z;
+      y.w = bf16_round(acc[4 * i + 3]) + coef * av.w;
+      sts128(stg_addr(stg, lane, i), *reinterpret_cast<uint4*>(&y));
     }
+    __syncwarp();
+    // x += y for rows row - lane .. + 31, 4 whole 128-byte rows per instruction
+    const int c = lane & 7;
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row - lane) * D + col) + c;
+    float4 xv[8];
 #pragma unroll
-    for (int i = 0; i < CH / 4; ++i) xr[i] = xv[i];
+    for (int i = 0; i < 8; ++i) xv[i] = xr[((lane >> 3) + 4 * i) * (D / 4)];  // all loads before any store
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (lane >> 3) + 4 * i;
+      const uint4 yv = lds128(stg_addr(stg, r, c));
+      const float4 y = *reinterpret_cast<const float4*>(&yv);
+      xv[i].x += y.x;
+      xv[i].y += y.y;
+      xv[i].z += y.z;
+      xv[i].w += y.w;
+      xr[r * (D / 4)] = xv[i];
+    }
+    __syncwarp();
   }
 };
 
 // hidden = bf16(relu(bf16(acc) + sign bf16(h.b_fc) a_fc)^2), and per N tile the partial dot hidden.b_mproj
 // (the next linear's rank-1 input dot), eggroll.py:93.
 struct EpiFC {
-  static constexpr int CH = 32;
+  static constexpr int CH = 64;
   static constexpr int NPARTS = 2 * (F / GEMM_BN);  // per row: one partial dot per (N tile, column half)
   int T;
   const float* sign;
@@ -372,6 +411,7 @@ struct EpiFC {
   float coef, pd;
   int col0;
   float* scratch;
+  uint32_t stg;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
@@ -391,7 +431,7 @@ struct EpiFC {
   }
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
-    uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row) * F + col);
+    const int lane = threadIdx.x & 31;
     const float* ap = scratch + (col - col0);
     const float* bp = ap + GEMM_BN;
 #pragma unroll
@@ -408,19 +448,38 @@ struct EpiFC {
         r[e] = bf16_round(rl * rl);
         pd += r[e] * bv[e];
       }
-      uint4 pk;
-      pk.x = pack_bf16x2(r[0], r[1]);
-      pk.y = pack_bf16x2(r[2], r[3]);
-      pk.z = pack_bf16x2(r[4], r[5]);
-      pk.w = pack_bf16x2(r[6], r[7]);
-      out[i / 8] = pk;
+      sts128(stg_addr(stg, lane, i / 8), make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
+                                                    pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7])));
     }
+    __syncwarp();
+    // rows row - lane .. + 31 of hidden, columns col .. col + 63: 4 whole 128-byte row segments per instruction
+    uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row - lane) * F + col);
+    const int c = lane & 7;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int rr = (lane >> 3) + 4 * k;
+      out[rr * (F / 8) + c] = lds128(stg_addr(stg, rr, c));
+    }
+    __syncwarp();
   }
 };
 
 // LM head: z = bf16(acc) + sign bf16(h.b) a; c = 15 tanh(z / 15); per row the cross-entropy
 // log sum_v exp(c_v) - c_target (eggroll.py:96-102). Since c <= 15, exp(c - 15) never overflows, so the
 // log-sum-exp needs no running maximum. tanh(y) = 1 - 2 / (exp(2|y|) + 1) keeps the absolute error ~1e-7.
+// 2^x for -126 <= x <= 126 on the FMA pipes: x = j + f, j = rint(x), f in [-1/2, 1/2]; 2^f by a degree-4 polynomial
+// (least-squares-weighted fit on Chebyshev nodes; max relative error 2.6e-6), 2^j added to the exponent field.
+__device__ __forceinline__ float exp2_poly4(float x) {
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: rint(x) in the low mantissa bits
+  const float j = t - 12582912.0f;
+  const float f = x - j;
+  float p = fmaf(0.00957009568810463f, f, 0.05591786280274391f);
+  p = fmaf(p, f, 0.240247443318367f);
+  p = fmaf(p, f, 0.6931217908859253f);
+  p = fmaf(p, f, 0.9999992847442627f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 struct EpiHeadCE {
   static constexpr int CH = 32;
   int T;
@@ -433,6 +492,7 @@ struct EpiHeadCE {
   float coef, sum, zt;
   int col0;
   float* scratch;
+  uint32_t stg;
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
@@ -447,16 +507,22 @@ struct EpiHeadCE {
   }
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int row, int part) { ce2[static_cast<int64_t>(row) * 2 + part] = make_float2(sum, zt); }
+  // With u = e^(2 z / 15): 15 tanh(z / 15) - 15 = -30 / (u + 1), so exp(c - 15) = 2^(-30 log2(e) / (u + 1)): one
+  // ex2 and one reciprocal on the MUFU pipe, the outer 2^x on the FMA pipes (exp2_poly4, rel. error 2.6e-6).
+  // c itself is only needed at the target column: c = 15 - 30 / (u + 1).
   __device__ __forceinline__ void chunk(int, int col, float* acc) {
-    const float* ap = scratch + (col - col0);
+    const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
 #pragma unroll
-    for (int i = 0; i < CH; ++i) {
-      const float z = bf16_round(acc[i]) + coef * ap[i];
-      const float y = fabsf(z) * (1.f / 15.f);
-      const float th = 1.f - 2.f * rcp_approx(ex2_approx(2.f * LOG2E * y) + 1.f);
-      const float c = copysignf(15.f * th, z);
-      sum += ex2_approx((c - 15.f) * LOG2E);
-      if (col + i == tgt) zt = c;
+    for (int i = 0; i < CH; i += 4) {
+      const float4 av = a4[i / 4];
+      const float aa[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float z = bf16_round(acc[i + e]) + coef * aa[e];
+        const float inv = rcp_approx(ex2_approx(z * (2.f / 15.f * LOG2E)) + 1.f);  // 1 / (u + 1)
+        sum += exp2_poly4(inv * (-30.f * LOG2E));
+        if (col + i + e == tgt) zt = 15.f - 30.f * inv;
+      }
     }
   }
 };
@@ -467,6 +533,7 @@ struct EpiStore {
   float* d;
   int ldd;
   float* scratch;
+  uint32_t stg;
   __device__ __forceinline__ void stage(int, int, float*, int) {}
   __device__ __forceinline__ void row_begin(int, int) {}
   __device__ __forceinline__ void tile_end(int, int, int) {}
