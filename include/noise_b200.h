@@ -148,6 +148,30 @@ int noise_moment_query_scores(const void* q, const void* k, const void* v, const
                               const float* hub_out, const float* steps, int rows, int tokens, int window,
                               const noise_rows_t* out, int out_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * The seed-rebuilt ES update (reference archive/10M/train/val/eggroll.py:151-167).
+ * ------------------------------------------------------------------------------------------------------------- */
+
+/* GEMM operands of the rebuild G = -(1 / count) sum_j w_j a_j b_j^T of one matrix parameter, straight from the noise
+ * buffer: dst[e, j] = weight_scale * weight[j] * buffer[offsets[j] + shift + e] as bf16 (weight NULL: no scaling),
+ * e < n_elem, j < pairs, and 0 for pairs <= j < k_padded. dst is [n_elem, k_padded] row-major. With shift = 0 and
+ * the fitness weights this is A' (the out-side vectors); with shift = out and weight NULL it is B' (in-side); then
+ * noise_gemm_bf16_tn(A', B', G, out, in, k_padded) gives G. Replaces the loop of eggroll.py:156-163. */
+int noise_rank1_operands(const float* buffer, const int64_t* offsets, const float* weight, float weight_scale,
+                         int64_t shift, int n_elem, int pairs, int k_padded, void* dst, void* stream);
+
+/* out[o, i] = scale * sum_j weight[j] a_j[o] b_j[i] (fp32) for parameters too small for GEMM tiles: a_j =
+ * buffer + offsets[j], b_j = a_j + n_out; with one_d != 0 the 1-D case out[i] = scale * sum_j weight[j] eps_j[i],
+ * eps_j = buffer + offsets[j] (eggroll.py:162-163). */
+int noise_rank1_small(const float* buffer, const int64_t* offsets, const float* weight, float scale, int n_out,
+                      int n_in, int one_d, int pairs, float* out, void* stream);
+
+/* torch.optim.AdamW with weight_decay = 0 (the reference's optimizer, eggroll.py:164-167, 205) on one flat fp32
+ * tensor: exp_avg, exp_avg_sq updated in place, param -= (lr / (1 - beta1^step)) exp_avg /
+ * (sqrt(exp_avg_sq) / sqrt(1 - beta2^step) + eps). */
+int noise_adam_step(float* param, float* exp_avg, float* exp_avg_sq, const float* grad, int64_t n, float lr,
+                    float beta1, float beta2, float eps, int step, void* stream);
+
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);
 

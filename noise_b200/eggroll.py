@@ -89,7 +89,7 @@ class Population:
         self.chunk = chunk
         self.launches = 0
 
-    def evaluate(self, tokens, step, rows_per_member=1, reduction='mean', gather=True):
+    def evaluate(self, tokens, step, rows_per_member=1, reduction='mean', gather=True, offsets=None):
         """tokens: int64 [rows, T + 1] on the device. With rows_per_member == 1 the reference layout holds (members
         split evenly over the rows); with rows_per_member == rows every member reads every row and its losses add up
         over the rows (each member scores 8 x 2048 tokens)."""
@@ -97,12 +97,17 @@ class Population:
         rows = tokens.shape[0]
         members, per_seq, per_rank, directions, signs, row_of = member_layout(
             self.pairs, rows if rows_per_member == 1 else 1, self.world, self.rank, self.device)
-        offsets = step_offsets(self.pairs, step, self.device, self.seed, self.buffer.numel())
+        if offsets is None:
+            offsets = step_offsets(self.pairs, step, self.device, self.seed, self.buffer.numel())
         first = self.rank * per_rank
         losses = torch.zeros(per_rank, device=self.device)
         self.launches = 0
-        for start in range(first, first + per_rank, self.chunk):
-            sel = slice(start, min(start + self.chunk, first + per_rank))
+        chunk = self.chunk
+        if rows_per_member == 1:  # a launch shares one token row: chunks may not straddle rows (eggroll.py:143)
+            while per_seq % chunk or per_rank % chunk:
+                chunk //= 2
+        for start in range(first, first + per_rank, chunk):
+            sel = slice(start, min(start + chunk, first + per_rank))
             off = member_offsets(offsets, directions[sel])
             sign = signs[sel] * self.sigma
             row_list = [int(row_of[sel.start])] if rows_per_member == 1 else range(rows)

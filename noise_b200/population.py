@@ -63,6 +63,11 @@ class PackedGPT:
         self._cos, self._sin = cos, sin
         self.refresh()
 
+    def invalidate(self):
+        """Force a re-pack at the next refresh (after the weights were written in place by a raw kernel, which does
+        not bump torch's version counter)."""
+        self._key = None
+
     def _source_key(self):
         return tuple((t.data_ptr(), t._version) for t in (self.params[n] for n in NAMES))
 
