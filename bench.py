@@ -41,7 +41,7 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='population', choices=['population', 'credit'])
+    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train'])
     return ap.parse_args()
 
 
@@ -72,6 +72,12 @@ def kernel_work(kind, members, length):
     if kind == 'attention':
         pairs = sum(visible_pairs(length, w) for w in WINDOWS) / len(WINDOWS)
         return 4.0 * 64 * pairs * members * 8, None
+    # HBM-bound kernels: algorithmic bytes (fp32 residual stream 2 KB / row, bf16 activations 1 KB / row)
+    per_row = {'norm_mix': 2048 + 2048 + 1024 + 48,  # read x, write mixed x, write h, rank-1 dots + gates
+               'norm_mid': 2048 + 1024 + 16, 'norm_final': 2048 + 1024 + 16,
+               'member_reduce': 16}
+    if kind in per_row:
+        return None, float(per_row[kind]) * M
     return None, None
 
 
@@ -249,24 +255,30 @@ def run_ours(a):
     total = sum(prof.ms.values())
     for k, kms in prof.ms.items():
         n = prof.count[k]
-        flops, _ = kernel_work(k, pop.chunk, T)
+        flops, nbytes = kernel_work(k, pop.chunk, T)
         per = kms / n
         kinds[k] = {'launches': n, 'ms_per_launch': round(per, 4), 'share': round(kms / total, 4)}
         if flops:
             kinds[k]['tflops'] = round(flops / (per / 1e3) / 1e12, 1)
+        if nbytes:
+            kinds[k]['gbs'] = round(nbytes / (per / 1e3) / 1e9, 1)
     dom = max(prof.ms, key=prof.ms.get)
-    flops, _ = kernel_work(dom, pop.chunk, T)
+    flops, nbytes = kernel_work(dom, pop.chunk, T)
     per_launch_s = prof.ms[dom] / prof.count[dom] / 1e3
     tr = traffic.get(dom)
-    roofline = {
-        'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1), 'peak': tf_peak,
-        'unit': 'TFLOP/s', 'frac': round(flops / per_launch_s / 1e12 / tf_peak, 4),
-        'peak_source': 'MEASURED_PEAKS.json bf16_tflops_sustained (of measured)' if peaks else 'fallback',
-        'traffic': (tr * pop.chunk * T if tr is not None else None),
-        'algorithmic_flops_per_launch': flops,
-        'step': {'achieved': round(MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12, 1),
-                 'frac': round(MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12 / tf_peak, 4)},
-    }
+    step_tf = MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12
+    src = 'MEASURED_PEAKS.json (of measured)' if peaks else 'fallback'
+    if flops:
+        roofline = {'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1),
+                    'peak': tf_peak, 'unit': 'TFLOP/s', 'frac': round(flops / per_launch_s / 1e12 / tf_peak, 4),
+                    'peak_source': src + ' bf16_tflops_sustained', 'algorithmic_flops_per_launch': flops}
+    else:
+        hbm = peaks.get('hbm_gbs', 6650.0)
+        roofline = {'kernel': dom, 'bound': 'hbm', 'achieved': round(nbytes / per_launch_s / 1e9, 1), 'peak': hbm,
+                    'unit': 'GB/s', 'frac': round(nbytes / per_launch_s / 1e9 / hbm, 4),
+                    'peak_source': src + ' hbm_gbs', 'algorithmic_bytes_per_launch': nbytes}
+    roofline['traffic'] = tr * pop.chunk * T if tr is not None else None
+    roofline['step'] = {'achieved_tflops': round(step_tf, 1), 'frac': round(step_tf / tf_peak, 4)}
 
     line = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
@@ -368,12 +380,72 @@ def run_credit(a):
                           'kernels': res}), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# one EGGROLL training update at population 24,576 (BASELINE configs 4 / 5)
+# ------------------------------------------------------------------------------------------------------------------
+TRAIN_PAIRS, TRAIN_ROWS = 12288, 8
+
+
+def run_train(a):
+    """Train tokens/s: each update consumes 8 rows x 2048 Zipf tokens (eggroll.py's BATCH), evaluates 24,576
+    antithetic members (3,072 per row, split over the ranks), all-gathers their losses, rebuilds the update on each
+    rank's pair shard (tcgen05 GEMM, K = pairs) with one NCCL all-reduce, and applies AdamW."""
+    from noise_b200.eggroll import make_params
+    from noise_b200.train import EggrollTrainer
+
+    rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=600))
+    tr = EggrollTrainer(make_params(device, 0), TRAIN_PAIRS, TRAIN_ROWS, sigma=SIGMA, lr=1e-3, rank=rank,
+                        world=world)
+    rows = [zipf_rows(TRAIN_ROWS, T + 1, seed=100 + s).pin_memory() for s in range(a.warmup + a.steps)]
+    for i in range(a.warmup):
+        tr.step(rows[i].to(device, non_blocking=True), step=i + 1)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.steps):
+        loss = tr.step(rows[a.warmup + i].to(device, non_blocking=True), step=a.warmup + i + 1)
+        loss_host = loss.item()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    tokens = TRAIN_ROWS * T * a.steps
+    if rank == 0:
+        print(json.dumps({
+            'metric': 'train tokens/sec at pop 24k (EGGROLL update: population forward + fitness all-gather + '
+                      'rebuilt update all-reduce + AdamW)',
+            'value': tokens / (ms / 1e3), 'unit': 'train tokens/s (all GPUs)', 'n_gpus': world, 'steps': a.steps,
+            'warmup': a.warmup, 'ms_per_step': ms / a.steps, 'higher_is_better': True, 'scaling': 'strong',
+            'dtype': 'bf16', 'data': 'synthetic Zipf(1.1) rows, random-init GPT (EGGROLL make_model)',
+            'config': {'workload': 'BASELINE config 4/5 update', 'population': 2 * TRAIN_PAIRS,
+                       'rows_per_update': TRAIN_ROWS, 'seq_len': T, 'members_per_row': 2 * TRAIN_PAIRS // TRAIN_ROWS,
+                       'member_tokens_per_s': 2 * TRAIN_PAIRS * T * a.steps / (ms / 1e3),
+                       'last_mean_loss': loss_host},
+            'e2e': {'value': tokens / (ms / 1e3), 'unit': 'train tokens/s', 'h2d_bytes_per_step': TRAIN_ROWS * (T + 1) * 8,
+                    'd2h_bytes_per_step': 4},
+        }), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main():
     a = args_()
     if a.impl == 'reference':
         run_reference(a)
     elif a.workload == 'credit':
         run_credit(a)
+    elif a.workload == 'train':
+        run_train(a)
     else:
         run_ours(a)
 

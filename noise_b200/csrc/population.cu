@@ -518,7 +518,7 @@ struct EpiHeadCE {
       const float aa[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float z = bf16_round(acc[i + e]) + coef * aa[e];
+        const float z = bf16_round_alu(acc[i + e]) + coef * aa[e];
         const float inv = rcp_approx(ex2_approx(z * (2.f / 15.f * LOG2E)) + 1.f);  // 1 / (u + 1)
         sum += exp2_poly4(inv * (-30.f * LOG2E));
         if (col + i + e == tgt) zt = 15.f - 30.f * inv;

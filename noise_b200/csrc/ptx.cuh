@@ -227,7 +227,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major 
 // ---------------------------------------------------------------------------------------------------------------
 // small numerics
 // ---------------------------------------------------------------------------------------------------------------
+// Round to bf16 (nearest even), result widened back to fp32: the hardware conversion.
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// The same rounding on the integer ALU pipe (round half to even on the 16 dropped bits), for a kernel whose
+// conversion/exponential pipe is the busier one (the LM-head cross-entropy rounds every logit next to its two MUFU
+// operations). Finite inputs (all values here are).
+__device__ __forceinline__ float bf16_round_alu(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return __uint_as_float((u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u);
+}
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -247,6 +256,7 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Two floats rounded to bf16 (nearest even) and packed, low half = lo: one packed conversion instruction.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&p);
