@@ -87,8 +87,11 @@ typedef struct {
   const void* sin;                   /* bf16 [>= T, 32] */
 } noise_gpt_t;
 
+/* Loss reductions: MEAN / SUM over a member's (or, for noise_gpt_loss, all rows') tokens; NONE one loss per token.
+ * A negative target (F.cross_entropy's ignore_index, -1 in GPT.forward) contributes 0 and is not counted. */
 #define NOISE_REDUCTION_MEAN 0
 #define NOISE_REDUCTION_SUM 1
+#define NOISE_REDUCTION_NONE 2
 
 /* ---------------------------------------------------------------------------------------------------------------
  * Credit-readout kernels (reference train/speedrun/moment_kernels.py). Rows are (layer, head, sequence) slices of
@@ -180,11 +183,34 @@ size_t noise_population_workspace_bytes(int members, int tokens);
  * helpers it calls (:56-63); the perturbed weights are never materialised: every linear layer is a tcgen05 GEMM
  * whose epilogue adds sign_j (x . b_j) a_j.
  *   noise[NOISE_N_PARAMS]: host array of slices in named_parameters order; sign[m] fp32 (+-sigma);
- *   idx[T], targets[T] int64 token ids; losses[m] fp32 out (mean or sum over T per `reduction`).
+ *   idx[T], targets[T] int64 token ids; losses[m] fp32 out (mean or sum over T per `reduction`), or with
+ *   NOISE_REDUCTION_NONE losses[m * T], member-major (the reference's `ce` before its .mean(-1), eggroll.py:101-102).
  * Requirements: T % 128 == 0, 128 <= T <= 2048, members >= 1. */
 int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
                           const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
                           float* losses, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of scratch noise_gpt_loss needs for `rows` rows of `tokens` tokens. */
+size_t noise_gpt_workspace_bytes(int rows, int tokens);
+
+/* The un-perturbed forward and loss on `rows` distinct token rows: GPT.forward(idx, targets, loss_reduction)
+ * (utils/model.py:193-209) with softcap 15 and ignore_index -1, computed as the population forward does (bf16
+ * tensor-core linears with fp32 accumulation and an fp32 residual stream, fp32 embeddings: the autocast numerics of
+ * EGGROLL's make_model weights, eggroll.py:38-53). idx, targets int64 [rows, T] row-major. out: one float (MEAN:
+ * sum / counted tokens; SUM) or [rows * T] (NONE). Requirements as noise_population_loss. */
+int noise_gpt_loss(const noise_gpt_t* model, const int64_t* idx, const int64_t* targets, int rows, int tokens,
+                   int reduction, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of scratch noise_head_loss needs for `rows` rows. */
+size_t noise_head_loss_workspace_bytes(int rows);
+
+/* Per-token loss of the final norm, LM head, softcap 15 and cross-entropy (reduction 'none', ignore_index -1):
+ * replaces dust.head_loss (train/val/dust.py:94-99) and the tail of GPT.forward (utils/model.py:202-208).
+ *   x fp32 [rows, 512] (the residual stream); weight bf16 [>= 4096, 512] row-major (rows past the vocabulary are
+ *   ignored, as the reference's [..., :vocab]); targets int64 [rows]; out fp32 [rows].
+ * Requirements: rows % 128 == 0, 128 <= rows <= 2^22; x and weight 16-byte aligned. */
+int noise_head_loss(const float* x, const void* weight, const int64_t* targets, int rows, float* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
 
 /* No counterpart in the reference: noise_population_loss for callers that cannot allocate device memory — a host
  * that embeds this library without a CUDA allocator of its own (a C/FFI caller that must not call cudaMalloc, which

@@ -6,6 +6,8 @@
 All compute runs in the in-tree ``libnoise_b200.so`` (C ABI: ``include/noise_b200.h``); there is no CPU fallback.
 """
 from . import _lib
-from .population import PackedGPT, member_offsets, param_shapes, population_loss, population_loss_offsets
+from .population import (PackedGPT, gpt_loss, head_loss, member_offsets, param_shapes, population_loss,
+                         population_loss_offsets)
 
-__all__ = ['PackedGPT', 'member_offsets', 'param_shapes', 'population_loss', 'population_loss_offsets', '_lib']
+__all__ = ['PackedGPT', 'gpt_loss', 'head_loss', 'member_offsets', 'param_shapes', 'population_loss',
+           'population_loss_offsets', '_lib']

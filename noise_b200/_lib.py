@@ -11,7 +11,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / 'libnoise_b200.so'
 
 N_LAYER, N_HEAD, HEAD_DIM, N_EMBD, VOCAB, N_PARAMS = 8, 8, 64, 512, 4096, 60
-REDUCTION = {'mean': 0, 'sum': 1}
+REDUCTION = {'mean': 0, 'sum': 1, 'none': 2}
 STATUS_BYTES = 256
 STATIC_SCRATCH_BYTES = 48 << 20  # NOISE_STATIC_SCRATCH_BYTES
 ERR_TOO_LARGE = 7
@@ -51,6 +51,14 @@ SIGNATURES = [
     ('noise_population_loss', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.POINTER(Slice), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_gpt_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_gpt_loss', ctypes.c_int,
+     [ctypes.POINTER(GPT), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_head_loss_workspace_bytes', ctypes.c_size_t, [ctypes.c_int]),
+    ('noise_head_loss', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_population_loss_noalloc', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.POINTER(Slice), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),

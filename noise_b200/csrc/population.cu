@@ -65,7 +65,8 @@ enum NormMode { NORM_BLOCK = 0, NORM_MID = 1, NORM_FINAL = 2 };
 
 struct NormArgs {
   int layer, T, M;
-  const int64_t* idx;
+  const int64_t* idx;  // token ids: member j, position t reads idx[j * row_stride + t]
+  int64_t row_stride;  // 0: every member reads the same row
   const float* sign;
   float* x;            // residual stream [M, 512] fp32
   __nv_bfloat16* h;    // out [M, 512] bf16
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(256) norm_kernel(NormArgs p) {
 
   if (MODE == NORM_BLOCK) {
     // x0 = norm(wte[idx] + sign a[idx] b), eggroll.py:61-63, 74
-    const int64_t tok = p.idx[t];
+    const int64_t tok = p.idx[j * p.row_stride + t];
     const float* w = p.wte + tok * D;
     const float* bw = p.n_wte.B(j);
     const float sa = sg * p.n_wte.A(j)[tok];
@@ -234,6 +235,7 @@ struct EpiQKV {
   const float* svec;
   const float* gate;  // NULL on blocks without value embeddings
   const int64_t* idx;
+  int64_t row_stride;
   const __nv_bfloat16* cosb;
   const __nv_bfloat16* sinb;
   const float* vew;  // value-embedding table [4096, 512] fp32 or NULL
@@ -302,7 +304,7 @@ struct EpiQKV {
     } else {
       if (gate) {
         const float g = gate[static_cast<int64_t>(row) * H + hh];
-        const int64_t tok = idx[t];
+        const int64_t tok = idx[j * row_stride + t];
         const float4* ver = reinterpret_cast<const float4*>(vew + tok * D + hh * HD);
         const float sa = sg * nve.A(j)[tok];
         const float* __restrict__ bve = nve.B(j) + hh * HD;
@@ -485,7 +487,8 @@ struct EpiHeadCE {
   int T;
   const float* sign;
   const float* svec;
-  const int64_t* targets;
+  const int64_t* targets;  // member j, position t: targets[j * row_stride + t]
+  int64_t row_stride;
   Slice n;
   float2* ce2;  // [M, 2]: per column half, (sum exp(c - 15), c_target or 0)
   int64_t tgt;
@@ -496,7 +499,7 @@ struct EpiHeadCE {
 
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
-    tgt = targets[row - j * T];
+    tgt = targets[j * row_stride + (row - j * T)];
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
     sum = 0.f;
     zt = 0.f;
@@ -726,23 +729,76 @@ __global__ void __launch_bounds__(128) attention_kernel(AttnArgs p) {
 namespace noise {
 
 // ---------------------------------------------------------------------------------------------------------------
-// Per-member reduction of the per-row cross-entropy (fixed order: deterministic).
+// Reductions of the per-row cross-entropy. Row r's loss is 15 + log(sum) - c_target from its two column halves'
+// (sum exp(c - 15), c_target); a negative target (F.cross_entropy's ignore_index, -1 in GPT.forward) adds nothing.
+// All sums run in a fixed order: the results are deterministic.
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) member_reduce_kernel(const float4* ce2, int T, float scale, float* out) {
-  __shared__ float part[8];
+__device__ __forceinline__ float row_ce(float4 c) { return 15.f + logf(c.x + c.z) - (c.y + c.w); }
+
+// out[j] = scale * sum of member j's token losses; cnt[j] (if given) = its number of counted tokens.
+__global__ void __launch_bounds__(256) member_reduce_kernel(const float4* ce2, const int64_t* targets, int T,
+                                                            int64_t row_stride, float scale, float* out, float* cnt) {
+  __shared__ float part[8], npart[8];
   const int j = blockIdx.x;
-  float s = 0.f;
+  float s = 0.f, n = 0.f;
   for (int t = threadIdx.x; t < T; t += 256) {
-    const float4 c = ce2[static_cast<int64_t>(j) * T + t];  // (sum, c_target) of both column halves
-    s += 15.f + logf(c.x + c.z) - (c.y + c.w);
+    if (targets[j * row_stride + t] < 0) continue;
+    s += row_ce(ce2[static_cast<int64_t>(j) * T + t]);
+    n += 1.f;
   }
   s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  n = warp_sum(n);
+  if ((threadIdx.x & 31) == 0) {
+    part[threadIdx.x >> 5] = s;
+    npart[threadIdx.x >> 5] = n;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    float tot = 0.f;
-    for (int w = 0; w < 8; ++w) tot += part[w];
+    float tot = 0.f, ntot = 0.f;
+    for (int w = 0; w < 8; ++w) {
+      tot += part[w];
+      ntot += npart[w];
+    }
     out[j] = tot * scale;
+    if (cnt) cnt[j] = ntot;
+  }
+}
+
+// reduction 'none': out[r] = loss of row r (0 for an ignored target).
+__global__ void __launch_bounds__(256) token_loss_kernel(const float4* ce2, const int64_t* targets, int T,
+                                                         int64_t row_stride, int64_t M, float* out) {
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < M;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t j = r / T, t = r - j * T;
+    out[r] = targets[j * row_stride + t] < 0 ? 0.f : row_ce(ce2[r]);
+  }
+}
+
+// One scalar over all members (one block, fp64 accumulation): sum, or sum / counted tokens for the mean.
+__global__ void __launch_bounds__(256) total_kernel(const float* sums, const float* cnt, int n, int mean, float* out) {
+  __shared__ double part[8], npart[8];
+  double s = 0.0, c = 0.0;
+  for (int j = threadIdx.x; j < n; j += 256) {
+    s += sums[j];
+    c += cnt[j];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    part[threadIdx.x >> 5] = s;
+    npart[threadIdx.x >> 5] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0, ntot = 0.0;
+    for (int w = 0; w < 8; ++w) {
+      tot += part[w];
+      ntot += npart[w];
+    }
+    out[0] = static_cast<float>(mean ? tot / ntot : tot);  // mean of no counted token: nan, as torch gives
   }
 }
 
@@ -871,6 +927,10 @@ struct Workspace {
   __nv_bfloat16 *h, *q, *k, *v, *y, *hidden;
   float *svec, *gate, *ydot, *pdot;
   float2* ce2;
+  float* zeros;   // V zero floats: the noise of the un-perturbed forward
+  float* zsign;   // [members] zero signs
+  float* msum;    // [members] per-member loss sums
+  float* mcnt;    // [members] per-member counted tokens
   size_t bytes;
 };
 
@@ -897,11 +957,36 @@ static Workspace carve(void* ws, int64_t M) {
   w.ydot = static_cast<float*>(take(M * H * 4));
   w.pdot = static_cast<float*>(take(M * EpiFC::NPARTS * 4));
   w.ce2 = static_cast<float2*>(take(M * 2 * 8));
+  const int64_t mmax = M / GEMM_BM + 1;  // rows per member >= 128
+  w.zeros = static_cast<float*>(take(V * 4));
+  w.zsign = static_cast<float*>(take(mmax * 4));
+  w.msum = static_cast<float*>(take(mmax * 4));
+  w.mcnt = static_cast<float*>(take(mmax * 4));
+  w.bytes = off;
+  return w;
+}
+
+// Scratch of noise_head_loss: the status word, h, the head dots, the cross-entropy halves and the zero noise.
+static Workspace carve_head(void* ws, int64_t rows) {
+  Workspace w{};
+  size_t off = NOISE_STATUS_BYTES;
+  auto take = [&](size_t n) {
+    void* p = ws ? static_cast<uint8_t*>(ws) + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  w.status = static_cast<int*>(ws);
+  w.h = static_cast<__nv_bfloat16*>(take(rows * D * 2));
+  w.svec = static_cast<float*>(take(rows * 4 * 4));
+  w.ce2 = static_cast<float2*>(take(rows * 2 * 8));
+  w.zeros = static_cast<float*>(take(V * 4));
+  w.zsign = static_cast<float*>(take(4));
   w.bytes = off;
   return w;
 }
 
 }  // namespace noise
+
 
 using namespace noise;
 
@@ -924,31 +1009,47 @@ size_t noise_population_workspace_bytes(int members, int tokens) {
   return carve(nullptr, static_cast<int64_t>(members) * tokens).bytes;
 }
 
-int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, const float* sign, const int64_t* idx,
-                          const int64_t* targets, int members, int tokens, int reduction, float* losses,
-                          void* workspace, size_t workspace_bytes, void* stream) {
-  if (!model || !nz || !sign || !idx || !targets || !losses) return NOISE_ERR_ARGUMENT;
-  if (reduction != NOISE_REDUCTION_MEAN && reduction != NOISE_REDUCTION_SUM) return NOISE_ERR_ARGUMENT;
-  if (members < 1 || tokens < GEMM_BM || tokens > 2048 || tokens % GEMM_BM) return NOISE_ERR_SHAPE;
-  const int64_t M = static_cast<int64_t>(members) * tokens;
-  if (M > (int64_t(1) << 31) / F) return NOISE_ERR_SHAPE;
-  const Workspace w = carve(workspace, M);
-  if (!workspace || workspace_bytes < w.bytes) return NOISE_ERR_WORKSPACE;
-  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+}  // extern "C"
+
+namespace noise {
+
+static int check_model(const noise_gpt_t* model) {
   for (int l = 0; l < NOISE_N_LAYER; ++l) {
     if (!model->wqkv[l] || !model->wproj[l] || !model->wfc[l] || !model->wmproj[l]) return NOISE_ERR_ARGUMENT;
     if ((l & 1) && (!model->wgate[l] || !model->ve[l])) return NOISE_ERR_ARGUMENT;
   }
   if (!model->whead || !model->wte || !model->resid_lambdas || !model->x0_lambdas || !model->cos || !model->sin)
     return NOISE_ERR_ARGUMENT;
-  int dev = 0, major = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-  if (major != 10) return NOISE_ERR_DEVICE;
+  return NOISE_OK;
+}
 
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int T = tokens, Mi = static_cast<int>(M);
-  g_launches = 0;
+static int check_device() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NOISE_ERR_CUDA;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  return major == 10 ? NOISE_OK : NOISE_ERR_DEVICE;
+}
+
+// Checks shared by the whole-model entries: members x tokens rows, T a multiple of 128 up to the rotary tables' 2048.
+static int check_forward(const noise_gpt_t* model, int members, int tokens, void* workspace, size_t workspace_bytes,
+                         Workspace* w) {
+  if (members < 1 || tokens < GEMM_BM || tokens > 2048 || tokens % GEMM_BM) return NOISE_ERR_SHAPE;
+  const int64_t M = static_cast<int64_t>(members) * tokens;
+  if (M > (int64_t(1) << 31) / F) return NOISE_ERR_SHAPE;
+  *w = carve(workspace, M);
+  if (!workspace || workspace_bytes < w->bytes) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  const int rc = check_model(model);
+  return rc ? rc : check_device();
+}
+
+// The perturbed forward up to the per-row cross-entropy halves in w.ce2: member j reads token row
+// idx + j * row_stride (row_stride 0: one shared row, as eggroll.py:143), its noise from nz and its sign from sign.
+static int run_forward(const noise_gpt_t* model, const noise_slice_t* nz, const float* sign, const int64_t* idx,
+                       const int64_t* targets, int64_t row_stride, int members, int T, const Workspace& w,
+                       cudaStream_t s) {
+  const int64_t M = static_cast<int64_t>(members) * T;
+  const int Mi = static_cast<int>(M);
   int rc;
   if (cudaMemsetAsync(w.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
   const int norm_blocks = static_cast<int>((M * 32 + 255) / 256);
@@ -960,6 +1061,7 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     na.T = T;
     na.M = Mi;
     na.idx = idx;
+    na.row_stride = row_stride;
     na.sign = sign;
     na.x = w.x;
     na.h = w.h;
@@ -986,6 +1088,7 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
     eq.svec = w.svec;
     eq.gate = ve ? w.gate : nullptr;
     eq.idx = idx;
+    eq.row_stride = row_stride;
     eq.cosb = static_cast<const __nv_bfloat16*>(model->cos);
     eq.sinb = static_cast<const __nv_bfloat16*>(model->sin);
     eq.vew = ve ? model->ve[l] : nullptr;
@@ -1046,6 +1149,7 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
   nf.T = T;
   nf.M = Mi;
   nf.idx = idx;
+  nf.row_stride = row_stride;
   nf.sign = sign;
   nf.x = w.x;
   nf.h = w.h;
@@ -1060,15 +1164,125 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, con
   eh.sign = sign;
   eh.svec = w.svec;
   eh.targets = targets;
+  eh.row_stride = row_stride;
   eh.n = nf.nb0;
   eh.ce2 = w.ce2;
   if ((rc = run_gemm(w.h, Mi, D, model->whead, V, eh, w.status, s, K_GEMM_HEAD))) return rc;
 
+  return NOISE_OK;
+}
+
+// nz[i] = the zero noise (a = b = w.zeros for every member) and w.zsign = 0 for `members` members.
+static int zero_noise(const Workspace& w, int members, noise_slice_t* nz, cudaStream_t s) {
+  if (cudaMemsetAsync(w.zeros, 0, V * sizeof(float), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (cudaMemsetAsync(w.zsign, 0, members * sizeof(float), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  for (int i = 0; i < NOISE_N_PARAMS; ++i) nz[i] = noise_slice_t{w.zeros, w.zeros, nullptr, 0, 0};
+  return NOISE_OK;
+}
+
+// reduction 'none': one loss per row into out[M]
+static int token_losses(const Workspace& w, const int64_t* targets, int T, int64_t row_stride, int64_t M, float* out,
+                        cudaStream_t s) {
   launch_begin(s, K_REDUCE);
-  member_reduce_kernel<<<members, 256, 0, s>>>(reinterpret_cast<const float4*>(w.ce2), T,
-                                               reduction == NOISE_REDUCTION_MEAN ? 1.f / T : 1.f, losses);
+  token_loss_kernel<<<static_cast<int>(std::min<int64_t>((M + 255) / 256, 148 * 16)), 256, 0, s>>>(
+      reinterpret_cast<const float4*>(w.ce2), targets, T, row_stride, M, out);
   launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+}  // namespace noise
+
+extern "C" {
+
+int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* nz, const float* sign, const int64_t* idx,
+                          const int64_t* targets, int members, int tokens, int reduction, float* losses,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model || !nz || !sign || !idx || !targets || !losses) return NOISE_ERR_ARGUMENT;
+  if (reduction != NOISE_REDUCTION_MEAN && reduction != NOISE_REDUCTION_SUM && reduction != NOISE_REDUCTION_NONE)
+    return NOISE_ERR_ARGUMENT;
+  Workspace w;
+  int rc = check_forward(model, members, tokens, workspace, workspace_bytes, &w);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  g_launches = 0;
+  if ((rc = run_forward(model, nz, sign, idx, targets, 0, members, tokens, w, s))) return rc;
+  if (reduction == NOISE_REDUCTION_NONE)
+    return token_losses(w, targets, tokens, 0, static_cast<int64_t>(members) * tokens, losses, s);
+  launch_begin(s, K_REDUCE);
+  member_reduce_kernel<<<members, 256, 0, s>>>(reinterpret_cast<const float4*>(w.ce2), targets, tokens, 0,
+                                               reduction == NOISE_REDUCTION_MEAN ? 1.f / tokens : 1.f, losses,
+                                               nullptr);
+  launch_end(s);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_gpt_workspace_bytes(int rows, int tokens) { return noise_population_workspace_bytes(rows, tokens); }
+
+int noise_gpt_loss(const noise_gpt_t* model, const int64_t* idx, const int64_t* targets, int rows, int tokens,
+                   int reduction, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model || !idx || !targets || !out) return NOISE_ERR_ARGUMENT;
+  if (reduction != NOISE_REDUCTION_MEAN && reduction != NOISE_REDUCTION_SUM && reduction != NOISE_REDUCTION_NONE)
+    return NOISE_ERR_ARGUMENT;
+  Workspace w;
+  int rc = check_forward(model, rows, tokens, workspace, workspace_bytes, &w);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  g_launches = 0;
+  noise_slice_t nz[NOISE_N_PARAMS];
+  if ((rc = zero_noise(w, rows, nz, s))) return rc;
+  if ((rc = run_forward(model, nz, w.zsign, idx, targets, tokens, rows, tokens, w, s))) return rc;
+  if (reduction == NOISE_REDUCTION_NONE)
+    return token_losses(w, targets, tokens, tokens, static_cast<int64_t>(rows) * tokens, out, s);
+  launch_begin(s, K_REDUCE);
+  member_reduce_kernel<<<rows, 256, 0, s>>>(reinterpret_cast<const float4*>(w.ce2), targets, tokens, tokens, 1.f,
+                                            w.msum, w.mcnt);
+  total_kernel<<<1, 256, 0, s>>>(w.msum, w.mcnt, rows, reduction == NOISE_REDUCTION_MEAN, out);
+  launch_end(s);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_head_loss_workspace_bytes(int rows) {
+  if (rows < 1) return 0;
+  return carve_head(nullptr, rows).bytes;
+}
+
+int noise_head_loss(const float* x, const void* weight, const int64_t* targets, int rows, float* out, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (!x || !weight || !targets || !out) return NOISE_ERR_ARGUMENT;
+  if (rows < GEMM_BM || rows % GEMM_BM || rows > (1 << 22)) return NOISE_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(weight) & 15)) return NOISE_ERR_ALIGN;
+  const Workspace w = carve_head(workspace, rows);
+  if (!workspace || workspace_bytes < w.bytes) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  int rc = check_device();
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  g_launches = 0;
+  if (cudaMemsetAsync(w.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  noise_slice_t nz[NOISE_N_PARAMS];
+  if ((rc = zero_noise(w, 1, nz, s))) return rc;
+  // one "member" of `rows` rows; the final norm reads x in place (NORM_FINAL never writes it)
+  NormArgs nf{};
+  nf.T = rows;
+  nf.M = rows;
+  nf.sign = w.zsign;
+  nf.x = const_cast<float*>(x);
+  nf.h = w.h;
+  nf.svec = w.svec;
+  nf.nb0 = to_slice(nz[NOISE_PARAM_HEAD]);
+  launch_begin(s, K_NORM_FINAL);
+  norm_kernel<NORM_FINAL><<<(rows * 32 + 255) / 256, 256, 0, s>>>(nf);
+  launch_end(s);
+  EpiHeadCE eh{};
+  eh.T = rows;
+  eh.sign = w.zsign;
+  eh.svec = w.svec;
+  eh.targets = targets;
+  eh.row_stride = 0;
+  eh.n = nf.nb0;
+  eh.ce2 = w.ce2;
+  if ((rc = run_gemm(w.h, rows, D, weight, V, eh, w.status, s, K_GEMM_HEAD))) return rc;
+  return token_losses(w, targets, rows, 0, rows, out, s);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

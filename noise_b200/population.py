@@ -151,7 +151,7 @@ def _run(packed, slices, keep, sign, idx, targets, reduction):
     L = _lib.lib()
     nbytes = L.noise_population_workspace_bytes(m, length)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
-    losses = torch.empty(m, dtype=torch.float32, device=dev)
+    losses = torch.empty((m, length) if reduction == 'none' else (m,), dtype=torch.float32, device=dev)
     arr = (_lib.Slice * len(NAMES))(*slices)
     rc = L.noise_population_loss(ctypes.byref(packed.struct), arr, sign.data_ptr(), idx.data_ptr(),
                                  targets.data_ptr(), m, length, _lib.REDUCTION[reduction], losses.data_ptr(),
@@ -163,7 +163,8 @@ def _run(packed, slices, keep, sign, idx, targets, reduction):
 
 
 def population_loss(model, p, noise, sign, idx, targets, reduction='mean'):
-    """Mean (or summed) cross-entropy [m] of m perturbed models on one sequence (eggroll.py:66-103).
+    """Mean (or summed) cross-entropy [m] of m perturbed models on one sequence (eggroll.py:66-103); with
+    reduction='none' the per-token losses [m, T] the reference averages (eggroll.py:101-102).
 
     model: the reference GPT module (its RoPE tables are used when present) or None; p: parameter name -> tensor;
     noise: name -> (a [m, out], b [m, in]) for matrices and embeddings, eps [m, numel] for the mixing scalars;
@@ -228,10 +229,65 @@ def population_loss_offsets_noalloc(packed, buffer, member_off, sign, idx, targe
     slices = [_lib.Slice(base, base + 4 * (shape[0] if len(shape) == 2 else 0), member_off[k].data_ptr(), 0, 0)
               for k, (name, shape) in enumerate(PARAMS)]
     m, length = sign.shape[0], idx.shape[0]
-    losses = torch.empty(m, dtype=torch.float32, device=packed.device)
+    losses = torch.empty((m, length) if reduction == 'none' else (m,), dtype=torch.float32, device=packed.device)
     arr = (_lib.Slice * len(NAMES))(*slices)
     rc = _lib.lib().noise_population_loss_noalloc(ctypes.byref(packed.struct), arr, sign.data_ptr(), idx.data_ptr(),
                                                   targets.data_ptr(), m, length, _lib.REDUCTION[reduction],
                                                   losses.data_ptr(), _lib.stream_handle(packed.device))
     _lib.check(rc, 'noise_population_loss_noalloc')
     return losses
+
+
+def gpt_loss(model, p, idx, targets, loss_reduction='mean'):
+    """GPT.forward(idx, targets, loss_reduction) (utils/model.py:193-209) of the un-perturbed model on B distinct
+    rows: softcap 15, cross-entropy with ignore_index -1; 'mean' and 'sum' give a 0-d tensor, 'none' [B * T].
+
+    The numerics are the population forward's (bf16 tensor-core linears, fp32 accumulation, fp32 residual stream and
+    embeddings), i.e. the reference run under ``torch.autocast('cuda', torch.bfloat16)`` with EGGROLL's fp32
+    embeddings. model: the reference GPT module (for its RoPE tables) or None; p: parameter name -> tensor;
+    idx, targets int64 [B, T] with T % 128 == 0, T <= 2048."""
+    packed = _packed_for(model, p)
+    dev = packed.device
+    idx = idx.detach().long().contiguous()
+    targets = targets.detach().long().contiguous()
+    _lib.require_cuda(idx, targets)
+    if idx.dim() != 2 or targets.shape != idx.shape:
+        raise ValueError('idx and targets must be [B, T] of the same shape')
+    rows, length = idx.shape
+    L = _lib.lib()
+    nbytes = L.noise_gpt_workspace_bytes(rows, length)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    out = torch.empty((rows * length,) if loss_reduction == 'none' else (), dtype=torch.float32, device=dev)
+    rc = L.noise_gpt_loss(ctypes.byref(packed.struct), idx.data_ptr(), targets.data_ptr(), rows, length,
+                          _lib.REDUCTION[loss_reduction], out.data_ptr(), ws.data_ptr(), nbytes,
+                          _lib.stream_handle(dev))
+    _lib.check(rc, 'noise_gpt_loss')
+    out._noise_workspace = ws
+    return out
+
+
+def head_loss(x, weight, targets, vocab=VOCAB):
+    """dust.head_loss (train/val/dust.py:94-99): norm(x), the LM head, softcap 15 and per-token cross-entropy
+    (ignore_index -1, reduction 'none') -> fp32 [N * T]. x [N, T, 512] (fp32; other dtypes are widened), weight
+    [>= vocab, 512] (bf16, or fp32 rounded to bf16 as autocast does), targets [N, T]; vocab must be 4096 and N * T a
+    multiple of 128."""
+    if vocab != VOCAB:
+        raise ValueError(f'vocab must be {VOCAB}')
+    dev = x.device
+    xs = x.detach().reshape(-1, N_EMBD).float().contiguous()
+    w = weight.detach()[:VOCAB]
+    w = (w if w.dtype == torch.bfloat16 else w.bfloat16()).contiguous()
+    tg = targets.detach().reshape(-1).long().contiguous()
+    _lib.require_cuda(xs, w, tg)
+    rows = xs.shape[0]
+    if tg.shape[0] != rows:
+        raise ValueError('targets must hold one id per row of x')
+    L = _lib.lib()
+    nbytes = L.noise_head_loss_workspace_bytes(rows)
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    out = torch.empty(rows, dtype=torch.float32, device=dev)
+    rc = L.noise_head_loss(xs.data_ptr(), w.data_ptr(), tg.data_ptr(), rows, out.data_ptr(), ws.data_ptr(), nbytes,
+                           _lib.stream_handle(dev))
+    _lib.check(rc, 'noise_head_loss')
+    out._noise_workspace = ws
+    return out

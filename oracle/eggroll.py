@@ -61,11 +61,12 @@ def lowrank_embed(weight, a, b, idx, sign):
     return weight[idx].unsqueeze(0) + sign[:, None, None] * a[:, idx].unsqueeze(-1) * b[:, None, :]
 
 
-def population_loss(w, nz, sign, idx, targets, autocast=False, reduction='mean', head_slice=32):
+def population_loss(w, nz, sign, idx, targets, autocast=False, reduction='mean', head_slice=32, ignore_index=-100):
     """Per-member cross-entropy [m] of m perturbed models on one sequence (eggroll.py:66-103).
 
     w: name -> fp32 weight; nz: ``noise()`` output for the m members; sign [m] (+-sigma); idx, targets [T] int64.
-    reduction 'mean' is the reference's output; 'sum' is mean * T (the summed per-member fitness)."""
+    reduction 'mean' is the reference's output; 'sum' is mean * T (the summed per-member fitness); 'none' the
+    per-token losses [m, T] it averages. ignore_index as F.cross_entropy's (the reference leaves the default)."""
     heads, dim = gpt.N_HEAD, gpt.HEAD_DIM
     m, length = sign.shape[0], idx.shape[0]
     cos, sin = (z[:length].float() for z in gpt.rotary())
@@ -100,10 +101,40 @@ def population_loss(w, nz, sign, idx, targets, autocast=False, reduction='mean',
         a, b = (t[part] for t in nz['lm_head.weight'])
         logits = lowrank(h[part], w['lm_head.weight'], a, b, sign[part], autocast)[..., :gpt.VOCAB].float()
         logits = 15 * torch.tanh(logits / 15)
-        ce = F.cross_entropy(logits.flatten(0, 1), targets.repeat(logits.shape[0]), reduction='none')
+        ce = F.cross_entropy(logits.flatten(0, 1), targets.repeat(logits.shape[0]), reduction='none',
+                             ignore_index=ignore_index)
         ce = ce.view(-1, length)
-        losses.append(ce.sum(-1) if reduction == 'sum' else ce.mean(-1))
+        losses.append(ce if reduction == 'none' else ce.sum(-1) if reduction == 'sum' else ce.mean(-1))
     return torch.cat(losses)
+
+
+def zero_noise(m=1):
+    """``noise()``-shaped all-zero perturbations for m members: the un-perturbed model."""
+    return {name: (tuple(torch.zeros(m, n) for n in shape) if len(shape) == 2 else torch.zeros(m, shape[0]))
+            for name, shape in gpt.param_shapes()}
+
+
+def forward_rows(w, idx, targets, autocast=True, loss_reduction='mean'):
+    """GPT.forward(idx, targets, loss_reduction) (utils/model.py:193-209: softcap 15, ignore_index -1) on B distinct
+    rows, with the population forward's arithmetic (``population_loss`` at sign 0, one row at a time). idx, targets
+    int64 [B, T]; 'mean' / 'sum' give a 0-d tensor, 'none' [B * T]."""
+    ce = torch.cat([population_loss(w, zero_noise(1), torch.zeros(1), idx[b], targets[b], autocast, 'none',
+                                    ignore_index=-1) for b in range(idx.shape[0])]).flatten()
+    if loss_reduction == 'none':
+        return ce
+    total = ce.double().sum()
+    return (total if loss_reduction == 'sum' else total / (targets != -1).sum()).float()
+
+
+def head_loss(x, weight, targets, autocast=True):
+    """dust.head_loss (train/val/dust.py:94-99): norm, LM head, [:vocab], softcap 15, per-token cross-entropy with
+    ignore_index -1 (reduction 'none'). x [N, T, 512] fp32; weight [>= vocab, 512]; targets [N, T] -> [N * T]. With
+    autocast the head matmul takes bf16 operands and returns bf16, as under torch.autocast."""
+    h = gpt.norm(x.float())
+    wv = weight[:gpt.VOCAB].float()
+    logits = _rb(_rb(h) @ _rb(wv).t()) if autocast else h @ wv.t()
+    logits = 15 * torch.tanh(logits.float() / 15)
+    return F.cross_entropy(logits.flatten(0, 1), targets.flatten(), ignore_index=-1, reduction='none')
 
 
 def member_layout(pairs, rows, world=1, rank=0):

@@ -72,6 +72,17 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_population_loss(*args, 4, 128, 7, fake, fake, 1 << 30, None) == 4   # reduction
     assert L.noise_population_loss(*args, 4, 128, 0, fake, fake, 16, None) == 3        # workspace too small
     assert L.noise_status_string(3) == b'workspace missing or too small'
+    assert L.noise_population_loss(*args, 4, 128, 2, fake, fake, 16, None) == 3        # 'none' is a reduction
+    # the un-perturbed forward and the head loss validate the same way
+    assert L.noise_gpt_loss(ctypes.byref(gpt), fake, fake, 2, 100, 0, fake, fake, 1 << 30, None) == 1
+    assert L.noise_gpt_loss(ctypes.byref(gpt), fake, fake, 2, 128, 3, fake, fake, 1 << 30, None) == 4
+    assert L.noise_gpt_loss(ctypes.byref(gpt), fake, fake, 2, 128, 2, fake, fake, 16, None) == 3
+    assert L.noise_gpt_loss(ctypes.byref(gpt), None, fake, 2, 128, 0, fake, fake, 1 << 30, None) == 4
+    assert L.noise_gpt_workspace_bytes(2, 128) == L.noise_population_workspace_bytes(2, 128)
+    assert L.noise_head_loss(fake, fake, fake, 100, fake, fake, 1 << 30, None) == 1     # rows % 128
+    assert L.noise_head_loss(fake + 4, fake, fake, 128, fake, fake, 1 << 30, None) == 2  # x not 16-byte aligned
+    assert L.noise_head_loss(fake, fake, fake, 128, fake, fake, 16, None) == 3
+    assert 0 < L.noise_head_loss_workspace_bytes(128) < L.noise_head_loss_workspace_bytes(256)
 
 
 def test_product_path_has_no_oracle_import():

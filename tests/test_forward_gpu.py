@@ -1,0 +1,123 @@
+"""Parity of the un-perturbed forward on distinct rows (GPT.forward, utils/model.py:193-209) and of the fused LM-head
+loss (dust.head_loss, train/val/dust.py:94-99) with the CPU oracle, plus the per-token ('none') reduction of the
+population forward.
+
+Tolerances: the CUDA path follows the autocast rounding points of the oracle (bf16 linears returning bf16, fp32
+residual stream) but rounds q, k, v and the attention probabilities to bf16 where the oracle attends in fp32, and its
+fp32 sums run in another order, so single bf16 roundings flip and the flips grow through the 8 blocks of the
+informative weights. Per token that is the size of the reference's own precision gap: on these weights and rows its
+autocast and fp32 losses differ by up to 0.048 per token (median 0.010, at losses near 9). Per-token losses agree within
+TOK_ATOL with a median gap below TOK_MEDIAN; means (where the flips average out) within RTOL.
+Against the reference's own fp32 GPT.forward (tests/golden/gpt_forward.pt) the bf16 linears add up to GOLDEN_ATOL
+per token."""
+import pytest
+import torch
+
+from oracle import eggroll, gpt
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
+RTOL = 5e-4
+TOK_ATOL = 0.1     # observed <= 0.056
+TOK_MEDIAN = 0.02  # observed ~0.01
+HEAD_ATOL = 2e-4   # the head alone: same rounding points, fp32 sums in another order
+GOLDEN_ATOL = 2e-3
+
+
+def _w(seed=0):
+    return {k: v.to(DEV) for k, v in gpt.informative_weights(seed).items()}
+
+
+def _rows(rows, length, seed=1, ignore=()):
+    tok = gpt.zipf_tokens(rows, length + 1, seed=seed)
+    idx, tgt = tok[:, :-1].contiguous(), tok[:, 1:].clone()
+    for r, t in ignore:
+        tgt[r, t] = -1
+    return idx, tgt
+
+
+def _check_tokens(got, ref):
+    gap = (got - ref).abs()
+    assert gap.max().item() <= TOK_ATOL, gap.max()
+    assert gap.median().item() <= TOK_MEDIAN, gap.median()
+
+
+def _status_ok(out):
+    import noise_b200
+    torch.cuda.synchronize()
+    assert noise_b200._lib.read_status(out._noise_workspace) == 0
+
+
+@pytest.mark.parametrize('rows,length', [(3, 256), (2, 1024)])
+def test_gpt_loss_matches_oracle(rows, length):
+    import noise_b200
+    w = gpt.informative_weights(0)
+    idx, tgt = _rows(rows, length, ignore=[(0, 3), (rows - 1, length - 1)])
+    ref = eggroll.forward_rows(w, idx, tgt, autocast=True, loss_reduction='none')
+    got = noise_b200.gpt_loss(None, _w(), idx.to(DEV), tgt.to(DEV), 'none')
+    _status_ok(got)
+    got = got.cpu()
+    assert got[3] == 0 and got[rows * length - 1] == 0
+    _check_tokens(got, ref)
+    # the reductions: sum over every counted token, mean over the counted tokens
+    total = noise_b200.gpt_loss(None, _w(), idx.to(DEV), tgt.to(DEV), 'sum')
+    mean = noise_b200.gpt_loss(None, _w(), idx.to(DEV), tgt.to(DEV), 'mean')
+    _status_ok(total)
+    assert total.shape == () and mean.shape == ()
+    torch.testing.assert_close(total.cpu(), got.double().sum().float(), rtol=1e-5, atol=0)
+    torch.testing.assert_close(mean.cpu(), (got.double().sum() / (tgt != -1).sum()).float(), rtol=1e-5, atol=0)
+    torch.testing.assert_close(mean.cpu(), eggroll.forward_rows(w, idx, tgt, True, 'mean'), rtol=RTOL, atol=0)
+
+
+def test_gpt_loss_rows_are_independent():
+    """Row b's losses depend on row b's tokens only: a batch of 3 rows equals the rows run one at a time."""
+    import noise_b200
+    idx, tgt = _rows(3, 128, seed=5)
+    w = _w()
+    both = noise_b200.gpt_loss(None, w, idx.to(DEV), tgt.to(DEV), 'none').view(3, 128)
+    for b in range(3):
+        one = noise_b200.gpt_loss(None, w, idx[b:b + 1].to(DEV), tgt[b:b + 1].to(DEV), 'none')
+        torch.testing.assert_close(one.cpu(), both[b].cpu(), rtol=0, atol=0)
+
+
+def test_gpt_loss_matches_reference_forward(golden):
+    """Config 1 on the GPU: the reference's fp32 GPT.forward per-token CE of its constructor weights."""
+    import noise_b200
+    g = golden('gpt_forward.pt')
+    tokens = g['tokens'].long()
+    w = {k: v.to(DEV) for k, v in gpt.init_weights(0).items()}
+    got = noise_b200.gpt_loss(None, w, tokens[:, :-1].to(DEV), tokens[:, 1:].to(DEV), 'none')
+    _status_ok(got)
+    torch.testing.assert_close(got.cpu().view(4, -1), g['ce'], atol=GOLDEN_ATOL, rtol=0)
+    total = noise_b200.gpt_loss(None, w, tokens[:, :-1].to(DEV), tokens[:, 1:].to(DEV), 'sum')
+    assert abs(total.item() - float(g['loss_sum'])) <= 1e-5 * float(g['loss_sum'])
+
+
+def test_head_loss_matches_oracle():
+    import noise_b200
+    torch.manual_seed(0)
+    x = torch.randn(2, 384, 512) * torch.rand(2, 384, 1) * 3
+    weight = torch.randn(4100, 512) * 0.05  # four padding rows past the vocabulary: ignored
+    weight[4096:] = 1e4
+    _, tgt = _rows(2, 384, seed=7, ignore=[(1, 0), (0, 200)])
+    ref = eggroll.head_loss(x, weight, tgt, autocast=True)
+    got = noise_b200.head_loss(x.to(DEV), weight.to(DEV), tgt.to(DEV), 4096)
+    _status_ok(got)
+    got = got.cpu()
+    assert got[384] == 0 and got[200] == 0
+    torch.testing.assert_close(got, ref, atol=HEAD_ATOL, rtol=0)
+
+
+def test_population_none_reduction():
+    """reduction='none' gives the per-token losses whose mean is the default output."""
+    import noise_b200
+    from test_population_gpu import _case, _to
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(4, 256)
+    args = (None, _to(w), _to(nz), sign.to(DEV), idx.to(DEV), tgt.to(DEV))
+    per_tok = noise_b200.population_loss(*args, reduction='none')
+    mean = noise_b200.population_loss(*args)
+    _status_ok(per_tok)
+    assert per_tok.shape == (4, 256)
+    torch.testing.assert_close(per_tok.mean(-1), mean, rtol=1e-5, atol=0)
+    ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True, reduction='none')
+    _check_tokens(per_tok.cpu(), ref)

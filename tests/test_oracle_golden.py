@@ -42,6 +42,19 @@ def test_forward_fp32_matches_reference(golden, rows):
     torch.testing.assert_close(ce, g['ce'][:rows], rtol=1e-5, atol=1e-5)
 
 
+def test_forward_rows_matches_reference(golden):
+    """The oracle of the un-perturbed forward on distinct rows (population_loss at sign 0, per row) against the
+    reference's GPT.forward, fp32, per-token CE, with ignore_index -1 on two targets."""
+    g = golden('gpt_forward.pt')
+    tokens = g['tokens'].long()[:1]
+    targets = tokens[:, 1:].clone()
+    targets[0, 7] = targets[0, 2000] = -1
+    ce = eggroll.forward_rows(gpt.init_weights(0), tokens[:, :-1], targets, autocast=False, loss_reduction='none')
+    want = g['ce'][0].clone()
+    want[7] = want[2000] = 0
+    torch.testing.assert_close(ce, want, rtol=1e-5, atol=1e-5)
+
+
 def _population_case(g):
     buf = eggroll.make_buffer(g['noise_size'], seed=0)
     assert torch.equal(buf[:16], g['buffer_head'])
