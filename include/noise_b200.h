@@ -103,13 +103,21 @@ typedef struct {
 /* A [rows, T, 64] view: element (row, t, c) at data + L * layer_stride + (row % heads) * 64 + t * token_stride + c,
  * L = row / heads, or layer_map[row / heads] when layer_map (int32, device) is set. The reference's stacked layout is
  * heads = 1, layer_stride = T * 64, token_stride = 64; its "by token" (layers, T, heads * 64) views
- * (moment_kernels.py:66-74) are heads = H, layer_stride = stride(0), token_stride = stride(1). 16-byte aligned. */
+ * (moment_kernels.py:66-74) are heads = H, layer_stride = stride(0), token_stride = stride(1). 16-byte aligned.
+ * With block_rows > 0 (heads = 1, no layer_map; moment-score raw inputs and outputs only) the blocked layout of the
+ * identity phase's all_to_all buffers (moment_kernels.py:200-220, run.py:3799-3803): element (row, t, c) at
+ * data + (row / block_rows) * layer_stride + (n / per_gpu) * gpu_stride + (n % per_gpu) * token_stride + c,
+ * n = (row % block_rows) * T + t; e.g. a (W, L, N, C) buffer is block_rows = rows / L, layer_stride = stride(1),
+ * gpu_stride = stride(0), token_stride = stride(2), per_gpu = N. Zero-initialised trailing fields mean "not blocked". */
 typedef struct {
   void* data;
   int64_t layer_stride;
   int64_t token_stride;
   int heads;
   const int32_t* layer_map;
+  int block_rows;
+  int64_t per_gpu;
+  int64_t gpu_stride;
 } noise_rows_t;
 
 /* lse[row, s] = logsumexp_t q_s.k_t / 8 and center[row, s] = sum_t p(s, t) (hub_s . v_t) over the window; q, k,
@@ -142,6 +150,14 @@ int noise_moment_key_scores(const void* q, const void* k, const void* v, const v
                             const float* hub_out, const float* steps, int rows, int tokens, const noise_rows_t* out,
                             const noise_rows_t* values_out, void* stream);
 
+/* noise_moment_key_scores with raw as a view of `raw_dtype` (fp32 or bf16, blocked allowed) and out / values_out
+ * views of `out_dtype`: the reference kernel's strided raw (RAW_BLK, RAW_GPU, RAW_STRIDE) and out arguments, as the
+ * identity phase passes them (raw = the received heads' key pieces, out / values = its bf16 return buffer). */
+int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                              int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                              const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                              const noise_rows_t* out, const noise_rows_t* values_out, int out_dtype, void* stream);
+
 /* Query credits: per query s and raw query coordinate d, zn / (1 + zd) / steps_s from the numerator / denominator
  * moments of its own softmax (moment_kernels._moment_queries_kernel, :197-365), rounded to bf16 (stored as bf16 or
  * as fp32 per out_dtype). q, k, v, hub bf16 [rows, T, 64]; raw (queries' raw coordinates), side (the keys' fp32 pair
@@ -150,6 +166,13 @@ int noise_moment_query_scores(const void* q, const void* k, const void* v, const
                               const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
                               const float* hub_out, const float* steps, int rows, int tokens, int window,
                               const noise_rows_t* out, int out_dtype, void* stream);
+
+/* noise_moment_query_scores with raw as a view of `raw_dtype` (fp32 or bf16, blocked allowed) and out any view of
+ * `out_dtype` (blocked allowed): the reference's strided raw / out arguments (moment_kernels.py:319-336). */
+int noise_moment_query_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                                int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                                const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                                int window, const noise_rows_t* out, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------------
  * The seed-rebuilt ES update (reference archive/10M/train/val/eggroll.py:151-167).
@@ -174,6 +197,68 @@ int noise_rank1_small(const float* buffer, const int64_t* offsets, const float* 
  * (sqrt(exp_avg_sq) / sqrt(1 - beta2^step) + eps). */
 int noise_adam_step(float* param, float* exp_avg, float* exp_avg_sq, const float* grad, int64_t n, float lr,
                     float beta1, float beta2, float eps, int step, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Identity-phase head sharding (reference train/speedrun/run.py:3694-3804): the all_to_all send buffer, the
+ * received heads' preparation and their moment credits.
+ * ------------------------------------------------------------------------------------------------------------- */
+#define NOISE_PACK (5 * NOISE_HEAD_DIM + 2) /* bf16 elements per packed row: q, k, v, o, target pieces + lse bits */
+#define NOISE_MAX_PACK_LAYERS 16
+
+/* One layer's pieces for noise_pack_heads: q, k, v, o (attention output) and target bf16 [tokens, >= 512] with row
+ * strides in elements (even, 4-byte aligned rows; head h at columns 64 h .. 64 h + 63); lse fp32 [tokens / T, 8, T]. */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* o;
+  const void* target;
+  int64_t q_stride, k_stride, v_stride, o_stride, target_stride;
+  const float* lse;
+} noise_head_pieces_t;
+
+/* out (8, n_layers, tokens, NOISE_PACK) bf16: row (h, l, t) = head h's 64 columns of q, k, v, o, target of layer l at
+ * token t, then the fp32 bits of lse[t / T, h, t % T] in its last two elements. Replaces run.py's pack_heads_kernel
+ * / _pack_heads_kernel (:3698-3731); tokens % 16 == 0, tokens % seq_len == 0, n_layers <= 16. */
+int noise_pack_heads(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len, void* out, void* stream);
+
+/* Outputs of noise_head_prep, rows = layers * world * n / T of T tokens each: q16, k16, v16, hub16 bf16 [rows, T, 64];
+ * q32 fp32 [rows, T, 64]; k32 fp32 [rows, T, 64] or NULL (the reference does not keep it); the keys' pair features
+ * f2 bf16 [rows, T, 64] (x_i, y_i interleaved), f4 [rows, T, 128] (x_i, x_i^2, y_i, y_i^2), xy [rows, T, 32], all three
+ * or none; lse, hub_out (= hub . o), sq_q, sq_k (raw square norms), steps_q, steps_k fp32 [rows, T]. */
+typedef struct {
+  void* q16;
+  void* k16;
+  void* v16;
+  void* hub16;
+  float* q32;
+  float* k32;
+  void* f2;
+  void* f4;
+  void* xy;
+  float* lse;
+  float* hub_out;
+  float* sq_q;
+  float* sq_k;
+  float* steps_q;
+  float* steps_k;
+} noise_head_prep_t;
+
+/* The received heads from got (world, layers, n, NOISE_PACK) bf16: received row (w, l, i) becomes output token
+ * (l * world + w) * n + i at position i % T; queries and keys RoPE'd (cos / sin fp32 [T, 32]) and RMS-normed with
+ * eps, steps = sigma * max(sqrt(sq / 64), 1e-6). Replaces run.py's head_prep_fused / _head_prep_kernel (:3734-3796;
+ * the reference calls it with sigma = KEY_SIGMA 0.003, eps = NORM_EPS 1e-6). n % 32 == 0, world * n % T == 0. */
+int noise_head_prep(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
+                    float sigma, float eps, const noise_head_prep_t* out, void* stream);
+
+/* Bytes of scratch noise_id_head_scores needs. */
+size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n);
+
+/* run.py's id_head_scores (:3799-3803): noise_head_prep, then the query-moment credits (full causal window) into
+ * back[:, :, 0] and the key-moment credits and value sums into back[:, :, 1] and back[:, :, 2], the raw coordinates
+ * read in place from got's q and k pieces. back: bf16 (world, layers, 3, n, 64). T % 64 == 0. */
+int noise_id_head_scores(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
+                         float sigma, float eps, void* back, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);

@@ -33,9 +33,22 @@ class GPT(ctypes.Structure):
 
 
 class Rows(ctypes.Structure):
-    """noise_rows_t."""
+    """noise_rows_t (block_rows = 0: not blocked)."""
     _fields_ = [('data', ctypes.c_void_p), ('layer_stride', ctypes.c_int64), ('token_stride', ctypes.c_int64),
-                ('heads', ctypes.c_int), ('layer_map', ctypes.c_void_p)]
+                ('heads', ctypes.c_int), ('layer_map', ctypes.c_void_p), ('block_rows', ctypes.c_int),
+                ('per_gpu', ctypes.c_int64), ('gpu_stride', ctypes.c_int64)]
+
+
+class HeadPieces(ctypes.Structure):
+    """noise_head_pieces_t."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ('q', 'k', 'v', 'o', 'target')] + \
+               [(n + '_stride', ctypes.c_int64) for n in ('q', 'k', 'v', 'o', 'target')] + [('lse', ctypes.c_void_p)]
+
+
+class HeadPrep(ctypes.Structure):
+    """noise_head_prep_t."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ('q16', 'k16', 'v16', 'hub16', 'q32', 'k32', 'f2', 'f4', 'xy', 'lse',
+                                               'hub_out', 'sq_q', 'sq_k', 'steps_q', 'steps_k')]
 
 
 class NoiseError(RuntimeError):
@@ -77,6 +90,14 @@ SIGNATURES = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
     ('noise_moment_query_scores', ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_moment_key_scores_v', ctypes.c_int,
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_moment_query_scores_v', ctypes.c_int,
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_pack_heads', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_head_prep', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
+    ('noise_id_head_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ('noise_id_head_scores', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),

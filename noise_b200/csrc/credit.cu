@@ -31,14 +31,37 @@ struct Rows {
   int64_t layer_stride, token_stride;
   int heads;
   const int32_t* map;
+  int block_rows;  // > 0: the blocked layout (row blocks of block_rows rows, tokens split over source GPUs)
+  int64_t per_gpu, gpu_stride;
   __device__ __forceinline__ int64_t base(int row) const {
     int l = row / heads;
     if (map) l = map[l];
     return static_cast<int64_t>(l) * layer_stride + static_cast<int64_t>(row % heads) * D;
   }
+  // element offset of (row, t, 0); T = tokens per row
+  __device__ __forceinline__ int64_t at(int row, int t, int T) const {
+    if (block_rows > 0) {  // moment_kernels._query_coefficients / _query_store addressing (:200-220)
+      const int blk = row / block_rows;
+      const int64_t n = static_cast<int64_t>(row - blk * block_rows) * T + t;
+      return blk * layer_stride + (n / per_gpu) * gpu_stride + (n % per_gpu) * token_stride;
+    }
+    return base(row) + static_cast<int64_t>(t) * token_stride;
+  }
 };
 
-__host__ Rows to_rows(const noise_rows_t& r) { return Rows{r.data, r.layer_stride, r.token_stride, r.heads, r.layer_map}; }
+__host__ Rows to_rows(const noise_rows_t& r) {
+  return Rows{r.data, r.layer_stride, r.token_stride, r.heads, r.layer_map, r.block_rows, r.per_gpu, r.gpu_stride};
+}
+
+// A contiguous [rows, T, 64] tensor as a view.
+__host__ Rows stacked_rows(const void* data, int T) {
+  return Rows{const_cast<void*>(data), static_cast<int64_t>(T) * D, D, 1, nullptr, 0, 0, 0};
+}
+
+// One element of a raw-coordinate view (fp32 or bf16) as fp32.
+__device__ __forceinline__ float raw_at(const Rows& r, bool bf16, int64_t i) {
+  return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(r.data)[i]) : static_cast<const float*>(r.data)[i];
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // tile staging
@@ -372,12 +395,14 @@ __device__ __forceinline__ int pxy(int c) { return 8 * (c >> 3) + 4 * (c & 1) + 
 struct KeyArgs {
   const void *qp, *kp, *values, *hub;  // [rows, T, 64]: fp32 (SCAN) or bf16 (IDENT)
   const float* side;                   // IDENT: receivers' fp32 pair-feature source [rows, T, 64]; SCAN uses qp
-  const float* raw;                    // raw key coordinates [rows, T, 64] fp32
+  Rows raw;                            // raw key coordinates (rows, T, 64) view
+  int raw_bf16;                        // raw holds bf16 (else fp32)
+  int out_bf16;                        // out / vout hold bf16 (else fp32)
   const float* sq;                     // IDENT: [rows, T]
   const float* steps;                  // IDENT: [rows, T]
   const float *lse, *center;           // [rows, T] (center = hub_out for IDENT)
   const float *cosb, *sinb;            // [T, 32] fp32
-  Rows out, vout;                      // fp32 views; vout.data NULL = no value credit
+  Rows out, vout;                      // output views; vout.data NULL = no value credit
   int T, window;
   float sigma;
 };
@@ -564,7 +589,8 @@ __global__ void __launch_bounds__(128) key_moments_kernel(KeyArgs p) {
     a2 += __shfl_xor_sync(0xffffffffu, a2, 1);
     a2 += __shfl_xor_sync(0xffffffffu, a2, 2);
     const int tk = t0 + r0 + g + 8 * hr;
-    const float* raw = p.raw + base + static_cast<int64_t>(tk) * D;
+    const int64_t ro = p.raw.at(row, tk, p.T);
+    const bool rb = p.raw_bf16;
     float sqv, stepv, den;
     if constexpr (IDENT) {
       sqv = p.sq[static_cast<int64_t>(row) * p.T + tk];
@@ -575,7 +601,8 @@ __global__ void __launch_bounds__(128) key_moments_kernel(KeyArgs p) {
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         const int P = 4 * n + q;
-        part += raw[P] * raw[P] + raw[P + 32] * raw[P + 32];
+        const float r0 = raw_at(p.raw, rb, ro + P), r1 = raw_at(p.raw, rb, ro + P + 32);
+        part += r0 * r0 + r1 * r1;
       }
       part += __shfl_xor_sync(0xffffffffu, part, 1);
       part += __shfl_xor_sync(0xffffffffu, part, 2);
@@ -584,7 +611,7 @@ __global__ void __launch_bounds__(128) key_moments_kernel(KeyArgs p) {
       den = sqv + 1.1920928955078125e-07f;
     }
     const float rs = rsqrtf(den);
-    float* out = static_cast<float*>(p.out.data) + p.out.base(row) + static_cast<int64_t>(tk) * p.out.token_stride;
+    const int64_t oo = p.out.at(row, tk, p.T);
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       const int P = 4 * n + q;
@@ -596,20 +623,31 @@ __global__ void __launch_bounds__(128) key_moments_kernel(KeyArgs p) {
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int d = P + 32 * half;
-        const float ratio = (2.f * stepv * raw[d] + stepv * stepv) / D / den;
+        const float ratio = (2.f * stepv * raw_at(p.raw, rb, ro + d) + stepv * stepv) / D / den;
         const float ca = expm1f(-0.5f * log1pf(ratio));
         const float cb = stepv * rs * (1.f + ca);
         const float bu = cb * (half ? sn : cs), bw = cb * (half ? cs : -sn);
         const float resp = px * bu + py * bw + qx * bu * bu + qy * bw * bw + 2.f * cxy * bu * bw +
                            2.f * ca * (rx * bu + ry * bw) + a1 * ca + a2 * ca * ca;
-        out[d] = resp / stepv;
+        if (p.out_bf16)
+          static_cast<__nv_bfloat16*>(p.out.data)[oo + d] = __float2bfloat16_rn(resp / stepv);
+        else
+          static_cast<float*>(p.out.data)[oo + d] = resp / stepv;
       }
     }
     if (values) {
-      float* vo = static_cast<float*>(p.vout.data) + p.vout.base(row) + static_cast<int64_t>(tk) * p.vout.token_stride;
+      const int64_t vo = p.vout.at(row, tk, p.T);
+      if (p.out_bf16) {
+        __nv_bfloat16* vb = static_cast<__nv_bfloat16*>(p.vout.data) + vo;
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
-        *reinterpret_cast<float2*>(vo + n * 8 + 2 * q) = make_float2(va[n][2 * hr], va[n][2 * hr + 1]);
+        for (int n = 0; n < 8; ++n)
+          *reinterpret_cast<__nv_bfloat162*>(vb + n * 8 + 2 * q) = __floats2bfloat162_rn(va[n][2 * hr], va[n][2 * hr + 1]);
+      } else {
+        float* vf = static_cast<float*>(p.vout.data) + vo;
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+          *reinterpret_cast<float2*>(vf + n * 8 + 2 * q) = make_float2(va[n][2 * hr], va[n][2 * hr + 1]);
+      }
     }
   }
 }
@@ -624,7 +662,8 @@ __device__ __forceinline__ int pq16(int c) { return 8 * (c >> 3) + 4 * (c & 1) +
 
 struct QueryArgs {
   const __nv_bfloat16 *q, *k, *v, *hub;  // [rows, T, 64]
-  const float* raw;                      // raw query coordinates [rows, T, 64]
+  Rows raw;                              // raw query coordinates (rows, T, 64) view
+  int raw_bf16;
   const float *sq, *steps, *lse, *hub_out;  // [rows, T]
   const float* side;                     // keys' pair-feature source [rows, T, 64] fp32
   const float *cosb, *sinb;              // [T, 32]
@@ -783,8 +822,8 @@ __global__ void __launch_bounds__(128) query_moments_kernel(QueryArgs p) {
     const int64_t ti = static_cast<int64_t>(row) * p.T + sq_;
     const float sqv = p.sq[ti], stepv = p.steps[ti];
     const float den = sqv / D + 1e-6f, rs = rsqrtf(den);
-    const float* raw = p.raw + base + static_cast<int64_t>(sq_) * D;
-    const int64_t ob = p.out.base(row) + static_cast<int64_t>(sq_) * p.out.token_stride;
+    const int64_t ro = p.raw.at(row, sq_, p.T);
+    const int64_t ob = p.out.at(row, sq_, p.T);
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
@@ -795,7 +834,7 @@ __global__ void __launch_bounds__(128) query_moments_kernel(QueryArgs p) {
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int d = P + 32 * half;
-          const float change = (2.f * stepv * raw[d] + stepv * stepv) / D / den;
+          const float change = (2.f * stepv * raw_at(p.raw, p.raw_bf16, ro + d) + stepv * stepv) / D / den;
           const float ca = expm1f(-0.5f * log1pf(change));
           const float b = stepv * rs * (1.f + ca);
           const float bu = b * (half ? sn : cs), bw = b * (half ? cs : -sn);
@@ -817,9 +856,20 @@ __global__ void __launch_bounds__(128) query_moments_kernel(QueryArgs p) {
 
 static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// A (by-layer / by-token) view the vectorised kernels accept: 16-byte aligned rows, no blocked layout.
 static bool rows_ok(const noise_rows_t& r, bool f32) {
-  return r.data && r.heads >= 1 && a16(r.data) && (r.token_stride * (f32 ? 4 : 2)) % 16 == 0 &&
+  return r.data && r.heads >= 1 && r.block_rows == 0 && a16(r.data) && (r.token_stride * (f32 ? 4 : 2)) % 16 == 0 &&
          (r.layer_stride * (f32 ? 4 : 2)) % 16 == 0;
+}
+
+// A view the moment-score epilogues accept (blocked allowed): element-aligned scalar accesses, and with `pairs` the
+// value sums' two-element stores (even strides).
+static bool view_ok(const noise_rows_t& r, bool bf16, bool pairs) {
+  const int64_t esz = bf16 ? 2 : 4, align = pairs ? 2 * esz : esz;
+  if (!r.data || r.heads < 1 || (reinterpret_cast<uintptr_t>(r.data) % align)) return false;
+  if (r.block_rows < 0 || (r.block_rows > 0 && (r.per_gpu < 1 || r.heads != 1 || r.layer_map))) return false;
+  if (pairs && ((r.token_stride | r.layer_stride | r.gpu_stride) & 1)) return false;
+  return true;
 }
 
 }  // namespace credit
@@ -884,7 +934,7 @@ int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const f
   a.kp = kp;
   a.values = values;
   a.hub = hub;
-  a.raw = k_raw;
+  a.raw = stacked_rows(k_raw, tokens);
   a.lse = lse;
   a.center = center;
   a.cosb = cos;
@@ -900,14 +950,19 @@ int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const f
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
-int noise_moment_key_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
-                            const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
-                            const float* hub_out, const float* steps, int rows, int tokens, const noise_rows_t* out,
-                            const noise_rows_t* values_out, void* stream) {
+int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                              int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                              const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                              const noise_rows_t* out, const noise_rows_t* values_out, int out_dtype, void* stream) {
   if (!q || !k || !v || !hub || !raw || !sq || !side || !cos || !sin || !lse || !hub_out || !steps || !out || !values_out)
     return NOISE_ERR_ARGUMENT;
+  if ((raw_dtype != NOISE_DTYPE_F32 && raw_dtype != NOISE_DTYPE_BF16) ||
+      (out_dtype != NOISE_DTYPE_F32 && out_dtype != NOISE_DTYPE_BF16))
+    return NOISE_ERR_ARGUMENT;
   if (rows < 1 || tokens < 64 || tokens % 64) return NOISE_ERR_SHAPE;
-  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !rows_ok(*out, true) || !rows_ok(*values_out, true))
+  const bool ob = out_dtype == NOISE_DTYPE_BF16;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) ||
+      !view_ok(*out, ob, false) || !view_ok(*values_out, ob, true))
     return NOISE_ERR_ALIGN;
   KeyArgs a{};
   a.qp = q;
@@ -915,7 +970,9 @@ int noise_moment_key_scores(const void* q, const void* k, const void* v, const v
   a.values = v;
   a.hub = hub;
   a.side = side;
-  a.raw = raw;
+  a.raw = to_rows(*raw);
+  a.raw_bf16 = raw_dtype == NOISE_DTYPE_BF16;
+  a.out_bf16 = ob;
   a.sq = sq;
   a.steps = steps;
   a.lse = lse;
@@ -932,21 +989,37 @@ int noise_moment_key_scores(const void* q, const void* k, const void* v, const v
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
-int noise_moment_query_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
-                              const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
-                              const float* hub_out, const float* steps, int rows, int tokens, int window,
-                              const noise_rows_t* out, int out_dtype, void* stream) {
+int noise_moment_key_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
+                            const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
+                            const float* hub_out, const float* steps, int rows, int tokens, const noise_rows_t* out,
+                            const noise_rows_t* values_out, void* stream) {
+  if (!raw || !out || !values_out) return NOISE_ERR_ARGUMENT;
+  if (!rows_ok(*out, true) || !rows_ok(*values_out, true)) return NOISE_ERR_ALIGN;
+  const noise_rows_t rv{const_cast<float*>(raw), static_cast<int64_t>(tokens) * D, D, 1, nullptr, 0, 0, 0};
+  return noise_moment_key_scores_v(q, k, v, hub, &rv, NOISE_DTYPE_F32, sq, side, cos, sin, lse, hub_out, steps, rows,
+                                   tokens, out, values_out, NOISE_DTYPE_F32, stream);
+}
+
+int noise_moment_query_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                                int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                                const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                                int window, const noise_rows_t* out, int out_dtype, void* stream) {
   if (!q || !k || !v || !hub || !raw || !sq || !side || !cos || !sin || !lse || !hub_out || !steps || !out)
     return NOISE_ERR_ARGUMENT;
-  if (out_dtype != NOISE_DTYPE_F32 && out_dtype != NOISE_DTYPE_BF16) return NOISE_ERR_ARGUMENT;
+  if ((raw_dtype != NOISE_DTYPE_F32 && raw_dtype != NOISE_DTYPE_BF16) ||
+      (out_dtype != NOISE_DTYPE_F32 && out_dtype != NOISE_DTYPE_BF16))
+    return NOISE_ERR_ARGUMENT;
   if (rows < 1 || tokens < 64 || tokens % 64 || window < 0) return NOISE_ERR_SHAPE;
-  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !out->data) return NOISE_ERR_ALIGN;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) ||
+      !view_ok(*out, out_dtype == NOISE_DTYPE_BF16, false))
+    return NOISE_ERR_ALIGN;
   QueryArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);
   a.v = static_cast<const __nv_bfloat16*>(v);
   a.hub = static_cast<const __nv_bfloat16*>(hub);
-  a.raw = raw;
+  a.raw = to_rows(*raw);
+  a.raw_bf16 = raw_dtype == NOISE_DTYPE_BF16;
   a.sq = sq;
   a.steps = steps;
   a.lse = lse;
@@ -961,6 +1034,16 @@ int noise_moment_query_scores(const void* q, const void* k, const void* v, const
   if (cudaFuncSetAttribute(query_moments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM)) return NOISE_ERR_CUDA;
   query_moments_kernel<<<dim3(tokens / 64, 2 * rows), 128, Q_SMEM, static_cast<cudaStream_t>(stream)>>>(a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_moment_query_scores(const void* q, const void* k, const void* v, const void* hub, const float* raw,
+                              const float* sq, const float* side, const float* cos, const float* sin, const float* lse,
+                              const float* hub_out, const float* steps, int rows, int tokens, int window,
+                              const noise_rows_t* out, int out_dtype, void* stream) {
+  if (!raw) return NOISE_ERR_ARGUMENT;
+  const noise_rows_t rv{const_cast<float*>(raw), static_cast<int64_t>(tokens) * D, D, 1, nullptr, 0, 0, 0};
+  return noise_moment_query_scores_v(q, k, v, hub, &rv, NOISE_DTYPE_F32, sq, side, cos, sin, lse, hub_out, steps, rows,
+                                     tokens, window, out, out_dtype, stream);
 }
 
 }  // extern "C"

@@ -116,9 +116,31 @@ def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, w
 
 # --- query and key moments ------------------------------------------------------------------------------------------
 
-def _stacked_raw(raw, rows, t):
-    """The raw coordinates as contiguous fp32 [rows, T, 64] (the reference passes (1, rows, T, 64))."""
-    return raw.detach().float().reshape(rows, t, 64).contiguous()
+def _blocked(t, rows, m, blocks):
+    """noise_rows_t of one of the reference's strided 4-D raw / out arguments (G, blocks, M, >= 64): row r, token s
+    at (r // (rows // blocks)) * stride(1) + (n // m) * stride(0) + (n % m) * stride(2), n = (r % (rows // blocks)) *
+    T + s (moment_kernels.py:200-220: RAW_BLK, RAW_GPU, RAW_STRIDE, M). (1, rows, T, 64) is the stacked layout; the
+    identity phase passes its (W, L, N, 322) received buffer and (W, L, N, 64) slices of the return buffer."""
+    if t.dim() != 4 or t.stride(-1) != 1:
+        raise ValueError('raw / out: 4-D with a unit last stride')
+    if rows % blocks:
+        raise ValueError('rows must split evenly over raw.shape[1] blocks')
+    v = _lib.Rows()
+    v.data = t.data_ptr()
+    v.heads = 1
+    v.block_rows = rows // blocks
+    v.layer_stride, v.gpu_stride, v.token_stride = t.stride(1), t.stride(0), t.stride(2)
+    v.per_gpu = m
+    return v
+
+
+def _raw4(raw, rows, t):
+    raw = raw.detach()
+    if raw.dim() == 3:
+        raw = raw.unsqueeze(0)
+    if raw.dtype not in _DT:
+        raw = raw.float()
+    return raw
 
 
 def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window=None, out_heads=0,
@@ -126,41 +148,49 @@ def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out
     rows, t, d = q.shape
     if d != 64:
         raise ValueError('head_dim 64 only (the reference asserts it)')
+    if side is None:
+        raise ValueError("side (the keys' fp32 pair-feature source) is required")
     q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
-    raw = _stacked_raw(raw, rows, t)
+    raw = _raw4(raw, rows, t)
     side = _c(side, torch.float32)
     sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
     cos, sin = _rope(cos, sin)
     window = t if window is None else min(window, t)
-    if out_heads:
-        target, heads, dt = out, out_heads, F32
-    else:  # the reference's (1, rows, T, D) bf16 output
-        target, heads = out[0], 1
-        dt = _DT[out.dtype]
-    o = _rows(target, heads, layers)
-    _check(_lib.lib().noise_moment_query_scores(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
-                                                raw.data_ptr(), sq.data_ptr(), side.data_ptr(), cos.data_ptr(),
-                                                sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(), steps.data_ptr(),
-                                                rows, t, window, ctypes.byref(o), dt, _stream(q)),
-           'noise_moment_query_scores')
+    blocks = raw.shape[1]
+    if out_heads:  # a (layers, T, heads * D) fp32 view, by token
+        o, dt, m = _rows(out, out_heads, layers), F32, t
+    else:  # the reference's 4-D out: (1, rows, T, D) bf16, or the identity phase's (W, L, N, D) slice
+        m = out.shape[2]
+        o, dt = _blocked(out, rows, m, blocks), _DT[out.dtype]
+    rv = _blocked(raw, rows, m, blocks)
+    _check(_lib.lib().noise_moment_query_scores_v(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
+                                                  ctypes.byref(rv), _DT[raw.dtype], sq.data_ptr(), side.data_ptr(),
+                                                  cos.data_ptr(), sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(),
+                                                  steps.data_ptr(), rows, t, window, ctypes.byref(o), dt, _stream(q)),
+           'noise_moment_query_scores_v')
 
 
 def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values):
     rows, t, d = q.shape
     q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
-    raw = _stacked_raw(raw, rows, t)
+    raw = _raw4(raw, rows, t)
     side = _c(side, torch.float32)
     sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
     cos, sin = _rope(cos, sin)
-    o, val = out.view(rows, t, d), values.view(rows, t, d)
-    if o.dtype != torch.float32 or o.stride(-1) != 1:
-        raise ValueError('out / values: fp32 [rows, T, 64] views')
-    ro, rv = _rows(o), _rows(val)
-    _check(_lib.lib().noise_moment_key_scores(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(), raw.data_ptr(),
-                                              sq.data_ptr(), side.data_ptr(), cos.data_ptr(), sin.data_ptr(),
-                                              lse.data_ptr(), hub_out.data_ptr(), steps.data_ptr(), rows, t,
-                                              ctypes.byref(ro), ctypes.byref(rv), _stream(q)),
-           'noise_moment_key_scores')
+    if out.dim() == 3:
+        out, values = out.unsqueeze(0), values.unsqueeze(0)
+    if values.shape != out.shape or values.stride() != out.stride() or values.dtype != out.dtype:
+        raise ValueError('out and values: same shape, strides and dtype (the reference asserts it)')
+    if out.dtype not in _DT:
+        raise ValueError('out / values: fp32 or bf16')
+    blocks, m = raw.shape[1], out.shape[2]
+    rv, ro, rvals = _blocked(raw, rows, m, blocks), _blocked(out, rows, m, blocks), _blocked(values, rows, m, blocks)
+    _check(_lib.lib().noise_moment_key_scores_v(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
+                                                ctypes.byref(rv), _DT[raw.dtype], sq.data_ptr(), side.data_ptr(),
+                                                cos.data_ptr(), sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(),
+                                                steps.data_ptr(), rows, t, ctypes.byref(ro), ctypes.byref(rvals),
+                                                _DT[out.dtype], _stream(q)),
+           'noise_moment_key_scores_v')
 
 
 # --- the reference's custom ops (names as in moment_kernels.py:184-717) ---------------------------------------------
@@ -305,8 +335,8 @@ def moment_key_scores(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, hub: to
                       sq: torch.Tensor, side: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, lse: torch.Tensor,
                       hub_out: torch.Tensor, steps: torch.Tensor, out: torch.Tensor, values: torch.Tensor,
                       repeat: int) -> None:
-    """The identity phase's key credits and value sums (moment_kernels.py:451-457); out / values fp32 with rows x T x
-    64 elements."""
+    """The identity phase's key credits and value sums (moment_kernels.py:451-457); out / values fp32 or bf16,
+    (rows, T, 64) or the reference's 4-D layouts (its (W, L, N, 64) return-buffer slices included)."""
     if repeat != 2 or q.shape[-1] != 64:
         raise ValueError("the identity phase's call (repeat = head_dim // 32, head_dim 64)")
     moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values)

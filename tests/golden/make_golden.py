@@ -15,7 +15,10 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 ``flex_attention`` (same function, no compilation). The noise buffer is shrunk from 2**28 to 2**20 values
 (``eggroll.NOISE``) and the chunk from 256 to 2 pairs (``eggroll.CHUNK``) so one step finishes in seconds.
 
-Usage: python tests/golden/make_golden.py /path/to/reference
+- ``train/speedrun/run.py``: pack_heads_kernel, head_prep_fused and id_head_scores (the identity phase's head
+  sharding) under the same patched interpreter, on tests/golden/heads_inputs.py's seeded inputs.
+
+Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
 import os
@@ -249,17 +252,54 @@ def golden_credit(root, rows=2, t=256):
     print('credit kernels: ok')
 
 
+def golden_heads(root):
+    """The identity phase's pack_heads_kernel, head_prep_fused and id_head_scores (speedrun/run.py:3694-3804) under
+    the patched interpreter, on heads_inputs' seeded inputs: world 8 (one head per rank), 2 layers, N = 64 tokens per
+    rank, t = 64 (b = 8 rows per layer); the pack on 2 layers of 64 tokens (t = 32)."""
+    patch_triton_interpreter()
+    sys.path.insert(0, str(root / 'train/speedrun'))
+    spec = importlib.util.spec_from_file_location('ref_run', root / 'train/speedrun/run.py')
+    run = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(run)
+    run.moment_kernels.libdevice = interpreter_libdevice()
+    from heads_inputs import got_inputs, pack_inputs, rotary
+    p = pack_inputs()
+    packed = run.pack_heads_kernel(p['qs'], p['ks'], p['vals'], p['outs'], p['targets'], p['lses'])
+    got, b = got_inputs()
+    t = 64
+    cos, sin = rotary(t)
+    assert torch.equal(cos, run.rotary(t, 'cpu')[0]) and torch.equal(sin, run.rotary(t, 'cpu')[1])
+    prep = run.head_prep_fused(got, cos, sin, b, t)
+    names = ('q16', 'k16', 'v16', 'hub16', 'q32', 'pairs', 'lse', 'hub_out', 'sq_q', 'sq_k', 'steps_q', 'steps_k')
+    prep = dict(zip(names, prep))
+    prep['f2'], prep['f4'], prep['xy'] = prep.pop('pairs')
+    back = torch.empty(got.shape[0], got.shape[1], 3, got.shape[2], 64, dtype=torch.bfloat16)
+    run.id_head_scores(got, (cos, sin), back, b, t)
+    torch.save(dict(pack=packed.view(torch.int16).clone(), prep={k: v.clone() for k, v in prep.items()},
+                    back=back.clone(), b=b, t=t), HERE / 'heads.pt')
+    print('heads: ok')
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
+    only = set(sys.argv[2].split(',')) if len(sys.argv) > 2 else None  # e.g. "heads": regenerate that fixture only
+    want = lambda name: only is None or name in only
     torch.set_num_threads(os.cpu_count())
     model, eggroll = load_reference(root)
-    golden_forward(model)
-    golden_population(eggroll, length=256)
-    golden_population(eggroll, length=2048)
-    golden_step(eggroll)
-    golden_implicit(root)
-    golden_credit(root)
+    if want('forward'):
+        golden_forward(model)
+    if want('population'):
+        golden_population(eggroll, length=256)
+        golden_population(eggroll, length=2048)
+    if want('step'):
+        golden_step(eggroll)
+    if want('implicit'):
+        golden_implicit(root)
+    if want('credit'):
+        golden_credit(root)
+    if want('heads'):
+        golden_heads(root)
 
 
 if __name__ == '__main__':

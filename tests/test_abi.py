@@ -83,6 +83,16 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_head_loss(fake + 4, fake, fake, 128, fake, fake, 1 << 30, None) == 2  # x not 16-byte aligned
     assert L.noise_head_loss(fake, fake, fake, 128, fake, fake, 16, None) == 3
     assert 0 < L.noise_head_loss_workspace_bytes(128) < L.noise_head_loss_workspace_bytes(256)
+    # head sharding: the reference's shape asserts
+    pieces = (_lib.HeadPieces * 2)()
+    assert L.noise_pack_heads(pieces, 2, 24, 8, fake, None) == 1          # tokens % 16
+    assert L.noise_pack_heads(pieces, 17, 32, 8, fake, None) == 1         # more layers than the launch carries
+    assert L.noise_pack_heads(pieces, 2, 32, 8, fake, None) == 4          # missing pieces
+    prep = _lib.HeadPrep()
+    assert L.noise_head_prep(fake, 8, 2, 48, fake, fake, 64, 0.003, 1e-6, ctypes.byref(prep), None) == 1  # n % 32
+    assert L.noise_head_prep(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, ctypes.byref(prep), None) == 4  # outputs
+    assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 96, 0.003, 1e-6, fake, fake, 1 << 30, None) == 1
+    assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, fake, fake, 16, None) == 3
 
 
 def test_product_path_has_no_oracle_import():
