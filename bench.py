@@ -5,9 +5,12 @@ One step = one population evaluation on every rank: 512 antithetic members (256 
 synthetic Zipf(1.1) tokens (summed cross-entropy = its fitness), the rank-1 noise read in place from EGGROLL's
 2**28-value N(0, 1) buffer at the step's offsets, then the NCCL all-gather of the fitness vector (N > 1). Ranks hold
 disjoint members of one population of 512 N (weak scaling). The unit of work is a population forward: one member
-over one 2048-token row (BASELINE.md's "population forwards/s").
+over one 2048-token row ("population forwards/s").
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload population|credit|train]
+
+--workload credit times the credit-readout kernels in isolation; --workload train one EGGROLL
+update at population 24,576 (configs 4 / 5: forward, fitness all-gather, rebuilt update all-reduce, AdamW).
 
 --impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
 fp32, all host threads) on a bounded sample of the same workload, rank 0 only.
@@ -31,6 +34,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = 'train tokens/sec at pop 24k on 1/2/4/8 B200; population forwards/sec/GPU'
 UNIT = 'population forwards/s (one member x one 2048-token row, all GPUs)'
 MEMBERS, ROWS, T, SIGMA = 512, 8, 2048, 1e-3
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per member-token row of each kernel kind, from one ncu
+# capture of a 64-member x 1-row call (bench.py --members 64 --rows 1), scaled by the rows of a launch
+TRAFFIC_BYTES_PER_ROW = {'norm_mix': 4437.3, 'gemm_qkv': 3750.1, 'attention': 9496.0, 'gemm_cproj': 4701.4,
+                         'norm_mid': 2846.1, 'gemm_cfc': 4835.0, 'gemm_mproj': 10803.6, 'norm_final': 2846.7,
+                         'gemm_head_ce': 1083.2, 'member_reduce': 16.2}
 FLOP_PER_MEMBER_TOKEN = 68.3e6  # algorithmic forward FLOPs per member-token (linears + attention)
 CPU_SAMPLE_MEMBERS, CPU_SAMPLE_T = 2, 2048
 
@@ -42,6 +50,9 @@ def args_():
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train'])
+    # smaller population cases for profiling captures only; the benchmark line uses the defaults
+    ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (population workload)')
+    ap.add_argument('--rows', type=int, default=ROWS, help='2048-token rows per member (population workload)')
     return ap.parse_args()
 
 
@@ -187,14 +198,14 @@ def run_ours(a):
     dist = world > 1
 
     params = make_params(device, seed=0)
-    pairs = MEMBERS // 2 * world
+    pairs = a.members // 2 * world
     pop = Population(params, pairs, sigma=SIGMA, seed=0, rank=rank, world=world)
-    host_rows = [zipf_rows(ROWS, T + 1, seed=1000 * s + 7).pin_memory() for s in range(2)]
+    host_rows = [zipf_rows(a.rows, T + 1, seed=1000 * s + 7).pin_memory() for s in range(2)]
     dev_rows = [r.to(device) for r in host_rows]
     torch.cuda.synchronize()
 
     def step(i, tokens):
-        _, fit = pop.evaluate(tokens, step=i + 1, rows_per_member=ROWS, reduction='sum')
+        _, fit = pop.evaluate(tokens, step=i + 1, rows_per_member=a.rows, reduction='sum')
         return fit
 
     for i in range(a.warmup):
@@ -223,7 +234,7 @@ def run_ours(a):
     ms = e0.elapsed_time(e1)
 
     # end-to-end: host token rows -> device, evaluate, fitness -> host, every step
-    fit_host = torch.empty(MEMBERS * world, pin_memory=True)
+    fit_host = torch.empty(a.members * world, pin_memory=True)
     if dist:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -242,20 +253,19 @@ def run_ours(a):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, ms_e2e = t.tolist()
 
-    work = MEMBERS * ROWS * world * a.steps  # population forwards (member x 2048-token row) in the timed region
+    work = a.members * a.rows * world * a.steps  # population forwards (member x 2048-token row) in the timed region
     value = work / (ms / 1e3)
     e2e_value = work / (ms_e2e / 1e3)
 
+    m_launch = min(pop.chunk, a.members)  # members per library call
     # roofline of the dominant kernel kind (CUDA-event times of every launch in the timed region)
     kinds = {}
     peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
     tf_peak = peaks.get('bf16_tflops_sustained', 1400.0)
-    traffic_file = ROOT / 'profiles' / 'traffic_per_row.json'
-    traffic = json.loads(traffic_file.read_text()) if traffic_file.exists() else {}
     total = sum(prof.ms.values())
     for k, kms in prof.ms.items():
         n = prof.count[k]
-        flops, nbytes = kernel_work(k, pop.chunk, T)
+        flops, nbytes = kernel_work(k, m_launch, T)
         per = kms / n
         kinds[k] = {'launches': n, 'ms_per_launch': round(per, 4), 'share': round(kms / total, 4)}
         if flops:
@@ -263,10 +273,10 @@ def run_ours(a):
         if nbytes:
             kinds[k]['gbs'] = round(nbytes / (per / 1e3) / 1e9, 1)
     dom = max(prof.ms, key=prof.ms.get)
-    flops, nbytes = kernel_work(dom, pop.chunk, T)
+    flops, nbytes = kernel_work(dom, m_launch, T)
     per_launch_s = prof.ms[dom] / prof.count[dom] / 1e3
-    tr = traffic.get(dom)
-    step_tf = MEMBERS * ROWS * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12
+    tr = TRAFFIC_BYTES_PER_ROW.get(dom)
+    step_tf = a.members * a.rows * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12
     src = 'MEASURED_PEAKS.json (of measured)' if peaks else 'fallback'
     if flops:
         roofline = {'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1),
@@ -277,7 +287,7 @@ def run_ours(a):
         roofline = {'kernel': dom, 'bound': 'hbm', 'achieved': round(nbytes / per_launch_s / 1e9, 1), 'peak': hbm,
                     'unit': 'GB/s', 'frac': round(nbytes / per_launch_s / 1e9 / hbm, 4),
                     'peak_source': src + ' hbm_gbs', 'algorithmic_bytes_per_launch': nbytes}
-    roofline['traffic'] = tr * pop.chunk * T if tr is not None else None
+    roofline['traffic'] = tr * m_launch * T if tr is not None else None
     roofline['step'] = {'achieved_tflops': round(step_tf, 1), 'frac': round(step_tf / tf_peak, 4)}
 
     line = {
@@ -286,14 +296,16 @@ def run_ours(a):
         'dtype': 'bf16',
         'data': 'synthetic: Zipf(1.1) token rows over vocab 4096; random-init weights of the utils/model.py GPT '
                 '(EGGROLL make_model); EGGROLL 2**28 N(0,1) noise buffer',
-        'config': {'workload': 'BASELINE config 2 per GPU: population forward of 512 antithetic members x 8 rows x '
-                               '2048 tokens (summed-CE fitness), NCCL all-gather of fitness',
-                   'members_per_gpu': MEMBERS, 'rows_per_member': ROWS, 'seq_len': T, 'sigma': SIGMA,
-                   'member_tokens_per_s': value * T, 'train_tokens_per_step': ROWS * T,
+        'config': {'workload': ('BASELINE config 2 per GPU: population forward of 512 antithetic members x 8 rows x '
+                                '2048 tokens (summed-CE fitness), NCCL all-gather of fitness'
+                                if (a.members, a.rows) == (MEMBERS, ROWS) else
+                                f'profiling case (not the benchmark config): {a.members} members x {a.rows} rows'),
+                   'members_per_gpu': a.members, 'rows_per_member': a.rows, 'seq_len': T, 'sigma': SIGMA,
+                   'member_tokens_per_s': value * T, 'train_tokens_per_step': a.rows * T,
                    'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}'},
         'roofline': roofline, 'kernels': kinds, 'clocks': clk,
-        'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': ROWS * (T + 1) * 8,
-                'd2h_bytes_per_step': MEMBERS * world * 4},
+        'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': a.rows * (T + 1) * 8,
+                'd2h_bytes_per_step': a.members * world * 4},
         'gpu_launches': launches,
     }
     if rank == 0 and world == 1:
