@@ -36,6 +36,19 @@ __device__ __forceinline__ bool epi_barrier_and(bool pred) {
   return r != 0;
 }
 
+// CH accumulator columns of this thread's row from TMEM (issued only: the caller waits with tc_wait_ld).
+template <int CH>
+__device__ __forceinline__ void load_chunk(uint32_t taddr, float* v) {
+  if constexpr (CH == 64) {
+    tmem_ld32(taddr, v);
+    tmem_ld32(taddr + 32, v + 32);
+  } else if constexpr (CH == 32) {
+    tmem_ld32(taddr, v);
+  } else {
+    tmem_ld16(taddr, v);
+  }
+}
+
 template <int BN, int STAGES>
 struct GemmLayout {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
@@ -54,6 +67,8 @@ struct GemmLayout {
 
 // Epilogue functor contract (all methods run on a thread that owns `row` and column half `part` of every tile):
 //   static constexpr int CH;                          columns per TMEM load (16, 32 or 64)
+//   static constexpr bool PIPELINED;                  load chunk i + 1 from TMEM while chunk i is processed (two
+//                                                     register buffers: for epilogues with registers to spare)
 //   void row_begin(int row, int part);                before the first N tile of the row block
 //   void stage(int row0, int col0, float* s, int tid); before every tile, all 256 epilogue threads (tid 0..255):
 //                                                     may fill s[0 .. 2 BN) (16-byte aligned shared memory) with
@@ -203,21 +218,40 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         e.stage(mb * GEMM_BM, nb * BN, scratch, threadIdx.x - 64);
         ok = epi_barrier_and(waited);
         e.scratch = scratch;
-        if (ok) {
+        if (ok && !Epi::PIPELINED) {
           const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN + part * HALF);
 #pragma unroll 1
           for (int c = 0; c < HALF; c += Epi::CH) {
             float v[Epi::CH];
-            if constexpr (Epi::CH == 64) {
-              tmem_ld32(base + c, v);
-              tmem_ld32(base + c + 32, v + 32);
-            } else if constexpr (Epi::CH == 32) {
-              tmem_ld32(base + c, v);
-            } else {
-              tmem_ld16(base + c, v);
-            }
+            load_chunk<Epi::CH>(base + c, v);
             tc_wait_ld();
+            reg_fence<Epi::CH>(v);
             e.chunk(row, nb * BN + part * HALF + c, v);
+          }
+          e.tile_end(row, nb, part);
+        } else if (ok) {
+          const uint32_t base = tmem + lane_base + static_cast<uint32_t>(buf * BN + part * HALF);
+          // two register buffers: chunk i + 1 is loaded from TMEM while chunk i is processed (a rolled loop over
+          // chunk pairs, so only two copies of the chunk code exist)
+          constexpr int NCH = HALF / Epi::CH;
+          static_assert(NCH % 2 == 0, "pipelined epilogues need an even number of chunks per half tile");
+          const int col = nb * BN + part * HALF;
+          float va[Epi::CH], vb[Epi::CH];
+          load_chunk<Epi::CH>(base, va);
+          tc_wait_ld();
+          reg_fence<Epi::CH>(va);
+#pragma unroll 1
+          for (int i = 0; i < NCH; i += 2) {
+            load_chunk<Epi::CH>(base + (i + 1) * Epi::CH, vb);
+            e.chunk(row, col + i * Epi::CH, va);
+            tc_wait_ld();
+            reg_fence<Epi::CH>(vb);
+            if (i + 2 < NCH) load_chunk<Epi::CH>(base + (i + 2) * Epi::CH, va);
+            e.chunk(row, col + (i + 1) * Epi::CH, vb);
+            if (i + 2 < NCH) {
+              tc_wait_ld();
+              reg_fence<Epi::CH>(va);
+            }
           }
           e.tile_end(row, nb, part);
         }

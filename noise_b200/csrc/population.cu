@@ -81,129 +81,164 @@ struct NormArgs {
   Slice n_gate;
 };
 
-__device__ __forceinline__ float dot_bf16_row(const float (&hb)[16], const float* b, int lane) {
-  // b is a noise slice at an arbitrary buffer offset: 4-byte aligned only, so scalar loads
-  float acc = 0.f;
+constexpr int NORM_ROWS = 64;  // rows per block: T % 128 == 0, so a block's rows are one member's
+
+// dot of the row's bf16-rounded h (lane's 16 columns) with a bf16-rounded b staged in shared memory, rounded to bf16
+// as autocast returns it
+__device__ __forceinline__ float dot_staged(const float (&hb)[16], const float* sb, int lane) {
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) acc += hb[4 * i + c] * bf16_round(b[4 * lane + 128 * i + c]);
-  return bf16_round(warp_sum(acc));
+  for (int i = 0; i < 4; ++i) {
+    const float4 bv = *reinterpret_cast<const float4*>(sb + 4 * lane + 128 * i);
+    acc[i] = fmaf(hb[4 * i + 0], bv.x, fmaf(hb[4 * i + 1], bv.y, fmaf(hb[4 * i + 2], bv.z, hb[4 * i + 3] * bv.w)));
+  }
+  return bf16_round(warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3])));
 }
 
+// One block = NORM_ROWS consecutive rows of one member; each warp takes every eighth row. The member's noise vectors
+// (read in place from the noise buffer at arbitrary 4-byte offsets) are staged once per block in shared memory,
+// already rounded to bf16 where autocast rounds them: the b of every rank-1 dot this kernel forms (BLOCK: c_q, c_k,
+// c_v and the ve_gate; MID: c_fc; FINAL: lm_head), the embedding's b (fp32), and bf16(ve_gate) itself.
 template <int MODE>
 __global__ void __launch_bounds__(256) norm_kernel(NormArgs p) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= p.M) return;
-  const int r = warp, j = r / p.T, t = r - j * p.T;
-  const float sg = p.sign[j];
-  float x[16];
-  float* xrow = p.x + static_cast<int64_t>(r) * D;
-
-  if (MODE == NORM_BLOCK) {
-    // x0 = norm(wte[idx] + sign a[idx] b), eggroll.py:61-63, 74
-    const int64_t tok = p.idx[j * p.row_stride + t];
-    const float* w = p.wte + tok * D;
-    const float* bw = p.n_wte.B(j);
-    const float sa = sg * p.n_wte.A(j)[tok];
-    float x0[16], ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * i);
-      const float* bp = bw + 4 * lane + 128 * i;  // noise slice: scalar loads
-      x0[4 * i + 0] = wv.x + sa * bp[0];
-      x0[4 * i + 1] = wv.y + sa * bp[1];
-      x0[4 * i + 2] = wv.z + sa * bp[2];
-      x0[4 * i + 3] = wv.w + sa * bp[3];
+  __shared__ __align__(16) float sb[3][D];
+  __shared__ __align__(16) float swb[MODE == NORM_BLOCK ? D : 4];
+  __shared__ __align__(16) float sgw[MODE == NORM_BLOCK ? (H + 1) * 32 : 4];  // bf16(W_gate) [8][32], bf16(b_gate)
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int row0 = blockIdx.x * NORM_ROWS;
+  const int j = row0 / p.T;
+  {
+    const float* b0 = p.nb0.B(j);
+    for (int i = threadIdx.x; i < D; i += 256) {
+      sb[0][i] = bf16_round(b0[i]);
+      if (MODE == NORM_BLOCK) {
+        sb[1][i] = bf16_round(p.nb1.B(j)[i]);
+        sb[2][i] = bf16_round(p.nb2.B(j)[i]);
+        swb[i] = p.n_wte.B(j)[i];
+      }
     }
+    if (MODE == NORM_BLOCK && p.wgate)
+      for (int i = threadIdx.x; i < (H + 1) * 32; i += 256)
+        sgw[i] = bf16_round(i < H * 32 ? p.wgate[i] : p.n_gate.B(j)[i - H * 32]);
+  }
+  __syncthreads();
+  const float sg = p.sign[j];
+
+  for (int rr = wib; rr < NORM_ROWS; rr += 8) {
+    const int r = row0 + rr;
+    if (r >= p.M) break;
+    const int t = r - j * p.T;
+    float x[16];
+    float* xrow = p.x + static_cast<int64_t>(r) * D;
+
+    if (MODE == NORM_BLOCK) {
+      // x0 = norm(wte[idx] + sign a[idx] b), eggroll.py:61-63, 74
+      const int64_t tok = p.idx[j * p.row_stride + t];
+      const float* w = p.wte + tok * D;
+      const float sa = sg * p.n_wte.A(j)[tok];
+      float x0[16], ss0[4];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) ss += x0[i] * x0[i];
-    const float inv0 = rsqrtf(warp_sum(ss) / D + RMS_EPS);
+      for (int i = 0; i < 4; ++i) {
+        const float4 wv = *reinterpret_cast<const float4*>(w + 4 * lane + 128 * i);
+        const float4 bv = *reinterpret_cast<const float4*>(swb + 4 * lane + 128 * i);
+        x0[4 * i + 0] = wv.x + sa * bv.x;
+        x0[4 * i + 1] = wv.y + sa * bv.y;
+        x0[4 * i + 2] = wv.z + sa * bv.z;
+        x0[4 * i + 3] = wv.w + sa * bv.w;
+        ss0[i] = x0[4 * i] * x0[4 * i] + x0[4 * i + 1] * x0[4 * i + 1] + x0[4 * i + 2] * x0[4 * i + 2] +
+                 x0[4 * i + 3] * x0[4 * i + 3];
+      }
+      const float inv0 = rsqrtf(warp_sum((ss0[0] + ss0[1]) + (ss0[2] + ss0[3])) / D + RMS_EPS);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) x0[i] *= inv0;
-    // mixing, eggroll.py:77-79
-    const float resid = p.resid_l[p.layer] + sg * p.n_resid.A(j)[p.layer];
-    const float mix = p.x0_l[p.layer] + sg * p.n_x0.A(j)[p.layer];
-    if (p.layer == 0) {
+      for (int i = 0; i < 16; ++i) x0[i] *= inv0;
+      // mixing, eggroll.py:77-79
+      const float resid = p.resid_l[p.layer] + sg * p.n_resid.A(j)[p.layer];
+      const float mix = p.x0_l[p.layer] + sg * p.n_x0.A(j)[p.layer];
+      if (p.layer == 0) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = resid * x0[i] + mix * x0[i];
+        for (int i = 0; i < 16; ++i) x[i] = resid * x0[i] + mix * x0[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 xv = *reinterpret_cast<const float4*>(xrow + 4 * lane + 128 * i);
+          x[4 * i + 0] = resid * xv.x + mix * x0[4 * i + 0];
+          x[4 * i + 1] = resid * xv.y + mix * x0[4 * i + 1];
+          x[4 * i + 2] = resid * xv.z + mix * x0[4 * i + 2];
+          x[4 * i + 3] = resid * xv.w + mix * x0[4 * i + 3];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<float4*>(xrow + 4 * lane + 128 * i) =
+            make_float4(x[4 * i + 0], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float4 xv = *reinterpret_cast<const float4*>(xrow + 4 * lane + 128 * i);
-        x[4 * i + 0] = resid * xv.x + mix * x0[4 * i + 0];
-        x[4 * i + 1] = resid * xv.y + mix * x0[4 * i + 1];
-        x[4 * i + 2] = resid * xv.z + mix * x0[4 * i + 2];
-        x[4 * i + 3] = resid * xv.w + mix * x0[4 * i + 3];
+        x[4 * i + 0] = xv.x;
+        x[4 * i + 1] = xv.y;
+        x[4 * i + 2] = xv.z;
+        x[4 * i + 3] = xv.w;
       }
     }
+
+    // h = norm(x) in fp32, rounded to bf16 as autocast feeds it to the matmuls
+    float ss4[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
-      *reinterpret_cast<float4*>(xrow + 4 * lane + 128 * i) =
-          make_float4(x[4 * i + 0], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
-  } else {
+      ss4[i] = x[4 * i] * x[4 * i] + x[4 * i + 1] * x[4 * i + 1] + x[4 * i + 2] * x[4 * i + 2] +
+               x[4 * i + 3] * x[4 * i + 3];
+    const float inv = rsqrtf(warp_sum((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / D + RMS_EPS);
+    float hb[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) hb[i] = bf16_round(x[i] * inv);
+    __nv_bfloat16* hrow = p.h + static_cast<int64_t>(r) * D;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float4 xv = *reinterpret_cast<const float4*>(xrow + 4 * lane + 128 * i);
-      x[4 * i + 0] = xv.x;
-      x[4 * i + 1] = xv.y;
-      x[4 * i + 2] = xv.z;
-      x[4 * i + 3] = xv.w;
+      uint2 pk;
+      pk.x = pack_bf16x2(hb[4 * i + 0], hb[4 * i + 1]);
+      pk.y = pack_bf16x2(hb[4 * i + 2], hb[4 * i + 3]);
+      *reinterpret_cast<uint2*>(hrow + 4 * lane + 128 * i) = pk;
     }
-  }
 
-  // h = norm(x) in fp32, rounded to bf16 as autocast feeds it to the matmuls
-  float ss = 0.f;
+    float* sv = p.svec + static_cast<int64_t>(r) * 4;
+    if (MODE == NORM_BLOCK) {
+      const float sq = dot_staged(hb, sb[0], lane);
+      const float sk = dot_staged(hb, sb[1], lane);
+      const float svv = dot_staged(hb, sb[2], lane);
+      float sgate = 0.f;
+      if (p.wgate) {
+        // value-embedding gate 2 sigmoid(lowrank(h[:32], W_g, a, b)), eggroll.py:88; h[:32] lives in lanes 0..7
+        // (i = 0): lane l < 8 holds h[4 l .. 4 l + 3]
+        const float* ag = p.n_gate.A(j);
+        float part[H + 1];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) ss += x[i] * x[i];
-  const float inv = rsqrtf(warp_sum(ss) / D + RMS_EPS);
-  float hb[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) hb[i] = bf16_round(x[i] * inv);
-  __nv_bfloat16* hrow = p.h + static_cast<int64_t>(r) * D;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint2 pk;
-    pk.x = pack_bf16x2(hb[4 * i + 0], hb[4 * i + 1]);
-    pk.y = pack_bf16x2(hb[4 * i + 2], hb[4 * i + 3]);
-    *reinterpret_cast<uint2*>(hrow + 4 * lane + 128 * i) = pk;
-  }
-
-  float* sv = p.svec + static_cast<int64_t>(r) * 4;
-  if (MODE == NORM_BLOCK) {
-    const float sq = dot_bf16_row(hb, p.nb0.B(j), lane);
-    const float sk = dot_bf16_row(hb, p.nb1.B(j), lane);
-    const float svv = dot_bf16_row(hb, p.nb2.B(j), lane);
-    float sgate = 0.f;
-    if (p.wgate) {
-      // value-embedding gate 2 sigmoid(lowrank(h[:32], W_g, a, b)), eggroll.py:88; h[:32] lives in lanes 0..7 (i = 0)
-      const float* bg = p.n_gate.B(j);
-      const float* ag = p.n_gate.A(j);
-      float part = 0.f;
-      if (lane < 8) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) part += hb[c] * bf16_round(bg[4 * lane + c]);
-      }
-      sgate = bf16_round(warp_sum(part));
-      float gsel = 0.f;
-#pragma unroll
-      for (int hh = 0; hh < H; ++hh) {
-        float z = 0.f;
-        if (lane < 8) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) z += hb[c] * bf16_round(p.wgate[hh * 32 + 4 * lane + c]);
+        for (int hh = 0; hh <= H; ++hh) {
+          part[hh] = 0.f;
+          if (lane < 8) {
+            const float4 wv = *reinterpret_cast<const float4*>(sgw + hh * 32 + 4 * lane);
+            part[hh] = hb[0] * wv.x + hb[1] * wv.y + hb[2] * wv.z + hb[3] * wv.w;
+          }
         }
-        z = bf16_round(warp_sum(z)) + sg * sgate * ag[hh];
-        const float g = 2.f / (1.f + __expf(-z));
-        if (lane == hh) gsel = g;
+        // nine 8-lane sums at once
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+          for (int hh = 0; hh <= H; ++hh) part[hh] += __shfl_xor_sync(0xffffffffu, part[hh], o);
+        sgate = bf16_round(__shfl_sync(0xffffffffu, part[H], 0));
+        float gsel = 0.f;
+#pragma unroll
+        for (int hh = 0; hh < H; ++hh) {
+          const float z = bf16_round(__shfl_sync(0xffffffffu, part[hh], 0)) + sg * sgate * ag[hh];
+          if (lane == hh) gsel = 2.f / (1.f + __expf(-z));
+        }
+        if (lane < H) p.gate[static_cast<int64_t>(r) * H + lane] = gsel;
       }
-      if (lane < H) p.gate[static_cast<int64_t>(r) * H + lane] = gsel;
+      if (lane == 0) *reinterpret_cast<float4*>(sv) = make_float4(sq, sk, svv, sgate);
+    } else {
+      const float s0 = dot_staged(hb, sb[0], lane);
+      if (lane == 0) sv[0] = s0;
     }
-    if (lane == 0) *reinterpret_cast<float4*>(sv) = make_float4(sq, sk, svv, sgate);
-  } else {
-    const float s0 = dot_bf16_row(hb, p.nb0.B(j), lane);
-    if (lane == 0) sv[0] = s0;
   }
 }
 
@@ -230,6 +265,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
 // (eggroll.py:82-90). Writes bf16 [m, H, T, 64].
 struct EpiQKV {
   static constexpr int CH = 64;
+  static constexpr bool PIPELINED = false;
   int T;
   const float* sign;
   const float* svec;
@@ -278,7 +314,7 @@ struct EpiQKV {
     if (sec < 2) {
       const uint4* cr = reinterpret_cast<const uint4*>(cosb + static_cast<int64_t>(t) * (HD / 2));
       const uint4* sr = reinterpret_cast<const uint4*>(sinb + static_cast<int64_t>(t) * (HD / 2));
-      float ss = 0.f;
+      float ss4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int g = 0; g < 4; ++g) {  // 8 rotary pairs per 16-byte load of the bf16 tables
         const uint4 cv = cr[g], sv = sr[g];
@@ -294,10 +330,10 @@ struct EpiQKV {
           const float o2 = x1 * -s + x2 * c;
           val[d] = o1;
           val[d + HD / 2] = o2;
-          ss += o1 * o1 + o2 * o2;
+          ss4[e & 3] += o1 * o1 + o2 * o2;
         }
       }
-      const float inv = rsqrtf(ss / HD + RMS_EPS);
+      const float inv = rsqrtf(((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / HD + RMS_EPS);
 #pragma unroll
       for (int d = 0; d < HD; ++d) val[d] *= inv;
       dst = sec == 0 ? q : k;
@@ -340,6 +376,7 @@ struct EpiQKV {
 // x += bf16(acc) + sign bf16(sum of the row's partial dots) a  (c_proj and mlp.c_proj, eggroll.py:92-93).
 struct EpiResid {
   static constexpr int CH = 32;
+  static constexpr bool PIPELINED = false;
   int T, nparts;
   const float* sign;
   const float* parts;  // [M, nparts] partial dots of the input row with this linear's b
@@ -403,6 +440,7 @@ struct EpiResid {
 // (the next linear's rank-1 input dot), eggroll.py:93.
 struct EpiFC {
   static constexpr int CH = 64;
+  static constexpr bool PIPELINED = true;
   static constexpr int NPARTS = 2 * (F / GEMM_BN);  // per row: one partial dot per (N tile, column half)
   int T;
   const float* sign;
@@ -410,7 +448,7 @@ struct EpiFC {
   Slice nfc, nmp;
   __nv_bfloat16* hidden;
   float* pdot;  // [M, NPARTS]
-  float coef, pd;
+  float coef, pd[8];  // eight partial sums: independent FMA chains
   int col0;
   float* scratch;
   uint32_t stg;
@@ -418,7 +456,8 @@ struct EpiFC {
   __device__ __forceinline__ void row_begin(int row, int) {
     const int j = row / T;
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
-    pd = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pd[i] = 0.f;
   }
   // the tile's slices of a_fc and of the bf16-rounded b of mlp.c_proj into shared memory
   __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
@@ -428,8 +467,9 @@ struct EpiFC {
     s[GEMM_BN + tid] = bf16_round(nmp.B(j)[c0 + tid]);
   }
   __device__ __forceinline__ void tile_end(int row, int nb, int part) {
-    pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] = pd;
-    pd = 0.f;
+    pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] = ((pd[0] + pd[1]) + (pd[2] + pd[3])) + ((pd[4] + pd[5]) + (pd[6] + pd[7]));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pd[i] = 0.f;
   }
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
@@ -448,18 +488,20 @@ struct EpiFC {
         const float u = bf16_round(acc[i + e]) + coef * av[e];
         const float rl = fmaxf(u, 0.f);
         r[e] = bf16_round(rl * rl);
-        pd += r[e] * bv[e];
+        pd[e] = fmaf(r[e], bv[e], pd[e]);
       }
       sts128(stg_addr(stg, lane, i / 8), make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
                                                     pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7])));
     }
     __syncwarp();
-    // rows row - lane .. + 31 of hidden, columns col .. col + 63: 4 whole 128-byte row segments per instruction
+    // rows row - lane .. + 31 of hidden, columns col .. col + CH - 1: whole CH * 2-byte row segments, NC 16-byte
+    // pieces per row, 32 / NC rows per instruction
+    constexpr int NC = CH / 8;
     uint4* out = reinterpret_cast<uint4*>(hidden + static_cast<int64_t>(row - lane) * F + col);
-    const int c = lane & 7;
+    const int c = lane % NC;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int rr = (lane >> 3) + 4 * k;
+    for (int k = 0; k < NC; ++k) {
+      const int rr = lane / NC + (32 / NC) * k;
       out[rr * (F / 8) + c] = lds128(stg_addr(stg, rr, c));
     }
     __syncwarp();
@@ -484,6 +526,7 @@ __device__ __forceinline__ float exp2_poly4(float x) {
 
 struct EpiHeadCE {
   static constexpr int CH = 32;
+  static constexpr bool PIPELINED = false;
   int T;
   const float* sign;
   const float* svec;
@@ -533,6 +576,7 @@ struct EpiHeadCE {
 // Plain fp32 store of the accumulator: D[row, col] = acc (the tcgen05 core without any fused arithmetic).
 struct EpiStore {
   static constexpr int CH = 32;
+  static constexpr bool PIPELINED = false;
   float* d;
   int ldd;
   float* scratch;
@@ -1052,7 +1096,7 @@ static int run_forward(const noise_gpt_t* model, const noise_slice_t* nz, const 
   const int Mi = static_cast<int>(M);
   int rc;
   if (cudaMemsetAsync(w.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
-  const int norm_blocks = static_cast<int>((M * 32 + 255) / 256);
+  const int norm_blocks = static_cast<int>((M + NORM_ROWS - 1) / NORM_ROWS);
 
   for (int l = 0; l < NOISE_N_LAYER; ++l) {
     const bool ve = l & 1;
@@ -1271,7 +1315,7 @@ int noise_head_loss(const float* x, const void* weight, const int64_t* targets, 
   nf.svec = w.svec;
   nf.nb0 = to_slice(nz[NOISE_PARAM_HEAD]);
   launch_begin(s, K_NORM_FINAL);
-  norm_kernel<NORM_FINAL><<<(rows * 32 + 255) / 256, 256, 0, s>>>(nf);
+  norm_kernel<NORM_FINAL><<<(rows + NORM_ROWS - 1) / NORM_ROWS, 256, 0, s>>>(nf);
   launch_end(s);
   EpiHeadCE eh{};
   eh.T = rows;

@@ -153,6 +153,16 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Ties N registers written by tcgen05.ld to the tcgen05.wait::ld before this point: the compiler sees them modified
+// here, so no use of them moves above the wait (they are only valid after it).
+template <int N>
+__device__ __forceinline__ void reg_fence(float* v) {
+#pragma unroll
+  for (int i = 0; i < N; i += 8)
+    asm volatile("" : "+f"(v[i]), "+f"(v[i + 1]), "+f"(v[i + 2]), "+f"(v[i + 3]), "+f"(v[i + 4]), "+f"(v[i + 5]),
+                 "+f"(v[i + 6]), "+f"(v[i + 7]));
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets row (lane base + i), columns c..c+31.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
