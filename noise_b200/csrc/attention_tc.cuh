@@ -46,6 +46,14 @@ struct TAttnArgs {
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
 
 // Key-tile range [lo, hi] of query tile qt and whether its first tile is cut by the window.
 struct TileRange {
@@ -317,6 +325,14 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           ok = masked ? tile(std::true_type{}, kt) : tile(std::false_type{}, kt);
         }
       }
+      // this head's 64 values of the c_proj noise b, two per lane: loaded before the wait for O, so their latency
+      // overlaps it
+      float bq0 = 0.f, bq1 = 0.f;
+      if (ok && active) {
+        const float* bproj = p.nproj.B(it.bh / NOISE_N_HEAD) + (it.bh % NOISE_N_HEAD) * 64;
+        bq0 = bproj[lane];
+        bq1 = bproj[lane + 32];
+      }
       if (!ok || !mbar_wait(&o_full[ob], static_cast<uint32_t>(nitem >> 1) & 1u, p.status)) {
         ok = false;
         break;
@@ -333,21 +349,41 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         const int j = it.bh / NOISE_N_HEAD, hh = it.bh % NOISE_N_HEAD;
         const int64_t row = static_cast<int64_t>(j) * p.T + tq;
         const float inv = 1.f / l;
-        const float* bproj = p.nproj.B(j) + hh * 64;
-        uint4* yr = reinterpret_cast<uint4*>(p.y + row * NOISE_N_EMBD + hh * 64);
-        float dp = 0.f;
+        // The warp's own 32 rows of this group's P buffer are free (every O MMA of the item is complete, and only
+        // this warp writes these rows): sub-tile 1 holds the head's b, sub-tile 0 stages the y rows (16-byte chunk c
+        // of row rl at c ^ (rl % 8)) so the global stores cover whole 128-byte row segments.
+        const uint32_t wst = sbase + TA_P + g * 2 * TA_TILE + quarter * 32 * 128;
+        const uint32_t wb = wst + TA_TILE;
+        st_shared_f32(wb + lane * 4, bf16_round(bq0));
+        st_shared_f32(wb + (lane + 32) * 4, bf16_round(bq1));
+        __syncwarp();
+        float dp[2] = {0.f, 0.f};
 #pragma unroll
         for (int d = 0; d < 64; d += 8) {
+          const uint4 b0 = ld_shared_v4(wb + d * 4), b1 = ld_shared_v4(wb + d * 4 + 16);
+          const float bv[8] = {__uint_as_float(b0.x), __uint_as_float(b0.y), __uint_as_float(b0.z),
+                               __uint_as_float(b0.w), __uint_as_float(b1.x), __uint_as_float(b1.y),
+                               __uint_as_float(b1.z), __uint_as_float(b1.w)};
           float yv[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             yv[e] = bf16_round(o[d + e] * inv);
-            dp += yv[e] * bf16_round(bproj[d + e]);
+            dp[e & 1] = fmaf(yv[e], bv[e], dp[e & 1]);
           }
-          yr[d / 8] = make_uint4(pack_bf16x2(yv[0], yv[1]), pack_bf16x2(yv[2], yv[3]), pack_bf16x2(yv[4], yv[5]),
-                                 pack_bf16x2(yv[6], yv[7]));
+          st_shared_v4(wst + lane * 128 + (((d >> 3) ^ (lane & 7)) << 4), pack_bf16x2(yv[0], yv[1]),
+                       pack_bf16x2(yv[2], yv[3]), pack_bf16x2(yv[4], yv[5]), pack_bf16x2(yv[6], yv[7]));
         }
-        p.ydot[row * NOISE_N_HEAD + hh] = dp;
+        p.ydot[row * NOISE_N_HEAD + hh] = dp[0] + dp[1];
+        __syncwarp();
+        const int64_t row_w0 = row - lane;  // the warp's 32 rows are consecutive
+        const int c = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rl = (lane >> 3) + 4 * i;
+          *reinterpret_cast<uint4*>(p.y + (row_w0 + rl) * NOISE_N_EMBD + hh * 64 + c * 8) =
+              ld_shared_v4(wst + rl * 128 + ((c ^ (rl & 7)) << 4));
+        }
+        __syncwarp();
       }
     }
   }
