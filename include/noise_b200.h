@@ -260,6 +260,47 @@ size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n);
 int noise_id_head_scores(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
                          float sigma, float eps, void* back, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * Track-1 readout scorers (reference train/val/run.py, `recipe` section): the noise_record custom ops, head_dim 64,
+ * fp32 arithmetic (the reference's tf32x3 dots are fp32-accurate).
+ * ------------------------------------------------------------------------------------------------------------- */
+/* A strided fp32 3-D view: element (i, j, k) at data[i * stride0 + j * stride1 + k * stride2] (torch strides). */
+typedef struct {
+  const float* data;
+  int64_t stride0, stride1, stride2;
+} noise_view3_t;
+
+/* noise_record::future_scores (run.py:1729-1745; dense form joint_scores :1671-1681): out[h, p, m] (fp32 [H, P, M])
+ * = sum over receivers s in (source_start + m, source_start + m + window] of (a (e^x - 1) c + (a + a (e^x - 1))
+ * target_s . dv) / (1 + a (e^x - 1)), x = q_s . dk / 8, a = a[h, s, m], c = contrast[h, s, m]. q, target (H, T, 64)
+ * views; dk, dv contiguous fp32 [H, P, M, 64] (16-byte aligned). */
+int noise_future_scores(const noise_view3_t* q, const noise_view3_t* target, const float* dk, const float* dv,
+                        const noise_view3_t* a, const noise_view3_t* contrast, int heads, int tokens, int probes,
+                        int sources, int source_start, int window, float* out, void* stream);
+
+/* noise_record::key_response (run.py:622-632, kernel :571-602): out[h, p, m] = sum over queries s (absolute position
+ * query_start + s in [source_start + m, source_start + m + window]) of change / (1 + change) c[h, s, m],
+ * change = a[h, s, m] (e^(q_s . dk / 8) - 1). q (H, T, 64) view; dk contiguous fp32 [H, P, M, 64]. */
+int noise_key_response(const noise_view3_t* q, const float* dk, const noise_view3_t* a, const noise_view3_t* c,
+                       int heads, int tokens, int probes, int sources, int source_start, int query_start, int window,
+                       float* out, void* stream);
+
+/* noise_record::future_query_response (run.py:1818-1834, kernel :1780-1815): out[m, p, h] (fp32 [M, P, H, 64]) =
+ * (sum_k change v_k - (sum_k change) base[h, m]) / (1 + sum_k change), change = probabilities[h, m, k]
+ * (e^(dq[m, p, h] . k_k / 8) - 1). dq contiguous fp32 [M, P, H, 64]; keys, values (H, T, 64), probabilities (H, M, T),
+ * base (H, M, 64) views. */
+int noise_query_response(const float* dq, const noise_view3_t* keys, const noise_view3_t* values,
+                         const noise_view3_t* probabilities, const noise_view3_t* base, int tokens, int probes,
+                         int heads, int keys_len, float* out, void* stream);
+
+/* noise_record::routed_response (run.py:604-619, kernel :548-569): out[m, p, h] = bf16(w V) + (e^-dlse - 1) rest,
+ * w = bf16(p_k (e^(ds - dlse) - 1)), ds = bf16(dq . k) / 8, dlse = log1p(sum_k p_k (e^ds - 1)). dq bf16
+ * [M, P, H, 64], keys, values bf16 [M, H, K, 64], probabilities fp32 [M, H, K], rest fp32 [M, H, 64], all
+ * contiguous; K <= 256. */
+int noise_routed_response(const void* dq, const void* keys, const void* values, const float* probabilities,
+                          const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
+                          void* stream);
+
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);
 

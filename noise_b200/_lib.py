@@ -39,6 +39,12 @@ class Rows(ctypes.Structure):
                 ('per_gpu', ctypes.c_int64), ('gpu_stride', ctypes.c_int64)]
 
 
+class View3(ctypes.Structure):
+    """noise_view3_t."""
+    _fields_ = [('data', ctypes.c_void_p), ('stride0', ctypes.c_int64), ('stride1', ctypes.c_int64),
+                ('stride2', ctypes.c_int64)]
+
+
 class HeadPieces(ctypes.Structure):
     """noise_head_pieces_t."""
     _fields_ = [(n, ctypes.c_void_p) for n in ('q', 'k', 'v', 'o', 'target')] + \
@@ -98,6 +104,10 @@ SIGNATURES = [
     ('noise_head_prep', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
     ('noise_id_head_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ('noise_id_head_scores', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_future_scores', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_key_response', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_query_response', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_routed_response', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),

@@ -18,6 +18,9 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 - ``train/speedrun/run.py``: pack_heads_kernel, head_prep_fused and id_head_scores (the identity phase's head
   sharding) under the same patched interpreter, on tests/golden/heads_inputs.py's seeded inputs.
 
+- ``train/val/run.py`` (its `recipe` section): the track-1 readout scorers' ops noise_record::future_scores,
+  ::future_query_response (CPU paths) and ::key_response, ::routed_response (Triton kernels, patched interpreter).
+
 Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
@@ -280,6 +283,63 @@ def golden_heads(root):
     print('heads: ok')
 
 
+def load_recipe(root):
+    """train/val/run.py keeps its modules as `# ==== module <name>` sections behind a loader; this loads the `recipe`
+    section (the record's ops) the same way, compiled at its own line numbers."""
+    import types
+    file = root / 'train/val/run.py'
+    mark = '# ' + '=' * 40 + ' module '
+    lines = file.read_text().splitlines(keepends=True)
+    starts = [(i, line[len(mark):].strip()) for i, line in enumerate(lines) if line.startswith(mark)]
+    spans = {n: (i + 1, j) for (i, n), (j, _) in zip(starts, starts[1:] + [(len(lines), '')])}
+    a, b = spans['recipe']
+    module = types.ModuleType('recipe')
+    module.__file__ = str(file)
+    sys.modules['recipe'] = module
+    exec(compile('\n' * a + ''.join(lines[a:b]), str(file), 'exec'), module.__dict__)
+    return module
+
+
+def golden_readout(root):
+    """The track-1 readout scorers' record ops on readout_inputs' seeded inputs: future_scores and
+    future_query_response through the ops themselves (CPU tensors take their dense paths), key_response and
+    routed_response through their Triton kernels under the patched interpreter (launched with the ops' arguments)."""
+    import triton
+    import triton.language as tl
+    patch_triton_interpreter()
+    R = load_recipe(root)
+    # the interpreter runs a kernel's source against its module's globals (the factories' local imports are not
+    # seen): give the recipe module the names the kernels use, libdevice as interpreter_libdevice's numpy versions
+    for name, value in (('libdevice', interpreter_libdevice()), ('tl', tl), ('triton', triton)):
+        if not hasattr(R, name) or name == 'libdevice':
+            setattr(R, name, value)
+    from readout_inputs import future_inputs, key_inputs, query_inputs, routed_inputs
+    out = {}
+    f = future_inputs()
+    out['future'] = R.fused_scores(f['q'], f['target'], f['dk'], f['dv'], f['a'], f['contrast'], f['source_start'],
+                                   f['window'])
+    qi = query_inputs()
+    out['query'] = R.query_response(qi['dq'], qi['keys'], qi['values'], qi['probabilities'], qi['base'])
+    routed, key_kernel = R.finite_attention_kernels()
+    k = key_inputs()
+    heads, probes, sources, width = k['dk'].shape
+    key_out = torch.empty(heads, probes, sources)
+    key_kernel[(triton.cdiv(probes * sources, 64), heads)](
+        k['q'], k['dk'].contiguous(), k['A'], k['C'], key_out, heads, k['q'].shape[1], sources, probes, width,
+        *k['q'].stride(), *k['A'].stride(), *k['C'].stride(), k['source_start'], k['query_start'], k['window'], 64, 64)
+    out['key'] = key_out
+    r = routed_inputs()
+    m, probes, heads, width = r['dq'].shape
+    count = r['keys'].shape[2]
+    routed_out = torch.empty(m, probes, heads, width)
+    routed[(triton.cdiv(probes, 32), m * heads)](
+        r['dq'].contiguous(), r['keys'].contiguous(), r['values'].contiguous(), r['probabilities'].contiguous(),
+        r['rest'].contiguous(), routed_out, probes, heads, count, width, 32, max(16, triton.next_power_of_2(count)))
+    out['routed'] = routed_out
+    torch.save({k: v.clone() for k, v in out.items()}, HERE / 'readout.pt')
+    print('readout: ok', {k: tuple(v.shape) for k, v in out.items()})
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -300,6 +360,8 @@ def main():
         golden_credit(root)
     if want('heads'):
         golden_heads(root)
+    if want('readout'):
+        golden_readout(root)
 
 
 if __name__ == '__main__':

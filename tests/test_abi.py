@@ -93,6 +93,14 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_head_prep(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, ctypes.byref(prep), None) == 4  # outputs
     assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 96, 0.003, 1e-6, fake, fake, 1 << 30, None) == 1
     assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, fake, fake, 16, None) == 3
+    # readout scorers
+    v = _lib.View3(fake, 1, 1, 1)
+    r = ctypes.byref(v)
+    assert L.noise_future_scores(r, r, fake, fake, r, r, 0, 64, 2, 2, 0, 8, fake, None) == 1   # no heads
+    assert L.noise_future_scores(r, r, fake + 4, fake, r, r, 2, 64, 2, 2, 0, 8, fake, None) == 2  # dk alignment
+    assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
+    assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
+    assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
 
 
 def test_product_path_has_no_oracle_import():
