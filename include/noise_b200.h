@@ -301,6 +301,47 @@ int noise_routed_response(const void* dq, const void* keys, const void* values, 
                           const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
                           void* stream);
 
+/* The true-path readout's scorer (reference train/val/run.py, `readout` section :5900-6040): width 512, 8 heads of
+ * 64. Moment tables of one block, per (global token, head): U, W fp32 [T, 8, 64]; M1, M2 bf16 [T, 8, 64, 64] (16-byte
+ * aligned); QD, GD fp32 [T, 8, 64]; AD, CD fp32 [T, 8]; VT, OT fp32 [T, 8, 64] (the self-edge only). */
+typedef struct {
+  const float* U;
+  const float* W;
+  const void* M1;
+  const void* M2;
+  const float* QD;
+  const float* GD;
+  const float* AD;
+  const float* CD;
+  const float* VT;
+  const float* OT;
+} noise_scorer_tables_t;
+
+/* stats_kernel (:5968-5988): for the first n rows of each of `tokens` tokens of delta [tokens, d_rows, 512] fp32:
+ * db bf16 [tokens, n, 512] = bf16(d), st fp32 [tokens, n, 2] = (inv', inv' / inv0 - 1) of the RMSNorm at x + d,
+ * x = x[start + t] fp32 [T, 512], sqx[start + t] = |x|^2, eps as given. */
+int noise_readout_stats(const float* delta, const float* x, const float* sqx, void* db, float* st, int start, int n,
+                        int d_rows, int tokens, float eps, void* stream);
+
+/* staged_kernel (:5991-6040): the rows' score against the tables from up bf16 [tokens * n, nc] (the projection
+ * d W_k^T | d W_v^T | d[:32] W_g^T padded to 16), st (noise_readout_stats), r0 fp32 [T, 8, 64] (rotated clean raw
+ * key), vc fp32 [T, 512] (raw value), gz fp32 [T, 8] and ve fp32 [T, 8, 64] (both NULL: no value-embedding gate),
+ * cs / sn fp32 [T, 32]: out fp32 [tokens, n]; with se (bf16 [tokens, se_rows, 512]) also the self-edge; diag: add the
+ * exact receiver s = t. */
+int noise_readout_staged(const void* up, const float* st, const float* r0, const float* vc, const float* gz,
+                         const float* ve, const float* cs, const float* sn, const noise_scorer_tables_t* tab,
+                         float* out, void* se, int start, int n, int se_rows, int tokens, int nc, int diag,
+                         void* stream);
+
+/* readout_kernel (:5906-5965): the same score from the projected change pj fp32 [tokens, probes, 2, 8, 64] (key and
+ * value parts), r0 fp32 [tokens, 8, 64], cos / sin rows of the chunk's tokens (strided: token, pair), gc fp32
+ * [tokens, probes, 8] and ve fp32 [tokens, 8, 64] (both NULL: ungated): out fp32 [tokens, probes]; se bf16
+ * [tokens, probes, 512] or NULL. Tables at global token start + t. */
+int noise_readout_direct(const float* pj, const float* r0, const float* cs, int64_t cs_token_stride,
+                         int64_t cs_pair_stride, const float* sn, int64_t sn_token_stride, int64_t sn_pair_stride,
+                         const float* gc, const float* ve, const noise_scorer_tables_t* tab, float* out, void* se,
+                         int start, int probes, int tokens, int diag, void* stream);
+
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);
 

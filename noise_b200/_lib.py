@@ -45,6 +45,11 @@ class View3(ctypes.Structure):
                 ('stride2', ctypes.c_int64)]
 
 
+class ScorerTables(ctypes.Structure):
+    """noise_scorer_tables_t."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ('U', 'W', 'M1', 'M2', 'QD', 'GD', 'AD', 'CD', 'VT', 'OT')]
+
+
 class HeadPieces(ctypes.Structure):
     """noise_head_pieces_t."""
     _fields_ = [(n, ctypes.c_void_p) for n in ('q', 'k', 'v', 'o', 'target')] + \
@@ -108,6 +113,9 @@ SIGNATURES = [
     ('noise_key_response', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_query_response', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_routed_response', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_readout_stats', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]),
+    ('noise_readout_staged', ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p]),
+    ('noise_readout_direct', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
     ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),

@@ -21,6 +21,9 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 - ``train/val/run.py`` (its `recipe` section): the track-1 readout scorers' ops noise_record::future_scores,
   ::future_query_response (CPU paths) and ::key_response, ::routed_response (Triton kernels, patched interpreter).
 
+- ``train/val/run.py`` (its `readout` section, through the file's own section loader): the true-path readout's
+  scorer kernels stats_kernel, staged_kernel, readout_kernel (patched interpreter).
+
 Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
@@ -340,6 +343,45 @@ def golden_readout(root):
     print('readout: ok', {k: tuple(v.shape) for k, v in out.items()})
 
 
+def golden_scorer(root):
+    """The true-path readout's scorer kernels (train/val/run.py `readout` section: stats_kernel, staged_kernel,
+    readout_kernel) under the patched interpreter on scorer_inputs' seeded inputs, gated, with the exact diagonal
+    and the self-edge. The section is imported through the file's own section loader (its bootstrap, run here)."""
+    import triton
+    patch_triton_interpreter()
+    file = root / 'train/val/run.py'
+    text = file.read_text()
+    boot = text[:text.index('LOADER = Sections()')] + 'LOADER = Sections()\n'
+    env = {'__name__': 'ref_val_boot', '__file__': str(file)}
+    exec(compile(boot, str(file), 'exec'), env)
+    sys.path.insert(0, str(root))
+    sys.meta_path.insert(0, env['LOADER'])
+    import readout as RO
+    RO.libdevice = interpreter_libdevice()
+    from scorer_inputs import scorer_inputs
+    x = scorer_inputs()
+    m, n, d_rows, start, nc = x['m'], x['n'], x['d_rows'], x['start'], x['nc']
+    db = torch.empty(m, n, 512, dtype=torch.bfloat16)
+    st = torch.empty(m, n, 2)
+    RO.stats_kernel[(triton.cdiv(n, 16), m)](x['delta'], x['X'], x['SQX'], db, st, start, n, d_rows, 512, 16, x['eps'])
+    out_s = torch.empty(m, n)
+    se_s = torch.zeros(m, d_rows, 512, dtype=torch.bfloat16)
+    RO.staged_kernel[(triton.cdiv(n, 64), m)](
+        x['UP'], st, x['R0'], x['VC'], x['GZ'], x['VE'], x['CS'], x['SN'], x['U'], x['W'], x['M1'], x['M2'], x['QD'],
+        x['GD'], x['AD'], x['CD'], x['VT'], x['OT'], out_s, se_s, start, n, d_rows, 512, 8, 64, True, True, True, 64,
+        nc)
+    tok = slice(start, start + m)
+    cs, sn = x['CS'][tok], x['SN'][tok]
+    out_d = torch.empty(m, n)
+    se_d = torch.zeros(m, n, 512, dtype=torch.bfloat16)
+    RO.readout_kernel[(m, triton.cdiv(n, RO.BPR))](
+        x['PJ'], x['R0'][tok].contiguous(), cs, sn, x['GC'], x['VE'][tok].contiguous(), x['U'], x['W'], x['M1'],
+        x['M2'], x['QD'], x['GD'], x['AD'], x['CD'], x['VT'], x['OT'], out_d, se_d, start, n, *cs.stride(),
+        *sn.stride(), 8, 64, True, True, True, RO.BPR)
+    torch.save(dict(db=db, st=st, staged=out_s, staged_se=se_s, direct=out_d, direct_se=se_d), HERE / 'scorer.pt')
+    print('scorer: ok')
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -362,6 +404,8 @@ def main():
         golden_heads(root)
     if want('readout'):
         golden_readout(root)
+    if want('scorer'):
+        golden_scorer(root)
 
 
 if __name__ == '__main__':

@@ -101,6 +101,17 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
+    # readout scorer
+    assert L.noise_readout_stats(fake, fake, fake, fake, fake, 0, 8, 4, 2, 1e-7, None) == 1    # d_rows < n
+    assert L.noise_readout_stats(fake + 4, fake, fake, fake, fake, 0, 8, 8, 2, 1e-7, None) == 2
+    tab = _lib.ScorerTables()
+    assert L.noise_readout_staged(fake, fake, fake, fake, None, None, fake, fake, ctypes.byref(tab), fake, None,
+                                  0, 8, 8, 2, 1040, 1, None) == 4                              # tables missing
+    tab = _lib.ScorerTables(*([fake] * 10))
+    assert L.noise_readout_staged(fake, fake, fake, fake, None, None, fake, fake, ctypes.byref(tab), fake, None,
+                                  0, 8, 8, 2, 1000, 1, None) == 1                              # nc < 1024
+    assert L.noise_readout_direct(fake, fake, fake, 32, 1, fake, 32, 1, fake, None, ctypes.byref(tab), fake, None,
+                                  0, 8, 2, 1, None) == 4                                       # gated without ve
 
 
 def test_product_path_has_no_oracle_import():
