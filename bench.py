@@ -10,7 +10,8 @@ over one 2048-token row ("population forwards/s").
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload population|credit|train]
 
 --workload credit times the credit-readout kernels in isolation; --workload train one EGGROLL
-update at population 24,576 (configs 4 / 5: forward, fitness all-gather, rebuilt update all-reduce, AdamW).
+update at population 24,576 (configs 4 / 5: forward, fitness all-gather, rebuilt update all-reduce, AdamW);
+--workload aux the other entry points (un-perturbed forward, head loss, head sharding, readout scorers).
 
 --impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
 fp32, all host threads) on a bounded sample of the same workload, rank 0 only.
@@ -49,7 +50,7 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train'])
+    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train', 'aux'])
     # smaller population cases for profiling captures only; the benchmark line uses the defaults
     ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (population workload)')
     ap.add_argument('--rows', type=int, default=ROWS, help='2048-token rows per member (population workload)')
@@ -450,6 +451,108 @@ def run_train(a):
         torch.distributed.destroy_process_group()
 
 
+def _timed(fn, steps, warmup):
+    """Microseconds per call of fn, CUDA events on the current stream after warm-up calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / steps
+
+
+def run_aux(a):
+    """The path's other entry points at representative shapes, one JSON line: per op the time per call and its
+    algorithmic rate (TFLOP/s for contractions, GB/s of compulsory bytes for data movement)."""
+    from noise_b200 import gpt_loss, head_loss, heads, readout, scorer
+    from noise_b200.eggroll import make_params
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    g = torch.Generator(device).manual_seed(0)
+    rn = lambda *s, scale=1.0: torch.randn(*s, device=device, generator=g) * scale
+    ru = lambda *s, scale=1.0: torch.rand(*s, device=device, generator=g) * scale
+    res = {}
+
+    def rate(name, us, flops=None, nbytes=None, **extra):
+        r = {'us': round(us, 1)}
+        if flops:
+            r['tflops'] = round(flops / us / 1e6, 2)
+        if nbytes:
+            r['gbs'] = round(nbytes / us / 1e3, 1)
+        r.update(extra)
+        res[name] = r
+
+    # GPT.forward (config 1 shape: 4 rows x 2048 tokens, un-perturbed) and the fused LM-head loss (16,384 rows)
+    params = make_params(device, 0)
+    tok = zipf_rows(4, T + 1, seed=5).to(device)
+    us = _timed(lambda: gpt_loss(None, params, tok[:, :-1], tok[:, 1:], 'sum'), a.steps, a.warmup)
+    rate('gpt_loss', us, flops=4 * T * FLOP_PER_MEMBER_TOKEN, tokens_per_s=round(4 * T / us * 1e6))
+    x = rn(16384, 512)
+    tg = torch.randint(0, 4096, (16384,), device=device, generator=g)
+    us = _timed(lambda: head_loss(x, params['lm_head.weight'], tg, 4096), a.steps, a.warmup)
+    rate('head_loss', us, flops=2 * 16384 * 4096 * 512)
+    # identity-phase head sharding: 8 layers, 8,192 local tokens (8 rows of 1,024); 8 source ranks x 1,024 tokens
+    n, t = 8192, 1024
+    pieces = [[rn(n, 512).bfloat16() for _ in range(8)] for _ in range(5)]
+    lses = [rn(n // t, 8, t) for _ in range(8)]
+    us = _timed(lambda: heads.pack_heads_kernel(*pieces, lses), a.steps, a.warmup)
+    rate('pack_heads', us, nbytes=8 * 8 * n * (5 * 128 + 4 + 644))
+    got = rn(8, 8, 1024, 322).bfloat16()
+    got.view(torch.int16)[..., 320:] = rn(8, 8, 1024).add_(3).unsqueeze(-1).view(torch.int16).view(8, 8, 1024, 2)
+    ang = torch.outer(torch.arange(t, device=device, dtype=torch.float32),
+                      1.0 / 10000 ** (torch.arange(0, 64, 2, device=device, dtype=torch.float32) / 64))
+    cs, sn = ang.cos(), ang.sin()
+    us = _timed(lambda: heads.head_prep_fused(got, cs, sn, 8, t), a.steps, a.warmup)
+    rate('head_prep', us, nbytes=65536 * (644 + 4 * 128 + 256 + 128 + 256 + 64 + 24))
+    back = torch.empty(8, 8, 3, 1024, 64, dtype=torch.bfloat16, device=device)
+    us = _timed(lambda: heads.id_head_scores(got, (cs, sn), back, 8, t), a.steps, a.warmup)
+    rate('id_head_scores', us, rows=64, tokens=t)
+    # track-1 readout scorers
+    H, Tq, P, M, start, window = 8, 2048, 16, 256, 512, 1024
+    q, tgt = rn(H, Tq, 64), rn(H, Tq, 64, scale=0.125)
+    dk, dv = rn(H, P, M, 64, scale=0.05), rn(H, P, M, 64, scale=0.05)
+    A, C = ru(H, Tq, M, scale=0.1), rn(H, Tq, M)
+    pairs = H * P * M * window
+    us = _timed(lambda: readout.future_scores(q, tgt, dk, dv, A, C, start, window), a.steps, a.warmup)
+    rate('future_scores', us, flops=pairs * 4 * 64)
+    us = _timed(lambda: readout.key_response(q, dk, A, C, start, start, window), a.steps, a.warmup)
+    rate('key_response', us, flops=pairs * 2 * 64)
+    mq, pq = 256, 64
+    dq, keys, vals = rn(mq, pq, H, 64, scale=0.3), rn(H, Tq, 64), rn(H, Tq, 64)
+    pos = torch.arange(mq, device=device) * (Tq // mq) + Tq // mq - 1
+    lag = pos[:, None] - torch.arange(Tq, device=device)[None]
+    prob = (ru(H, mq, Tq) * ((lag >= 0) & (lag <= window))).contiguous()
+    base = rn(H, mq, 64)
+    visible = int(((lag >= 0) & (lag <= window)).sum())
+    us = _timed(lambda: readout.query_response(dq, keys, vals, prob, base), a.steps, a.warmup)
+    rate('query_response', us, flops=H * pq * visible * 4 * 64)
+    mr, pr, kr = 2048, 64, 128
+    rdq, rk, rv = (rn(mr, pr, H, 64, scale=0.3).bfloat16(), rn(mr, H, kr, 64).bfloat16(), rn(mr, H, kr, 64).bfloat16())
+    rp, rest = ru(mr, H, kr, scale=1.0 / kr), rn(mr, H, 64, scale=0.1)
+    us = _timed(lambda: readout.routed_response(rdq, rk, rv, rp, rest), a.steps, a.warmup)
+    rate('routed_response', us, flops=mr * H * pr * kr * 4 * 64)
+    # the true-path readout's scorer: a chunk of 128 tokens x 256 moved rows, tables of a 2,048-token sequence
+    Ts, ms, ns = 2048, 128, 256
+    up, st = rn(ms * ns, 1040, scale=0.05).bfloat16(), torch.stack([ru(ms, ns) + 0.5, rn(ms, ns, scale=0.01)], -1)
+    r0, vc, gz, ve = rn(Ts, 8, 64), rn(Ts, 512), rn(Ts, 8), rn(Ts, 8, 64, scale=0.1)
+    tabs = [rn(Ts, 8, 64, scale=0.1), rn(Ts, 8, 64, scale=0.1), rn(Ts, 8, 64, 64, scale=0.05).bfloat16(),
+            rn(Ts, 8, 64, 64, scale=0.05).bfloat16(), rn(Ts, 8, 64), rn(Ts, 8, 64, scale=0.1), ru(Ts, 8, scale=0.2),
+            rn(Ts, 8), rn(Ts, 8, 64), rn(Ts, 8, 64)]
+    rcs, rsn = torch.ones(Ts, 32, device=device), torch.zeros(Ts, 32, device=device)
+    out = torch.empty(ms, ns, device=device)
+    se = torch.empty(ms, ns, 512, dtype=torch.bfloat16, device=device)
+    us = _timed(lambda: scorer.staged_kernel(up, st, r0, vc, gz, ve, rcs, rsn, *tabs, out, se, 0, ns, ns, True, True,
+                                             True, 1040), a.steps, a.warmup)
+    rate('readout_staged', us, flops=ms * ns * 8 * 2 * 2 * 64 * 64)
+    print(json.dumps({'metric': 'auxiliary entry points of the path: time per call', 'unit': 'us per call',
+                      'steps': a.steps, 'warmup': a.warmup,
+                      'config': {'workload': 'representative shapes (bench.py run_aux)'}, 'kernels': res}), flush=True)
+
+
 def main():
     a = args_()
     if a.impl == 'reference':
@@ -458,6 +561,8 @@ def main():
         run_credit(a)
     elif a.workload == 'train':
         run_train(a)
+    elif a.workload == 'aux':
+        run_aux(a)
     else:
         run_ours(a)
 

@@ -226,18 +226,21 @@ __global__ void __launch_bounds__(256) routed_response_kernel(const __nv_bfloat1
                                                               const float* __restrict__ rest, int P, int H, int K,
                                                               float* __restrict__ out) {
   extern __shared__ __align__(16) float rsm[];
-  float* sk = rsm;                  // [RK][D + 1] keys (fp32 copies of bf16)
-  float* sv = sk + RK * (D + 1);    // [RK][D] values
-  float* sds = sv + RK * D;         // [RP][RK + 1] ds, then the bf16 weights
-  float* sq = sds + RP * (RK + 1);  // [RP][D] probes
-  float* sp = sq + RP * D;          // [RK] probabilities
-  float* sdl = sp + RK;             // [RP] dlse
+  // shared memory sized by the routed keys K (K <= 256)
+  constexpr int KP = D + 4;         // key row pitch: the 8 key-parts of a quarter warp hit distinct banks
+  const int KS = K + 1;             // row pitch of the ds / weight rows
+  float* sk = rsm;                  // [K][D + 4] keys (fp32 copies of bf16)
+  float* sv = sk + K * KP;          // [K][D] values
+  float* sds = sv + K * D;          // [RP][K + 1] ds, then the bf16 weights
+  float* sq = sds + RP * KS;        // [RP][D] probes
+  float* sp = sq + RP * D;          // [K] probabilities
+  float* sdl = sp + K;              // [RP] dlse
   const int tm = blockIdx.y / H, h = blockIdx.y % H, tid = threadIdx.x;
   const int p0 = blockIdx.x * RP;
   const int64_t kvb = (static_cast<int64_t>(tm) * H + h) * K;
   for (int i = tid; i < K * D; i += 256) {
     const int r = i / D, d = i % D;
-    sk[r * (D + 1) + d] = __bfloat162float(keys[(kvb + r) * D + d]);
+    sk[r * KP + d] = __bfloat162float(keys[(kvb + r) * D + d]);
     sv[r * D + d] = __bfloat162float(values[(kvb + r) * D + d]);
   }
   for (int i = tid; i < K; i += 256) sp[i] = prob[kvb + i];
@@ -246,33 +249,51 @@ __global__ void __launch_bounds__(256) routed_response_kernel(const __nv_bfloat1
     sq[i] = p < P ? __bfloat162float(dq[((static_cast<int64_t>(tm) * P + p) * H + h) * D + d]) : 0.f;
   }
   __syncthreads();
-  // ds[p][k] = bf16(q . k) / 8 (the dot's bf16 output, as the reference's), 8 threads per probe
+  // ds[p][k] = bf16(q . k) / 8 (the dot's bf16 output, as the reference's); 8 threads per probe (one warp holds 4
+  // probes), the probe row in registers, key rows read as float4
   const int pr = tid / 8, part = tid % 8;
+  float qv[D];
+#pragma unroll
+  for (int d = 0; d < D; d += 4) {
+    const float4 t4 = *reinterpret_cast<const float4*>(sq + pr * D + d);
+    qv[d] = t4.x, qv[d + 1] = t4.y, qv[d + 2] = t4.z, qv[d + 3] = t4.w;
+  }
   float lsum = 0.f;
   for (int kr = part; kr < K; kr += 8) {
     float x0 = 0.f, x1 = 0.f;
 #pragma unroll
-    for (int d = 0; d < D; d += 2) {
-      x0 = fmaf(sq[pr * D + d], sk[kr * (D + 1) + d], x0);
-      x1 = fmaf(sq[pr * D + d + 1], sk[kr * (D + 1) + d + 1], x1);
+    for (int d = 0; d < D; d += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(sk + kr * KP + d);
+      x0 = fmaf(qv[d], k4.x, x0);
+      x1 = fmaf(qv[d + 1], k4.y, x1);
+      x0 = fmaf(qv[d + 2], k4.z, x0);
+      x1 = fmaf(qv[d + 3], k4.w, x1);
     }
     const float ds = bf16r(x0 + x1) * SCALE;
-    sds[pr * (RK + 1) + kr] = ds;
+    sds[pr * KS + kr] = ds;
     lsum += sp[kr] * expm1f(ds);
   }
 #pragma unroll
   for (int o = 1; o < 8; o <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
   const float dlse = log1pf(lsum);
-  for (int kr = part; kr < K; kr += 8)
-    sds[pr * (RK + 1) + kr] = bf16r(sp[kr] * expm1f(sds[pr * (RK + 1) + kr] - dlse));
+  for (int kr = part; kr < K; kr += 8) sds[pr * KS + kr] = bf16r(sp[kr] * expm1f(sds[pr * KS + kr] - dlse));
   if (part == 0) sdl[pr] = dlse;
-  __syncthreads();
+  __syncwarp();  // a probe's weights come from its own 8 threads, all in this warp
   // moved[p][d] = bf16(sum_k w[p][k] v[k][d]) + (e^-dlse - 1) rest[d]; thread: probe pr, dims 8 part .. + 7
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
   for (int kr = 0; kr < K; ++kr) {
-    const float w = sds[pr * (RK + 1) + kr];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, sv[kr * D + part * 8 + e], acc[e]);
+    const float w = sds[pr * KS + kr];
+    const float4 v0 = *reinterpret_cast<const float4*>(sv + kr * D + part * 8);
+    const float4 v1 = *reinterpret_cast<const float4*>(sv + kr * D + part * 8 + 4);
+    acc[0] = fmaf(w, v0.x, acc[0]);
+    acc[1] = fmaf(w, v0.y, acc[1]);
+    acc[2] = fmaf(w, v0.z, acc[2]);
+    acc[3] = fmaf(w, v0.w, acc[3]);
+    acc[4] = fmaf(w, v1.x, acc[4]);
+    acc[5] = fmaf(w, v1.y, acc[5]);
+    acc[6] = fmaf(w, v1.z, acc[6]);
+    acc[7] = fmaf(w, v1.w, acc[7]);
   }
   const int p = p0 + pr;
   if (p < P) {
@@ -284,7 +305,7 @@ __global__ void __launch_bounds__(256) routed_response_kernel(const __nv_bfloat1
   }
 }
 
-constexpr int ROUTED_SMEM = (RK * (D + 1) + RK * D + RP * (RK + 1) + RP * D + RK + RP) * 4;
+constexpr int routed_smem(int K) { return (K * (D + 4) + K * D + RP * (K + 1) + RP * D + K + RP) * 4; }
 
 static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -343,10 +364,10 @@ int noise_routed_response(const void* dq, const void* keys, const void* values, 
                           void* stream) {
   if (!dq || !keys || !values || !probabilities || !rest || !out) return NOISE_ERR_ARGUMENT;
   if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1 || keys_len > RK) return NOISE_ERR_SHAPE;
-  if (cudaFuncSetAttribute(routed_response_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ROUTED_SMEM))
+  if (cudaFuncSetAttribute(routed_response_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, routed_smem(RK)))
     return NOISE_ERR_CUDA;
   dim3 grid((probes + RP - 1) / RP, tokens * heads);
-  routed_response_kernel<<<grid, 256, ROUTED_SMEM, static_cast<cudaStream_t>(stream)>>>(
+  routed_response_kernel<<<grid, 256, routed_smem(keys_len), static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(dq), static_cast<const __nv_bfloat16*>(keys),
       static_cast<const __nv_bfloat16*>(values), probabilities, rest, probes, heads, keys_len, out);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
