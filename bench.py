@@ -548,6 +548,22 @@ def run_aux(a):
     us = _timed(lambda: scorer.staged_kernel(up, st, r0, vc, gz, ve, rcs, rsn, *tabs, out, se, 0, ns, ns, True, True,
                                              True, 1040), a.steps, a.warmup)
     rate('readout_staged', us, flops=ms * ns * 8 * 2 * 2 * 64 * 64)
+    # the identity phase's readout cycle: 4,096 tokens (its 7 GEMMs of 4,096 x 4,096 x 512, fp32 ones at the caller's
+    # matmul precision)
+    import types
+    from noise_b200 import cycle
+    nc_ = 4096
+    hmat = torch.ones(1, 1, device=device)
+    while hmat.shape[0] < 512:
+        hmat = torch.cat([torch.cat([hmat, hmat], 1), torch.cat([hmat, -hmat], 1)], 0)
+    model = types.SimpleNamespace(H=hmat, step_t=torch.tensor(3, device=device), lm_head=rn(512, 4096, scale=0.05))
+    xc, yc = rn(nc_, 512), torch.randint(0, 4096, (nc_,), device=device, generator=g)
+    us = _timed(lambda: cycle.top_credit(model, xc, yc), a.steps, a.warmup)
+    rate('top_credit', us, flops=nc_ * (7 * 2 * 4096 * 512 + 2 * 512 * 512), tokens=nc_,
+         matmul_precision=torch.get_float32_matmul_precision())
+    raw = rn(nc_, 4096, scale=3)
+    us = _timed(lambda: cycle.coordinate_change(raw, yc), a.steps, a.warmup)
+    rate('coordinate_change', us, nbytes=nc_ * 4096 * 8)
     print(json.dumps({'metric': 'auxiliary entry points of the path: time per call', 'unit': 'us per call',
                       'steps': a.steps, 'warmup': a.warmup,
                       'config': {'workload': 'representative shapes (bench.py run_aux)'}, 'kernels': res}), flush=True)

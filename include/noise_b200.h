@@ -342,6 +342,32 @@ int noise_readout_direct(const float* pj, const float* r0, const float* cs, int6
                          const float* gc, const float* ve, const noise_scorer_tables_t* tab, float* out, void* se,
                          int start, int probes, int tokens, int diag, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------------
+ * The identity phase's readout cycle (reference train/speedrun/run.py:3569-3686), width 512, vocabulary 4096,
+ * softcap 15. The GEMMs between these kernels (x W, h W, x h^T, fg1 c^T in fp32; fast_k c^p^T in bf16; the final
+ * (moved - clean) / steps h) are the caller's.
+ * ------------------------------------------------------------------------------------------------------------- */
+/* _cycle_weights_kernel with cycle_scales' |x|^2 (run.py:3596-3647): per token of x fp32 [tokens, 512] and its
+ * logits base fp32 [tokens, 4096]: fg1 fp32 [tokens, 4096] = f g1; fast bf16 [5, tokens, 4096] = (f z g2, f z^2 g3,
+ * f g2, f z g3, f g3); rows fp32 [tokens, 3] = (sum f z g1, sum f z^2 g2, sum f z^3 g3); total, sq (|x|^2), base_y
+ * (= base[targets]) fp32 [tokens]. */
+int noise_cycle_weights(const float* x, const float* base, const int64_t* targets, int tokens, float* fg1, void* fast,
+                        float* rows, float* total, float* sq, float* base_y, void* stream);
+
+/* cycle_scales + cycle_finish up to its last GEMM (run.py:3588-3597, 3650-3662): out fp32 [tokens, directions] =
+ * (moved - clean) / steps per (token, direction) from dots = x h^T, sq, exact = fg1 c^T and prods fp32
+ * [5, tokens, directions] (the bf16 GEMMs' fp32 accumulators, rounded to bf16 here as the reference's bf16 outputs),
+ * rows, total, base_y, c fp32 [directions, 4096], targets int64 [tokens], sigma (SIGMA 0.005). */
+int noise_cycle_finish(const float* dots, const float* sq, const float* exact, const float* prods, const float* rows,
+                       const float* total, const float* base_y, const float* c, const int64_t* targets, int tokens,
+                       int directions, float sigma, float* out, void* stream);
+
+/* coordinate_change (run.py:3569-3577): out fp32 [rows, 4096] = (log1p(w expm1(up - z)) - log1p(w expm1(down - z))
+ * - onehot(targets) (up - down)) / (2 head_sigma), z = softcap(raw), up / down = softcap(raw +- head_sigma),
+ * w = softmax(z); raw fp32 or bf16 [rows, 4096] contiguous. */
+int noise_coordinate_change(const void* raw, int raw_dtype, const int64_t* targets, int rows, float head_sigma,
+                            float* out, void* stream);
+
 /* Bytes of scratch noise_population_loss needs for `members` members of `tokens` tokens each. */
 size_t noise_population_workspace_bytes(int members, int tokens);
 

@@ -24,6 +24,9 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 - ``train/val/run.py`` (its `readout` section, through the file's own section loader): the true-path readout's
   scorer kernels stats_kernel, staged_kernel, readout_kernel (patched interpreter).
 
+- ``train/speedrun/run.py``: the identity phase's readout cycle top_credit and coordinate_change (compiled helpers
+  as their original functions, the Triton weights kernel under the patched interpreter).
+
 Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
@@ -382,6 +385,41 @@ def golden_scorer(root):
     print('scorer: ok')
 
 
+def golden_cycle(root):
+    """The identity phase's readout cycle (train/speedrun/run.py top_credit, coordinate_change) on cycle_inputs'
+    seeded inputs: its torch.compile'd helpers called as their original functions, its Triton weights kernel under the
+    patched interpreter (libdevice tanh / exp as numpy's)."""
+    import types
+    import numpy as np
+    patch_triton_interpreter()
+    sys.path.insert(0, str(root / 'train/speedrun'))
+    spec = importlib.util.spec_from_file_location('ref_run_cycle', root / 'train/speedrun/run.py')
+    run = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(run)
+    for name in ('coordinate_change', 'cycle_scales', 'cycle_finish', 'cycle_powers'):
+        fn = getattr(run, name)
+        setattr(run, name, getattr(fn, '_torchdynamo_orig_callable', fn))
+    lib = interpreter_libdevice()
+    base = vars(lib)
+    from triton.runtime import interpreter as ti
+    import triton.language as tl
+
+    def unary(fn):
+        def f(x, *args, **kwargs):
+            data = fn(np.asarray(x.handle.data, dtype=np.float32)).astype(np.float32)
+            return tl.core.tensor(ti.TensorHandle(data, x.handle.dtype.scalar), x.type)
+        return f
+    run.libdevice = types.SimpleNamespace(**base, tanh=unary(np.tanh), exp=unary(np.exp))
+    from cycle_inputs import cycle_inputs
+    x = cycle_inputs()
+    model = types.SimpleNamespace(H=x['H'], step_t=x['step_t'], lm_head=x['lm_head'])
+    credit = run.top_credit(model, x['x'], x['y'])
+    coords = run.coordinate_change(x['raw'], x['y'])
+    signs = run.step_signs(x['step_t'], 'cpu')
+    torch.save(dict(credit=credit.clone(), coords=coords.clone(), signs=signs.clone()), HERE / 'cycle.pt')
+    print('cycle: ok', tuple(credit.shape), tuple(coords.shape))
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -406,6 +444,8 @@ def main():
         golden_readout(root)
     if want('scorer'):
         golden_scorer(root)
+    if want('cycle'):
+        golden_cycle(root)
 
 
 if __name__ == '__main__':

@@ -101,6 +101,11 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
+    # readout cycle
+    assert L.noise_cycle_weights(None, fake, fake, 4, fake, fake, fake, fake, fake, fake, None) == 4
+    assert L.noise_cycle_finish(fake, fake, fake, fake, fake, fake, fake, fake, fake, 4, 0, 0.005, fake, None) == 1
+    assert L.noise_coordinate_change(fake, 5, fake, 4, 0.1, fake, None) == 4                  # dtype
+    assert L.noise_coordinate_change(fake, 0, fake, 4, 0.0, fake, None) == 1                  # head_sigma
     # readout scorer
     assert L.noise_readout_stats(fake, fake, fake, fake, fake, 0, 8, 4, 2, 1e-7, None) == 1    # d_rows < n
     assert L.noise_readout_stats(fake + 4, fake, fake, fake, fake, 0, 8, 8, 2, 1e-7, None) == 2
