@@ -394,6 +394,28 @@ size_t noise_gpt_workspace_bytes(int rows, int tokens);
 int noise_gpt_loss(const noise_gpt_t* model, const int64_t* idx, const int64_t* targets, int rows, int tokens,
                    int reduction, float* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Dust's additive jitter sites of one block (train/val/dust.py:102-125), each fp32 row-major or NULL: o [rows, 512]
+ * on the attention output before c_proj, attn [rows, 512] on c_proj's output, fc [rows, 2048] on c_fc's
+ * pre-activation, mlp [rows, 512] on mlp.c_proj's output. */
+typedef struct {
+  const float* o;
+  const float* attn;
+  const float* fc;
+  const float* mlp;
+} noise_jitter_t;
+
+/* Bytes of scratch noise_block_forward needs for `seqs` sequences of `tokens` tokens. */
+size_t noise_block_workspace_bytes(int seqs, int tokens);
+
+/* Dust's block_forward (train/val/dust.py:102-125): one block `layer` of the un-perturbed model on x fp32
+ * [seqs * tokens, 512] (the block's input, already mixed; updated in place to its output) with the jitter sites
+ * added; ve fp32 [seqs * tokens, 512] (the captured value-embedding rows) on value-embedding blocks, NULL on the
+ * others; window as the reference passes it. Numerics as the population forward's (bf16 linears, fp32 stream).
+ * Requirements as noise_population_loss (tokens % 128 == 0, <= 2048); the model needs the layer's weights and the
+ * RoPE tables only. */
+int noise_block_forward(const noise_gpt_t* model, int layer, float* x, const float* ve, const noise_jitter_t* jit,
+                        int seqs, int tokens, int window, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Bytes of scratch noise_head_loss needs for `rows` rows. */
 size_t noise_head_loss_workspace_bytes(int rows);
 

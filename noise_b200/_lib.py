@@ -45,6 +45,11 @@ class View3(ctypes.Structure):
                 ('stride2', ctypes.c_int64)]
 
 
+class Jitter(ctypes.Structure):
+    """noise_jitter_t."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ('o', 'attn', 'fc', 'mlp')]
+
+
 class ScorerTables(ctypes.Structure):
     """noise_scorer_tables_t."""
     _fields_ = [(n, ctypes.c_void_p) for n in ('U', 'W', 'M1', 'M2', 'QD', 'GD', 'AD', 'CD', 'VT', 'OT')]
@@ -119,6 +124,10 @@ SIGNATURES = [
     ('noise_cycle_weights', ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 7),
     ('noise_cycle_finish', ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_coordinate_change', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_block_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_block_forward', ctypes.c_int,
+     [ctypes.POINTER(GPT), ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Jitter), ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),

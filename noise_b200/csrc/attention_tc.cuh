@@ -41,6 +41,7 @@ struct TAttnArgs {
   float* ydot;       // [M, 8]
   Slice nproj;       // c_proj noise: b used
   int* status;
+  const float* jit;  // [M, 512] fp32 added to the attention output before c_proj, or NULL (Dust's o jitter site)
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -368,6 +369,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             yv[e] = bf16_round(o[d + e] * inv);
+            if (p.jit) yv[e] = bf16_round(yv[e] + p.jit[row * NOISE_N_EMBD + hh * 64 + d + e]);
             dp[e & 1] = fmaf(yv[e], bv[e], dp[e & 1]);
           }
           st_shared_v4(wst + lane * 128 + (((d >> 3) ^ (lane & 7)) << 4), pack_bf16x2(yv[0], yv[1]),

@@ -79,6 +79,7 @@ struct NormArgs {
   Slice nb0, nb1, nb2;  // b sources of the dot products (BLOCK: c_q, c_k, c_v; MID: c_fc; FINAL: lm_head)
   const float* wgate;  // [8, 32] fp32 or NULL
   Slice n_gate;
+  int no_mix;          // BLOCK: x is the block's input as is (no x0 mixing; Dust's block_forward)
 };
 
 constexpr int NORM_ROWS = 64;  // rows per block: T % 128 == 0, so a block's rows are one member's
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) norm_kernel(NormArgs p) {
     float x[16];
     float* xrow = p.x + static_cast<int64_t>(r) * D;
 
-    if (MODE == NORM_BLOCK) {
+    if (MODE == NORM_BLOCK && !p.no_mix) {
       // x0 = norm(wte[idx] + sign a[idx] b), eggroll.py:61-63, 74
       const int64_t tok = p.idx[j * p.row_stride + t];
       const float* w = p.wte + tok * D;
@@ -274,7 +275,8 @@ struct EpiQKV {
   int64_t row_stride;
   const __nv_bfloat16* cosb;
   const __nv_bfloat16* sinb;
-  const float* vew;  // value-embedding table [4096, 512] fp32 or NULL
+  const float* vew;  // value-embedding table [4096, 512] fp32, or (ve_rows) one row per output row, or NULL
+  int ve_rows;       // vew holds the value embedding of each row (Dust's captured rows): no token gather, no noise
   Slice nq, nk, nv, nve;
   __nv_bfloat16* q;
   __nv_bfloat16* k;
@@ -340,6 +342,19 @@ struct EpiQKV {
     } else {
       if (gate) {
         const float g = gate[static_cast<int64_t>(row) * H + hh];
+        if (ve_rows) {
+          const float4* vr = reinterpret_cast<const float4*>(vew + static_cast<int64_t>(row) * D + hh * HD);
+#pragma unroll
+          for (int d4 = 0; d4 < HD / 4; ++d4) {
+            const float4 w4 = vr[d4];
+            val[4 * d4 + 0] += g * w4.x;
+            val[4 * d4 + 1] += g * w4.y;
+            val[4 * d4 + 2] += g * w4.z;
+            val[4 * d4 + 3] += g * w4.w;
+          }
+          dst = v;
+          goto staged;
+        }
         const int64_t tok = idx[j * row_stride + t];
         const float4* ver = reinterpret_cast<const float4*>(vew + tok * D + hh * HD);
         const float sa = sg * nve.A(j)[tok];
@@ -355,6 +370,7 @@ struct EpiQKV {
       }
       dst = v;
     }
+  staged:
     // this thread's head row (128 bytes) -> staging; then rows t0 .. t0 + 31 of the head, 4 per instruction
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -380,6 +396,7 @@ struct EpiResid {
   int T, nparts;
   const float* sign;
   const float* parts;  // [M, nparts] partial dots of the input row with this linear's b
+  const float* jit;    // [M, 512] fp32 added to the linear's output, or NULL (Dust's attn / mlp jitter sites)
   Slice n;
   float* x;
   float coef;
@@ -412,6 +429,13 @@ struct EpiResid {
       y.y = bf16_round(acc[4 * i + 1]) + coef * av.y;
       y.z = bf16_round(acc[4 * i + 2]) + coef * av.z;
       y.w = bf16_round(acc[4 * i + 3]) + coef * av.w;
+      if (jit) {
+        const float4 jv = *reinterpret_cast<const float4*>(jit + static_cast<int64_t>(row) * D + col + 4 * i);
+        y.x += jv.x;
+        y.y += jv.y;
+        y.z += jv.z;
+        y.w += jv.w;
+      }
       sts128(stg_addr(stg, lane, i), *reinterpret_cast<uint4*>(&y));
     }
     __syncwarp();
@@ -447,6 +471,7 @@ struct EpiFC {
   const float* svec;
   Slice nfc, nmp;
   __nv_bfloat16* hidden;
+  const float* jit;  // [M, 2048] fp32 added to the pre-activation, or NULL (Dust's fc jitter site)
   float* pdot;  // [M, NPARTS]
   float coef, pd[8];  // eight partial sums: independent FMA chains
   int col0;
@@ -485,7 +510,8 @@ struct EpiFC {
       const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float u = bf16_round(acc[i + e]) + coef * av[e];
+        float u = bf16_round(acc[i + e]) + coef * av[e];
+        if (jit) u += jit[static_cast<int64_t>(row) * F + col + i + e];
         const float rl = fmaxf(u, 0.f);
         r[e] = bf16_round(rl * rl);
         pd[e] = fmaf(r[e], bv[e], pd[e]);
@@ -1327,6 +1353,116 @@ int noise_head_loss(const float* x, const void* weight, const int64_t* targets, 
   eh.ce2 = w.ce2;
   if ((rc = run_gemm(w.h, rows, D, weight, V, eh, w.status, s, K_GEMM_HEAD))) return rc;
   return token_losses(w, targets, rows, 0, rows, out, s);
+}
+
+size_t noise_block_workspace_bytes(int seqs, int tokens) { return noise_population_workspace_bytes(seqs, tokens); }
+
+int noise_block_forward(const noise_gpt_t* model, int layer, float* x, const float* ve, const noise_jitter_t* jit,
+                        int seqs, int tokens, int window, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!model || !x || layer < 0 || layer >= NOISE_N_LAYER) return NOISE_ERR_ARGUMENT;
+  if (!model->wqkv[layer] || !model->wproj[layer] || !model->wfc[layer] || !model->wmproj[layer] || !model->cos ||
+      !model->sin)
+    return NOISE_ERR_ARGUMENT;
+  const bool gated = model->wgate[layer] != nullptr;
+  if (gated != (ve != nullptr)) return NOISE_ERR_ARGUMENT;  // a value-embedding block takes its ve rows, others none
+  if (seqs < 1 || tokens < GEMM_BM || tokens > 2048 || tokens % GEMM_BM || window < 0) return NOISE_ERR_SHAPE;
+  const int64_t M = static_cast<int64_t>(seqs) * tokens;
+  if (M > (int64_t(1) << 31) / F) return NOISE_ERR_SHAPE;
+  const Workspace w = carve(workspace, M);
+  if (!workspace || workspace_bytes < w.bytes) return NOISE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (ve && (reinterpret_cast<uintptr_t>(ve) & 15)))
+    return NOISE_ERR_ALIGN;
+  int rc = check_device();
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int T = tokens, Mi = static_cast<int>(M);
+  g_launches = 0;
+  if (cudaMemsetAsync(w.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  noise_slice_t nz[NOISE_N_PARAMS];
+  if ((rc = zero_noise(w, seqs, nz, s))) return rc;
+  const Slice zs = to_slice(nz[0]);
+  const int norm_blocks = static_cast<int>((M + NORM_ROWS - 1) / NORM_ROWS);
+  const noise_jitter_t none{};
+  const noise_jitter_t& j = jit ? *jit : none;
+
+  NormArgs na{};
+  na.layer = layer;
+  na.T = T;
+  na.M = Mi;
+  na.sign = w.zsign;
+  na.x = x;
+  na.h = w.h;
+  na.svec = w.svec;
+  na.gate = w.gate;
+  na.n_wte = na.n_resid = na.n_x0 = na.nb0 = na.nb1 = na.nb2 = na.n_gate = zs;
+  na.wgate = gated ? model->wgate[layer] : nullptr;
+  na.no_mix = 1;
+  launch_begin(s, K_NORM_BLOCK);
+  norm_kernel<NORM_BLOCK><<<norm_blocks, 256, 0, s>>>(na);
+  launch_end(s);
+
+  EpiQKV eq{};
+  eq.T = T;
+  eq.sign = w.zsign;
+  eq.svec = w.svec;
+  eq.gate = gated ? w.gate : nullptr;
+  eq.cosb = static_cast<const __nv_bfloat16*>(model->cos);
+  eq.sinb = static_cast<const __nv_bfloat16*>(model->sin);
+  eq.vew = ve;
+  eq.ve_rows = 1;
+  eq.nq = eq.nk = eq.nv = eq.nve = zs;
+  eq.q = w.q;
+  eq.k = w.k;
+  eq.v = w.v;
+  if ((rc = run_gemm(w.h, Mi, D, model->wqkv[layer], 3 * D, eq, w.status, s, K_GEMM_QKV))) return rc;
+
+  TAttnArgs aa{};
+  aa.T = T;
+  aa.window = window;
+  aa.y = w.y;
+  aa.ydot = w.ydot;
+  aa.nproj = zs;
+  aa.status = w.status;
+  aa.jit = j.o;
+  if ((rc = run_attention(w.q, w.k, w.v, Mi, T, seqs, aa, s))) return rc;
+
+  EpiResid er{};
+  er.T = T;
+  er.nparts = H;
+  er.sign = w.zsign;
+  er.parts = w.ydot;
+  er.n = zs;
+  er.x = x;
+  er.jit = j.attn;
+  if ((rc = run_gemm(w.y, Mi, D, model->wproj[layer], D, er, w.status, s, K_GEMM_PROJ))) return rc;
+
+  NormArgs nm = na;
+  nm.wgate = nullptr;
+  launch_begin(s, K_NORM_MID);
+  norm_kernel<NORM_MID><<<norm_blocks, 256, 0, s>>>(nm);
+  launch_end(s);
+
+  EpiFC ef{};
+  ef.T = T;
+  ef.sign = w.zsign;
+  ef.svec = w.svec;
+  ef.nfc = ef.nmp = zs;
+  ef.hidden = w.hidden;
+  ef.pdot = w.pdot;
+  ef.jit = j.fc;
+  if ((rc = run_gemm(w.h, Mi, D, model->wfc[layer], F, ef, w.status, s, K_GEMM_FC))) return rc;
+
+  EpiResid em{};
+  em.T = T;
+  em.nparts = EpiFC::NPARTS;
+  em.sign = w.zsign;
+  em.parts = w.pdot;
+  em.n = zs;
+  em.x = x;
+  em.jit = j.mlp;
+  if ((rc = run_gemm(w.hidden, Mi, F, model->wmproj[layer], D, em, w.status, s, K_GEMM_MPROJ))) return rc;
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
 // ---------------------------------------------------------------------------------------------------------------

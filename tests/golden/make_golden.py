@@ -27,6 +27,8 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 - ``train/speedrun/run.py``: the identity phase's readout cycle top_credit and coordinate_change (compiled helpers
   as their original functions, the Triton weights kernel under the patched interpreter).
 
+- ``train/val/dust.py``: block_forward (its compiled function as the original) with jitter at every site.
+
 Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
@@ -420,6 +422,27 @@ def golden_cycle(root):
     print('cycle: ok', tuple(credit.shape), tuple(coords.shape))
 
 
+def golden_dust(root):
+    """Dust's block_forward (train/val/dust.py, its compiled function called as the original, eager flex attention)
+    on dust_inputs' seeded inputs, fp32 on the CPU: a value-embedding block with jitter at all four sites, and a plain
+    block with none."""
+    import utils.model as model
+    from torch.nn.attention.flex_attention import flex_attention
+    model.flex = flex_attention
+    spec = importlib.util.spec_from_file_location('ref_dust', root / 'train/val/dust.py')
+    dust = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(dust)
+    bf = getattr(dust.block_forward, '_torchdynamo_orig_callable', dust.block_forward)
+    from dust_inputs import dust_inputs
+    x = dust_inputs()
+    cos, sin = x['cos'][None, :, None, :], x['sin'][None, :, None, :]
+    with torch.no_grad():
+        gated = bf(x['x'], x['w'], x['ve'], cos, sin, x['windows'][0], **x['jitter'])
+        plain = bf(x['x'], x['plain'], None, cos, sin, x['windows'][1])
+    torch.save(dict(gated=gated.clone(), plain=plain.clone()), HERE / 'dust.pt')
+    print('dust: ok', tuple(gated.shape))
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -446,6 +469,8 @@ def main():
         golden_scorer(root)
     if want('cycle'):
         golden_cycle(root)
+    if want('dust'):
+        golden_dust(root)
 
 
 if __name__ == '__main__':

@@ -101,6 +101,12 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
+    # Dust block rerun
+    jit = _lib.Jitter()
+    assert L.noise_block_forward(ctypes.byref(gpt), 0, fake, None, ctypes.byref(jit), 2, 256, 128, fake, 1 << 30,
+                                 None) == 4                                                   # no weights
+    assert L.noise_block_forward(None, 0, fake, None, None, 2, 256, 128, fake, 1 << 30, None) == 4
+    assert L.noise_block_workspace_bytes(2, 256) == L.noise_population_workspace_bytes(2, 256)
     # readout cycle
     assert L.noise_cycle_weights(None, fake, fake, 4, fake, fake, fake, fake, fake, fake, None) == 4
     assert L.noise_cycle_finish(fake, fake, fake, fake, fake, fake, fake, fake, fake, 4, 0, 0.005, fake, None) == 1
