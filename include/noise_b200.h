@@ -416,6 +416,21 @@ size_t noise_block_workspace_bytes(int seqs, int tokens);
 int noise_block_forward(const noise_gpt_t* model, int layer, float* x, const float* ve, const noise_jitter_t* jit,
                         int seqs, int tokens, int window, void* workspace, size_t workspace_bytes, void* stream);
 
+/* DUST.head_error's cached clean sums (train/val/dust.py:272-278): per row of raw [rows, >= 4096] (fp32 or bf16,
+ * row stride raw_stride elements): slab_sums fp32 [rows, 16] = sum over each 256-column slab of e^(softcap(raw)),
+ * total fp32 [rows], clean_target fp32 [rows] = softcap(raw[max(target, 0)]). */
+int noise_head_error_prep(const void* raw, int raw_dtype, int64_t raw_stride, const int64_t* targets, int rows,
+                          float* slab_sums, float* total, float* clean_target, void* stream);
+
+/* One chunk of DUST.head_error (dust.py:281-301): `draws` jitters noise bf16 [draws * batch, tokens, 256] of slab
+ * `slab` of raw (rows b * tokens + t); each draw's loss from the cached sums, its reward clean_loss - loss (0 where the
+ * target is -1) centred across the batch rows, and error fp32 [rows, raw_stride] columns of the slab -=
+ * bf16(sum over draws of bf16(reward / sigma) noise). draws * batch <= 8192. */
+int noise_head_error_chunk(const void* raw, int raw_dtype, int64_t raw_stride, const void* noise,
+                           const int64_t* targets, const float* clean_loss, const float* slab_sums,
+                           const float* total, const float* clean_target, int batch, int tokens, int draws, int slab,
+                           float sigma, float* error, void* stream);
+
 /* Bytes of scratch noise_head_loss needs for `rows` rows. */
 size_t noise_head_loss_workspace_bytes(int rows);
 

@@ -128,6 +128,11 @@ SIGNATURES = [
     ('noise_block_forward', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Jitter), ctypes.c_int,
       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_head_error_prep', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 4),
+    ('noise_head_error_chunk', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64] + [ctypes.c_void_p] * 6 + [ctypes.c_int] * 4 +
+     [ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_read_status', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_clear_status', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_status_string', ctypes.c_char_p, [ctypes.c_int]),

@@ -5,6 +5,12 @@ arguments and result (dust.py:102-125): Block.forward of one block with a draw's
 output (o), the attention or MLP output projections (attn, mlp) or the MLP hidden layer (fc). It runs the population
 forward's block kernels with zero weight noise and the jitter added in their epilogues (numerics as the population
 forward's: bf16 linears, fp32 residual stream). ``head_loss`` (dust.py:94-99) is noise_b200.head_loss.
+
+``head_error(raw, y, clean_loss, draws, sigma, nrep, noise, vocab)`` is DUST.head_error (dust.py:265-303): one
+256-column slab of the cached LM-head logits jittered per chunk of draws, each draw's loss recomputed from the cached
+slab sums, the centred rewards contracted with the draws' noise, all on the GPU in one kernel per chunk. The draws
+come from the caller's ``noise`` (DUST.noise), in the reference's order. ``install(DUST)`` makes it the class's
+head_error.
 """
 import ctypes
 
@@ -76,3 +82,54 @@ def block_forward(x, w, ve, cos, sin, window, o=None, attn=None, fc=None, mlp=No
                'noise_block_forward')
     out._noise_workspace = ws
     return out.view(B, T, D)
+
+
+SLAB = 256
+
+
+def chunk_size(draws, cap):
+    """The largest count up to cap that divides draws (draws that share one pass, dust.py:80-82)."""
+    return next(n for n in range(min(cap, draws), 0, -1) if draws % n == 0)
+
+
+def head_error(raw, y, clean_loss, draws, sigma=0.1, nrep=16, noise=None, vocab=4096):
+    """DUST.head_error: fp32 [b, t, V] error of the LM head's logits raw [b, t, V] (fp32 or bf16) for targets y [b, t]
+    (-1: ignored) and the clean per-token losses clean_loss [b, t]; noise(n * b, t, 256) draws the jitter (bf16)."""
+    if vocab != 4096:
+        raise ValueError('vocab must be 4096')
+    b, t = y.shape
+    n = chunk_size(draws, nrep)
+    slabs = vocab // SLAB
+    raw2 = raw.detach()
+    if raw2.dtype not in (torch.float32, torch.bfloat16):
+        raw2 = raw2.float()
+    raw2 = raw2.contiguous().view(b * t, raw.shape[-1])
+    y2 = y.detach().long().contiguous().view(-1)
+    cl = clean_loss.detach().float().contiguous().view(-1)
+    _lib.require_cuda(raw2, y2, cl)
+    dt = 1 if raw2.dtype == torch.bfloat16 else 0
+    dev = raw2.device
+    sums, total, clean_t = torch.empty(b * t, slabs, device=dev), torch.empty(b * t, device=dev), \
+        torch.empty(b * t, device=dev)
+    error = torch.zeros(b * t, raw.shape[-1], device=dev)
+    L, stream = _lib.lib(), _lib.stream_handle(dev)
+    _lib.check(L.noise_head_error_prep(raw2.data_ptr(), dt, raw2.stride(0), y2.data_ptr(), b * t, sums.data_ptr(),
+                                       total.data_ptr(), clean_t.data_ptr(), stream), 'noise_head_error_prep')
+    for chunk in range(draws // n):
+        a = noise(n * b, t, SLAB).to(torch.bfloat16).contiguous()
+        _lib.check(L.noise_head_error_chunk(raw2.data_ptr(), dt, raw2.stride(0), a.data_ptr(), y2.data_ptr(),
+                                            cl.data_ptr(), sums.data_ptr(), total.data_ptr(), clean_t.data_ptr(), b,
+                                            t, n, chunk % slabs, float(sigma), error.data_ptr(), stream),
+                   'noise_head_error_chunk')
+    return error.view(b, t, -1) / (draws // slabs)
+
+
+def install(DUST):
+    """DUST.head_error -> this implementation (same arguments: draws, sigma), reading the instance's cached logits,
+    targets, clean losses, chunk cap and noise generator. Returns DUST."""
+    def method(self, draws, sigma=0.1):
+        return head_error(self.outputs['lm_head'], self.y, self.clean_loss, draws, sigma, self.recipe.nrep,
+                          self.noise, self.model.config.vocab_size)
+    DUST.head_error = method
+    return DUST
+

@@ -24,3 +24,16 @@ def dust_inputs(B=2, T=256, seed=41, sigma=0.05):
     cos, sin = rotary(T)
     return dict(x=r(B, T, C), ve=r(B, T, C, scale=0.5), w=w, plain=plain, jitter=jitter, cos=cos, sin=sin,
                 windows=(128, 256))
+
+
+def head_error_inputs(b=2, t=128, draws=64, nrep=16, seed=43):
+    """Cached LM-head logits (bf16 [b, t, 4096]), targets (two ignored), clean losses, and the draws' generator
+    (bf16 N(0, 1) in the reference's call order)."""
+    g = torch.Generator().manual_seed(seed)
+    raw = (torch.randn(b, t, 4096, generator=g) * 3).bfloat16()
+    y = torch.randint(0, 4096, (b, t), generator=g)
+    y[0, 5] = y[1, 17] = -1
+    clean = torch.randn(b, t, generator=g).abs() + 8
+    draw_gen = torch.Generator().manual_seed(seed + 1)
+    noise = lambda *shape: torch.randn(*shape, generator=draw_gen).bfloat16()
+    return dict(raw=raw, y=y, clean_loss=clean, draws=draws, nrep=nrep, noise=noise, sigma=0.1)

@@ -422,6 +422,10 @@ def golden_cycle(root):
     print('cycle: ok', tuple(credit.shape), tuple(coords.shape))
 
 
+def chunk_size_ref(draws, cap):
+    return next(n for n in range(min(cap, draws), 0, -1) if draws % n == 0)
+
+
 def golden_dust(root):
     """Dust's block_forward (train/val/dust.py, its compiled function called as the original, eager flex attention)
     on dust_inputs' seeded inputs, fp32 on the CPU: a value-embedding block with jitter at all four sites, and a plain
@@ -439,8 +443,22 @@ def golden_dust(root):
     with torch.no_grad():
         gated = bf(x['x'], x['w'], x['ve'], cos, sin, x['windows'][0], **x['jitter'])
         plain = bf(x['x'], x['plain'], None, cos, sin, x['windows'][1])
-    torch.save(dict(gated=gated.clone(), plain=plain.clone()), HERE / 'dust.pt')
-    print('dust: ok', tuple(gated.shape))
+    # DUST.head_error, run as the class's own method on a stand-in instance (the attributes it reads)
+    import types
+    from dust_inputs import head_error_inputs
+    h = head_error_inputs()
+    b, t = h['y'].shape
+    inst = types.SimpleNamespace(outputs={'lm_head': h['raw']}, y=h['y'], clean_loss=h['clean_loss'], batch=b,
+                                 length=t, dtype=torch.bfloat16, device=torch.device('cpu'),
+                                 recipe=types.SimpleNamespace(nrep=h['nrep']),
+                                 model=types.SimpleNamespace(config=types.SimpleNamespace(vocab_size=4096)))
+    inst.noise = lambda *shape, dtype=None: h['noise'](*shape)
+    error = dust.DUST.head_error(inst, h['draws'], h['sigma'])
+    touched = h['draws'] // chunk_size_ref(h['draws'], h['nrep']) * 256  # the slabs the chunks jittered
+    assert not error[..., touched:].any()
+    torch.save(dict(gated=gated.clone(), plain=plain.clone(), head_error=error[..., :touched].clone()),
+               HERE / 'dust.pt')
+    print('dust: ok', tuple(gated.shape), tuple(error.shape))
 
 
 def main():

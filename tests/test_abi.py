@@ -107,6 +107,9 @@ def test_rejects_bad_shapes_before_launch(L):
                                  None) == 4                                                   # no weights
     assert L.noise_block_forward(None, 0, fake, None, None, 2, 256, 128, fake, 1 << 30, None) == 4
     assert L.noise_block_workspace_bytes(2, 256) == L.noise_population_workspace_bytes(2, 256)
+    assert L.noise_head_error_prep(fake, 3, 4096, fake, 4, fake, fake, fake, None) == 4      # dtype
+    assert L.noise_head_error_chunk(fake, 0, 4096, fake, fake, fake, fake, fake, fake, 2, 8, 16, 16, 0.1, fake,
+                                    None) == 1                                                  # slab out of range
     # readout cycle
     assert L.noise_cycle_weights(None, fake, fake, 4, fake, fake, fake, fake, fake, fake, None) == 4
     assert L.noise_cycle_finish(fake, fake, fake, fake, fake, fake, fake, fake, fake, 4, 0, 0.005, fake, None) == 1

@@ -51,3 +51,52 @@ def test_each_site_against_oracle(sites):
     # the jitter moves the output: the site is wired
     clean = oracle.block_forward(x['x'], x['w'], x['ve'], x['cos'], x['sin'], 256)
     assert _rel(got, clean) > 10 * _rel(got, ref)
+
+
+def _head_case():
+    from dust_inputs import head_error_inputs
+    return head_error_inputs()
+
+
+def test_head_error_against_reference(golden):
+    """Same draws (the seeded generator, in the reference's order) on the GPU: within 1e-2 of max |ref| with under 2%
+    of elements off by a bf16 rounding of the draw contraction; untouched slabs stay zero."""
+    from noise_b200 import dust
+    h = _head_case()
+    noise = h['noise']
+    err = dust.head_error(h['raw'].to(DEV), h['y'].to(DEV), h['clean_loss'].to(DEV), h['draws'], h['sigma'],
+                          h['nrep'], lambda *s: noise(*s).to(DEV)).cpu()
+    ref = golden('dust.pt')['head_error']
+    touched = ref.shape[-1]
+    assert not err[..., touched:].any()
+    assert _rel(err[..., :touched], ref) < 1e-2
+    assert (err[..., :touched] - ref).abs().gt(1e-2 * ref.abs().max()).float().mean() < 0.02
+
+
+def test_head_error_install_and_oracle():
+    """install(DUST) routes a DUST-like instance's head_error here; 96 draws of 12 per chunk (8 slabs) against the
+    oracle with the same draws."""
+    import types
+    from noise_b200 import dust
+    h = _head_case()
+    draws, nrep = 96, 12
+    g = torch.Generator().manual_seed(99)
+    drawn = []
+
+    def noise(*shape, dtype=None):
+        a = torch.randn(*shape, generator=g).bfloat16()
+        drawn.append(a)
+        return a.to(DEV)
+
+    class Dust:
+        def head_error(self, draws, sigma=0.1):
+            raise AssertionError('not installed')
+    dust.install(Dust)
+    inst = Dust()
+    inst.outputs = {'lm_head': h['raw'].to(DEV)}
+    inst.y, inst.clean_loss = h['y'].to(DEV), h['clean_loss'].to(DEV)
+    inst.recipe, inst.noise = types.SimpleNamespace(nrep=nrep), noise
+    inst.model = types.SimpleNamespace(config=types.SimpleNamespace(vocab_size=4096))
+    err = inst.head_error(draws, 0.1).cpu()
+    ref = oracle.head_error(h['raw'], h['y'], h['clean_loss'], drawn, 0.1)
+    assert _rel(err, ref) < 1e-2

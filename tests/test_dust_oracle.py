@@ -18,3 +18,15 @@ def test_block_forward_fp32(golden):
                                **x['jitter'])
     plain = dust.block_forward(x['x'], x['plain'], None, x['cos'], x['sin'], x['windows'][1], autocast=False)
     assert _rel(gated, g['gated']) < 1e-5 and _rel(plain, g['plain']) < 1e-5
+
+
+def test_head_error(golden):
+    from dust_inputs import head_error_inputs
+    h = head_error_inputs()
+    n = 16
+    noises = [h['noise'](n * 2, 128, 256) for _ in range(h['draws'] // n)]
+    err = dust.head_error(h['raw'], h['y'], h['clean_loss'], noises, h['sigma'])
+    ref = golden('dust.pt')['head_error']
+    touched = ref.shape[-1]
+    assert not err[..., touched:].any()
+    assert _rel(err[..., :touched], ref) < 1e-2 and (err[..., :touched] != ref).float().mean() < 0.02
