@@ -79,6 +79,7 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+template <bool JIT>  // JIT: add TAttnArgs::jit to the attention output (Dust's o jitter site)
 __global__ void __launch_bounds__(TA_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, TAttnArgs p) {
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             yv[e] = bf16_round(o[d + e] * inv);
-            if (p.jit) yv[e] = bf16_round(yv[e] + p.jit[row * NOISE_N_EMBD + hh * 64 + d + e]);
+            if constexpr (JIT) yv[e] = bf16_round(yv[e] + p.jit[row * NOISE_N_EMBD + hh * 64 + d + e]);
             dp[e & 1] = fmaf(yv[e], bv[e], dp[e & 1]);
           }
           st_shared_v4(wst + lane * 128 + (((d >> 3) ^ (lane & 7)) << 4), pack_bf16x2(yv[0], yv[1]),

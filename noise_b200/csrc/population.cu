@@ -462,7 +462,8 @@ struct EpiResid {
 
 // hidden = bf16(relu(bf16(acc) + sign bf16(h.b_fc) a_fc)^2), and per N tile the partial dot hidden.b_mproj
 // (the next linear's rank-1 input dot), eggroll.py:93.
-struct EpiFC {
+template <bool JIT>
+struct EpiFCImpl {
   static constexpr int CH = 64;
   static constexpr bool PIPELINED = true;
   static constexpr int NPARTS = 2 * (F / GEMM_BN);  // per row: one partial dot per (N tile, column half)
@@ -471,7 +472,7 @@ struct EpiFC {
   const float* svec;
   Slice nfc, nmp;
   __nv_bfloat16* hidden;
-  const float* jit;  // [M, 2048] fp32 added to the pre-activation, or NULL (Dust's fc jitter site)
+  const float* jit;  // JIT: [M, 2048] fp32 added to the pre-activation (Dust's fc jitter site)
   float* pdot;  // [M, NPARTS]
   float coef, pd[8];  // eight partial sums: independent FMA chains
   int col0;
@@ -511,7 +512,7 @@ struct EpiFC {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float u = bf16_round(acc[i + e]) + coef * av[e];
-        if (jit) u += jit[static_cast<int64_t>(row) * F + col + i + e];
+        if constexpr (JIT) u += jit[static_cast<int64_t>(row) * F + col + i + e];
         const float rl = fmaxf(u, 0.f);
         r[e] = bf16_round(rl * rl);
         pd[e] = fmaf(r[e], bv[e], pd[e]);
@@ -533,6 +534,8 @@ struct EpiFC {
     __syncwarp();
   }
 };
+using EpiFC = EpiFCImpl<false>;     // the population forward
+using EpiFCJit = EpiFCImpl<true>;   // Dust's block rerun with an fc jitter site
 
 // LM head: z = bf16(acc) + sign bf16(h.b) a; c = 15 tanh(z / 15); per row the cross-entropy
 // log sum_v exp(c_v) - c_target (eggroll.py:96-102). Since c <= 15, exp(c - 15) never overflows, so the
@@ -978,7 +981,8 @@ static int run_attention(const void* q, const void* k, const void* v, int M, int
   if ((rc = make_map(&mq, q, HD, rows, TA_BQ)) || (rc = make_map(&mk, k, HD, rows, TA_BK)) ||
       (rc = make_map(&mv, v, HD, rows, TA_BK)))
     return rc;
-  if (cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
+  auto kern = args.jit ? attention_tc_kernel<true> : attention_tc_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
     return NOISE_ERR_CUDA;
   launch_begin(s, K_ATTENTION);
   const int sms = sm_count();
@@ -986,7 +990,7 @@ static int run_attention(const void* q, const void* k, const void* v, int M, int
   TAttnArgs a = args;
   a.bh = members * H;
   const int items = (T / TA_BQ + 1) / 2 * a.bh;
-  attention_tc_kernel<<<items < sms ? items : sms, TA_THREADS, TA_SMEM, s>>>(mq, mk, mv, a);
+  kern<<<items < sms ? items : sms, TA_THREADS, TA_SMEM, s>>>(mq, mk, mv, a);
   launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
@@ -1443,15 +1447,24 @@ int noise_block_forward(const noise_gpt_t* model, int layer, float* x, const flo
   norm_kernel<NORM_MID><<<norm_blocks, 256, 0, s>>>(nm);
   launch_end(s);
 
-  EpiFC ef{};
-  ef.T = T;
-  ef.sign = w.zsign;
-  ef.svec = w.svec;
-  ef.nfc = ef.nmp = zs;
-  ef.hidden = w.hidden;
-  ef.pdot = w.pdot;
-  ef.jit = j.fc;
-  if ((rc = run_gemm(w.h, Mi, D, model->wfc[layer], F, ef, w.status, s, K_GEMM_FC))) return rc;
+  auto fc_epi = [&](auto& ef) {
+    ef.T = T;
+    ef.sign = w.zsign;
+    ef.svec = w.svec;
+    ef.nfc = ef.nmp = zs;
+    ef.hidden = w.hidden;
+    ef.pdot = w.pdot;
+    ef.jit = j.fc;
+    return run_gemm(w.h, Mi, D, model->wfc[layer], F, ef, w.status, s, K_GEMM_FC);
+  };
+  if (j.fc) {
+    EpiFCJit ef{};
+    rc = fc_epi(ef);
+  } else {
+    EpiFC ef{};
+    rc = fc_epi(ef);
+  }
+  if (rc) return rc;
 
   EpiResid em{};
   em.T = T;
