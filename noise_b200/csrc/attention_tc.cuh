@@ -14,9 +14,9 @@
 //               key tile (M=128, N=64, K=128; V an MN-major operand);
 //   warps 2..5  softmax group A, warps 6..9 group B: one query row per thread; S_w is read with one batched
 //               tcgen05.ld and released at once, P = exp2(s log2(e) / 8 - 8 log2(e)) goes as bf16 into 128-byte-
-//               swizzled shared memory (the A operand of the next O MMA), one in four exponentials on the FMA pipes
-//               (Cody-Waite split, cubic on [-1/2, 1/2], rel. error 7.5e-5) to offload the MUFU pipe; at the end
-//               y = O / l (bf16) and the per-head partial dot y . b of the c_proj rank-1 term.
+//               swizzled shared memory (the A operand of the next O MMA), every exponential on the MUFU pipe (it is
+//               under half busy: moving a share to an FMA polynomial measured slower); at the end y = O / l (bf16)
+//               and the per-head partial dot y . b of the c_proj rank-1 term.
 // Only the diagonal key tile and the window's first tile take the masked path.
 #pragma once
 #include <type_traits>
@@ -65,18 +65,6 @@ __device__ __forceinline__ TileRange tile_range(int qt, int window) {
   const int q0 = qt * TA_BQ;
   const bool edge = q0 - window >= 0;
   return TileRange{edge ? (q0 - window) / TA_BK : 0, q0 / TA_BK, edge};
-}
-
-// 2^x for x <= 8.1 on the FMA pipes: x = j + f with j = rint(x), f in [-1/2, 1/2], 2^f by a cubic, 2^j by adding j
-// to the exponent field (x >= -126 here, so the result stays normal).
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float t = x + 12582912.0f;  // 1.5 * 2^23: rint(x) in the low mantissa bits
-  const float j = t - 12582912.0f;
-  const float f = x - j;
-  float p = fmaf(0.05517161265015602f, f, 0.2426111400127411f);
-  p = fmaf(p, f, 0.6932610273361206f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 template <bool JIT>  // JIT: add TAttnArgs::jit to the attention output (Dust's o jitter site)
@@ -293,7 +281,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float x = fmaf(v[c + e], SL2, -OFF);
-            pe[e] = (e & 3) == 3 ? exp2_poly(x) : ex2_approx(x);
+            pe[e] = ex2_approx(x);
             if constexpr (MASKED) {
               const int key = kt * TA_BK + c + e;
               if (key > tq || tq - key > p.window) pe[e] = 0.f;
