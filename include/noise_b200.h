@@ -133,6 +133,20 @@ int noise_implicit_key_context(const void* q, const void* k, const void* values,
 int noise_value_pass(const void* q, const void* k, int dtype, const float* lse, const noise_rows_t* source,
                      const noise_rows_t* out, int rows, int tokens, int window, void* stream);
 
+/* Bytes of the caller's workspace for noise_value_pass_ws: a 256-byte status block, then the source's bf16 hi and lo
+ * halves ([rows, T, 64] each). 0 for rows < 1 or tokens < 1. */
+size_t noise_value_pass_workspace_bytes(int rows, int tokens);
+
+/* noise_value_pass with a caller workspace (256-byte aligned, noise_value_pass_workspace_bytes large): bf16 q / k with
+ * T % 128 == 0 run on tcgen05 (one pass splitting the source into bf16 hi / lo, then a persistent kernel computing
+ * S = K Q^T into TMEM and O += P hi + P lo per pair of 128-key tiles); anything else falls through to
+ * noise_value_pass. Same result definition as noise_value_pass (moment_kernels.py:612-717). The workspace's first
+ * int32 is the device status after the call completes: 0, or 1 if a pipeline wait gave up (the output is then
+ * incomplete). */
+int noise_value_pass_ws(const void* q, const void* k, int dtype, const float* lse, const noise_rows_t* source,
+                        const noise_rows_t* out, int rows, int tokens, int window, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* Key credits: per key t and raw key coordinate d, the degree-2 moment response of the receivers' softmax to a finite
  * step sigma * rms(k_raw[t]) of k_raw[t, d] through RoPE and the RMS norm (moment_kernels.py:467-607; key_gluon.py);
  * with value_out (data != NULL) also the raw value credit sum_s p hub_s. All inputs fp32 contiguous; cos / sin

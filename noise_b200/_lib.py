@@ -100,6 +100,8 @@ SIGNATURES = [
     ('noise_adam_step', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
     ('noise_implicit_key_context', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_value_pass', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    ('noise_value_pass_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_value_pass_ws', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_key_scan', ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
     ('noise_moment_key_scores', ctypes.c_int,

@@ -10,10 +10,14 @@
 //   query_moments   per query and raw direction: numerator / denominator moments of its own softmax (:197-365)
 // All run on warp-level tensor cores (mma.sync bf16 m16n8k16, tf32 m16n8k8), 4 warps x 16 rows per CTA, with
 // cp.async-staged shared-memory tiles. The moment dots take bf16 operands exactly where the reference rounds to bf16.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "noise_b200.h"
 #include "ptx.cuh"
@@ -875,7 +879,50 @@ static bool view_ok(const noise_rows_t& r, bool bf16, bool pairs) {
 }  // namespace credit
 }  // namespace noise
 
+#include "value_tc.cuh"
+
 using namespace noise::credit;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tv_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [n, 64] bf16 rows, box 128 rows x 64 with 128-byte swizzle; or (lse) fp32 [rows, T], box 1 x 128, no swizzle
+int tv_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer) {
+  auto fn = tv_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  const uint64_t es = bf16 ? 2 : 4;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * es};
+  cuuint32_t box[2] = {bf16 ? 64u : static_cast<cuuint32_t>(TV_B), bf16 ? static_cast<cuuint32_t>(TV_B) : 1u};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, el, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  bf16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int tv_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return n;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -919,6 +966,45 @@ int noise_value_pass(const void* q, const void* k, int dtype, const float* lse, 
     if (cudaFuncSetAttribute(value_pass_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) return NOISE_ERR_CUDA;
     value_pass_kernel<false><<<grid, 128, smem, s>>>(a);
   }
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_value_pass_workspace_bytes(int rows, int tokens) {
+  if (rows < 1 || tokens < 1) return 0;
+  return 256 + 2 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16);
+}
+
+int noise_value_pass_ws(const void* q, const void* k, int dtype, const float* lse, const noise_rows_t* source,
+                        const noise_rows_t* out, int rows, int tokens, int window, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!q || !k || !lse || !source || !out) return NOISE_ERR_ARGUMENT;
+  if (dtype != NOISE_DTYPE_F32 && dtype != NOISE_DTYPE_BF16) return NOISE_ERR_ARGUMENT;
+  if (dtype != NOISE_DTYPE_BF16 || tokens % TV_B)  // fp32 operands or T % 128 != 0: the warp-MMA kernel
+    return noise_value_pass(q, k, dtype, lse, source, out, rows, tokens, window, stream);
+  if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
+  if (!a16(q) || !a16(k) || !a16(lse) || !rows_ok(*source, true) || !rows_ok(*out, true)) return NOISE_ERR_ALIGN;
+  if (!workspace || workspace_bytes < noise_value_pass_workspace_bytes(rows, tokens)) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  const int sms = tv_sms();
+  if (sms < 1) return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + 256);
+  __nv_bfloat16* lo = hi + static_cast<int64_t>(rows) * tokens * D;
+  const uint64_t n = static_cast<uint64_t>(rows) * tokens;
+  CUtensorMap mk, mq, mhi, mlo, mlse;
+  int rc;
+  if ((rc = tv_map(&mk, k, true, D, n)) || (rc = tv_map(&mq, q, true, D, n)) || (rc = tv_map(&mhi, hi, true, D, n)) ||
+      (rc = tv_map(&mlo, lo, true, D, n)) || (rc = tv_map(&mlse, lse, false, tokens, rows)))
+    return rc;
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  const int64_t n4 = static_cast<int64_t>(n) * (D / 4);
+  const int split_blocks = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8));
+  split_source_kernel<<<split_blocks, 256, 0, s>>>(to_rows(*source), tokens, n4, hi, lo);
+  if (cudaFuncSetAttribute(value_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TV_SMEM)) return NOISE_ERR_CUDA;
+  const TValueArgs a{tokens, std::min(window, tokens), rows, to_rows(*out), status};
+  const int items = (tokens / TV_B + 1) / 2 * rows;
+  value_tc_kernel<<<std::min(items, sms), TV_THREADS, TV_SMEM, s>>>(mk, mq, mhi, mlo, mlse, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

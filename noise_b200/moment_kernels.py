@@ -65,10 +65,11 @@ def implicit_key_context_edges_impl(q, k, values, hub, window):
 
 # --- value credits --------------------------------------------------------------------------------------------------
 
-def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, layers=None):
+def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, layers=None, tc=True):
     """sum_s p * source (moment_kernels._value_pass): source stacked (rows, T, C) or (in_heads > 1) by token
     (rows // in_heads, T, in_heads * C); the output stacked or (out_heads > 1) by token, into ``out`` when given.
-    The signature of the reference's VALUE_IMPL plug-in."""
+    The signature of the reference's VALUE_IMPL plug-in. bf16 q / k with T % 128 == 0 run on the tcgen05 kernel
+    (``tc=False``: the warp-MMA kernel, for comparison); the workspace's status word rides on ``out``."""
     h, t, _ = q.shape
     dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, lse = _c(q, dt), _c(k, dt), _c(lse, torch.float32)
@@ -82,6 +83,15 @@ def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, lay
         out = source.new_empty((h // out_heads, t, out_heads * channels), dtype=torch.float32)
     src_rows = _rows(source, in_heads)
     out_rows = _rows(out, out_heads, layers)
+    if tc and dt == torch.bfloat16 and t % 128 == 0:
+        L = _lib.lib()
+        nbytes = L.noise_value_pass_workspace_bytes(h, t)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        _check(L.noise_value_pass_ws(q.data_ptr(), k.data_ptr(), _DT[dt], lse.data_ptr(), ctypes.byref(src_rows),
+                                     ctypes.byref(out_rows), h, t, window, ws.data_ptr(), nbytes, _stream(q)),
+               'noise_value_pass_ws')
+        out._noise_workspace = ws
+        return out
     _check(_lib.lib().noise_value_pass(q.data_ptr(), k.data_ptr(), _DT[dt], lse.data_ptr(), ctypes.byref(src_rows),
                                        ctypes.byref(out_rows), h, t, window, _stream(q)), 'noise_value_pass')
     return out

@@ -93,6 +93,17 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_head_prep(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, ctypes.byref(prep), None) == 4  # outputs
     assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 96, 0.003, 1e-6, fake, fake, 1 << 30, None) == 1
     assert L.noise_id_head_scores(fake, 8, 2, 64, fake, fake, 64, 0.003, 1e-6, fake, fake, 16, None) == 3
+    # the workspace value pass: a 256-byte status block, then bf16 hi + lo of the source
+    assert L.noise_value_pass_workspace_bytes(2, 256) == 256 + 2 * 2 * 256 * 64 * 2
+    assert L.noise_value_pass_workspace_bytes(0, 256) == 0
+    src = _lib.Rows(fake, 256 * 64, 64, 1)
+    vp = (fake, fake, 1, fake, ctypes.byref(src), ctypes.byref(src), 2, 256, 128)
+    assert L.noise_value_pass_ws(*vp, fake, 16, None) == 3                                     # workspace too small
+    assert L.noise_value_pass_ws(*vp, fake + 16, 1 << 30, None) == 2                           # not 256-byte aligned
+    assert L.noise_value_pass_ws(fake, fake, 1, fake, ctypes.byref(src), ctypes.byref(src), 2, 256, -1, fake,
+                                 1 << 30, None) == 1                                           # negative window
+    assert L.noise_value_pass_ws(fake, fake, 7, fake, ctypes.byref(src), ctypes.byref(src), 2, 256, 128, fake,
+                                 1 << 30, None) == 4                                           # dtype
     # readout scorers
     v = _lib.View3(fake, 1, 1, 1)
     r = ctypes.byref(v)
