@@ -511,6 +511,26 @@ def run_aux(a):
     back = torch.empty(8, 8, 3, 1024, 64, dtype=torch.bfloat16, device=device)
     us = _timed(lambda: heads.id_head_scores(got, (cs, sn), back, 8, t), a.steps, a.warmup)
     rate('id_head_scores', us, rows=64, tokens=t)
+    # identity-phase GEMMs on the same 8,192 local tokens, 8 layers, D 512, hidden 2048
+    from noise_b200 import id_kernels
+    m = n
+    fc = [rn(m, 2048).bfloat16() for _ in range(8)]
+    credb = rn(8, m, 512, scale=0.1).bfloat16()
+    w_out_t = rn(8, 512, 2048, scale=0.05).bfloat16()
+    fc_steps = ru(8, m, scale=0.5).add_(0.01)
+    us = _timed(lambda: id_kernels.hidden_credits_fused(fc, fc_steps, credb, w_out_t), a.steps, a.warmup)
+    rate('hidden_credits', us, flops=2 * 8 * m * 512 * 2048)
+    n2s = [rn(m, 512).bfloat16() for _ in range(8)]
+    hid = [rn(m, 2048, scale=0.1).bfloat16() for _ in range(8)]
+    gwide = torch.empty(16, 512, 2048, dtype=torch.bfloat16, device=device)
+    us = _timed(lambda: id_kernels.at_b_layers(n2s, hid, gwide[:8]), a.steps, a.warmup)
+    rate('at_b_layers_wide', us, flops=2 * 8 * m * 512 * 2048)
+    gsq = torch.empty(32, 512, 512, dtype=torch.bfloat16, device=device)
+    us = _timed(lambda: id_kernels.at_b_layers(n2s, list(credb), gsq[24:]), a.steps, a.warmup)
+    rate('at_b_layers_square', us, flops=2 * 8 * m * 512 * 512)
+    got2 = rn(8, 8, 3, m, 64, scale=0.2).bfloat16()
+    us = _timed(lambda: id_kernels.square_credit_grads(n2s, got2, gsq[:24]), a.steps, a.warmup)
+    rate('square_credit_grads', us, flops=2 * 24 * m * 512 * 512)
     # track-1 readout scorers
     H, Tq, P, M, start, window = 8, 2048, 16, 256, 512, 1024
     q, tgt = rn(H, Tq, 64), rn(H, Tq, 64, scale=0.125)

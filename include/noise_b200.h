@@ -274,6 +274,30 @@ size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n);
 int noise_id_head_scores(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
                          float sigma, float eps, void* back, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The identity phase's batched GEMMs (tcgen05, fp32 accumulation, bf16 out); each takes a workspace of at least
+ * NOISE_STATUS_BYTES (the device status word) and at most 8 layers.
+ *
+ * out[l] = bf16(slope(us[l], steps[l]) * float(bf16(credb[l] @ w_out_t[l]))) with slope(u, s) = (max(u + s, 0)^2 -
+ * max(u - s, 0)^2) / (2 s) in fp32: credb bf16 (layers, m, k), w_out_t bf16 (layers, k, n), us[l] bf16 (m, n), steps
+ * fp32 (layers, m), out bf16 (layers, m, n); all contiguous; m % 128, n % 128, k % 64 == 0. Replaces
+ * id_kernels.hidden_credits_fused / _hidden_credit_kernel (id_kernels.py:19-84; run.py:3818-3820). */
+int noise_hidden_credits(const void* const* us, const float* steps, const void* credb, const void* w_out_t,
+                         int layers, int m, int n, int k, void* out, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* out[l] = bf16(as[l]^T @ bs[l]) for as[l] bf16 (k, p), bs[l] bf16 (k, q) row-major, out bf16 (layers, p, q)
+ * contiguous; k % 64, p % 128, q % 128 == 0. Replaces id_kernels.at_b_layers / _at_b_kernel (id_kernels.py:136-170;
+ * run.py:3895-3896, 3911). */
+int noise_at_b_layers(const void* const* as, const void* const* bs, int layers, int k, int p, int q, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[j * layers + l] = bf16(n1s[l]^T @ B_jl), B_jl[tok, w * 64 + c] = got2[w, l, j, tok, c]: n1s[l] bf16 (m, d)
+ * row-major, got2 bf16 (world, layers, 3, m, 64) contiguous (the received heads_out), out bf16 (3 layers, d, d);
+ * world * 64 == d, d % 128 == 0, m % 64 == 0. Replaces id_kernels.square_credit_grads / _square_credit_kernel
+ * (id_kernels.py:87-133; run.py:3913). */
+int noise_square_credit_grads(const void* const* n1s, const void* got2, int world, int layers, int m, int d,
+                              void* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * Track-1 readout scorers (reference train/val/run.py, `recipe` section): the noise_record custom ops, head_dim 64,
  * fp32 arithmetic (the reference's tf32x3 dots are fp32-accurate).

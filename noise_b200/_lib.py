@@ -116,6 +116,9 @@ SIGNATURES = [
     ('noise_head_prep', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
     ('noise_id_head_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ('noise_id_head_scores', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_hidden_credits', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_at_b_layers', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_square_credit_grads', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_future_scores', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_key_response', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_query_response', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),

@@ -29,6 +29,9 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 
 - ``train/val/dust.py``: block_forward (its compiled function as the original) with jitter at every site.
 
+- ``train/speedrun/id_kernels.py``: hidden_credits_fused, at_b_layers, square_credit_grads (their Triton kernels
+  under the patched interpreter) on id_inputs.py's seeded inputs.
+
 Usage: python tests/golden/make_golden.py /path/to/reference [fixture,...]
 """
 import importlib.util
@@ -461,6 +464,27 @@ def golden_dust(root):
     print('dust: ok', tuple(gated.shape), tuple(error.shape))
 
 
+def golden_id_kernels(root):
+    """The identity phase's batched GEMMs (speedrun/id_kernels.py: hidden_credits_fused, at_b_layers,
+    square_credit_grads) through their Triton kernels under the patched interpreter, on id_inputs' seeded inputs."""
+    patch_triton_interpreter()
+    spec = importlib.util.spec_from_file_location('ref_id_kernels', root / 'train/speedrun/id_kernels.py')
+    idk = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(idk)
+    from id_inputs import at_b_inputs, hidden_inputs, square_inputs
+    us, steps, credb, w_out_t = hidden_inputs()
+    hidden = idk.hidden_credits_fused(us, steps, credb, w_out_t)
+    As, Bs = at_b_inputs()
+    at_b = torch.empty(8, As[0].shape[-1], Bs[0].shape[-1], dtype=torch.bfloat16)
+    idk.at_b_layers(As, Bs, at_b)
+    n1s, got2 = square_inputs()
+    d = n1s[0].shape[1]
+    square = torch.empty(3 * len(n1s), d, d, dtype=torch.bfloat16)
+    idk.square_credit_grads(n1s, got2, square)
+    torch.save(dict(hidden=hidden.clone(), at_b=at_b.clone(), square=square.clone()), HERE / 'id_kernels.pt')
+    print('id_kernels: ok')
+
+
 def main():
     root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get('NOISE_REFERENCE', ''))
     assert (root / 'utils/model.py').exists(), 'pass the reference checkout as argv[1]'
@@ -489,6 +513,8 @@ def main():
         golden_cycle(root)
     if want('dust'):
         golden_dust(root)
+    if want('id_kernels'):
+        golden_id_kernels(root)
 
 
 if __name__ == '__main__':

@@ -104,6 +104,15 @@ def test_rejects_bad_shapes_before_launch(L):
                                  1 << 30, None) == 1                                           # negative window
     assert L.noise_value_pass_ws(fake, fake, 7, fake, ctypes.byref(src), ctypes.byref(src), 2, 256, 128, fake,
                                  1 << 30, None) == 4                                           # dtype
+    # identity-phase GEMMs
+    ptrs = (ctypes.c_void_p * 8)(*([fake] * 8))
+    assert L.noise_hidden_credits(ptrs, fake, fake, fake, 8, 128, 256, 128, fake, fake, 16, None) == 3  # workspace
+    assert L.noise_hidden_credits(ptrs, fake, fake, fake, 8, 100, 256, 128, fake, fake, 256, None) == 1  # m % 128
+    assert L.noise_hidden_credits(ptrs, fake, fake, fake, 9, 128, 256, 128, fake, fake, 256, None) == 1  # > 8 layers
+    assert L.noise_at_b_layers(ptrs, ptrs, 8, 100, 128, 128, fake, fake, 256, None) == 1               # k % 64
+    assert L.noise_at_b_layers(ptrs, ptrs, 8, 128, 128, 128, fake + 8, fake, 256, None) == 2           # out align
+    assert L.noise_square_credit_grads(ptrs, fake, 2, 8, 64, 256, fake, fake, 256, None) == 1         # world 64 != d
+    assert L.noise_square_credit_grads(ptrs, None, 2, 8, 64, 128, fake, fake, 256, None) == 4
     # readout scorers
     v = _lib.View3(fake, 1, 1, 1)
     r = ctypes.byref(v)
