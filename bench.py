@@ -11,7 +11,9 @@ over one 2048-token row ("population forwards/s").
 
 --workload credit times the credit-readout kernels in isolation; --workload train one EGGROLL
 update at population 24,576 (configs 4 / 5: forward, fitness all-gather, rebuilt update all-reduce, AdamW);
---workload aux the other entry points (un-perturbed forward, head loss, head sharding, readout scorers).
+--workload aux the other entry points (un-perturbed forward, head loss, head sharding, readout scorers);
+--workload exchange the identity phase's head exchange (pack + heads-in + heads-out all_to_all) as the reference does
+it (pack kernel, NCCL all_to_all_single) and fused over peer memory (HeadExchange), N ranks under torchrun.
 
 --impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
 fp32, all host threads) on a bounded sample of the same workload, rank 0 only.
@@ -50,7 +52,7 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train', 'aux'])
+    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train', 'aux', 'exchange'])
     # smaller population cases for profiling captures only; the benchmark line uses the defaults
     ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (population workload)')
     ap.add_argument('--rows', type=int, default=ROWS, help='2048-token rows per member (population workload)')
@@ -589,6 +591,78 @@ def run_aux(a):
                       'config': {'workload': 'representative shapes (bench.py run_aux)'}, 'kernels': res}), flush=True)
 
 
+def run_exchange(a):
+    """The identity phase's two exchanges at 8 layers x 8,192 local tokens per rank (rows of 1,024): the reference's
+    way (pack_heads_kernel, then NCCL all_to_all_single for heads in and for heads out) against HeadExchange (the pack
+    writing straight into the owners' buffers, the heads-out stores, the epoch-flag waits). One step = both
+    exchanges; CUDA events over K steps after W warm-ups, max over ranks. One JSON line (rank 0)."""
+    from noise_b200 import heads
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    dist = torch.distributed
+    if world > 1:
+        dist.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=120))
+    rank = dist.get_rank() if world > 1 else 0
+    layers, n, t = 8, 8192, 1024
+    g = torch.Generator(device).manual_seed(rank)
+    pieces = [[torch.randn(n, 512, device=device, generator=g).bfloat16() for _ in range(layers)] for _ in range(5)]
+    lses = [torch.randn(n // t, 8, t, device=device, generator=g) for _ in range(layers)]
+    back = torch.randn(world, layers, 3, n, 64, device=device, generator=g).bfloat16()
+    ex = heads.HeadExchange(layers, n, t)
+
+    def reference_step():
+        send = heads.pack_heads_kernel(*pieces, lses)
+        got, got2 = torch.empty_like(send), torch.empty_like(back)
+        if world > 1:
+            dist.all_to_all_single(got, send)
+            dist.all_to_all_single(got2, back)
+        else:
+            got.copy_(send)
+            got2.copy_(back)
+
+    def fused_step():
+        ex.send_heads(*pieces, lses)
+        ex.wait_heads()
+        ex.send_back(back)
+        ex.wait_back()
+
+    def timed(fn):
+        for _ in range(a.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        us = torch.tensor([e0.elapsed_time(e1) * 1e3 / a.steps], device=device)
+        if world > 1:
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+        return us.item()
+
+    ref_us = timed(reference_step)
+    ours_us = timed(fused_step)
+    status = ex.read_status()
+    ex.close()
+    moved = 8 * layers * n * heads.PACK * 2 + back.numel() * 2  # bytes a rank sends per step (own share included)
+    remote = moved * (world - 1) / world
+    if rank == 0:
+        print(json.dumps({'metric': 'identity-phase head exchange time per step (pack + heads in + heads out)',
+                          'unit': 'us per step', 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
+                          'config': {'workload': 'head exchange', 'layers': layers, 'tokens_per_rank': n,
+                                     'seq_len': t, 'bytes_sent_per_rank': moved},
+                          'fused_us': round(ours_us, 1), 'reference_us': round(ref_us, 1),
+                          'speedup': round(ref_us / ours_us, 3),
+                          'nvlink_gbs_per_rank_fused': round(remote / ours_us / 1e3, 1) if world > 1 else None,
+                          'status': status}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     a = args_()
     if a.impl == 'reference':
@@ -599,6 +673,8 @@ def main():
         run_train(a)
     elif a.workload == 'aux':
         run_aux(a)
+    elif a.workload == 'exchange':
+        run_exchange(a)
     else:
         run_ours(a)
 

@@ -274,6 +274,52 @@ size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n);
 int noise_id_head_scores(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
                          float sigma, float eps, void* back, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The identity phase's two all_to_all_single exchanges (run.py:3887-3888 heads in, :3905-3906 heads out, completed by
+ * heads_in.wait() :3902 / heads_out.wait() :3912) over peer memory: every rank owns one exchange buffer (device memory
+ * from noise_exchange_alloc, mapped into the other ranks with CUDA IPC: plain NVLink loads and stores, no multicast).
+ * Its first NOISE_EXCHANGE_HEAD_BYTES are control words (epoch flags per (slot, source rank), a local block counter
+ * per slot); the rest holds the received data at offsets the caller chooses. A send writes chunk p of its data into
+ * rank p's buffer at dst_offset + rank * chunk (all_to_all_single's layout) and then publishes `epoch` in rank p's
+ * flag (slot, rank); noise_exchange_wait on rank p returns (on the stream) once every source's flag of the slot has
+ * reached `epoch`. Epochs grow by one per exchange and slot; one exchange per slot is in flight at a time, and a rank
+ * may send epoch e + 1 into a buffer only after its owner has finished reading epoch e (the identity phase's order:
+ * heads out of step e is received before heads in of step e + 1 is sent). */
+#define NOISE_MAX_PEERS 8
+#define NOISE_EXCHANGE_HEAD_BYTES 1024
+#define NOISE_IPC_HANDLE_BYTES 64
+typedef struct {
+  void* base[NOISE_MAX_PEERS]; /* every rank's exchange buffer as mapped in this process (own one included) */
+  int rank;
+  int world;
+} noise_peers_t;
+
+/* A zeroed exchange buffer of `bytes` (cudaMalloc, so it can be shared) and its IPC handle (NOISE_IPC_HANDLE_BYTES). */
+int noise_exchange_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another rank's exchange buffer from its IPC handle (peer access enabled). */
+int noise_exchange_open(const void* ipc_handle, void** ptr);
+/* Unmap a buffer from noise_exchange_open. */
+int noise_exchange_close(void* ptr);
+/* Free a buffer from noise_exchange_alloc (after every other rank has closed its mapping). */
+int noise_exchange_free(void* ptr);
+
+/* Stream-ordered wait until flags (slot, w) of this rank's buffer reach epoch for every w < world; a wait longer than
+ * limit_ns sets the workspace's status word to NOISE_DEVICE_TIMEOUT (NOISE_STATUS_BYTES workspace). */
+int noise_exchange_wait(const noise_peers_t* peers, int slot, uint32_t epoch, int64_t limit_ns, void* workspace,
+                        void* stream);
+
+/* all_to_all_single over peer memory: chunk p of send (chunk_bytes, 16-byte multiple) to rank p's buffer at
+ * dst_offset + rank * chunk_bytes, then epoch to flag (slot, rank) of every rank. Replaces the heads-out
+ * dist.all_to_all_single(got2, back) (run.py:3905-3906). */
+int noise_alltoall_peer(const void* send, size_t chunk_bytes, const noise_peers_t* peers, size_t dst_offset, int slot,
+                        uint32_t epoch, void* stream);
+
+/* noise_pack_heads fused with the heads-in exchange (run.py:3885-3888): row (h, l, t) of the pack goes straight to
+ * rank p = h / (8 / world) at dst_offset + ((rank * (8 / world) + h % (8 / world)) * n_layers + l) * tokens + t rows
+ * of NOISE_PACK bf16 (the all_to_all_single output layout), then epoch to flag (slot, rank) of every rank. world
+ * divides 8. */
+int noise_pack_heads_peer(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len,
+                          const noise_peers_t* peers, size_t dst_offset, int slot, uint32_t epoch, void* stream);
+
 /* The identity phase's batched GEMMs (tcgen05, fp32 accumulation, bf16 out); each takes a workspace of at least
  * NOISE_STATUS_BYTES (the device status word) and at most 8 layers.
  *

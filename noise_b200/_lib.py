@@ -61,6 +61,11 @@ class HeadPieces(ctypes.Structure):
                [(n + '_stride', ctypes.c_int64) for n in ('q', 'k', 'v', 'o', 'target')] + [('lse', ctypes.c_void_p)]
 
 
+class Peers(ctypes.Structure):
+    """noise_peers_t."""
+    _fields_ = [('base', ctypes.c_void_p * 8), ('rank', ctypes.c_int), ('world', ctypes.c_int)]
+
+
 class HeadPrep(ctypes.Structure):
     """noise_head_prep_t."""
     _fields_ = [(n, ctypes.c_void_p) for n in ('q16', 'k16', 'v16', 'hub16', 'q32', 'k32', 'f2', 'f4', 'xy', 'lse',
@@ -116,6 +121,13 @@ SIGNATURES = [
     ('noise_head_prep', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
     ('noise_id_head_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ('noise_id_head_scores', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_exchange_alloc', ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
+    ('noise_exchange_open', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    ('noise_exchange_close', ctypes.c_int, [ctypes.c_void_p]),
+    ('noise_exchange_free', ctypes.c_int, [ctypes.c_void_p]),
+    ('noise_exchange_wait', ctypes.c_int, [ctypes.POINTER(Peers), ctypes.c_int, ctypes.c_uint32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_alltoall_peer', ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(Peers), ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
+    ('noise_pack_heads_peer', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Peers), ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
     ('noise_hidden_credits', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_at_b_layers', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_square_credit_grads', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),

@@ -13,8 +13,10 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
+#include "exchange.cuh"
 #include "noise_b200.h"
 
 namespace noise {
@@ -38,13 +40,9 @@ struct PackArgs {
 };
 
 // grid (ceil(n / 8), H, L): warp w of block x copies token x * 8 + w of head blockIdx.y, layer blockIdx.z.
-__global__ void __launch_bounds__(256) pack_heads_kernel(const __grid_constant__ PackArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int tok = blockIdx.x * WARPS + (threadIdx.x >> 5);
-  if (tok >= a.n) return;
-  const int h = blockIdx.y, l = blockIdx.z;
+// Row (h, l, tok) of the pack: 161 32-bit words (5 pieces x 32 words, then the lse's fp32 bits), one warp.
+__device__ __forceinline__ void pack_row(const PackArgs& a, int h, int l, int tok, uint32_t* dst, int lane) {
   const noise_head_pieces_t& P = a.layer[l];
-  uint32_t* dst = a.out + (static_cast<int64_t>(h * a.L + l) * a.n + tok) * (PACK / 2);
   const void* src[5] = {P.q, P.k, P.v, P.o, P.target};
   const int64_t stride[5] = {P.q_stride, P.k_stride, P.v_stride, P.o_stride, P.target_stride};
 #pragma unroll
@@ -57,6 +55,34 @@ __global__ void __launch_bounds__(256) pack_heads_kernel(const __grid_constant__
     const int64_t li = (static_cast<int64_t>(tok / a.T) * H + h) * a.T + tok % a.T;  // lse (rows, H, T)
     dst[5 * 32] = __float_as_uint(P.lse[li]);
   }
+}
+
+__global__ void __launch_bounds__(256) pack_heads_kernel(const __grid_constant__ PackArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int tok = blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (tok >= a.n) return;
+  const int h = blockIdx.y, l = blockIdx.z;
+  pack_row(a, h, l, tok, a.out + (static_cast<int64_t>(h * a.L + l) * a.n + tok) * (PACK / 2), lane);
+}
+
+// The pack written straight into the destination ranks' exchange buffers (grid-stride over (h, l, tok) rows, one
+// warp per row), then the send's epoch flag (exchange.cuh).
+__global__ void __launch_bounds__(256) pack_heads_peer_kernel(const __grid_constant__ PackArgs a,
+                                                              const __grid_constant__ xch::Peers peers,
+                                                              int64_t dst_offset, int slot, uint32_t epoch) {
+  const int lane = threadIdx.x & 31;
+  const int hp = H / peers.world;  // heads per destination rank
+  const int64_t rows = static_cast<int64_t>(H) * a.L * a.n;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * WARPS + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * WARPS) {
+    const int tok = static_cast<int>(row % a.n);
+    const int hl = static_cast<int>(row / a.n);
+    const int l = hl % a.L, h = hl / a.L;
+    const int p = h / hp;
+    const int64_t drow = (static_cast<int64_t>(peers.rank * hp + h % hp) * a.L + l) * a.n + tok;
+    pack_row(a, h, l, tok, reinterpret_cast<uint32_t*>(peers.base[p] + dst_offset) + drow * (PACK / 2), lane);
+  }
+  xch::send_done(peers, slot, epoch);
 }
 
 struct PrepArgs {
@@ -190,15 +216,11 @@ static IdScratch carve(void* ws, int64_t total) {
 
 using namespace noise::heads;
 
-extern "C" {
-
-int noise_pack_heads(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len, void* out, void* stream) {
-  if (!layers || !out) return NOISE_ERR_ARGUMENT;
+static int pack_args(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len, PackArgs* a) {
+  if (!layers) return NOISE_ERR_ARGUMENT;
   if (n_layers < 1 || n_layers > NOISE_MAX_PACK_LAYERS || tokens < 16 || tokens % 16 || seq_len < 1 ||
       tokens % seq_len)
     return NOISE_ERR_SHAPE;
-  if (!a4(out)) return NOISE_ERR_ALIGN;
-  PackArgs a{};
   for (int l = 0; l < n_layers; ++l) {
     const noise_head_pieces_t& P = layers[l];
     if (!P.q || !P.k || !P.v || !P.o || !P.target || !P.lse) return NOISE_ERR_ARGUMENT;
@@ -208,14 +230,44 @@ int noise_pack_heads(const noise_head_pieces_t* layers, int n_layers, int tokens
       if (st[k] < H * HD) return NOISE_ERR_SHAPE;
       if (!a4(ptr[k]) || (st[k] & 1)) return NOISE_ERR_ALIGN;
     }
-    a.layer[l] = P;
+    a->layer[l] = P;
   }
-  a.L = n_layers;
-  a.n = tokens;
-  a.T = seq_len;
+  a->L = n_layers;
+  a->n = tokens;
+  a->T = seq_len;
+  return NOISE_OK;
+}
+
+extern "C" {
+
+int noise_pack_heads(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len, void* out, void* stream) {
+  if (!layers || !out) return NOISE_ERR_ARGUMENT;
+  PackArgs a{};
+  int rc = pack_args(layers, n_layers, tokens, seq_len, &a);
+  if (rc) return rc;
+  if (!a4(out)) return NOISE_ERR_ALIGN;
   a.out = static_cast<uint32_t*>(out);
   dim3 grid((tokens + WARPS - 1) / WARPS, H, n_layers);
   pack_heads_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_pack_heads_peer(const noise_head_pieces_t* layers, int n_layers, int tokens, int seq_len,
+                          const noise_peers_t* peers, size_t dst_offset, int slot, uint32_t epoch, void* stream) {
+  PackArgs a{};
+  int rc = pack_args(layers, n_layers, tokens, seq_len, &a);
+  if (rc) return rc;
+  noise::xch::Peers P;
+  if ((rc = noise::xch::peers_check(peers, &P))) return rc;
+  if (H % P.world || slot < 0 || slot > 1) return NOISE_ERR_SHAPE;
+  if (dst_offset < NOISE_EXCHANGE_HEAD_BYTES || dst_offset % 16) return NOISE_ERR_ALIGN;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))
+    return NOISE_ERR_CUDA;
+  const int64_t rows = static_cast<int64_t>(H) * n_layers * tokens;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows + WARPS - 1) / WARPS, static_cast<int64_t>(sms) * 8));
+  pack_heads_peer_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, P, static_cast<int64_t>(dst_offset), slot, epoch);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

@@ -25,13 +25,11 @@ def _two_byte(t, what):
     return t
 
 
-def pack_heads_kernel(qs, ks, vals, outs, targets, lses):
-    """identity_grad's (H, L, n, PACK) all_to_all send buffer from each layer's (tokens, D) pieces and its lse
-    (rows, H, t) (run.py:3718-3731)."""
+def _pieces(qs, ks, vals, outs, targets, lses):
+    """noise_head_pieces_t per layer from each layer's (tokens, D) pieces and its lse (rows, H, t); returns (pieces,
+    tensors to keep alive, n, t, layers)."""
     n, t = qs[0].shape[0], lses[0].shape[-1]
-    dev = qs[0].device
     layers = len(qs)
-    out = torch.empty(H, layers, n, PACK, device=dev, dtype=torch.bfloat16)
     pieces = (_lib.HeadPieces * layers)()
     keep = []
     for i, group in enumerate(zip(qs, ks, vals, outs, targets, lses)):
@@ -44,6 +42,15 @@ def pack_heads_kernel(qs, ks, vals, outs, targets, lses):
         p.q, p.k, p.v, p.o, p.target = (m.data_ptr() for m in mats)
         p.q_stride, p.k_stride, p.v_stride, p.o_stride, p.target_stride = (m.stride(0) for m in mats)
         p.lse = lse.data_ptr()
+    return pieces, keep, n, t, layers
+
+
+def pack_heads_kernel(qs, ks, vals, outs, targets, lses):
+    """identity_grad's (H, L, n, PACK) all_to_all send buffer from each layer's (tokens, D) pieces and its lse
+    (rows, H, t) (run.py:3718-3731)."""
+    pieces, keep, n, t, layers = _pieces(qs, ks, vals, outs, targets, lses)
+    dev = qs[0].device
+    out = torch.empty(H, layers, n, PACK, device=dev, dtype=torch.bfloat16)
     _lib.check(_lib.lib().noise_pack_heads(pieces, layers, n, t, out.data_ptr(), _lib.stream_handle(dev)),
                'noise_pack_heads')
     return out
@@ -108,3 +115,135 @@ def id_head_scores(got, rope32, back, b, t):
     _lib.check(L.noise_id_head_scores(got.data_ptr(), w, layers, n, cos.data_ptr(), sin.data_ptr(), t, KEY_SIGMA,
                                       NORM_EPS, back.data_ptr(), ws.data_ptr(), nbytes,
                                       _lib.stream_handle(got.device)), 'noise_id_head_scores')
+
+
+class _DeviceArray:
+    """A device allocation of the library, seen by torch through the CUDA array interface (no copy)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {'shape': tuple(shape), 'typestr': typestr, 'data': (ptr, False),
+                                         'version': 3, 'strides': None}
+
+
+class HeadExchange:
+    """identity_grad's two all_to_all_single exchanges (run.py:3887-3888 heads in, :3905-3906 heads out) over peer
+    memory: the pack writes every head's rows straight into the owning rank's buffer over NVLink, the heads-out
+    credits are stored the same way, and a bounded wait on per-source epoch flags replaces heads_in.wait() /
+    heads_out.wait() (run.py:3902, 3912). One buffer per rank, shared with CUDA IPC (no multicast).
+
+    ``send_heads(qs, ks, vals, outs, targets, lses)`` + ``wait_heads()`` -> got, the (H, L, n, PACK) bf16 buffer
+    dist.all_to_all_single(got, pack_heads_kernel(...)) fills (with world 8: (W, L, N, PACK)); ``send_back(back)``
+    + ``wait_back()`` -> got2 = all_to_all_single of back (W, L, 3, n, 64). Per step the order is send_heads,
+    wait_heads, send_back, wait_back (what the reference does): a rank sends the next step's heads only after it has
+    the previous step's credits back, which is also what tells it every peer has finished reading its buffer.
+    Construct and ``close()`` collectively on every rank of ``group``."""
+
+    def __init__(self, layers, tokens, seq_len, group=None, wait_seconds=60.0, device=None):
+        import torch.distributed as dist
+        self.dist = dist if dist.is_available() and dist.is_initialized() else None
+        self.group = group
+        self.world = self.dist.get_world_size(group) if self.dist else 1
+        self.rank = self.dist.get_rank(group) if self.dist else 0
+        if H % self.world or self.world > 8:
+            raise ValueError('the exchange needs a world size dividing 8')
+        self.layers, self.n, self.t = layers, tokens, seq_len
+        self.device = torch.device('cuda', torch.cuda.current_device()) if device is None else device
+        self.limit_ns = int(wait_seconds * 1e9)
+        got_bytes = H * layers * tokens * PACK * 2
+        back_bytes = self.world * layers * 3 * tokens * HD * 2
+        self.got_offset = 1024
+        self.got2_offset = (self.got_offset + got_bytes + 255) // 256 * 256
+        L = _lib.lib()
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _lib.check(L.noise_exchange_alloc(self.got2_offset + back_bytes, ctypes.byref(ptr), handle),
+                       'noise_exchange_alloc')
+        self.ptr = ptr.value
+        handles = [handle.raw]
+        if self.dist:
+            handles = [None] * self.world
+            self.dist.all_gather_object(handles, handle.raw, group=group)
+        self.opened = []
+        self.peers = _lib.Peers()
+        self.peers.rank, self.peers.world = self.rank, self.world
+        for w in range(self.world):
+            if w == self.rank:
+                self.peers.base[w] = self.ptr
+                continue
+            p = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(L.noise_exchange_open(ctypes.create_string_buffer(handles[w], 64), ctypes.byref(p)),
+                           'noise_exchange_open')
+            self.opened.append(p.value)
+            self.peers.base[w] = p.value
+        as_bf16 = lambda off, shape: torch.as_tensor(_DeviceArray(self.ptr + off, shape, '<i2'),
+                                                     device=self.device).view(torch.bfloat16)
+        self.got = as_bf16(self.got_offset, (H, layers, tokens, PACK))
+        self.got2 = as_bf16(self.got2_offset, (self.world, layers, 3, tokens, HD))
+        self.status = torch.zeros(_lib.STATUS_BYTES, dtype=torch.uint8, device=self.device)
+        self.epoch = [0, 0]
+        self.phase = 'send_heads'
+
+    def _step(self, want, nxt):
+        if self.phase != want:
+            raise RuntimeError(f'HeadExchange: {want} called out of order (expected {self.phase})')
+        self.phase = nxt
+
+    def send_heads(self, qs, ks, vals, outs, targets, lses):
+        """pack_heads_kernel + the heads-in all_to_all_single, one kernel (run.py:3885-3888)."""
+        self._step('send_heads', 'wait_heads')
+        pieces, keep, n, t, layers = _pieces(qs, ks, vals, outs, targets, lses)
+        if (n, t, layers) != (self.n, self.t, self.layers):
+            raise ValueError('send_heads: pieces do not match the exchange\'s layers / tokens / seq_len')
+        self.epoch[0] += 1
+        _lib.check(_lib.lib().noise_pack_heads_peer(pieces, layers, n, t, ctypes.byref(self.peers), self.got_offset,
+                                                    0, self.epoch[0], _lib.stream_handle(self.device)),
+                   'noise_pack_heads_peer')
+        self._keep = keep
+
+    def wait_heads(self):
+        """heads_in.wait() (run.py:3902): the stream waits until every rank's heads have landed; returns got."""
+        self._step('wait_heads', 'send_back')
+        _lib.check(_lib.lib().noise_exchange_wait(ctypes.byref(self.peers), 0, self.epoch[0], self.limit_ns,
+                                                  self.status.data_ptr(), _lib.stream_handle(self.device)),
+                   'noise_exchange_wait')
+        return self.got
+
+    def send_back(self, back):
+        """The heads-out all_to_all_single of back (W, L, 3, n, 64) bf16 (run.py:3905-3906)."""
+        self._step('send_back', 'wait_back')
+        if back.dtype != torch.bfloat16 or tuple(back.shape) != tuple(self.got2.shape) or not back.is_contiguous():
+            raise ValueError('back: contiguous bf16 (W, L, 3, n, 64)')
+        _lib.require_cuda(back)
+        self.epoch[1] += 1
+        _lib.check(_lib.lib().noise_alltoall_peer(back.data_ptr(), back[0].numel() * 2, ctypes.byref(self.peers),
+                                                  self.got2_offset, 1, self.epoch[1],
+                                                  _lib.stream_handle(self.device)), 'noise_alltoall_peer')
+        self._keep_back = back
+
+    def wait_back(self):
+        """heads_out.wait() (run.py:3912); returns got2."""
+        self._step('wait_back', 'send_heads')
+        _lib.check(_lib.lib().noise_exchange_wait(ctypes.byref(self.peers), 1, self.epoch[1], self.limit_ns,
+                                                  self.status.data_ptr(), _lib.stream_handle(self.device)),
+                   'noise_exchange_wait')
+        return self.got2
+
+    def read_status(self):
+        """The device status word of the waits (0, or NOISE_DEVICE_TIMEOUT); synchronises the stream."""
+        return _lib.read_status(self.status)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""
+        torch.cuda.synchronize(self.device)
+        L = _lib.lib()
+        for p in self.opened:
+            _lib.check(L.noise_exchange_close(p), 'noise_exchange_close')
+        self.opened = []
+        if self.dist:
+            self.dist.barrier(group=self.group)
+        if self.ptr:
+            self.got = self.got2 = None
+            _lib.check(L.noise_exchange_free(self.ptr), 'noise_exchange_free')
+            self.ptr = None
