@@ -126,6 +126,14 @@ typedef struct {
 int noise_implicit_key_context(const void* q, const void* k, const void* values, const void* hub, int dtype, int rows,
                                int tokens, int window, float* lse, float* center, void* stream);
 
+/* noise_implicit_key_context with a workspace of at least NOISE_STATUS_BYTES (the device status word): bf16 operands
+ * with T % 128 == 0 run on tcgen05 (S = Q K^T and the scores H V^T into TMEM per pair of 128-query tiles, an online
+ * softmax on 32-column chunks); anything else falls through to noise_implicit_key_context. Same results
+ * (moment_kernels.py:137-194); window % 64 == 0. */
+int noise_implicit_key_context_ws(const void* q, const void* k, const void* values, const void* hub, int dtype,
+                                  int rows, int tokens, int window, float* lse, float* center, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* out[row, t] = sum_{s: 0 <= s - t <= window} exp(q_s.k_t / 8 - lse_s) source[row, s] (64 channels), the
  * probabilities rounded to bf16 and the fp32 source split into bf16 hi + lo, fp32 accumulation. Replaces
  * moment_kernels._value_pass / _value_credit_kernel (moment_kernels.py:612-717) and value_gluon.value_pass_gluon:
@@ -171,6 +179,21 @@ int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const
                               int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
                               const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
                               const noise_rows_t* out, const noise_rows_t* values_out, int out_dtype, void* stream);
+
+/* Bytes of the caller's workspace for noise_moment_key_scores_ws: a 256-byte status block, then the receivers' pair
+ * features (bf16 [rows, T, 64] x 3). 0 for rows < 1 or tokens < 1. */
+size_t noise_moment_key_scores_workspace_bytes(int rows, int tokens);
+
+/* noise_moment_key_scores_v with a caller workspace (256-byte aligned): T % 128 == 0 with out / values_out views whose
+ * strides are 16-byte multiples run on tcgen05 (a pass writing the receivers' pair features as bf16, then one
+ * persistent kernel per 128-key tile: S = K Q^T and the scores V H^T into TMEM, the moment weights as bf16 A operands,
+ * the five moment sums as tcgen05 MMAs, the response epilogue from TMEM); anything else falls through to
+ * noise_moment_key_scores_v. Same results (moment_kernels.py:368-462). */
+int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                               int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                               const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                               const noise_rows_t* out, const noise_rows_t* values_out, int out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* Query credits: per query s and raw query coordinate d, zn / (1 + zd) / steps_s from the numerator / denominator
  * moments of its own softmax (moment_kernels._moment_queries_kernel, :197-365), rounded to bf16 (stored as bf16 or

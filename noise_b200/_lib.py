@@ -105,6 +105,7 @@ SIGNATURES = [
     ('noise_adam_step', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
     ('noise_implicit_key_context', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_value_pass', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    ('noise_implicit_key_context_ws', ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_value_pass_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_value_pass_ws', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_key_scan', ctypes.c_int,
@@ -115,6 +116,9 @@ SIGNATURES = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_moment_key_scores_v', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_moment_key_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_moment_key_scores_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_moment_query_scores_v', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_pack_heads', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),

@@ -879,6 +879,8 @@ static bool view_ok(const noise_rows_t& r, bool bf16, bool pairs) {
 }  // namespace credit
 }  // namespace noise
 
+#include "context_tc.cuh"
+#include "keymom_tc.cuh"
 #include "value_tc.cuh"
 
 using namespace noise::credit;
@@ -915,6 +917,36 @@ int tv_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
+// bf16 [n, 64] rows with 64-row boxes (the key moments' receiver-side tiles), 128-byte swizzle
+int km_map(CUtensorMap* map, const void* base, uint64_t n) {
+  auto fn = tv_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), n};
+  cuuint64_t strides[1] = {D * 2};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, el,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+// fp32 [rows, T] with 64 x 1 boxes (per-receiver lse / center of one 64-receiver tile)
+int km_map_f32(CUtensorMap* map, const float* base, uint64_t t, uint64_t rows) {
+  auto fn = tv_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {t, rows};
+  cuuint64_t strides[1] = {t * 4};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, el,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
 int tv_sms() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -944,6 +976,35 @@ int noise_implicit_key_context(const void* q, const void* k, const void* values,
     if (cudaFuncSetAttribute(implicit_ctx_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) return NOISE_ERR_CUDA;
     implicit_ctx_kernel<false><<<grid, 128, smem, s>>>(a);
   }
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_implicit_key_context_ws(const void* q, const void* k, const void* values, const void* hub, int dtype,
+                                  int rows, int tokens, int window, float* lse, float* center, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!q || !k || !values || !hub || !lse || !center) return NOISE_ERR_ARGUMENT;
+  if (dtype != NOISE_DTYPE_F32 && dtype != NOISE_DTYPE_BF16) return NOISE_ERR_ARGUMENT;
+  if (dtype != NOISE_DTYPE_BF16 || tokens % TC_B)  // fp32 operands (tf32 dots) or T % 128 != 0: the warp-MMA kernel
+    return noise_implicit_key_context(q, k, values, hub, dtype, rows, tokens, window, lse, center, stream);
+  if (rows < 1 || window < 0 || window % 64) return NOISE_ERR_SHAPE;
+  if (!a16(q) || !a16(k) || !a16(values) || !a16(hub)) return NOISE_ERR_ALIGN;
+  if (!workspace || workspace_bytes < NOISE_STATUS_BYTES) return NOISE_ERR_WORKSPACE;
+  const int sms = tv_sms();
+  if (sms < 1) return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t n = static_cast<uint64_t>(rows) * tokens;
+  CUtensorMap mq, mk, mh, mv;
+  int rc;
+  if ((rc = tv_map(&mq, q, true, D, n)) || (rc = tv_map(&mk, k, true, D, n)) || (rc = tv_map(&mh, hub, true, D, n)) ||
+      (rc = tv_map(&mv, values, true, D, n)))
+    return rc;
+  int* status = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (cudaFuncSetAttribute(context_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM))
+    return NOISE_ERR_CUDA;
+  const TContextArgs a{tokens, std::min(window, tokens), rows, lse, center, status};
+  const int items = (tokens / TC_B + 1) / 2 * rows;
+  context_tc_kernel<<<std::min(items, sms), TC_THREADS, TC_SMEM, s>>>(mq, mk, mh, mv, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
@@ -1072,6 +1133,78 @@ int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const
   const int smem = KeyLayout<true>::SMEM;
   if (cudaFuncSetAttribute(key_moments_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) return NOISE_ERR_CUDA;
   key_moments_kernel<true><<<dim3(tokens / 64, rows), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_moment_key_scores_workspace_bytes(int rows, int tokens) {
+  if (rows < 1 || tokens < 1) return 0;
+  return 256 + 3 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16);
+}
+
+int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                               int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                               const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                               const noise_rows_t* out, const noise_rows_t* values_out, int out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !hub || !raw || !sq || !side || !cos || !sin || !lse || !hub_out || !steps || !out || !values_out)
+    return NOISE_ERR_ARGUMENT;
+  if ((raw_dtype != NOISE_DTYPE_F32 && raw_dtype != NOISE_DTYPE_BF16) ||
+      (out_dtype != NOISE_DTYPE_F32 && out_dtype != NOISE_DTYPE_BF16))
+    return NOISE_ERR_ARGUMENT;
+  const bool ob = out_dtype == NOISE_DTYPE_BF16;
+  // the tcgen05 kernel stores 16 consecutive outputs per vector: every view stride a 16-byte multiple
+  auto vec_ok = [&](const noise_rows_t& r) {
+    const int64_t es = ob ? 2 : 4;
+    return r.data && a16(r.data) && (r.layer_stride * es) % 16 == 0 && (r.token_stride * es) % 16 == 0 &&
+           (r.block_rows == 0 || (r.gpu_stride * es) % 16 == 0);
+  };
+  if (tokens % KM_B || !vec_ok(*out) || !vec_ok(*values_out))
+    return noise_moment_key_scores_v(q, k, v, hub, raw, raw_dtype, sq, side, cos, sin, lse, hub_out, steps, rows,
+                                     tokens, out, values_out, out_dtype, stream);
+  if (rows < 1) return NOISE_ERR_SHAPE;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !a16(lse) || !a16(hub_out) ||
+      !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) || !view_ok(*out, ob, false) ||
+      !view_ok(*values_out, ob, true))
+    return NOISE_ERR_ALIGN;
+  if (!workspace || workspace_bytes < noise_moment_key_scores_workspace_bytes(rows, tokens)) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  const int sms = tv_sms();
+  if (sms < 1) return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  const int64_t n = static_cast<int64_t>(rows) * tokens;
+  __nv_bfloat16* f2 = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + 256);
+  __nv_bfloat16* g2 = f2 + n * D;
+  __nv_bfloat16* xy = g2 + n * D;
+  KeyMomMaps m;
+  int rc;
+  if ((rc = tv_map(&m.k, k, true, D, n)) || (rc = tv_map(&m.v, v, true, D, n)) ||
+      (rc = km_map(&m.q, q, n)) || (rc = km_map(&m.h, hub, n)) || (rc = km_map(&m.f2, f2, n)) ||
+      (rc = km_map(&m.g2, g2, n)) || (rc = km_map(&m.xy, xy, n)) || (rc = km_map_f32(&m.lse, lse, tokens, rows)) ||
+      (rc = km_map_f32(&m.ctr, hub_out, tokens, rows)))
+    return rc;
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  const int64_t n_pairs = n * 32;
+  keymom_features_kernel<<<static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8)),
+                           256, 0, s>>>(side, n_pairs, f2, g2, xy);
+  if (cudaFuncSetAttribute(keymom_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KM_SMEM))
+    return NOISE_ERR_CUDA;
+  KeyMomTcArgs a{};
+  a.T = tokens;
+  a.window = tokens;
+  a.rows = rows;
+  a.raw = to_rows(*raw);
+  a.raw_bf16 = raw_dtype == NOISE_DTYPE_BF16;
+  a.out_bf16 = ob;
+  a.sq = sq;
+  a.steps = steps;
+  a.cosb = cos;
+  a.sinb = sin;
+  a.out = to_rows(*out);
+  a.vout = to_rows(*values_out);
+  a.status = status;
+  const int items = tokens / KM_B * rows;
+  keymom_tc_kernel<<<std::min(items, sms), KM_THREADS, KM_SMEM, s>>>(m, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

@@ -50,13 +50,23 @@ def _rope(cos, sin):
 
 # --- lse and center -----------------------------------------------------------------------------------------------
 
-def implicit_key_context_edges_impl(q, k, values, hub, window):
+def implicit_key_context_edges_impl(q, k, values, hub, window, tc=True):
+    """(lse, center); bf16 operands with T % 128 == 0 on the tcgen05 kernel (``tc=False``: the warp-MMA kernel, for
+    comparison), the workspace's status word riding on lse."""
     h, t, _ = q.shape
     dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, values, hub = (_c(z, dt) for z in (q, k, values, hub))
     _lib.require_cuda(q)
     lse = torch.empty((h, t), device=q.device, dtype=torch.float32)
     center = torch.empty_like(lse)
+    if tc and dt == torch.bfloat16 and t % 128 == 0:
+        ws = torch.empty(_lib.STATUS_BYTES, dtype=torch.uint8, device=q.device)
+        _check(_lib.lib().noise_implicit_key_context_ws(q.data_ptr(), k.data_ptr(), values.data_ptr(), hub.data_ptr(),
+                                                        _DT[dt], h, t, window, lse.data_ptr(), center.data_ptr(),
+                                                        ws.data_ptr(), ws.numel(), _stream(q)),
+               'noise_implicit_key_context_ws')
+        lse._noise_workspace = ws
+        return lse, center
     _check(_lib.lib().noise_implicit_key_context(q.data_ptr(), k.data_ptr(), values.data_ptr(), hub.data_ptr(),
                                                  _DT[dt], h, t, window, lse.data_ptr(), center.data_ptr(),
                                                  _stream(q)), 'noise_implicit_key_context')
@@ -180,7 +190,10 @@ def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out
            'noise_moment_query_scores_v')
 
 
-def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values):
+def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values, tc=True):
+    """The identity phase's key moments into out / values; T % 128 == 0 runs on the tcgen05 kernel when the output
+    views allow 16-byte stores (``tc=False``: the warp-MMA kernel, for comparison). Returns the workspace (its first
+    int is the device status word) or None."""
     rows, t, d = q.shape
     q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
     raw = _raw4(raw, rows, t)
@@ -195,12 +208,23 @@ def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, 
         raise ValueError('out / values: fp32 or bf16')
     blocks, m = raw.shape[1], out.shape[2]
     rv, ro, rvals = _blocked(raw, rows, m, blocks), _blocked(out, rows, m, blocks), _blocked(values, rows, m, blocks)
+    if tc and t % 128 == 0:
+        L = _lib.lib()
+        nbytes = L.noise_moment_key_scores_workspace_bytes(rows, t)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        _check(L.noise_moment_key_scores_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(), ctypes.byref(rv),
+                                            _DT[raw.dtype], sq.data_ptr(), side.data_ptr(), cos.data_ptr(),
+                                            sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(), steps.data_ptr(), rows,
+                                            t, ctypes.byref(ro), ctypes.byref(rvals), _DT[out.dtype], ws.data_ptr(),
+                                            nbytes, _stream(q)), 'noise_moment_key_scores_ws')
+        return ws
     _check(_lib.lib().noise_moment_key_scores_v(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
                                                 ctypes.byref(rv), _DT[raw.dtype], sq.data_ptr(), side.data_ptr(),
                                                 cos.data_ptr(), sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(),
                                                 steps.data_ptr(), rows, t, ctypes.byref(ro), ctypes.byref(rvals),
                                                 _DT[out.dtype], _stream(q)),
            'noise_moment_key_scores_v')
+    return None
 
 
 # --- the reference's custom ops (names as in moment_kernels.py:184-717) ---------------------------------------------
