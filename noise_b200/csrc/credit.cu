@@ -917,14 +917,14 @@ int tv_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
-// bf16 [n, 64] rows with 64-row boxes (the key moments' receiver-side tiles), 128-byte swizzle
+// bf16 [n, 64] rows with KM_R-row boxes (the key moments' receiver-side tiles), 128-byte swizzle
 int km_map(CUtensorMap* map, const void* base, uint64_t n) {
   auto fn = tv_encode();
   if (!fn) return NOISE_ERR_CUDA;
   if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), n};
   cuuint64_t strides[1] = {D * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(KM_R)};
   cuuint32_t el[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, el,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -932,14 +932,14 @@ int km_map(CUtensorMap* map, const void* base, uint64_t n) {
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
-// fp32 [rows, T] with 64 x 1 boxes (per-receiver lse / center of one 64-receiver tile)
+// fp32 [rows, T] with KM_R x 1 boxes (per-receiver lse / center of one receiver tile)
 int km_map_f32(CUtensorMap* map, const float* base, uint64_t t, uint64_t rows) {
   auto fn = tv_encode();
   if (!fn) return NOISE_ERR_CUDA;
   if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
   cuuint64_t dims[2] = {t, rows};
   cuuint64_t strides[1] = {t * 4};
-  cuuint32_t box[2] = {64, 1};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(KM_R), 1};
   cuuint32_t el[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, el,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1158,7 +1158,7 @@ int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, cons
     return r.data && a16(r.data) && (r.layer_stride * es) % 16 == 0 && (r.token_stride * es) % 16 == 0 &&
            (r.block_rows == 0 || (r.gpu_stride * es) % 16 == 0);
   };
-  if (tokens % KM_B || !vec_ok(*out) || !vec_ok(*values_out))
+  if (tokens % KM_B || !vec_ok(*out) || !vec_ok(*values_out) || !a16(cos) || !a16(sin))
     return noise_moment_key_scores_v(q, k, v, hub, raw, raw_dtype, sq, side, cos, sin, lse, hub_out, steps, rows,
                                      tokens, out, values_out, out_dtype, stream);
   if (rows < 1) return NOISE_ERR_SHAPE;

@@ -9,14 +9,15 @@
 // with the receivers' pair features f2 = (x_i, y_i), g2 = (x_i^2, y_i^2), xy = x_i y_i of side / 8 (bf16, from
 // keymom_features_kernel), then per key the response of every raw coordinate through RoPE and the RMS norm.
 //
-// One work item = one 128-key tile of one row; receivers stream in 64-wide tiles. 320 threads, one CTA per SM:
-//   warp 0      TMA: K, V once per item; per receiver tile q, hub, f2, g2, xy (64 rows each) and lse / center
-//               into a 2-stage ring;
-//   warp 1      TMEM (512 columns): S (64) = K Q^T, C (64) = V H^T, then the accumulators P2 (64), R2 (64),
-//               Q2 | QXY (128: g2 and the zero-padded xy as one 128-wide B operand) and VA (64); one lane issues
-//               S / C of tile j, then the moment MMAs of tile j - 1 (M = 128 keys, K = 64 receivers);
-//   warps 2..9  warp w: key rows of TMEM lane quarter w % 4, receiver half (w - 2) / 4 of each tile: the weights
-//               as bf16 into swizzled shared memory (the moment MMAs' A operands); at the item's end the response
+// One work item = one 128-key tile of one row; receivers stream in 32-wide tiles. 320 threads, one CTA per SM:
+//   warp 0      TMA: K, V once per item; per receiver tile q, hub, f2, g2, xy (32 rows each) and lse / center
+//               into a 5-stage ring;
+//   warp 1      TMEM (512 columns): S = K Q^T and C = V H^T (32 columns each, double-buffered), the accumulators
+//               P2 (64), R2 (64), Q2 | QXY (96: g2 and xy as one 96-wide B operand) and VA (64); one lane issues
+//               S / C of tile j + 1 ahead of the moment MMAs of tile j (M = 128 keys, K = 32 receivers);
+//   warps 2..9  warp w: key rows of TMEM lane quarter w % 4, receivers half (w - 2) / 4 of each tile: the weights
+//               as bf16 into one of two 64-byte-swizzled shared buffers (the moment MMAs' A operands), so a tile's
+//               weights are written while the previous tile's moment MMAs run; at the item's end the response
 //               epilogue for its 16 rotary pairs and 32 value columns.
 #pragma once
 #include "ptx.cuh"
@@ -24,21 +25,34 @@
 namespace noise {
 namespace credit {
 
-constexpr int KM_B = 128, KM_R = 64, KM_STAGES = 2, KM_THREADS = 320;
+constexpr int KM_B = 128, KM_R = 32, KM_STAGES = 5, KM_THREADS = 320;
 constexpr int KM_KT = KM_B * 128;            // [128][64] bf16 key-side tile: 16 KB
-constexpr int KM_RT = KM_R * 128;            // [64][64] bf16 receiver-side tile: 8 KB
+constexpr int KM_RT = KM_R * 128;            // [32][64] bf16 receiver-side tile: 4 KB
+constexpr int KM_WT = KM_B * KM_R * 2;       // [128][32] bf16 weight matrix (64-byte rows): 8 KB
 constexpr int KM_K = 0, KM_V = KM_KT;
-constexpr int KM_W = 2 * KM_KT;              // W1, W2, W2L, P: [128][64] bf16 each
-constexpr int KM_RING = KM_W + 4 * KM_KT;
-// stage: q, hub, f2, g2, xy (g2 and xy adjacent: one 128-wide MN-major operand), then lse, center (64 floats each)
+constexpr int KM_W = 2 * KM_KT;              // 2 buffers x (W1, W2, W2L, P)
+constexpr int KM_RING = KM_W + 8 * KM_WT;
+// stage: q, hub, f2, g2, xy (g2 and xy adjacent: one 96-wide MN-major operand), then lse, center (32 floats each)
 constexpr int KM_SQ = 0, KM_SH = KM_RT, KM_SF2 = 2 * KM_RT, KM_SG2 = 3 * KM_RT, KM_SXY = 4 * KM_RT,
-              KM_SLSE = 5 * KM_RT, KM_SCTR = KM_SLSE + 256;
+              KM_SLSE = 5 * KM_RT, KM_SCTR = KM_SLSE + 128;
 constexpr int KM_STAGE = 5 * KM_RT + 1024;
 constexpr int KM_SUMS = KM_RING + KM_STAGES * KM_STAGE;  // s1 / s2 per (half, key row): 2 x 2 x 128 floats
 constexpr int KM_BAR = KM_SUMS + 2048;
 constexpr int KM_SMEM = KM_BAR + 256 + 1024;
-// TMEM columns
-constexpr uint32_t KM_TS = 0, KM_TC = 64, KM_TP2 = 128, KM_TR2 = 192, KM_TQ2 = 256, KM_TXY = 320, KM_TVA = 384;
+// TMEM columns: S / C buffer b at 64 b (S) and 64 b + 32 (C)
+constexpr uint32_t KM_TSC = 0, KM_TP2 = 128, KM_TR2 = 192, KM_TQ2 = 256, KM_TXY = 320, KM_TVA = 384;
+
+// K-major operand in 64-byte swizzled rows (32 bf16 of K per row): 8-row groups 512 bytes apart, layout type 4
+// (SWIZZLE_64B); the K step inside a row advances the start address by 32 bytes per 16 bf16 values.
+__device__ __forceinline__ uint64_t km_sdesc_kmajor_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(4u) << 61;
+  return d;
+}
 
 struct KeyMomTcArgs {
   int T, window, rows;
@@ -76,9 +90,9 @@ __device__ __forceinline__ void km_bar_sync() {  // named barrier 1 over the 256
 }
 
 struct KeyMomMaps {
-  CUtensorMap k, v;           // bf16 [rows * T, 64], 128-row boxes
-  CUtensorMap q, h, f2, g2, xy;  // bf16 [rows * T, 64], 64-row boxes
-  CUtensorMap lse, ctr;       // fp32 [rows, T], 64 x 1 boxes
+  CUtensorMap k, v;              // bf16 [rows * T, 64], 128-row boxes
+  CUtensorMap q, h, f2, g2, xy;  // bf16 [rows * T, 64], 32-row boxes
+  CUtensorMap lse, ctr;          // fp32 [rows, T], 32 x 1 boxes
 };
 
 __global__ void __launch_bounds__(KM_THREADS, 1)
@@ -88,13 +102,13 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + KM_BAR);
   uint64_t* kv_full = bar;
   uint64_t* kv_empty = bar + 1;
-  uint64_t* st_full = bar + 2;              // STAGES
+  uint64_t* st_full = bar + 2;               // STAGES
   uint64_t* st_empty = st_full + KM_STAGES;  // STAGES
-  uint64_t* s_full = st_empty + KM_STAGES;
-  uint64_t* s_empty = s_full + 1;
-  uint64_t* w_full = s_empty + 1;
-  uint64_t* w_empty = w_full + 1;
-  uint64_t* acc_full = w_empty + 1;
+  uint64_t* s_full = st_empty + KM_STAGES;   // 2 (S / C buffers)
+  uint64_t* s_empty = s_full + 2;            // 2
+  uint64_t* w_full = s_empty + 2;            // 2 (weight buffers)
+  uint64_t* w_empty = w_full + 2;            // 2
+  uint64_t* acc_full = w_empty + 2;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* drain = acc_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
@@ -103,7 +117,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
   const int nkt = p.T / KM_B, nrt = p.T / KM_R;
   const int items = nkt * p.rows;
   // item w: key tile w / rows (the first tiles have the most receivers: heaviest first) of row w % rows; its
-  // receiver tiles run from the key tile's first 64 receivers to the window's end
+  // receiver tiles run from the key tile's first receivers to the window's end
   auto tiles_of = [&](int kt, int& lo, int& hi) {
     lo = kt * KM_B / KM_R;
     hi = min((kt * KM_B + KM_B - 1 + p.window) / KM_R, nrt - 1);
@@ -116,12 +130,14 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       mbar_init(&st_full[s], 1);
       mbar_init(&st_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(s_empty, 256);
-    mbar_init(w_full, 256);
-    mbar_init(w_empty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 8);  // one arrival per weight warp (its lanes joined by __syncwarp first)
+      mbar_init(&w_full[b], 8);
+      mbar_init(&w_empty[b], 1);
+    }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 256);
+    mbar_init(acc_empty, 8);
     mbar_init(drain, 1);
     fence_barrier_init();
   }
@@ -179,27 +195,28 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_bf16(KM_B, KM_R);             // S, C: B = q / hub rows (K-major)
       constexpr uint32_t id_f = idesc_bf16(KM_B, 64, false, true);  // P2, R2, VA: B MN-major
-      constexpr uint32_t id_q = idesc_bf16(KM_B, 128, false, true);  // Q2 | QXY
+      constexpr uint32_t id_q = idesc_bf16(KM_B, 96, false, true);  // Q2 | QXY
       int sv = 0, nitem = 0;
       bool ok = true;
-      // the moment MMAs of the receiver tile in ring slot svj (the item's first when first)
+      // the moment MMAs of the receiver tile with global index svj (the item's first when first)
       auto moments = [&](int svj, bool first) {
-        if (!mbar_wait(w_full, static_cast<uint32_t>(svj) & 1u, p.status)) return false;
+        const int wb = svj & 1;
+        if (!mbar_wait(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
         tc_fence_after();
         const uint32_t st = sbase + KM_RING + (svj % KM_STAGES) * KM_STAGE;
-        const uint32_t w = sbase + KM_W;
+        const uint32_t w = sbase + KM_W + wb * 4 * KM_WT;  // W1, W2, W2L, P
 #pragma unroll
         for (int ks = 0; ks < KM_R / 16; ++ks) {
           const uint32_t acc = (first && ks == 0) ? 0u : 1u;
           const uint64_t f2d = sdesc_mnmajor_sw128(st + KM_SF2 + ks * 2048, 16);
-          tc_mma(tmem + KM_TP2, sdesc_kmajor_sw128(w) + 2u * ks, f2d, id_f, acc);
-          tc_mma(tmem + KM_TR2, sdesc_kmajor_sw128(w + 2 * KM_KT) + 2u * ks, f2d, id_f, acc);
-          tc_mma(tmem + KM_TQ2, sdesc_kmajor_sw128(w + KM_KT) + 2u * ks,
+          tc_mma(tmem + KM_TP2, km_sdesc_kmajor_sw64(w) + 2u * ks, f2d, id_f, acc);
+          tc_mma(tmem + KM_TR2, km_sdesc_kmajor_sw64(w + 2 * KM_WT) + 2u * ks, f2d, id_f, acc);
+          tc_mma(tmem + KM_TQ2, km_sdesc_kmajor_sw64(w + KM_WT) + 2u * ks,
                  sdesc_mnmajor_sw128(st + KM_SG2 + ks * 2048, KM_RT), id_q, acc);
-          tc_mma(tmem + KM_TVA, sdesc_kmajor_sw128(w + 3 * KM_KT) + 2u * ks,
+          tc_mma(tmem + KM_TVA, km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks,
                  sdesc_mnmajor_sw128(st + KM_SH + ks * 2048, 16), id_f, acc);
         }
-        tc_commit(w_empty);
+        tc_commit(&w_empty[wb]);
         tc_commit(&st_empty[svj % KM_STAGES]);
         return true;
       };
@@ -207,36 +224,44 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         const int kt = w / p.rows;
         int lo, hi;
         tiles_of(kt, lo, hi);
-        if (!mbar_wait(kv_full, static_cast<uint32_t>(nitem) & 1u, p.status) ||
-            !mbar_wait(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status)) {
+        if (!mbar_wait(kv_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
-        const int sv0 = sv;
-        for (int j = lo; j <= hi && ok; ++j, ++sv) {
-          const int sl = sv % KM_STAGES;
-          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(sv / KM_STAGES) & 1u, p.status) ||
-              !mbar_wait(s_empty, (static_cast<uint32_t>(sv) & 1u) ^ 1u, p.status)) {
-            ok = false;
-            break;
-          }
+        // the accumulators are free once the previous item's epilogue has read them (S / C may start before)
+        auto acc_free = [&]() { return mbar_wait(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status); };
+        // S / C of the tile with global index svj into buffer svj & 1 (free once the tile two back was read)
+        auto scores = [&](int svj) {
+          const int sl = svj % KM_STAGES, b = svj & 1;
+          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(svj / KM_STAGES) & 1u, p.status) ||
+              !mbar_wait(&s_empty[b], (static_cast<uint32_t>(svj >> 1) & 1u) ^ 1u, p.status))
+            return false;
           tc_fence_after();
           const uint32_t st = sbase + KM_RING + sl * KM_STAGE;
           const uint64_t kd = sdesc_kmajor_sw128(sbase + KM_K), vd = sdesc_kmajor_sw128(sbase + KM_V);
           const uint64_t qd = sdesc_kmajor_sw128(st + KM_SQ), hd = sdesc_kmajor_sw128(st + KM_SH);
+          const uint32_t ts = tmem + KM_TSC + b * 64;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(tmem + KM_TS, kd + 2u * k, qd + 2u * k, id_s, k > 0);
+          for (int k = 0; k < 4; ++k) tc_mma(ts, kd + 2u * k, qd + 2u * k, id_s, k > 0);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(tmem + KM_TC, vd + 2u * k, hd + 2u * k, id_s, k > 0);
-          tc_commit(s_full);
-          if (j > lo) ok = moments(sv - 1, j - 1 == lo);
+          for (int k = 0; k < 4; ++k) tc_mma(ts + 32, vd + 2u * k, hd + 2u * k, id_s, k > 0);
+          tc_commit(&s_full[b]);
+          return true;
+        };
+        // S / C run two tiles ahead of the moment MMAs, so a tile's moments issue as soon as its weights are
+        // written (not behind the next tile's loads)
+        const int sv0 = sv;
+        ok = scores(sv0);
+        if (ok && lo + 1 <= hi) ok = scores(sv0 + 1);
+        for (int j = lo; j <= hi && ok; ++j, ++sv) {
+          if (j == lo) ok = acc_free();
+          if (ok) ok = moments(sv, j == lo);
+          if (ok && j + 2 <= hi) ok = scores(sv + 2);
         }
-        if (ok) ok = moments(sv - 1, hi == lo);
         if (ok) {
           tc_commit(kv_empty);
           tc_commit(acc_full);
         }
-        (void)sv0;
       }
       tc_commit(drain);
       mbar_wait(drain, 0, p.status);
@@ -258,27 +283,29 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       tiles_of(kt, lo, hi);
       float s1 = 0.f, s2 = 0.f;
       for (int j = lo; j <= hi && ok; ++j, ++sv) {
-        if (!mbar_wait(s_full, static_cast<uint32_t>(sv) & 1u, p.status)) {
+        const int b = sv & 1;
+        if (!mbar_wait(&s_full[b], static_cast<uint32_t>(sv >> 1) & 1u, p.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        float s[32], c[32];
-        tmem_ld32(trow + KM_TS + half * 32, s);
-        tmem_ld32(trow + KM_TC + half * 32, c);
+        float s[16], c[16];
+        tmem_ld16(trow + KM_TSC + b * 64 + half * 16, s);
+        tmem_ld16(trow + KM_TSC + b * 64 + 32 + half * 16, c);
         tc_wait_ld();
-        reg_fence<32>(s);
-        reg_fence<32>(c);
+        reg_fence<16>(s);
+        reg_fence<16>(c);
         tc_fence_before();
-        mbar_arrive(s_empty);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[b]);
         const uint8_t* st = smem + KM_RING + (sv % KM_STAGES) * KM_STAGE;
-        const float* lse = reinterpret_cast<const float*>(st + KM_SLSE) + half * 32;
-        const float* ctr = reinterpret_cast<const float*>(st + KM_SCTR) + half * 32;
-        const int s0 = j * KM_R + half * 32;
-        const bool full = s0 >= tk - r + KM_B - 1 && s0 + 31 - (tk - r) <= p.window;
-        uint32_t pw1[16], pw2[16], pw2l[16], pp[16];
+        const float* lse = reinterpret_cast<const float*>(st + KM_SLSE) + half * 16;
+        const float* ctr = reinterpret_cast<const float*>(st + KM_SCTR) + half * 16;
+        const int s0 = j * KM_R + half * 16;
+        const bool full = s0 >= kt * KM_B + KM_B - 1 && s0 + 15 - kt * KM_B <= p.window;
+        uint32_t pw1[8], pw2[8], pw2l[8], pp[8];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
+        for (int e = 0; e < 16; e += 2) {
           float x1v[2], x2v[2], x2lv[2], av[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
@@ -302,22 +329,23 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
           pw2l[e / 2] = pack_bf16x2(x2lv[0], x2lv[1]);
           pp[e / 2] = pack_bf16x2(av[0], av[1]);
         }
-        if (!mbar_wait(w_empty, (static_cast<uint32_t>(sv) & 1u) ^ 1u, p.status)) {
+        if (!mbar_wait(&w_empty[b], (static_cast<uint32_t>(sv >> 1) & 1u) ^ 1u, p.status)) {
           ok = false;
           break;
         }
-        // row r, receivers half * 32 .. + 31: 16-byte chunks half * 4 + i of the 128-byte row, 128-byte swizzle
-        const uint32_t wrow = sbase + KM_W + r * 128;
+        // row r, receivers half * 16 .. + 15: 16-byte chunks half * 2 + i of the 64-byte row, 64-byte swizzle
+        const uint32_t wrow = sbase + KM_W + b * 4 * KM_WT + r * 64;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t off = static_cast<uint32_t>(((half * 4 + i) ^ (r & 7)) << 4);
+        for (int i = 0; i < 2; ++i) {
+          const uint32_t off = static_cast<uint32_t>(((half * 2 + i) ^ ((r >> 1) & 3)) << 4);
           km_st_v4(wrow + off, pw1[4 * i], pw1[4 * i + 1], pw1[4 * i + 2], pw1[4 * i + 3]);
-          km_st_v4(wrow + KM_KT + off, pw2[4 * i], pw2[4 * i + 1], pw2[4 * i + 2], pw2[4 * i + 3]);
-          km_st_v4(wrow + 2 * KM_KT + off, pw2l[4 * i], pw2l[4 * i + 1], pw2l[4 * i + 2], pw2l[4 * i + 3]);
-          km_st_v4(wrow + 3 * KM_KT + off, pp[4 * i], pp[4 * i + 1], pp[4 * i + 2], pp[4 * i + 3]);
+          km_st_v4(wrow + KM_WT + off, pw2[4 * i], pw2[4 * i + 1], pw2[4 * i + 2], pw2[4 * i + 3]);
+          km_st_v4(wrow + 2 * KM_WT + off, pw2l[4 * i], pw2l[4 * i + 1], pw2l[4 * i + 2], pw2l[4 * i + 3]);
+          km_st_v4(wrow + 3 * KM_WT + off, pp[4 * i], pp[4 * i + 1], pp[4 * i + 2], pp[4 * i + 3]);
         }
         fence_proxy_async_smem();
-        mbar_arrive(w_full);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_full[b]);
       }
       if (!ok) break;
       // the two halves' s1 / s2 of each key row
@@ -330,59 +358,64 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      float p2[32], r2[32], q2[32], xy[16];
-      tmem_ld32(trow + KM_TP2 + half * 32, p2);
-      tmem_ld32(trow + KM_TR2 + half * 32, r2);
-      tmem_ld32(trow + KM_TQ2 + half * 32, q2);
-      tmem_ld16(trow + KM_TXY + half * 16, xy);
-      tc_wait_ld();
-      reg_fence<32>(p2);
-      reg_fence<32>(r2);
-      reg_fence<32>(q2);
-      reg_fence<16>(xy);
-      // response per raw coordinate d = P and P + 32 of this half's pairs P = half * 16 + i
+      // response per raw coordinate d = P and P + 32 of this half's pairs P = half * 16 + g * 8 + i, 8 pairs at a time
       const int64_t ro = p.raw.at(row, tk, p.T);
       const float sqv = p.sq[static_cast<int64_t>(row) * p.T + tk];
       const float stepv = p.steps[static_cast<int64_t>(row) * p.T + tk];
       const float den = sqv / D + 1e-6f;
-      const float rs = rsqrtf(den);
-      float res[32];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int P = half * 16 + i;
-        const float px = p2[2 * i], py = p2[2 * i + 1], qx = q2[2 * i], qy = q2[2 * i + 1];
-        const float rx = r2[2 * i], ry = r2[2 * i + 1], cxy = xy[i];
-        const float cs = p.cosb[static_cast<int64_t>(tk) * 32 + P], sn = p.sinb[static_cast<int64_t>(tk) * 32 + P];
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const int d = P + 32 * hf;
-          const float ratio = (2.f * stepv * raw_at(p.raw, p.raw_bf16, ro + d) + stepv * stepv) / D / den;
-          const float ca = expm1f(-0.5f * log1pf(ratio));
-          const float cb = stepv * rs * (1.f + ca);
-          const float bu = cb * (hf ? sn : cs), bw = cb * (hf ? cs : -sn);
-          const float resp = px * bu + py * bw + qx * bu * bu + qy * bw * bw + 2.f * cxy * bu * bw +
-                             2.f * ca * (rx * bu + ry * bw) + a1 * ca + a2 * ca * ca;
-          res[hf * 16 + i] = resp / stepv;
-        }
-      }
+      // per key: ratio = (2 step raw + step^2) / 64 / den = ka raw + kb, response / step = response * rstep
+      const float inv = 1.f / (D * den);
+      const float ka = 2.f * stepv * inv, kb = stepv * stepv * inv, cbk = stepv * rsqrtf(den), rstep = 1.f / stepv;
       const int64_t oo = p.out.at(row, tk, p.T);
+#pragma unroll 1
+      for (int g8 = 0; g8 < 2; ++g8) {
+        float p2[16], r2[16], q2[16], xy[16];
+        tmem_ld16(trow + KM_TP2 + half * 32 + g8 * 16, p2);
+        tmem_ld16(trow + KM_TR2 + half * 32 + g8 * 16, r2);
+        tmem_ld16(trow + KM_TQ2 + half * 32 + g8 * 16, q2);
+        tmem_ld16(trow + KM_TXY + half * 16, xy);
+        tc_wait_ld();
+        reg_fence<16>(p2);
+        reg_fence<16>(r2);
+        reg_fence<16>(q2);
+        reg_fence<16>(xy);
+        const int P0 = half * 16 + g8 * 8;  // this chunk's 8 rotary pairs: cos / sin as two float4 each
+        const float4 c0 = *reinterpret_cast<const float4*>(p.cosb + static_cast<int64_t>(tk) * 32 + P0);
+        const float4 c1 = *reinterpret_cast<const float4*>(p.cosb + static_cast<int64_t>(tk) * 32 + P0 + 4);
+        const float4 n0 = *reinterpret_cast<const float4*>(p.sinb + static_cast<int64_t>(tk) * 32 + P0);
+        const float4 n1 = *reinterpret_cast<const float4*>(p.sinb + static_cast<int64_t>(tk) * 32 + P0 + 4);
+        const float csv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const float snv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {  // coordinates d = P + 32 hf
+          float res[8], rv[8];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int64_t o = oo + hf * 32 + half * 16;  // 16 consecutive coordinates, 16-byte aligned (host check)
-        if (p.out_bf16) {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out.data) + o);
+          for (int i = 0; i < 8; ++i) rv[i] = raw_at(p.raw, p.raw_bf16, ro + P0 + i + 32 * hf);
 #pragma unroll
-          for (int q = 0; q < 2; ++q)
-            dst[q] = make_uint4(pack_bf16x2(res[hf * 16 + 8 * q], res[hf * 16 + 8 * q + 1]),
-                                pack_bf16x2(res[hf * 16 + 8 * q + 2], res[hf * 16 + 8 * q + 3]),
-                                pack_bf16x2(res[hf * 16 + 8 * q + 4], res[hf * 16 + 8 * q + 5]),
-                                pack_bf16x2(res[hf * 16 + 8 * q + 6], res[hf * 16 + 8 * q + 7]));
-        } else {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out.data) + o);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_float4(res[hf * 16 + 4 * q], res[hf * 16 + 4 * q + 1], res[hf * 16 + 4 * q + 2],
-                                 res[hf * 16 + 4 * q + 3]);
+          for (int i = 0; i < 8; ++i) {
+            // ca = (1 + ratio)^(-1/2) - 1 = -ratio s^2 / (1 + s), s = (1 + ratio)^(-1/2): no cancellation for small
+            // ratios (the reference's expm1(-log1p(ratio) / 2))
+            const float ratio = fmaf(ka, rv[i], kb);
+            const float sr = rsqrtf(1.f + ratio);
+            const float ca = __fdividef(-ratio * sr * sr, 1.f + sr);
+            const float cb = cbk * (1.f + ca);
+            const float bu = cb * (hf ? snv[i] : csv[i]), bw = cb * (hf ? csv[i] : -snv[i]);
+            const float cxy = g8 ? xy[8 + i] : xy[i];
+            const float resp = p2[2 * i] * bu + p2[2 * i + 1] * bw + q2[2 * i] * bu * bu + q2[2 * i + 1] * bw * bw +
+                               2.f * cxy * bu * bw + 2.f * ca * (r2[2 * i] * bu + r2[2 * i + 1] * bw) + a1 * ca +
+                               a2 * ca * ca;
+            res[i] = resp * rstep;
+          }
+          const int64_t o = oo + hf * 32 + half * 16 + g8 * 8;  // 8 consecutive coordinates (host: 16-byte strides)
+          if (p.out_bf16) {
+            *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out.data) + o) =
+                make_uint4(pack_bf16x2(res[0], res[1]), pack_bf16x2(res[2], res[3]), pack_bf16x2(res[4], res[5]),
+                           pack_bf16x2(res[6], res[7]));
+          } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out.data) + o);
+            dst[0] = make_float4(res[0], res[1], res[2], res[3]);
+            dst[1] = make_float4(res[4], res[5], res[6], res[7]);
+          }
         }
       }
       // value sums: 32 columns of VA
@@ -391,7 +424,8 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       tc_wait_ld();
       reg_fence<32>(va);
       tc_fence_before();
-      mbar_arrive(acc_empty);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
       const int64_t vo = p.vout.at(row, tk, p.T) + half * 32;
       if (p.out_bf16) {
         uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.vout.data) + vo);
