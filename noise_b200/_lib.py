@@ -116,6 +116,8 @@ SIGNATURES = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_moment_key_scores_v', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_key_scan_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_key_scan_ws', ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_moment_key_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_moment_key_scores_ws', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),

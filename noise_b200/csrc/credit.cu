@@ -932,6 +932,21 @@ int km_map(CUtensorMap* map, const void* base, uint64_t n) {
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
+// [n, 64] rows of bf16 or fp32 with box_rows x box_cols boxes, 128-byte swizzle (box_cols x element = 128 bytes)
+int km_map_rows(CUtensorMap* map, const void* base, bool bf16, uint64_t n, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = tv_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), n};
+  cuuint64_t strides[1] = {D * (bf16 ? 2u : 4u)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                  const_cast<void*>(base), dims, strides, box, el, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
 // fp32 [rows, T] with KM_R x 1 boxes (per-receiver lse / center of one receiver tile)
 int km_map_f32(CUtensorMap* map, const float* base, uint64_t t, uint64_t rows) {
   auto fn = tv_encode();
@@ -1097,6 +1112,94 @@ int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const f
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
+size_t noise_key_scan_workspace_bytes(int rows, int tokens) {
+  if (rows < 1 || tokens < 1) return 0;
+  return 256 + 5 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16) +
+         4 * static_cast<size_t>(rows) * tokens * D * sizeof(float);
+}
+
+int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, const float* lse, const float* values,
+                      const float* hub, const float* center, const float* cos, const float* sin, int rows, int tokens,
+                      int window, float sigma, const noise_rows_t* key_out, const noise_rows_t* value_out,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (!qp || !kp || !k_raw || !lse || !values || !hub || !center || !cos || !sin || !key_out) return NOISE_ERR_ARGUMENT;
+  const bool with_values = value_out && value_out->data;
+  auto vec_ok = [&](const noise_rows_t& r) {  // fp32 views with 16-byte strides (the kernel's vector stores)
+    return r.data && rows_ok(r, true) && r.block_rows == 0;
+  };
+  if (tokens % KM_B || !vec_ok(*key_out) || (with_values && !vec_ok(*value_out)) || !a16(cos) || !a16(sin) ||
+      !a16(lse) || !a16(center))
+    return noise_key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, rows, tokens, window, sigma, key_out,
+                          value_out, stream);
+  if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
+  if (!a16(qp) || !a16(kp) || !a16(values) || !a16(hub)) return NOISE_ERR_ALIGN;
+  if (!workspace || workspace_bytes < noise_key_scan_workspace_bytes(rows, tokens)) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  const int sms = tv_sms();
+  if (sms < 1) return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  const int64_t n = static_cast<int64_t>(rows) * tokens;
+  __nv_bfloat16* f2 = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + 256);
+  __nv_bfloat16* g2 = f2 + n * D;
+  __nv_bfloat16* xy = g2 + n * D;
+  __nv_bfloat16* hi = xy + n * D;
+  __nv_bfloat16* lo = hi + n * D;
+  float* qt = reinterpret_cast<float*>(lo + n * D);  // tf32-rounded qp, kp, values, hub
+  float* kt = qt + n * D;
+  float* vt = kt + n * D;
+  float* ht = vt + n * D;
+  KeyMomMaps m;
+  int rc;
+  if ((rc = km_map_rows(&m.k, kt, false, n, 32, KM_B)) || (rc = km_map_rows(&m.v, vt, false, n, 32, KM_B)) ||
+      (rc = km_map_rows(&m.q, qt, false, n, 32, KM_R)) || (rc = km_map_rows(&m.h, ht, false, n, 32, KM_R)) ||
+      (rc = km_map(&m.f2, f2, n)) || (rc = km_map(&m.g2, g2, n)) || (rc = km_map(&m.xy, xy, n)) ||
+      (rc = km_map(&m.hi, hi, n)) || (rc = km_map(&m.lo, lo, n)) || (rc = km_map_f32(&m.lse, lse, tokens, rows)) ||
+      (rc = km_map_f32(&m.ctr, center, tokens, rows)))
+    return rc;
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  const int64_t n_pairs = n * 32;
+  keymom_features_kernel<<<static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8)),
+                           256, 0, s>>>(qp, n_pairs, f2, g2, xy);
+  {
+    Tf32Job job;
+    const float* src[4] = {qp, kp, values, hub};
+    float* dst[4] = {qt, kt, vt, ht};
+    for (int t = 0; t < 4; ++t) {
+      job.src[t] = reinterpret_cast<const float4*>(src[t]);
+      job.dst[t] = reinterpret_cast<float4*>(dst[t]);
+    }
+    const int64_t n4 = n * (D / 4);
+    tf32_round_kernel<<<static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8)), 256, 0,
+                        s>>>(job, n4);
+  }
+  if (with_values) {
+    const Rows hub_rows = stacked_rows(hub, tokens);
+    const int64_t n4 = n * (D / 4);
+    split_source_kernel<<<static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8)), 256,
+                          0, s>>>(hub_rows, tokens, n4, hi, lo);
+  }
+  if (cudaFuncSetAttribute(keymom_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           KmLayout<true>::SMEM))
+    return NOISE_ERR_CUDA;
+  KeyMomTcArgs a{};
+  a.T = tokens;
+  a.window = std::min(window, tokens);
+  a.rows = rows;
+  a.raw = stacked_rows(k_raw, tokens);
+  a.raw_bf16 = 0;
+  a.out_bf16 = 0;
+  a.sigma = sigma;
+  a.cosb = cos;
+  a.sinb = sin;
+  a.out = to_rows(*key_out);
+  a.vout = with_values ? to_rows(*value_out) : Rows{};
+  a.status = status;
+  const int items = tokens / KM_B * rows;
+  keymom_tc_kernel<true><<<std::min(items, sms), KM_THREADS, KmLayout<true>::SMEM, s>>>(m, a);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
 int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
                               int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
                               const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
@@ -1183,11 +1286,13 @@ int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, cons
       (rc = km_map(&m.g2, g2, n)) || (rc = km_map(&m.xy, xy, n)) || (rc = km_map_f32(&m.lse, lse, tokens, rows)) ||
       (rc = km_map_f32(&m.ctr, hub_out, tokens, rows)))
     return rc;
+  m.hi = m.lo = m.xy;  // unused by the identity-phase variant
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
   const int64_t n_pairs = n * 32;
   keymom_features_kernel<<<static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8)),
                            256, 0, s>>>(side, n_pairs, f2, g2, xy);
-  if (cudaFuncSetAttribute(keymom_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, KM_SMEM))
+  if (cudaFuncSetAttribute(keymom_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           KmLayout<false>::SMEM))
     return NOISE_ERR_CUDA;
   KeyMomTcArgs a{};
   a.T = tokens;
@@ -1204,7 +1309,7 @@ int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, cons
   a.vout = to_rows(*values_out);
   a.status = status;
   const int items = tokens / KM_B * rows;
-  keymom_tc_kernel<<<std::min(items, sms), KM_THREADS, KM_SMEM, s>>>(m, a);
+  keymom_tc_kernel<false><<<std::min(items, sms), KM_THREADS, KmLayout<false>::SMEM, s>>>(m, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

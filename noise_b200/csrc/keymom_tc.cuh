@@ -1,20 +1,24 @@
-// The identity phase's key moments on tcgen05 (sm_100a): per key t and raw key coordinate d the degree-2 moment
-// response of the receivers' softmax to a finite step of k_raw[t, d], and the value sums sum_s p hub_s (reference
-// train/speedrun/moment_kernels.py:368-462, moment_key_scores; bf16 operands, full causal window).
+// Key moments on tcgen05 (sm_100a): per key t and raw key coordinate d the degree-2 moment response of the receivers'
+// softmax to a finite step of k_raw[t, d], and the value sums sum_s p hub_s. Two variants of one kernel:
+//   IDENT  the identity phase's key moments (reference train/speedrun/moment_kernels.py:368-462,
+//          moment_key_scores): bf16 q / k / v / hub, full causal window, the key's sq and step given;
+//   SCAN   the key scan (moment_kernels.py:467-607, key_credits / key_and_raw_value_credits): fp32 q / k / v / hub
+//          with tf32 logits and scores (kind::tf32 MMAs), receivers 0 <= s - t <= window, the key's step from its
+//          own raw coordinates, and the optional value credits with hub split into bf16 hi + lo.
 //
-// Per key t and receiver s >= t (logit x = q_s . k_t / 8, p = e^(x - lse_s), c = hub_s . v_t - center_s):
+// Per key t and receiver s (logit x = q_s . k_t / 8, p = e^(x - lse_s), c = hub_s . v_t - center_s):
 //   w1 = p c, w2 = (p / 2 - p^2) c, w2l = w2 x;  s1 = sum w1 x, s2 = sum w2 x^2 (fp32)
 //   P2 = sum bf16(w1) f2_s, R2 = sum bf16(w2l) f2_s, Q2 = sum bf16(w2) g2_s, QXY = sum bf16(w2) xy_s,
-//   VA = sum bf16(p) hub_s
+//   VA = sum bf16(p) hub_s (IDENT) or sum bf16(p) (hi_s + lo_s) (SCAN)
 // with the receivers' pair features f2 = (x_i, y_i), g2 = (x_i^2, y_i^2), xy = x_i y_i of side / 8 (bf16, from
 // keymom_features_kernel), then per key the response of every raw coordinate through RoPE and the RMS norm.
 //
 // One work item = one 128-key tile of one row; receivers stream in 32-wide tiles. 320 threads, one CTA per SM:
-//   warp 0      TMA: K, V once per item; per receiver tile q, hub, f2, g2, xy (32 rows each) and lse / center
-//               into a 5-stage ring;
+//   warp 0      TMA: K, V once per item; per receiver tile q, hub, f2, g2, xy (and hi, lo) and lse / center into
+//               a ring (5 stages IDENT, 2 SCAN);
 //   warp 1      TMEM (512 columns): S = K Q^T and C = V H^T (32 columns each, double-buffered), the accumulators
 //               P2 (64), R2 (64), Q2 | QXY (96: g2 and xy as one 96-wide B operand) and VA (64); one lane issues
-//               S / C of tile j + 1 ahead of the moment MMAs of tile j (M = 128 keys, K = 32 receivers);
+//               S / C of tile j + AHEAD ahead of the moment MMAs of tile j (M = 128 keys, K = 32 receivers);
 //   warps 2..9  warp w: key rows of TMEM lane quarter w % 4, receivers half (w - 2) / 4 of each tile: the weights
 //               as bf16 into one of two 64-byte-swizzled shared buffers (the moment MMAs' A operands), so a tile's
 //               weights are written while the previous tile's moment MMAs run; at the item's end the response
@@ -25,22 +29,30 @@
 namespace noise {
 namespace credit {
 
-constexpr int KM_B = 128, KM_R = 32, KM_STAGES = 5, KM_THREADS = 320;
-constexpr int KM_KT = KM_B * 128;            // [128][64] bf16 key-side tile: 16 KB
-constexpr int KM_RT = KM_R * 128;            // [32][64] bf16 receiver-side tile: 4 KB
-constexpr int KM_WT = KM_B * KM_R * 2;       // [128][32] bf16 weight matrix (64-byte rows): 8 KB
-constexpr int KM_K = 0, KM_V = KM_KT;
-constexpr int KM_W = 2 * KM_KT;              // 2 buffers x (W1, W2, W2L, P)
-constexpr int KM_RING = KM_W + 8 * KM_WT;
-// stage: q, hub, f2, g2, xy (g2 and xy adjacent: one 96-wide MN-major operand), then lse, center (32 floats each)
-constexpr int KM_SQ = 0, KM_SH = KM_RT, KM_SF2 = 2 * KM_RT, KM_SG2 = 3 * KM_RT, KM_SXY = 4 * KM_RT,
-              KM_SLSE = 5 * KM_RT, KM_SCTR = KM_SLSE + 128;
-constexpr int KM_STAGE = 5 * KM_RT + 1024;
-constexpr int KM_SUMS = KM_RING + KM_STAGES * KM_STAGE;  // s1 / s2 per (half, key row): 2 x 2 x 128 floats
-constexpr int KM_BAR = KM_SUMS + 2048;
-constexpr int KM_SMEM = KM_BAR + 256 + 1024;
+constexpr int KM_B = 128, KM_R = 32, KM_THREADS = 320;
+constexpr int KM_KT = KM_B * 128;       // [128][64] bf16 (or [128][32] fp32) key-side tile: 16 KB
+constexpr int KM_RT = KM_R * 128;       // [32][64] bf16 (or [32][32] fp32) receiver-side tile: 4 KB
+constexpr int KM_WT = KM_B * KM_R * 2;  // [128][32] bf16 weight matrix (64-byte rows): 8 KB
 // TMEM columns: S / C buffer b at 64 b (S) and 64 b + 32 (C)
 constexpr uint32_t KM_TSC = 0, KM_TP2 = 128, KM_TR2 = 192, KM_TQ2 = 256, KM_TXY = 320, KM_TVA = 384;
+
+template <bool SCAN>
+struct KmLayout {
+  static constexpr int KV = SCAN ? 2 * KM_KT : KM_KT;  // K or V: fp32 as two 32-wide halves (128-byte rows)
+  static constexpr int RQ = SCAN ? 2 * KM_RT : KM_RT;  // q or hub of a receiver tile
+  static constexpr int K = 0, V = KV, W = 2 * KV;       // W: 2 buffers x (W1, W2, W2L, P)
+  static constexpr int RING = W + 8 * KM_WT;
+  // stage: q, hub, f2, g2, xy (g2 and xy adjacent: one 96-wide MN-major operand), [hi, lo], lse, center
+  static constexpr int SQ = 0, SH = RQ, SF2 = 2 * RQ, SG2 = SF2 + KM_RT, SXY = SG2 + KM_RT, SHI = SXY + KM_RT,
+                       SLO = SHI + KM_RT;
+  static constexpr int SLSE = SCAN ? SLO + KM_RT : SHI, SCTR = SLSE + 128;
+  static constexpr int STAGE = (SCTR + 128 + 1023) / 1024 * 1024;
+  static constexpr int STAGES = SCAN ? 2 : 5;
+  static constexpr int AHEAD = SCAN ? 1 : 2;  // S / C run this many receiver tiles ahead of the moment MMAs
+  static constexpr int SUMS = RING + STAGES * STAGE;  // s1, s2 and (SCAN) |raw|^2 per (half, key row)
+  static constexpr int BAR = SUMS + 3 * 2 * 128 * 4;
+  static constexpr int SMEM = BAR + 256 + 1024;
+};
 
 // K-major operand in 64-byte swizzled rows (32 bf16 of K per row): 8-row groups 512 bytes apart, layout type 4
 // (SWIZZLE_64B); the K step inside a row advances the start address by 32 bytes per 16 bf16 values.
@@ -54,13 +66,30 @@ __device__ __forceinline__ uint64_t km_sdesc_kmajor_sw64(uint32_t saddr) {
   return d;
 }
 
+// Instruction descriptor of tcgen05.mma kind::tf32: tf32 A and B (fp32 in shared memory), fp32 D, M x N.
+__host__ __device__ constexpr uint32_t km_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (K = 8 per instruction: 32 bytes of each row, as kind::f16's 16).
+__device__ __forceinline__ void km_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 struct KeyMomTcArgs {
   int T, window, rows;
   Rows raw;
   int raw_bf16, out_bf16;
-  const float *sq, *steps;     // [rows, T]
+  const float *sq, *steps;     // IDENT: [rows, T]
+  float sigma;                 // SCAN: step = sigma max(rms(k_raw[t]), 1e-6)
   const float *cosb, *sinb;    // [T, 32]
-  Rows out, vout;
+  Rows out, vout;              // vout.data NULL (SCAN): no value credits
   int* status;
 };
 
@@ -82,6 +111,30 @@ __global__ void __launch_bounds__(256) keymom_features_kernel(const float* __res
   }
 }
 
+// fp32 -> tf32 (round to nearest, ties away from zero) of up to four [n] fp32 arrays into copies: the key scan's
+// operands as the warp kernels and the lse / center pass round them, so the tcgen05 kind::tf32 MMAs (which read the
+// top 19 bits of each fp32 operand) see the same values.
+struct Tf32Job {
+  const float4* src[4];
+  float4* dst[4];
+};
+__global__ void __launch_bounds__(256) tf32_round_kernel(Tf32Job job, int64_t n4) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float4 v = job.src[t][i];
+      uint32_t r[4];
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[0]) : "f"(v.x));
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[1]) : "f"(v.y));
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[2]) : "f"(v.z));
+      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[3]) : "f"(v.w));
+      job.dst[t][i] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]),
+                                  __uint_as_float(r[3]));
+    }
+  }
+}
+
 __device__ __forceinline__ void km_st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -90,21 +143,24 @@ __device__ __forceinline__ void km_bar_sync() {  // named barrier 1 over the 256
 }
 
 struct KeyMomMaps {
-  CUtensorMap k, v;              // bf16 [rows * T, 64], 128-row boxes
-  CUtensorMap q, h, f2, g2, xy;  // bf16 [rows * T, 64], 32-row boxes
-  CUtensorMap lse, ctr;          // fp32 [rows, T], 32 x 1 boxes
+  CUtensorMap k, v;                // [rows * T, 64]: bf16 128 x 64 boxes (IDENT) or fp32 128 x 32 boxes (SCAN)
+  CUtensorMap q, h;                // [rows * T, 64]: bf16 32 x 64 boxes or fp32 32 x 32 boxes
+  CUtensorMap f2, g2, xy, hi, lo;  // bf16 [rows * T, 64], 32 x 64 boxes
+  CUtensorMap lse, ctr;            // fp32 [rows, T], 32 x 1 boxes
 };
 
+template <bool SCAN>
 __global__ void __launch_bounds__(KM_THREADS, 1)
     keymom_tc_kernel(const __grid_constant__ KeyMomMaps m, const __grid_constant__ KeyMomTcArgs p) {
+  using L = KmLayout<SCAN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + KM_BAR);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* kv_full = bar;
   uint64_t* kv_empty = bar + 1;
   uint64_t* st_full = bar + 2;               // STAGES
-  uint64_t* st_empty = st_full + KM_STAGES;  // STAGES
-  uint64_t* s_full = st_empty + KM_STAGES;   // 2 (S / C buffers)
+  uint64_t* st_empty = st_full + L::STAGES;  // STAGES
+  uint64_t* s_full = st_empty + L::STAGES;   // 2 (S / C buffers)
   uint64_t* s_empty = s_full + 2;            // 2
   uint64_t* w_full = s_empty + 2;            // 2 (weight buffers)
   uint64_t* w_empty = w_full + 2;            // 2
@@ -116,6 +172,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = p.T / KM_B, nrt = p.T / KM_R;
   const int items = nkt * p.rows;
+  const bool values = !SCAN || p.vout.data != nullptr;
   // item w: key tile w / rows (the first tiles have the most receivers: heaviest first) of row w % rows; its
   // receiver tiles run from the key tile's first receivers to the window's end
   auto tiles_of = [&](int kt, int& lo, int& hi) {
@@ -126,7 +183,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     mbar_init(kv_empty, 1);
-    for (int s = 0; s < KM_STAGES; ++s) {
+    for (int s = 0; s < L::STAGES; ++s) {
       mbar_init(&st_full[s], 1);
       mbar_init(&st_empty[s], 1);
     }
@@ -142,8 +199,8 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    const CUtensorMap* maps[9] = {&m.k, &m.v, &m.q, &m.h, &m.f2, &m.g2, &m.xy, &m.lse, &m.ctr};
-    for (int i = 0; i < 9; ++i) tma_prefetch_desc(maps[i]);
+    const CUtensorMap* maps[11] = {&m.k, &m.v, &m.q, &m.h, &m.f2, &m.g2, &m.xy, &m.lse, &m.ctr, &m.hi, &m.lo};
+    for (int i = 0; i < (SCAN && values ? 11 : 9); ++i) tma_prefetch_desc(maps[i]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, 512);
@@ -159,43 +216,56 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
     if (lane == 0) {
       int sv = 0, nitem = 0;
       bool ok = true;
+      const uint32_t stage_tx = 2 * L::RQ + 3 * KM_RT + (SCAN && values ? 2 * KM_RT : 0) + 2 * KM_R * 4;
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
         const int kt = w / p.rows, row = w % p.rows;
         const int row0 = row * p.T;
         int lo, hi;
         tiles_of(kt, lo, hi);
         if (!mbar_wait(kv_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status)) break;
-        mbar_arrive_expect_tx(kv_full, 2 * KM_KT);
-        tma_load_2d(smem + KM_K, &m.k, kv_full, 0, row0 + kt * KM_B);
-        tma_load_2d(smem + KM_V, &m.v, kv_full, 0, row0 + kt * KM_B);
+        mbar_arrive_expect_tx(kv_full, 2 * L::KV);
+        tma_load_2d(smem + L::K, &m.k, kv_full, 0, row0 + kt * KM_B);
+        tma_load_2d(smem + L::V, &m.v, kv_full, 0, row0 + kt * KM_B);
+        if constexpr (SCAN) {  // the fp32 rows' second 32-wide half
+          tma_load_2d(smem + L::K + KM_KT, &m.k, kv_full, 32, row0 + kt * KM_B);
+          tma_load_2d(smem + L::V + KM_KT, &m.v, kv_full, 32, row0 + kt * KM_B);
+        }
         for (int j = lo; j <= hi; ++j, ++sv) {
-          const int sl = sv % KM_STAGES;
-          if (!mbar_wait(&st_empty[sl], (static_cast<uint32_t>(sv / KM_STAGES) & 1u) ^ 1u, p.status)) {
+          const int sl = sv % L::STAGES;
+          if (!mbar_wait(&st_empty[sl], (static_cast<uint32_t>(sv / L::STAGES) & 1u) ^ 1u, p.status)) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + KM_RING + sl * KM_STAGE;
+          uint8_t* st = smem + L::RING + sl * L::STAGE;
           uint64_t* b = &st_full[sl];
           const int r = row0 + j * KM_R;
-          mbar_arrive_expect_tx(b, 5 * KM_RT + 2 * KM_R * 4);
-          tma_load_2d(st + KM_SQ, &m.q, b, 0, r);
-          tma_load_2d(st + KM_SH, &m.h, b, 0, r);
-          tma_load_2d(st + KM_SF2, &m.f2, b, 0, r);
-          tma_load_2d(st + KM_SG2, &m.g2, b, 0, r);
-          tma_load_2d(st + KM_SXY, &m.xy, b, 0, r);
-          tma_load_2d(st + KM_SLSE, &m.lse, b, j * KM_R, row);
-          tma_load_2d(st + KM_SCTR, &m.ctr, b, j * KM_R, row);
+          mbar_arrive_expect_tx(b, stage_tx);
+          tma_load_2d(st + L::SQ, &m.q, b, 0, r);
+          tma_load_2d(st + L::SH, &m.h, b, 0, r);
+          if constexpr (SCAN) {
+            tma_load_2d(st + L::SQ + KM_RT, &m.q, b, 32, r);
+            tma_load_2d(st + L::SH + KM_RT, &m.h, b, 32, r);
+            if (values) {
+              tma_load_2d(st + L::SHI, &m.hi, b, 0, r);
+              tma_load_2d(st + L::SLO, &m.lo, b, 0, r);
+            }
+          }
+          tma_load_2d(st + L::SF2, &m.f2, b, 0, r);
+          tma_load_2d(st + L::SG2, &m.g2, b, 0, r);
+          tma_load_2d(st + L::SXY, &m.xy, b, 0, r);
+          tma_load_2d(st + L::SLSE, &m.lse, b, j * KM_R, row);
+          tma_load_2d(st + L::SCTR, &m.ctr, b, j * KM_R, row);
         }
       }
       if (nitem > 0) mbar_wait(kv_full, static_cast<uint32_t>(nitem - 1) & 1u, p.status);
-      for (int j = sv - 1; j >= 0 && j >= sv - KM_STAGES; --j)
-        mbar_wait(&st_full[j % KM_STAGES], static_cast<uint32_t>(j / KM_STAGES) & 1u, p.status);
+      for (int j = sv - 1; j >= 0 && j >= sv - L::STAGES; --j)
+        mbar_wait(&st_full[j % L::STAGES], static_cast<uint32_t>(j / L::STAGES) & 1u, p.status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc_bf16(KM_B, KM_R);             // S, C: B = q / hub rows (K-major)
-      constexpr uint32_t id_f = idesc_bf16(KM_B, 64, false, true);  // P2, R2, VA: B MN-major
-      constexpr uint32_t id_q = idesc_bf16(KM_B, 96, false, true);  // Q2 | QXY
+      constexpr uint32_t id_s = SCAN ? km_idesc_tf32(KM_B, KM_R) : idesc_bf16(KM_B, KM_R);  // S, C (K-major B)
+      constexpr uint32_t id_f = idesc_bf16(KM_B, 64, false, true);   // P2, R2, VA: B MN-major
+      constexpr uint32_t id_q = idesc_bf16(KM_B, 96, false, true);   // Q2 | QXY
       int sv = 0, nitem = 0;
       bool ok = true;
       // the moment MMAs of the receiver tile with global index svj (the item's first when first)
@@ -203,21 +273,29 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         const int wb = svj & 1;
         if (!mbar_wait(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
         tc_fence_after();
-        const uint32_t st = sbase + KM_RING + (svj % KM_STAGES) * KM_STAGE;
-        const uint32_t w = sbase + KM_W + wb * 4 * KM_WT;  // W1, W2, W2L, P
+        const uint32_t st = sbase + L::RING + (svj % L::STAGES) * L::STAGE;
+        const uint32_t w = sbase + L::W + wb * 4 * KM_WT;  // W1, W2, W2L, P
 #pragma unroll
         for (int ks = 0; ks < KM_R / 16; ++ks) {
           const uint32_t acc = (first && ks == 0) ? 0u : 1u;
-          const uint64_t f2d = sdesc_mnmajor_sw128(st + KM_SF2 + ks * 2048, 16);
+          const uint64_t f2d = sdesc_mnmajor_sw128(st + L::SF2 + ks * 2048, 16);
           tc_mma(tmem + KM_TP2, km_sdesc_kmajor_sw64(w) + 2u * ks, f2d, id_f, acc);
           tc_mma(tmem + KM_TR2, km_sdesc_kmajor_sw64(w + 2 * KM_WT) + 2u * ks, f2d, id_f, acc);
           tc_mma(tmem + KM_TQ2, km_sdesc_kmajor_sw64(w + KM_WT) + 2u * ks,
-                 sdesc_mnmajor_sw128(st + KM_SG2 + ks * 2048, KM_RT), id_q, acc);
-          tc_mma(tmem + KM_TVA, km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks,
-                 sdesc_mnmajor_sw128(st + KM_SH + ks * 2048, 16), id_f, acc);
+                 sdesc_mnmajor_sw128(st + L::SG2 + ks * 2048, KM_RT), id_q, acc);
+          if constexpr (SCAN) {
+            if (values) {
+              const uint64_t pd = km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks;
+              tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SHI + ks * 2048, 16), id_f, acc);
+              tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SLO + ks * 2048, 16), id_f, 1u);
+            }
+          } else {
+            tc_mma(tmem + KM_TVA, km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks,
+                   sdesc_mnmajor_sw128(st + L::SH + ks * 2048, 16), id_f, acc);
+          }
         }
         tc_commit(&w_empty[wb]);
-        tc_commit(&st_empty[svj % KM_STAGES]);
+        tc_commit(&st_empty[svj % L::STAGES]);
         return true;
       };
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
@@ -232,31 +310,45 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         auto acc_free = [&]() { return mbar_wait(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status); };
         // S / C of the tile with global index svj into buffer svj & 1 (free once the tile two back was read)
         auto scores = [&](int svj) {
-          const int sl = svj % KM_STAGES, b = svj & 1;
-          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(svj / KM_STAGES) & 1u, p.status) ||
+          const int sl = svj % L::STAGES, b = svj & 1;
+          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(svj / L::STAGES) & 1u, p.status) ||
               !mbar_wait(&s_empty[b], (static_cast<uint32_t>(svj >> 1) & 1u) ^ 1u, p.status))
             return false;
           tc_fence_after();
-          const uint32_t st = sbase + KM_RING + sl * KM_STAGE;
-          const uint64_t kd = sdesc_kmajor_sw128(sbase + KM_K), vd = sdesc_kmajor_sw128(sbase + KM_V);
-          const uint64_t qd = sdesc_kmajor_sw128(st + KM_SQ), hd = sdesc_kmajor_sw128(st + KM_SH);
+          const uint32_t st = sbase + L::RING + sl * L::STAGE;
           const uint32_t ts = tmem + KM_TSC + b * 64;
+          if constexpr (SCAN) {  // tf32: 8 K-steps of 8, 4 per 32-wide half
 #pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(ts, kd + 2u * k, qd + 2u * k, id_s, k > 0);
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t ho = (k >> 2);
+              km_mma_tf32(ts, sdesc_kmajor_sw128(sbase + L::K + ho * KM_KT) + 2u * (k & 3),
+                          sdesc_kmajor_sw128(st + L::SQ + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
+            }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(ts + 32, vd + 2u * k, hd + 2u * k, id_s, k > 0);
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t ho = (k >> 2);
+              km_mma_tf32(ts + 32, sdesc_kmajor_sw128(sbase + L::V + ho * KM_KT) + 2u * (k & 3),
+                          sdesc_kmajor_sw128(st + L::SH + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
+            }
+          } else {
+            const uint64_t kd = sdesc_kmajor_sw128(sbase + L::K), vd = sdesc_kmajor_sw128(sbase + L::V);
+            const uint64_t qd = sdesc_kmajor_sw128(st + L::SQ), hd = sdesc_kmajor_sw128(st + L::SH);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tc_mma(ts, kd + 2u * k, qd + 2u * k, id_s, k > 0);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tc_mma(ts + 32, vd + 2u * k, hd + 2u * k, id_s, k > 0);
+          }
           tc_commit(&s_full[b]);
           return true;
         };
-        // S / C run two tiles ahead of the moment MMAs, so a tile's moments issue as soon as its weights are
+        // S / C run AHEAD tiles ahead of the moment MMAs, so a tile's moments issue as soon as its weights are
         // written (not behind the next tile's loads)
         const int sv0 = sv;
-        ok = scores(sv0);
-        if (ok && lo + 1 <= hi) ok = scores(sv0 + 1);
+        for (int a = 0; a < L::AHEAD && ok && lo + a <= hi; ++a) ok = scores(sv0 + a);
         for (int j = lo; j <= hi && ok; ++j, ++sv) {
           if (j == lo) ok = acc_free();
           if (ok) ok = moments(sv, j == lo);
-          if (ok && j + 2 <= hi) ok = scores(sv + 2);
+          if (ok && j + L::AHEAD <= hi) ok = scores(sv + L::AHEAD);
         }
         if (ok) {
           tc_commit(kv_empty);
@@ -271,7 +363,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
     const int r = quarter * 32 + lane;  // key row of the tile
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t trow = tmem + lane_base;
-    float* sums = reinterpret_cast<float*>(smem + KM_SUMS);  // [half][2][128]
+    float* sums = reinterpret_cast<float*>(smem + L::SUMS);  // [half][3][128]: s1, s2, |raw|^2
     constexpr float SL2 = 0.125f * 1.4426950408889634f;
     constexpr float L2E = 1.4426950408889634f;
     int sv = 0, nitem = 0;
@@ -298,9 +390,9 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[b]);
-        const uint8_t* st = smem + KM_RING + (sv % KM_STAGES) * KM_STAGE;
-        const float* lse = reinterpret_cast<const float*>(st + KM_SLSE) + half * 16;
-        const float* ctr = reinterpret_cast<const float*>(st + KM_SCTR) + half * 16;
+        const uint8_t* st = smem + L::RING + (sv % L::STAGES) * L::STAGE;
+        const float* lse = reinterpret_cast<const float*>(st + L::SLSE) + half * 16;
+        const float* ctr = reinterpret_cast<const float*>(st + L::SCTR) + half * 16;
         const int s0 = j * KM_R + half * 16;
         const bool full = s0 >= kt * KM_B + KM_B - 1 && s0 + 15 - kt * KM_B <= p.window;
         uint32_t pw1[8], pw2[8], pw2l[8], pp[8];
@@ -334,7 +426,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
           break;
         }
         // row r, receivers half * 16 .. + 15: 16-byte chunks half * 2 + i of the 64-byte row, 64-byte swizzle
-        const uint32_t wrow = sbase + KM_W + b * 4 * KM_WT + r * 64;
+        const uint32_t wrow = sbase + L::W + b * 4 * KM_WT + r * 64;
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const uint32_t off = static_cast<uint32_t>(((half * 2 + i) ^ ((r >> 1) & 3)) << 4);
@@ -349,20 +441,40 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       }
       if (!ok) break;
       // the two halves' s1 / s2 of each key row
-      sums[(half * 2) * 128 + r] = s1;
-      sums[(half * 2 + 1) * 128 + r] = s2;
+      // this thread's 32 raw coordinates d = half * 16 + i and 32 + half * 16 + i (and SCAN: their square sum)
+      const int64_t ro = p.raw.at(row, tk, p.T);
+      float rv[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        rv[i] = raw_at(p.raw, p.raw_bf16, ro + half * 16 + i);
+        rv[16 + i] = raw_at(p.raw, p.raw_bf16, ro + 32 + half * 16 + i);
+      }
+      float rsq = 0.f;
+      if constexpr (SCAN) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rsq = fmaf(rv[i], rv[i], rsq);
+      }
+      sums[(half * 3) * 128 + r] = s1;
+      sums[(half * 3 + 1) * 128 + r] = s2;
+      sums[(half * 3 + 2) * 128 + r] = rsq;
       km_bar_sync();
-      const float a1 = sums[r] + sums[2 * 128 + r], a2 = sums[128 + r] + sums[3 * 128 + r];
+      const float a1 = sums[r] + sums[3 * 128 + r], a2 = sums[128 + r] + sums[4 * 128 + r];
+      const float rsq_all = sums[2 * 128 + r] + sums[5 * 128 + r];
       if (!mbar_wait(acc_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
       // response per raw coordinate d = P and P + 32 of this half's pairs P = half * 16 + g * 8 + i, 8 pairs at a time
-      const int64_t ro = p.raw.at(row, tk, p.T);
-      const float sqv = p.sq[static_cast<int64_t>(row) * p.T + tk];
-      const float stepv = p.steps[static_cast<int64_t>(row) * p.T + tk];
-      const float den = sqv / D + 1e-6f;
+      float stepv, den;
+      if constexpr (SCAN) {  // the key's own step: sigma max(rms(k_raw[t]), 1e-6), RMS eps = finfo(fp32).eps
+        const float sqv = rsq_all / D;
+        stepv = p.sigma * fmaxf(sqrtf(sqv), 1e-6f);
+        den = sqv + 1.1920928955078125e-07f;
+      } else {
+        stepv = p.steps[static_cast<int64_t>(row) * p.T + tk];
+        den = p.sq[static_cast<int64_t>(row) * p.T + tk] / D + 1e-6f;
+      }
       // per key: ratio = (2 step raw + step^2) / 64 / den = ka raw + kb, response / step = response * rstep
       const float inv = 1.f / (D * den);
       const float ka = 2.f * stepv * inv, kb = stepv * stepv * inv, cbk = stepv * rsqrtf(den), rstep = 1.f / stepv;
@@ -388,14 +500,12 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         const float snv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
 #pragma unroll 1
         for (int hf = 0; hf < 2; ++hf) {  // coordinates d = P + 32 hf
-          float res[8], rv[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) rv[i] = raw_at(p.raw, p.raw_bf16, ro + P0 + i + 32 * hf);
+          float res[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             // ca = (1 + ratio)^(-1/2) - 1 = -ratio s^2 / (1 + s), s = (1 + ratio)^(-1/2): no cancellation for small
             // ratios (the reference's expm1(-log1p(ratio) / 2))
-            const float ratio = fmaf(ka, rv[i], kb);
+            const float ratio = fmaf(ka, (g8 ? (hf ? rv[24 + i] : rv[8 + i]) : (hf ? rv[16 + i] : rv[i])), kb);
             const float sr = rsqrtf(1.f + ratio);
             const float ca = __fdividef(-ratio * sr * sr, 1.f + sr);
             const float cb = cbk * (1.f + ca);
@@ -420,12 +530,18 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       }
       // value sums: 32 columns of VA
       float va[32];
-      tmem_ld32(trow + KM_TVA + half * 32, va);
-      tc_wait_ld();
-      reg_fence<32>(va);
+      if (values) {
+        tmem_ld32(trow + KM_TVA + half * 32, va);
+        tc_wait_ld();
+        reg_fence<32>(va);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
+      if (!values) {
+        km_bar_sync();  // both halves have read sums before the next item overwrites them
+        continue;
+      }
       const int64_t vo = p.vout.at(row, tk, p.T) + half * 32;
       if (p.out_bf16) {
         uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.vout.data) + vo);

@@ -110,10 +110,12 @@ def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, lay
 # --- key credits ----------------------------------------------------------------------------------------------------
 
 def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, with_values=False, out_heads=1, key=None,
-             layers=None):
+             layers=None, tc=True):
     """The key credits (and with_values the raw value credits), stacked (rows, T, D) or by token
     (rows // out_heads, T, out_heads * D), into ``key`` when given (moment_kernels._key_scan). The signature of the
-    reference's KEY_IMPL plug-in; returns (key, raw_value) (raw_value is key when with_values is False)."""
+    reference's KEY_IMPL plug-in; returns (key, raw_value) (raw_value is key when with_values is False). T % 128 == 0
+    runs on the tcgen05 kernel (``tc=False``: the warp-MMA kernel, for comparison); its workspace rides on the key
+    output as ``_noise_workspace``."""
     h, t, d = k_raw.shape
     qp, kp, k_raw, values, hub = (_c(z, torch.float32) for z in (qp, kp, k_raw, values, hub))
     lse, center = _c(lse, torch.float32), _c(center, torch.float32)
@@ -124,11 +126,23 @@ def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, w
     raw_value = qp.new_empty(shape) if with_values else None
     key_rows = _rows(key, out_heads, layers)
     val_rows = _rows(raw_value, out_heads, layers) if with_values else _lib.Rows()
-    _check(_lib.lib().noise_key_scan(qp.data_ptr(), kp.data_ptr(), k_raw.data_ptr(), lse.data_ptr(), values.data_ptr(),
-                                     hub.data_ptr(), center.data_ptr(), cos.data_ptr(), sin.data_ptr(), h, t, window,
-                                     float(sigma), ctypes.byref(key_rows), ctypes.byref(val_rows), _stream(qp)),
-           'noise_key_scan')
+    ws = None
+    if tc and t % 128 == 0:
+        L = _lib.lib()
+        nbytes = L.noise_key_scan_workspace_bytes(h, t)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=qp.device)
+        _check(L.noise_key_scan_ws(qp.data_ptr(), kp.data_ptr(), k_raw.data_ptr(), lse.data_ptr(), values.data_ptr(),
+                                   hub.data_ptr(), center.data_ptr(), cos.data_ptr(), sin.data_ptr(), h, t, window,
+                                   float(sigma), ctypes.byref(key_rows), ctypes.byref(val_rows), ws.data_ptr(), nbytes,
+                                   _stream(qp)), 'noise_key_scan_ws')
+    else:
+        _check(_lib.lib().noise_key_scan(qp.data_ptr(), kp.data_ptr(), k_raw.data_ptr(), lse.data_ptr(),
+                                         values.data_ptr(), hub.data_ptr(), center.data_ptr(), cos.data_ptr(),
+                                         sin.data_ptr(), h, t, window, float(sigma), ctypes.byref(key_rows),
+                                         ctypes.byref(val_rows), _stream(qp)), 'noise_key_scan')
     k_out = key.view(h, t, d) if out_heads == 1 and layers is None else key
+    if ws is not None:
+        key._noise_workspace = k_out._noise_workspace = ws
     if not with_values:
         return k_out, k_out
     return k_out, raw_value.view(h, t, d) if out_heads == 1 else raw_value

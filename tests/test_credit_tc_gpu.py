@@ -1,6 +1,7 @@
 """The tcgen05 credit kernels (bf16 operands, T % 128 == 0) against the dense CPU oracle (oracle/credit.py, with the
 kernels' bf16 roundings) and against the warp-MMA kernels on the same inputs: the value pass (noise_value_pass_ws),
-lse / center (noise_implicit_key_context_ws) and the identity phase's key moments (noise_moment_key_scores_ws).
+lse / center (noise_implicit_key_context_ws), the identity phase's key moments (noise_moment_key_scores_ws) and the
+key scan (noise_key_scan_ws, tf32 logits and scores).
 
 Value pass:
 Stated tolerance: 2e-3 of the largest |reference| of the output (bf16 probabilities; the two GPU kernels round the
@@ -182,3 +183,44 @@ def test_key_moments_full_size(mk):
     from noise_b200 import _lib
     assert _lib.read_status(ws) == 0
     assert rel(out, wout) < 5e-3 and rel(vals, wvals) < 2e-3
+
+
+# --- key scan (noise_key_scan_ws) -------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize('rows,t,window,with_values', [(2, 256, 128, True), (3, 384, 320, False), (2, 512, 64, True),
+                                                       (1, 384, 2048, True)])
+def test_key_scan_against_oracle_and_warp_kernel(mk, rows, t, window, with_values):
+    """Key credits within 5e-3 of max |ref| and raw value credits within 2e-3 of the warp kernel (same tf32-rounded
+    operands), windows below, across and beyond the tiles; against the fp64 oracle (exact logits) the value credits
+    within 4e-3 (the tf32 logits' error averages over fewer receivers in a 64-wide window)."""
+    from noise_b200 import _lib
+    x = credit_inputs(rows, t, seed=31 * rows + window)
+    d = {k: v.to(DEV) for k, v in x.items()}
+    w_ctx = window if window % 64 == 0 else 512
+    lse, center = mk.implicit_key_context_edges_impl(d['qp'], d['kp'], d['values'], d['hub'], w_ctx)
+    args = (d['qp'], d['kp'], d['k_raw'], lse, d['values'], d['hub'], center, d['cos'], d['sin'], window, 0.003)
+    key, val = mk.key_scan(*args, with_values=with_values)
+    assert _lib.read_status(key._noise_workspace) == 0
+    wkey, wval = mk.key_scan(*args, with_values=with_values, tc=False)
+    assert rel(key, wkey) < 5e-3
+    ref = credit.key_scan(x['qp'], x['kp'], x['k_raw'], lse.cpu(), x['values'], x['hub'], center.cpu(), x['cos'],
+                          x['sin'], window, 0.003, with_values=with_values, emulate=True)
+    if with_values:
+        ref, ref_val = ref
+        assert rel(val, wval) < 2e-3 and rel(val, ref_val) < 4e-3
+    assert rel(key, ref) < 5e-3
+
+
+def test_key_scan_full_size(mk):
+    """rows 128, T 2048 (config 3) at windows 2048 and 1024, with the raw value credits: the tcgen05 and warp kernels
+    agree (5e-3 / 2e-3 of max |ref|)."""
+    from noise_b200 import _lib
+    x = credit_inputs(128, 2048, seed=12)
+    d = {k: v.to(DEV) for k, v in x.items()}
+    for window in (2048, 1024):
+        lse, center = mk.implicit_key_context_edges_impl(d['qp'], d['kp'], d['values'], d['hub'], window)
+        args = (d['qp'], d['kp'], d['k_raw'], lse, d['values'], d['hub'], center, d['cos'], d['sin'], window, 0.003)
+        key, val = mk.key_scan(*args, with_values=True)
+        wkey, wval = mk.key_scan(*args, with_values=True, tc=False)
+        assert _lib.read_status(key._noise_workspace) == 0
+        assert rel(key, wkey) < 5e-3 and rel(val, wval) < 2e-3
