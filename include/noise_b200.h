@@ -226,6 +226,21 @@ int noise_moment_query_scores_v(const void* q, const void* k, const void* v, con
                                 const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
                                 int window, const noise_rows_t* out, int out_dtype, void* stream);
 
+/* Bytes of the caller's workspace for noise_moment_query_scores_ws: a 256-byte status block, then the keys' pair
+ * features (bf16 [rows, T, 64] x 3). 0 for rows < 1 or tokens < 1. */
+size_t noise_moment_query_scores_workspace_bytes(int rows, int tokens);
+
+/* noise_moment_query_scores_v with a caller workspace (256-byte aligned): T % 128 == 0 with an out view whose strides
+ * are 16-byte multiples runs on tcgen05 (a pass writing the keys' pair features as bf16, then one persistent kernel per
+ * 128-query tile: S = Q K^T and the scores H V^T into TMEM, the four moment weights as bf16 A operands, the numerator,
+ * denominator and logit-weighted moments as 160- and 64-wide tcgen05 MMAs, the response epilogue from TMEM); anything
+ * else falls through to noise_moment_query_scores_v. Same results (moment_kernels.py:197-365). */
+int noise_moment_query_scores_ws(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                                 int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                                 const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                                 int window, const noise_rows_t* out, int out_dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * The seed-rebuilt ES update (reference archive/10M/train/val/eggroll.py:151-167).
  * ------------------------------------------------------------------------------------------------------------- */

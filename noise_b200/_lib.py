@@ -121,6 +121,9 @@ SIGNATURES = [
     ('noise_moment_key_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_moment_key_scores_ws', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_moment_query_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ('noise_moment_query_scores_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_moment_query_scores_v', ctypes.c_int,
      [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_pack_heads', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),

@@ -881,6 +881,7 @@ static bool view_ok(const noise_rows_t& r, bool bf16, bool pairs) {
 
 #include "context_tc.cuh"
 #include "keymom_tc.cuh"
+#include "querymom_tc.cuh"
 #include "value_tc.cuh"
 
 using namespace noise::credit;
@@ -1357,6 +1358,79 @@ int noise_moment_query_scores_v(const void* q, const void* k, const void* v, con
   a.window = window < tokens ? window : tokens;
   if (cudaFuncSetAttribute(query_moments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q_SMEM)) return NOISE_ERR_CUDA;
   query_moments_kernel<<<dim3(tokens / 64, 2 * rows), 128, Q_SMEM, static_cast<cudaStream_t>(stream)>>>(a);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_moment_query_scores_workspace_bytes(int rows, int tokens) {
+  if (rows < 1 || tokens < 1) return 0;
+  return 256 + 3 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16);
+}
+
+int noise_moment_query_scores_ws(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,
+                                 int raw_dtype, const float* sq, const float* side, const float* cos, const float* sin,
+                                 const float* lse, const float* hub_out, const float* steps, int rows, int tokens,
+                                 int window, const noise_rows_t* out, int out_dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !hub || !raw || !sq || !side || !cos || !sin || !lse || !hub_out || !steps || !out)
+    return NOISE_ERR_ARGUMENT;
+  if ((raw_dtype != NOISE_DTYPE_F32 && raw_dtype != NOISE_DTYPE_BF16) ||
+      (out_dtype != NOISE_DTYPE_F32 && out_dtype != NOISE_DTYPE_BF16))
+    return NOISE_ERR_ARGUMENT;
+  const bool ob = out_dtype == NOISE_DTYPE_BF16;
+  // the tcgen05 kernel stores 8 consecutive outputs per vector: every view stride a 16-byte multiple
+  auto vec_ok = [&](const noise_rows_t& r) {
+    const int64_t es = ob ? 2 : 4;
+    return r.data && a16(r.data) && (r.layer_stride * es) % 16 == 0 && (r.token_stride * es) % 16 == 0 &&
+           (r.block_rows == 0 || (r.gpu_stride * es) % 16 == 0);
+  };
+  if (tokens % QM_B || !vec_ok(*out) || !a16(cos) || !a16(sin))
+    return noise_moment_query_scores_v(q, k, v, hub, raw, raw_dtype, sq, side, cos, sin, lse, hub_out, steps, rows,
+                                       tokens, window, out, out_dtype, stream);
+  if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
+  if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) ||
+      !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) || !view_ok(*out, ob, false))
+    return NOISE_ERR_ALIGN;
+  if (!workspace || workspace_bytes < noise_moment_query_scores_workspace_bytes(rows, tokens))
+    return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  const int sms = tv_sms();
+  if (sms < 1) return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  const int64_t n = static_cast<int64_t>(rows) * tokens;
+  __nv_bfloat16* fa = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + 256);
+  __nv_bfloat16* fb = fa + n * D;
+  __nv_bfloat16* fc = fb + n * D;
+  QueryMomMaps m;
+  int rc;
+  if ((rc = tv_map(&m.q, q, true, D, n)) || (rc = tv_map(&m.h, hub, true, D, n)) || (rc = km_map(&m.k, k, n)) ||
+      (rc = km_map(&m.v, v, n)) || (rc = km_map(&m.fa, fa, n)) || (rc = km_map(&m.fb, fb, n)) ||
+      (rc = km_map(&m.fc, fc, n)))
+    return rc;
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  const int64_t n_pairs = n * 32;
+  querymom_features_kernel<<<static_cast<int>(
+                                 std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8)),
+                             256, 0, s>>>(side, n_pairs, fa, fb, fc);
+  if (cudaFuncSetAttribute(querymom_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, QM_SMEM))
+    return NOISE_ERR_CUDA;
+  QueryMomTcArgs a{};
+  a.T = tokens;
+  a.window = std::min(window, tokens);
+  a.rows = rows;
+  a.raw = to_rows(*raw);
+  a.raw_bf16 = raw_dtype == NOISE_DTYPE_BF16;
+  a.out_bf16 = ob;
+  a.sq = sq;
+  a.steps = steps;
+  a.lse = lse;
+  a.hub_out = hub_out;
+  a.cosb = cos;
+  a.sinb = sin;
+  a.out = to_rows(*out);
+  a.status = status;
+  const int items = tokens / QM_B * rows;
+  querymom_tc_kernel<<<std::min(items, sms), QM_THREADS, QM_SMEM, s>>>(m, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

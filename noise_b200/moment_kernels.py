@@ -178,7 +178,10 @@ def _raw4(raw, rows, t):
 
 
 def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, window=None, out_heads=0,
-                             layers=None):
+                             layers=None, tc=True):
+    """The query credits into out; T % 128 == 0 runs on the tcgen05 kernel when the output view allows 16-byte
+    stores (``tc=False``: the warp-MMA kernel, for comparison). Returns the workspace (its first int is the device
+    status word) or None."""
     rows, t, d = q.shape
     if d != 64:
         raise ValueError('head_dim 64 only (the reference asserts it)')
@@ -197,11 +200,22 @@ def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out
         m = out.shape[2]
         o, dt = _blocked(out, rows, m, blocks), _DT[out.dtype]
     rv = _blocked(raw, rows, m, blocks)
+    if tc and t % 128 == 0:
+        L = _lib.lib()
+        nbytes = L.noise_moment_query_scores_workspace_bytes(rows, t)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        _check(L.noise_moment_query_scores_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
+                                              ctypes.byref(rv), _DT[raw.dtype], sq.data_ptr(), side.data_ptr(),
+                                              cos.data_ptr(), sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(),
+                                              steps.data_ptr(), rows, t, window, ctypes.byref(o), dt, ws.data_ptr(),
+                                              nbytes, _stream(q)), 'noise_moment_query_scores_ws')
+        return ws
     _check(_lib.lib().noise_moment_query_scores_v(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(),
                                                   ctypes.byref(rv), _DT[raw.dtype], sq.data_ptr(), side.data_ptr(),
                                                   cos.data_ptr(), sin.data_ptr(), lse.data_ptr(), hub_out.data_ptr(),
                                                   steps.data_ptr(), rows, t, window, ctypes.byref(o), dt, _stream(q)),
            'noise_moment_query_scores_v')
+    return None
 
 
 def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, steps, out, values, tc=True):

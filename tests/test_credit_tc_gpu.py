@@ -224,3 +224,51 @@ def test_key_scan_full_size(mk):
         wkey, wval = mk.key_scan(*args, with_values=True, tc=False)
         assert _lib.read_status(key._noise_workspace) == 0
         assert rel(key, wkey) < 5e-3 and rel(val, wval) < 2e-3
+
+
+# --- query moments (noise_moment_query_scores_ws) ---------------------------------------------------------------------
+
+@pytest.mark.parametrize('rows,t,window', [(2, 256, 256), (3, 384, 128), (2, 512, 320), (1, 384, 2048)])
+def test_query_moments_against_oracle_and_warp_kernel(mk, rows, t, window):
+    """Query credits within 1e-2 of max |ref| (bf16-rounded outputs, as the warp kernel's tests) against the oracle
+    and the warp kernel, bf16 out (1, rows, T, 64); windows below and beyond the tiles."""
+    x = credit_inputs(rows, t, seed=57 * rows + window)
+    d = {k: v.to(DEV) for k, v in x.items()}
+    b = {k: d[k].bfloat16() for k in ('qp', 'kp', 'values', 'hub')}
+    w_ctx = window if window % 64 == 0 else 512
+    lse, center = mk.implicit_key_context_edges_impl(b["qp"], b["kp"], b["values"], b["hub"], min(w_ctx, t))
+    sq = x['q_raw'].square().sum(-1)
+    steps = 0.01 * (sq / 64).sqrt().clamp(min=1e-6)
+    args = (b['qp'], b['kp'], b['values'], b['hub'], d['q_raw'].unsqueeze(0), sq.to(DEV), d['kp'], d['cos'],
+            d['sin'], lse, center, steps.to(DEV))
+    out = torch.empty(1, rows, t, 64, dtype=torch.bfloat16, device=DEV)
+    ws = mk.moment_query_scores_impl(*args, out, window)
+    assert ws is not None
+    from noise_b200 import _lib
+    assert _lib.read_status(ws) == 0
+    wout = torch.empty_like(out)
+    assert mk.moment_query_scores_impl(*args, wout, window, tc=False) is None
+    assert rel(out[0].float(), wout[0].float()) < 1e-2
+    bd = {k: x[k].bfloat16().double() for k in ('qp', 'kp', 'values', 'hub')}
+    ref = credit.moment_query_scores(bd['qp'], bd['kp'], bd['values'], bd['hub'], x['q_raw'], sq, x['kp'], x['cos'],
+                                     x['sin'], lse.cpu(), center.cpu(), steps, window, emulate=True)
+    assert rel(out[0].float(), ref) < 1e-2
+
+
+def test_query_moments_full_size(mk):
+    """rows 128, T 2048 (config 3), fp32 out: the tcgen05 and warp kernels agree within 1e-2 of max |ref|."""
+    x = credit_inputs(128, 2048, seed=21)
+    d = {k: v.to(DEV) for k, v in x.items()}
+    b = {k: d[k].bfloat16() for k in ('qp', 'kp', 'values', 'hub')}
+    lse, center = mk.implicit_key_context_edges_impl(b['qp'], b['kp'], b['values'], b['hub'], 2048)
+    sq = d['q_raw'].square().sum(-1)
+    steps = 0.01 * (sq / 64).sqrt().clamp(min=1e-6)
+    args = (b['qp'], b['kp'], b['values'], b['hub'], d['q_raw'].unsqueeze(0), sq, d['kp'], d['cos'], d['sin'], lse,
+            center, steps)
+    out = torch.empty(1, 128, 2048, 64, device=DEV)
+    wout = torch.empty_like(out)
+    ws = mk.moment_query_scores_impl(*args, out, 2048)
+    mk.moment_query_scores_impl(*args, wout, 2048, tc=False)
+    from noise_b200 import _lib
+    assert _lib.read_status(ws) == 0
+    assert rel(out, wout) < 1e-2
