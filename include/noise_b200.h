@@ -318,7 +318,8 @@ typedef struct {
 int noise_head_prep(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
                     float sigma, float eps, const noise_head_prep_t* out, void* stream);
 
-/* Bytes of scratch noise_id_head_scores needs. */
+/* Bytes of scratch noise_id_head_scores needs (its first int is the device status word of the tcgen05 moment
+ * kernels). */
 size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n);
 
 /* run.py's id_head_scores (:3799-3803): noise_head_prep, then the query-moment credits (full causal window) into

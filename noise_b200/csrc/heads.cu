@@ -300,9 +300,14 @@ int noise_head_prep(const void* got, int world, int layers, int n, const float* 
   return launch_prep(got, world, layers, n, cos, sin, tokens, sigma, eps, *out, static_cast<cudaStream_t>(stream));
 }
 
+// The moment kernels' own workspace (a status word and the pair features; the query and key passes run one after the
+// other and share it) sits at the head of id_head_scores' workspace, head_prep's outputs after it.
+static size_t moment_ws_bytes(int64_t total) { return 256 + 3 * static_cast<size_t>(total) * HD * 2; }
+
 size_t noise_id_head_scores_workspace_bytes(int world, int layers, int n) {
   if (world < 1 || layers < 1 || n < 1) return 0;
-  return carve(nullptr, static_cast<int64_t>(world) * layers * n).bytes;
+  const int64_t total = static_cast<int64_t>(world) * layers * n;
+  return moment_ws_bytes(total) + carve(nullptr, total).bytes;
 }
 
 int noise_id_head_scores(const void* got, int world, int layers, int n, const float* cos, const float* sin, int tokens,
@@ -312,8 +317,9 @@ int noise_id_head_scores(const void* got, int world, int layers, int n, const fl
   if (!back) return NOISE_ERR_ARGUMENT;
   if (tokens < 64 || tokens % 64) return NOISE_ERR_SHAPE;
   const int64_t total = static_cast<int64_t>(world) * layers * n;
-  const IdScratch w = carve(workspace, total);
-  if (!workspace || workspace_bytes < w.bytes) return NOISE_ERR_WORKSPACE;
+  const size_t mws = moment_ws_bytes(total);
+  const IdScratch w = carve(workspace ? static_cast<uint8_t*>(workspace) + mws : nullptr, total);
+  if (!workspace || workspace_bytes < mws + w.bytes) return NOISE_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
   if (!a4(back)) return NOISE_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -340,15 +346,18 @@ int noise_id_head_scores(const void* got, int world, int layers, int n, const fl
   out.token_stride = HD;
   out.per_gpu = n;
   const noise_head_prep_t& o = w.o;
-  rc = noise_moment_query_scores_v(o.q16, o.k16, o.v16, o.hub16, &raw, NOISE_DTYPE_BF16, o.sq_q, o.k32, cos, sin,
-                                   o.lse, o.hub_out, o.steps_q, rows, tokens, tokens, &out, NOISE_DTYPE_BF16, stream);
+  // T % 128 == 0: the tcgen05 moment kernels (their status word at the workspace's head); else the warp-MMA ones
+  rc = noise_moment_query_scores_ws(o.q16, o.k16, o.v16, o.hub16, &raw, NOISE_DTYPE_BF16, o.sq_q, o.k32, cos, sin,
+                                    o.lse, o.hub_out, o.steps_q, rows, tokens, tokens, &out, NOISE_DTYPE_BF16,
+                                    workspace, mws, stream);
   if (rc) return rc;
   noise_rows_t rawk = raw, keys = out, vals = out;
   rawk.data = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(got) + HD);
   keys.data = static_cast<__nv_bfloat16*>(back) + static_cast<int64_t>(n) * HD;
   vals.data = static_cast<__nv_bfloat16*>(back) + 2 * static_cast<int64_t>(n) * HD;
-  return noise_moment_key_scores_v(o.q16, o.k16, o.v16, o.hub16, &rawk, NOISE_DTYPE_BF16, o.sq_k, o.q32, cos, sin,
-                                   o.lse, o.hub_out, o.steps_k, rows, tokens, &keys, &vals, NOISE_DTYPE_BF16, stream);
+  return noise_moment_key_scores_ws(o.q16, o.k16, o.v16, o.hub16, &rawk, NOISE_DTYPE_BF16, o.sq_k, o.q32, cos, sin,
+                                    o.lse, o.hub_out, o.steps_k, rows, tokens, &keys, &vals, NOISE_DTYPE_BF16, workspace,
+                                    mws, stream);
 }
 
 }  // extern "C"
