@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
+#include <type_traits>
 
 #include "noise_b200.h"
 #include "ptx.cuh"
@@ -1180,9 +1181,6 @@ int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, cons
     split_source_kernel<<<static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8)), 256,
                           0, s>>>(hub_rows, tokens, n4, hi, lo);
   }
-  if (cudaFuncSetAttribute(keymom_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           KmLayout<true>::SMEM))
-    return NOISE_ERR_CUDA;
   KeyMomTcArgs a{};
   a.T = tokens;
   a.window = std::min(window, tokens);
@@ -1197,8 +1195,16 @@ int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, cons
   a.vout = with_values ? to_rows(*value_out) : Rows{};
   a.status = status;
   const int items = tokens / KM_B * rows;
-  keymom_tc_kernel<true><<<std::min(items, sms), KM_THREADS, KmLayout<true>::SMEM, s>>>(m, a);
-  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+  // without value credits the stages drop the hub's hi / lo tiles, leaving room for a third stage
+  auto launch = [&](auto vals_tag) {
+    constexpr bool VALS = decltype(vals_tag)::value;
+    if (cudaFuncSetAttribute(keymom_tc_kernel<true, VALS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             KmLayout<true, VALS>::SMEM))
+      return NOISE_ERR_CUDA;
+    keymom_tc_kernel<true, VALS><<<std::min(items, sms), KM_THREADS, KmLayout<true, VALS>::SMEM, s>>>(m, a);
+    return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+  };
+  return with_values ? launch(std::true_type{}) : launch(std::false_type{});
 }
 
 int noise_moment_key_scores_v(const void* q, const void* k, const void* v, const void* hub, const noise_rows_t* raw,

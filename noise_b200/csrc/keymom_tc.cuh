@@ -36,7 +36,9 @@ constexpr int KM_WT = KM_B * KM_R * 2;  // [128][32] bf16 weight matrix (64-byte
 // TMEM columns: S / C buffer b at 64 b (S) and 64 b + 32 (C)
 constexpr uint32_t KM_TSC = 0, KM_TP2 = 128, KM_TR2 = 192, KM_TQ2 = 256, KM_TXY = 320, KM_TVA = 384;
 
-template <bool SCAN>
+// VALS: the value sums are computed (always for IDENT; for SCAN when value credits are requested, which adds the hub's
+// hi / lo tiles to every stage and leaves room for 2 stages instead of 3)
+template <bool SCAN, bool VALS = true>
 struct KmLayout {
   static constexpr int KV = SCAN ? 2 * KM_KT : KM_KT;  // K or V: fp32 as two 32-wide halves (128-byte rows)
   static constexpr int RQ = SCAN ? 2 * KM_RT : KM_RT;  // q or hub of a receiver tile
@@ -45,13 +47,14 @@ struct KmLayout {
   // stage: q, hub, f2, g2, xy (g2 and xy adjacent: one 96-wide MN-major operand), [hi, lo], lse, center
   static constexpr int SQ = 0, SH = RQ, SF2 = 2 * RQ, SG2 = SF2 + KM_RT, SXY = SG2 + KM_RT, SHI = SXY + KM_RT,
                        SLO = SHI + KM_RT;
-  static constexpr int SLSE = SCAN ? SLO + KM_RT : SHI, SCTR = SLSE + 128;
+  static constexpr int SLSE = SCAN && VALS ? SLO + KM_RT : SHI, SCTR = SLSE + 128;
   static constexpr int STAGE = (SCTR + 128 + 1023) / 1024 * 1024;
-  static constexpr int STAGES = SCAN ? 2 : 5;
-  static constexpr int AHEAD = SCAN ? 1 : 2;  // S / C run this many receiver tiles ahead of the moment MMAs
+  static constexpr int STAGES = SCAN ? (VALS ? 2 : 3) : 5;
+  static constexpr int AHEAD = STAGES >= 3 ? 2 : 1;  // S / C run this many receiver tiles ahead of the moment MMAs
   static constexpr int SUMS = RING + STAGES * STAGE;  // s1, s2 and (SCAN) |raw|^2 per (half, key row)
   static constexpr int BAR = SUMS + 3 * 2 * 128 * 4;
   static constexpr int SMEM = BAR + 256 + 1024;
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
 // K-major operand in 64-byte swizzled rows (32 bf16 of K per row): 8-row groups 512 bytes apart, layout type 4
@@ -149,10 +152,10 @@ struct KeyMomMaps {
   CUtensorMap lse, ctr;            // fp32 [rows, T], 32 x 1 boxes
 };
 
-template <bool SCAN>
+template <bool SCAN, bool VALS = true>
 __global__ void __launch_bounds__(KM_THREADS, 1)
     keymom_tc_kernel(const __grid_constant__ KeyMomMaps m, const __grid_constant__ KeyMomTcArgs p) {
-  using L = KmLayout<SCAN>;
+  using L = KmLayout<SCAN, VALS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::BAR);
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkt = p.T / KM_B, nrt = p.T / KM_R;
   const int items = nkt * p.rows;
-  const bool values = !SCAN || p.vout.data != nullptr;
+  constexpr bool values = !SCAN || VALS;
   // item w: key tile w / rows (the first tiles have the most receivers: heaviest first) of row w % rows; its
   // receiver tiles run from the key tile's first receivers to the window's end
   auto tiles_of = [&](int kt, int& lo, int& hi) {

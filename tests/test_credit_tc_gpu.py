@@ -212,8 +212,8 @@ def test_key_scan_against_oracle_and_warp_kernel(mk, rows, t, window, with_value
 
 
 def test_key_scan_full_size(mk):
-    """rows 128, T 2048 (config 3) at windows 2048 and 1024, with the raw value credits: the tcgen05 and warp kernels
-    agree (5e-3 / 2e-3 of max |ref|)."""
+    """rows 128, T 2048 (config 3) at windows 2048 and 1024, with the raw value credits (2-stage kernel) and without
+    (3-stage kernel): the tcgen05 and warp kernels agree (5e-3 / 2e-3 of max |ref|)."""
     from noise_b200 import _lib
     x = credit_inputs(128, 2048, seed=12)
     d = {k: v.to(DEV) for k, v in x.items()}
@@ -224,6 +224,9 @@ def test_key_scan_full_size(mk):
         wkey, wval = mk.key_scan(*args, with_values=True, tc=False)
         assert _lib.read_status(key._noise_workspace) == 0
         assert rel(key, wkey) < 5e-3 and rel(val, wval) < 2e-3
+        key_only, _ = mk.key_scan(*args, with_values=False)
+        assert _lib.read_status(key_only._noise_workspace) == 0
+        assert rel(key_only, key) < 1e-6
 
 
 # --- query moments (noise_moment_query_scores_ws) ---------------------------------------------------------------------
