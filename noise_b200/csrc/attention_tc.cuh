@@ -274,23 +274,30 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         tc_fence_before();
         mbar_arrive(&s_empty[g]);  // S is in registers: the next S MMA may overwrite it
         uint32_t pk[TA_BK / 2];
-        float rs = 0.f;
+        // packed fp32x2 FMA / add (one instruction for two keys; the same rounding as two scalar ones)
+        float2 rs2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < TA_BK; c += 8) {
           float pe[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float x = fmaf(v[c + e], SL2, -OFF);
-            pe[e] = ex2_approx(x);
+          for (int e = 0; e < 8; e += 2) {
+            const float2 x = __ffma2_rn(make_float2(v[c + e], v[c + e + 1]), make_float2(SL2, SL2),
+                                        make_float2(-OFF, -OFF));
+            pe[e] = ex2_approx(x.x);
+            pe[e + 1] = ex2_approx(x.y);
             if constexpr (MASKED) {
-              const int key = kt * TA_BK + c + e;
-              if (key > tq || tq - key > p.window) pe[e] = 0.f;
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const int key = kt * TA_BK + c + e + i;
+                if (key > tq || tq - key > p.window) pe[e + i] = 0.f;
+              }
             }
-            rs += pe[e];
+            rs2 = __fadd2_rn(rs2, make_float2(pe[e], pe[e + 1]));
           }
 #pragma unroll
           for (int e = 0; e < 4; ++e) pk[c / 2 + e] = pack_bf16x2(pe[2 * e], pe[2 * e + 1]);
         }
+        const float rs = rs2.x + rs2.y;
         // the P buffer is free once the previous O MMA of this group completed
         if (!mbar_wait(&p_empty[g], (static_cast<uint32_t>(cnt) & 1u) ^ 1u, p.status)) return false;
 #pragma unroll
