@@ -474,7 +474,8 @@ struct EpiFCImpl {
   __nv_bfloat16* hidden;
   const float* jit;  // JIT: [M, 2048] fp32 added to the pre-activation (Dust's fc jitter site)
   float* pdot;  // [M, NPARTS]
-  float coef, pd[8];  // eight partial sums: independent FMA chains
+  float coef;
+  float2 pd[4];  // eight partial sums (independent FMA chains), updated two at a time by packed fp32x2 FMAs
   int col0;
   float* scratch;
   uint32_t stg;
@@ -483,7 +484,7 @@ struct EpiFCImpl {
     const int j = row / T;
     coef = sign[j] * svec[static_cast<int64_t>(row) * 4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pd[i] = 0.f;
+    for (int i = 0; i < 4; ++i) pd[i] = make_float2(0.f, 0.f);
   }
   // the tile's slices of a_fc and of the bf16-rounded b of mlp.c_proj into shared memory
   __device__ __forceinline__ void stage(int row0, int c0, float* s, int tid) {
@@ -493,32 +494,40 @@ struct EpiFCImpl {
     s[GEMM_BN + tid] = bf16_round(nmp.B(j)[c0 + tid]);
   }
   __device__ __forceinline__ void tile_end(int row, int nb, int part) {
-    pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] = ((pd[0] + pd[1]) + (pd[2] + pd[3])) + ((pd[4] + pd[5]) + (pd[6] + pd[7]));
+    pdot[static_cast<int64_t>(row) * NPARTS + 2 * nb + part] =
+        ((pd[0].x + pd[0].y) + (pd[1].x + pd[1].y)) + ((pd[2].x + pd[2].y) + (pd[3].x + pd[3].y));
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pd[i] = 0.f;
+    for (int i = 0; i < 4; ++i) pd[i] = make_float2(0.f, 0.f);
   }
   __device__ __forceinline__ void row_end(int, int) {}
+  // Columns in pairs: each bf16 rounding is one packed conversion (its fp32 values are the halves shifted back), and
+  // the rank-1 term, the square and the partial dots are packed fp32x2 operations with the rounding of scalar ones.
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
     const int lane = threadIdx.x & 31;
     const float* ap = scratch + (col - col0);
     const float* bp = ap + GEMM_BN;
+    const float2 coef2 = make_float2(coef, coef);
 #pragma unroll
     for (int i = 0; i < CH; i += 8) {
-      float r[8];
+      uint32_t pk[4];
       const float4 a0 = *reinterpret_cast<const float4*>(ap + i), a1 = *reinterpret_cast<const float4*>(ap + i + 4);
       const float4 b0 = *reinterpret_cast<const float4*>(bp + i), b1 = *reinterpret_cast<const float4*>(bp + i + 4);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float2 av[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                            make_float2(a1.z, a1.w)};
+      const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                            make_float2(b1.z, b1.w)};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float u = bf16_round(acc[i + e]) + coef * av[e];
-        if constexpr (JIT) u += jit[static_cast<int64_t>(row) * F + col + i + e];
-        const float rl = fmaxf(u, 0.f);
-        r[e] = bf16_round(rl * rl);
-        pd[e] = fmaf(r[e], bv[e], pd[e]);
+      for (int e = 0; e < 4; ++e) {
+        float2 u = __ffma2_rn(coef2, av[e], unpack_bf16x2(pack_bf16x2(acc[i + 2 * e], acc[i + 2 * e + 1])));
+        if constexpr (JIT) {
+          const float* jp = jit + static_cast<int64_t>(row) * F + col + i + 2 * e;
+          u = __fadd2_rn(u, make_float2(jp[0], jp[1]));
+        }
+        const float2 rl = make_float2(fmaxf(u.x, 0.f), fmaxf(u.y, 0.f));
+        pk[e] = pack_bf16x2_f2(__fmul2_rn(rl, rl));
+        pd[e] = __ffma2_rn(unpack_bf16x2(pk[e]), bv[e], pd[e]);
       }
-      sts128(stg_addr(stg, lane, i / 8), make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]),
-                                                    pack_bf16x2(r[4], r[5]), pack_bf16x2(r[6], r[7])));
+      sts128(stg_addr(stg, lane, i / 8), make_uint4(pk[0], pk[1], pk[2], pk[3]));
     }
     __syncwarp();
     // rows row - lane .. + 31 of hidden, columns col .. col + CH - 1: whole CH * 2-byte row segments, NC 16-byte

@@ -285,4 +285,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2_f2(float2 v) { return pack_bf16x2(v.x, v.y); }
+
+// The two bf16 halves of a packed pair widened back to fp32 (x = low half): exact, two integer operations.
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t p) {
+  return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));
+}
+
 }  // namespace noise
