@@ -303,14 +303,20 @@ struct EpiQKV {
   __device__ __forceinline__ void chunk(int row, int col, float* val) {
     const int sec = col / D, hh = (col % D) / HD;
     const float coef = sg * svec[static_cast<int64_t>(row) * 4 + sec];
+    const float2 coef2 = make_float2(coef, coef);
     const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
+    // columns in pairs: one packed bf16 conversion per rounding (its fp32 values are the halves shifted back) and
+    // fp32x2 FMAs, with the rounding of scalar ones
 #pragma unroll
     for (int d = 0; d < HD; d += 4) {
       const float4 av = a4[d / 4];
-      val[d + 0] = bf16_round(val[d + 0]) + coef * av.x;
-      val[d + 1] = bf16_round(val[d + 1]) + coef * av.y;
-      val[d + 2] = bf16_round(val[d + 2]) + coef * av.z;
-      val[d + 3] = bf16_round(val[d + 3]) + coef * av.w;
+      const float2 u0 = __ffma2_rn(coef2, make_float2(av.x, av.y), unpack_bf16x2(pack_bf16x2(val[d], val[d + 1])));
+      const float2 u1 =
+          __ffma2_rn(coef2, make_float2(av.z, av.w), unpack_bf16x2(pack_bf16x2(val[d + 2], val[d + 3])));
+      val[d + 0] = u0.x;
+      val[d + 1] = u0.y;
+      val[d + 2] = u1.x;
+      val[d + 3] = u1.y;
     }
     __nv_bfloat16* dst;
     if (sec < 2) {
@@ -336,8 +342,13 @@ struct EpiQKV {
         }
       }
       const float inv = rsqrtf(((ss4[0] + ss4[1]) + (ss4[2] + ss4[3])) / HD + RMS_EPS);
+      const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-      for (int d = 0; d < HD; ++d) val[d] *= inv;
+      for (int d = 0; d < HD; d += 2) {
+        const float2 w = __fmul2_rn(make_float2(val[d], val[d + 1]), inv2);
+        val[d] = w.x;
+        val[d + 1] = w.y;
+      }
       dst = sec == 0 ? q : k;
     } else {
       if (gate) {
@@ -421,22 +432,21 @@ struct EpiResid {
     // the linear's output for this thread's row (32 columns, 128 bytes) -> staging
     const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
     const int lane = threadIdx.x & 31;
+    const float2 coef2 = make_float2(coef, coef);
+    // columns in pairs: one packed bf16 conversion per rounding and fp32x2 FMAs, with the rounding of scalar ones
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) {
       const float4 av = a4[i];
-      float4 y;
-      y.x = bf16_round(acc[4 * i + 0]) + coef * av.x;
-      y.y = bf16_round(acc[4 * i + 1]) + coef * av.y;
-      y.z = bf16_round(acc[4 * i + 2]) + coef * av.z;
-      y.w = bf16_round(acc[4 * i + 3]) + coef * av.w;
+      float2 y0 = __ffma2_rn(coef2, make_float2(av.x, av.y), unpack_bf16x2(pack_bf16x2(acc[4 * i], acc[4 * i + 1])));
+      float2 y1 =
+          __ffma2_rn(coef2, make_float2(av.z, av.w), unpack_bf16x2(pack_bf16x2(acc[4 * i + 2], acc[4 * i + 3])));
       if (jit) {
         const float4 jv = *reinterpret_cast<const float4*>(jit + static_cast<int64_t>(row) * D + col + 4 * i);
-        y.x += jv.x;
-        y.y += jv.y;
-        y.z += jv.z;
-        y.w += jv.w;
+        y0 = __fadd2_rn(y0, make_float2(jv.x, jv.y));
+        y1 = __fadd2_rn(y1, make_float2(jv.z, jv.w));
       }
-      sts128(stg_addr(stg, lane, i), *reinterpret_cast<uint4*>(&y));
+      sts128(stg_addr(stg, lane, i), make_uint4(__float_as_uint(y0.x), __float_as_uint(y0.y), __float_as_uint(y1.x),
+                                                __float_as_uint(y1.y)));
     }
     __syncwarp();
     // x += y for rows row - lane .. + 31, 4 whole 128-byte rows per instruction
@@ -449,12 +459,11 @@ struct EpiResid {
     for (int i = 0; i < 8; ++i) {
       const int r = (lane >> 3) + 4 * i;
       const uint4 yv = lds128(stg_addr(stg, r, c));
-      const float4 y = *reinterpret_cast<const float4*>(&yv);
-      xv[i].x += y.x;
-      xv[i].y += y.y;
-      xv[i].z += y.z;
-      xv[i].w += y.w;
-      xr[r * (D / 4)] = xv[i];
+      const float2 s0 =
+          __fadd2_rn(make_float2(xv[i].x, xv[i].y), make_float2(__uint_as_float(yv.x), __uint_as_float(yv.y)));
+      const float2 s1 =
+          __fadd2_rn(make_float2(xv[i].z, xv[i].w), make_float2(__uint_as_float(yv.z), __uint_as_float(yv.w)));
+      xr[r * (D / 4)] = make_float4(s0.x, s0.y, s1.x, s1.y);
     }
     __syncwarp();
   }
