@@ -9,12 +9,14 @@
 // One CTA per (member x head, pair of 128-query tiles A = 2i, B = 2i + 1), 320 threads:
 //   warp 0      TMA: Q_A, Q_B once, then 128-key K / V tiles (the union of both tiles' key ranges) into a 3-stage
 //               ring (128-byte swizzle); both query tiles share every K / V load;
-//   warp 1      TMEM (512 columns: S_A, S_B 128 each, O_A, O_B 64 each) and one lane issuing, per key tile,
-//               S_w = Q_w K^T (M=128, N=128, K=64) for each tile w that sees it, then O_w += P_w V of the previous
-//               key tile (M=128, N=64, K=128; V an MN-major operand);
+//   warp 1      TMEM (512 columns: S_A, S_B 128 each, O_A, O_B 64 each, P_A, P_B 64 each) and one lane issuing,
+//               per key tile, S_w = Q_w K^T (M=128, N=128, K=64) for each tile w that sees it, then O_w += P_w V of
+//               the previous key tile (M=128, N=64, K=128; P the A operand read from tensor memory, V an MN-major
+//               shared-memory operand);
 //   warps 2..5  softmax group A, warps 6..9 group B: one query row per thread; S_w is read with one batched
-//               tcgen05.ld and released at once, P = exp2(s log2(e) / 8 - 8 log2(e)) goes as bf16 into 128-byte-
-//               swizzled shared memory (the A operand of the next O MMA), every exponential on the MUFU pipe (it is
+//               tcgen05.ld and released at once, P = exp2(s log2(e) / 8 - 8 log2(e)) goes as packed bf16 pairs into
+//               the group's P columns of tensor memory (tcgen05.st; the A operand of the next O MMA, so the MMAs read
+//               only V from shared memory), every exponential on the MUFU pipe (it is
 //               under half busy: moving a share to an FMA polynomial measured slower); at the end y = O / l (bf16)
 //               and the per-head partial dot y . b of the c_proj rank-1 term.
 // Only the diagonal key tile and the window's first tile take the masked path.
@@ -30,9 +32,10 @@ constexpr int TA_TILE = 128 * 128;  // bytes of one [128][64] bf16 tile
 constexpr int TA_Q = 0;             // Q_A, Q_B
 constexpr int TA_K = TA_Q + 2 * TA_TILE;
 constexpr int TA_V = TA_K + TA_STAGES * TA_TILE;
-constexpr int TA_P = TA_V + TA_STAGES * TA_TILE;  // P_A, P_B: 2 sub-tiles each (keys 0..63, 64..127)
+constexpr int TA_P = TA_V + TA_STAGES * TA_TILE;  // epilogue staging per group: y rows, the head's b
 constexpr int TA_BAR = TA_P + 4 * TA_TILE;
 constexpr int TA_SMEM = TA_BAR + 256 + 1024;
+constexpr uint32_t TA_TS = 0, TA_TO = 256, TA_TP = 384;  // TMEM columns: S_A | S_B, O_A | O_B, P_A | P_B
 
 struct TAttnArgs {
   int T, window;
@@ -82,8 +85,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* p_empty = p_full + 2;
-  uint64_t* o_full = p_empty + 2;            // per O buffer (items alternate): all MMAs of the item done
-  uint64_t* o_empty = o_full + 2;            // per O buffer: both groups read their O
+  uint64_t* o_full = p_empty + 2;            // [0]: all MMAs of the item done ([1] unused)
+  uint64_t* o_empty = o_full + 2;            // per group: the group's warps read its O
   uint64_t* drain = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -125,7 +128,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       mbar_init(&p_full[b], 128);
       mbar_init(&p_empty[b], 1);
       mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 256);
+      mbar_init(&o_empty[b], 128);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -181,30 +184,34 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       bool ok = true;
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
         const Item it = item(w);
-        const int ob = nitem & 1;
         const TileRange rg[2] = {it.ra, it.rb};
         auto sees = [&](int g, int kt) { return kt >= rg[g].lo && kt <= rg[g].hi; };
         int first_pv[2] = {1, 1};  // the item's first O MMA overwrites the accumulator
+        bool o_free = false;       // both groups have read O of the previous item
         auto issue_pv = [&](int g, int kt, int kvi) {  // O_g += P_g V of key tile kt (ring slot of tile kvi)
           const int st = kvi % TA_STAGES;
+          // the item's first O MMA overwrites O: both groups must have read theirs (item nitem - 1). Waiting for both
+          // keeps o_full at most one phase ahead of every group's wait on it, inactive group B included.
+          if (!o_free) {
+            const uint32_t par = (static_cast<uint32_t>(nitem) & 1u) ^ 1u;
+            if (!mbar_wait(&o_empty[0], par, p.status) || !mbar_wait(&o_empty[1], par, p.status)) return false;
+            o_free = true;
+          }
           if (!mbar_wait(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
           tc_fence_after();
-          const uint32_t pbase = sbase + TA_P + g * 2 * TA_TILE;
           const uint32_t vbase = sbase + TA_V + st * TA_TILE;
 #pragma unroll
-          for (int ks = 0; ks < TA_BK / 16; ++ks) {
-            const uint64_t ad = sdesc_kmajor_sw128(pbase + (ks >> 2) * TA_TILE) + 2u * (ks & 3);
+          for (int ks = 0; ks < TA_BK / 16; ++ks) {  // P columns ks * 8 .. + 7: keys 16 ks .. 16 ks + 15
             const uint64_t bd = sdesc_mnmajor_sw128(vbase + ks * 2048, 16);
-            tc_mma(tmem + 256 + ob * 128 + g * 64, ad, bd, idesc_pv, !(first_pv[g] && ks == 0));
+            tc_mma_ts(tmem + TA_TO + g * 64, tmem + TA_TP + g * 64 + ks * 8, bd, idesc_pv,
+                      !(first_pv[g] && ks == 0));
           }
           first_pv[g] = 0;
           tc_commit(&p_empty[g]);
           ++pv_count[g];
           return true;
         };
-        // the O buffer of this item must have been read by both groups (item nitem - 2)
-        if (!mbar_wait(&o_empty[ob], (static_cast<uint32_t>(nitem >> 1) & 1u) ^ 1u, p.status) ||
-            !mbar_wait(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+        if (!mbar_wait(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           for (int g = 0; g < 2 && ok; ++g)
             if (sees(g, it.hi)) ok = issue_pv(g, it.hi, kv0 + (it.hi - it.lo));
           tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
-          tc_commit(&o_full[ob]);
+          tc_commit(&o_full[0]);
         }
       }
       tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
@@ -253,14 +260,13 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + g * TA_BK;
-    const uint32_t prow = sbase + TA_P + g * 2 * TA_TILE + r * 128;
+    const uint32_t p_addr = tmem + lane_base + TA_TP + g * 64;  // this row's 64 P columns
     constexpr float SL2 = 0.125f * 1.4426950408889634f;  // 1/8 in base 2
     constexpr float OFF = 8.f * 1.4426950408889634f;     // the fixed offset 8 in base 2
     int cnt = 0, nitem = 0;
     bool ok = true;
     for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
       const Item it = item(w);
-      const int ob = nitem & 1;
       const TileRange rg = g == 0 ? it.ra : it.rb;
       const int tq = (g == 0 ? it.qa : it.qb) * TA_BQ + r;
       const bool active = g == 0 || it.has_b;
@@ -300,13 +306,13 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         const float rs = rs2.x + rs2.y;
         // the P buffer is free once the previous O MMA of this group completed
         if (!mbar_wait(&p_empty[g], (static_cast<uint32_t>(cnt) & 1u) ^ 1u, p.status)) return false;
+        __syncwarp();  // tcgen05.st is warp-aligned
+        tc_fence_after();
+        // column i of the row holds keys 2 i (low half) and 2 i + 1 (high half)
 #pragma unroll
-        for (int c = 0; c < TA_BK; c += 8) {  // keys c .. c + 7: sub-tile c / 64, chunk (c % 64) / 8, 128-B swizzle
-          const int chunk = (c & 63) >> 3;
-          st_shared_v4(prow + (c >> 6) * TA_TILE + ((chunk ^ (r & 7)) << 4), pk[c / 2], pk[c / 2 + 1],
-                       pk[c / 2 + 2], pk[c / 2 + 3]);
-        }
-        fence_proxy_async_smem();
+        for (int c = 0; c < TA_BK / 2; c += 16) tmem_st16(p_addr + c, pk + c);
+        tc_wait_st();
+        tc_fence_before();
         mbar_arrive(&p_full[g]);
         l += rs;
         return true;
@@ -330,25 +336,25 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         bq0 = bproj[lane];
         bq1 = bproj[lane + 32];
       }
-      if (!ok || !mbar_wait(&o_full[ob], static_cast<uint32_t>(nitem >> 1) & 1u, p.status)) {
+      if (!ok || !mbar_wait(&o_full[0], static_cast<uint32_t>(nitem) & 1u, p.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
       float o[64];
-      const uint32_t o_addr = tmem + lane_base + 256 + ob * 128 + g * 64;
+      const uint32_t o_addr = tmem + lane_base + TA_TO + g * 64;
       tmem_ld32(o_addr, o);
       tmem_ld32(o_addr + 32, o + 32);
       tc_wait_ld();
       tc_fence_before();
-      mbar_arrive(&o_empty[ob]);
+      mbar_arrive(&o_empty[g]);
       if (active) {
         const int j = it.bh / NOISE_N_HEAD, hh = it.bh % NOISE_N_HEAD;
         const int64_t row = static_cast<int64_t>(j) * p.T + tq;
         const float inv = 1.f / l;
-        // The warp's own 32 rows of this group's P buffer are free (every O MMA of the item is complete, and only
-        // this warp writes these rows): sub-tile 1 holds the head's b, sub-tile 0 stages the y rows (16-byte chunk c
-        // of row rl at c ^ (rl % 8)) so the global stores cover whole 128-byte row segments.
+        // The warp's own 32 rows of this group's staging area (only this warp uses them): sub-tile 1 holds the
+        // head's b, sub-tile 0 stages the y rows (16-byte chunk c of row rl at c ^ (rl % 8)) so the global stores
+        // cover whole 128-byte row segments.
         const uint32_t wst = sbase + TA_P + g * 2 * TA_TILE + quarter * 32 * 128;
         const uint32_t wb = wst + TA_TILE;
         st_shared_f32(wb + lane * 4, bf16_round(bq0));

@@ -49,7 +49,7 @@ def _check_fitness(got, ref):
     assert (fg - fr).abs().max().item() <= FIT_TOL * scale, (fg, fr)
 
 
-@pytest.mark.parametrize('members,length', [(4, 128), (4, 256), (2, 1024)])
+@pytest.mark.parametrize('members,length', [(4, 128), (4, 256), (2, 384), (2, 1024)])
 def test_matches_oracle_autocast(members, length):
     w, buf, offs, directions, nz, sign, idx, tgt = _case(members, length)
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
