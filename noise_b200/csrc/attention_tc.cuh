@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         mbar_wait(&kv_full[j % TA_STAGES], static_cast<uint32_t>(j / TA_STAGES) & 1u, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issuer; one elected lane issues the MMAs and commits
       constexpr uint32_t idesc_s = idesc_bf16(TA_BQ, TA_BK);
       constexpr uint32_t idesc_pv = idesc_bf16(TA_BQ, 64, false, true);
       int kv = 0, nitem = 0;
@@ -194,64 +194,68 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
           // keeps o_full at most one phase ahead of every group's wait on it, inactive group B included.
           if (!o_free) {
             const uint32_t par = (static_cast<uint32_t>(nitem) & 1u) ^ 1u;
-            if (!mbar_wait(&o_empty[0], par, p.status) || !mbar_wait(&o_empty[1], par, p.status)) return false;
+            if (!mbar_wait_warp(&o_empty[0], par, p.status) || !mbar_wait_warp(&o_empty[1], par, p.status))
+              return false;
             o_free = true;
           }
-          if (!mbar_wait(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
+          if (!mbar_wait_warp(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
           tc_fence_after();
           const uint32_t vbase = sbase + TA_V + st * TA_TILE;
 #pragma unroll
           for (int ks = 0; ks < TA_BK / 16; ++ks) {  // P columns ks * 8 .. + 7: keys 16 ks .. 16 ks + 15
             const uint64_t bd = sdesc_mnmajor_sw128(vbase + ks * 2048, 16);
-            tc_mma_ts(tmem + TA_TO + g * 64, tmem + TA_TP + g * 64 + ks * 8, bd, idesc_pv,
-                      !(first_pv[g] && ks == 0));
+            if (elect_one())
+              tc_mma_ts(tmem + TA_TO + g * 64, tmem + TA_TP + g * 64 + ks * 8, bd, idesc_pv, !(first_pv[g] && ks == 0));
           }
           first_pv[g] = 0;
-          tc_commit(&p_empty[g]);
+          if (elect_one()) tc_commit(&p_empty[g]);
           ++pv_count[g];
           return true;
         };
-        if (!mbar_wait(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+        if (!mbar_wait_warp(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
         const int kv0 = kv;
         for (int kt = it.lo; kt <= it.hi && ok; ++kt, ++kv) {
           const int st = kv % TA_STAGES;
-          if (!mbar_wait(&kv_full[st], static_cast<uint32_t>(kv / TA_STAGES) & 1u, p.status)) {
+          if (!mbar_wait_warp(&kv_full[st], static_cast<uint32_t>(kv / TA_STAGES) & 1u, p.status)) {
             ok = false;
             break;
           }
           const uint64_t kd = sdesc_kmajor_sw128(sbase + TA_K + st * TA_TILE);
           for (int g = 0; g < 2 && ok; ++g) {
             if (!sees(g, kt)) continue;
-            if (!mbar_wait(&s_empty[g], (static_cast<uint32_t>(s_count[g]) & 1u) ^ 1u, p.status)) {
+            if (!mbar_wait_warp(&s_empty[g], (static_cast<uint32_t>(s_count[g]) & 1u) ^ 1u, p.status)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint64_t qd = sdesc_kmajor_sw128(sbase + TA_Q + g * TA_TILE);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tc_mma(tmem + g * TA_BK, qd + 2u * k, kd + 2u * k, idesc_s, k > 0);
-            tc_commit(&s_full[g]);
+            for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(tmem + g * TA_BK, qd + 2u * k, kd + 2u * k, idesc_s, k > 0);
+            if (elect_one()) tc_commit(&s_full[g]);
             ++s_count[g];
           }
-          if (kt == it.hi && ok) tc_commit(q_empty);  // the item's last S MMAs read Q
+          if (kt == it.hi && ok && elect_one()) tc_commit(q_empty);  // the item's last S MMAs read Q
           if (kt > it.lo && ok) {  // O MMAs of the previous key tile, then release its ring slot
             for (int g = 0; g < 2 && ok; ++g)
               if (sees(g, kt - 1)) ok = issue_pv(g, kt - 1, kv - 1);
-            tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
+            if (elect_one()) tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
           }
         }
         if (ok) {
           for (int g = 0; g < 2 && ok; ++g)
             if (sees(g, it.hi)) ok = issue_pv(g, it.hi, kv0 + (it.hi - it.lo));
-          tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
-          tc_commit(&o_full[0]);
+          if (elect_one()) {
+            tc_commit(&kv_empty[(kv - 1) % TA_STAGES]);
+            tc_commit(&o_full[0]);
+          }
         }
       }
-      tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
-      mbar_wait(drain, 0, p.status);
+      if (elect_one()) tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
+      mbar_wait_warp(drain, 0, p.status);
     }
   } else {
     // softmax groups: warps 2..5 -> group A, 6..9 -> group B; thread = query row of the group's tile
