@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         mbar_wait(&st_full[j % L::STAGES], static_cast<uint32_t>(j / L::STAGES) & 1u, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issuer; one elected lane issues the MMAs and commits
       constexpr uint32_t id_s = SCAN ? km_idesc_tf32(KM_B, KM_R) : idesc_bf16(KM_B, KM_R);  // S, C (K-major B)
       constexpr uint32_t id_f = idesc_bf16(KM_B, 64, false, true);   // P2, R2, VA: B MN-major
       constexpr uint32_t id_q = idesc_bf16(KM_B, 96, false, true);   // Q2 | QXY
@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       // the moment MMAs of the receiver tile with global index svj (the item's first when first)
       auto moments = [&](int svj, bool first) {
         const int wb = svj & 1;
-        if (!mbar_wait(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
+        if (!mbar_wait_warp(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
         tc_fence_after();
         const uint32_t st = sbase + L::RING + (svj % L::STAGES) * L::STAGE;
         const uint32_t w = sbase + L::W + wb * 4 * KM_WT;  // W1, W2, W2L, P
@@ -282,40 +282,40 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         for (int ks = 0; ks < KM_R / 16; ++ks) {
           const uint32_t acc = (first && ks == 0) ? 0u : 1u;
           const uint64_t f2d = sdesc_mnmajor_sw128(st + L::SF2 + ks * 2048, 16);
-          tc_mma(tmem + KM_TP2, km_sdesc_kmajor_sw64(w) + 2u * ks, f2d, id_f, acc);
-          tc_mma(tmem + KM_TR2, km_sdesc_kmajor_sw64(w + 2 * KM_WT) + 2u * ks, f2d, id_f, acc);
-          tc_mma(tmem + KM_TQ2, km_sdesc_kmajor_sw64(w + KM_WT) + 2u * ks,
+          if (elect_one()) tc_mma(tmem + KM_TP2, km_sdesc_kmajor_sw64(w) + 2u * ks, f2d, id_f, acc);
+          if (elect_one()) tc_mma(tmem + KM_TR2, km_sdesc_kmajor_sw64(w + 2 * KM_WT) + 2u * ks, f2d, id_f, acc);
+          if (elect_one()) tc_mma(tmem + KM_TQ2, km_sdesc_kmajor_sw64(w + KM_WT) + 2u * ks,
                  sdesc_mnmajor_sw128(st + L::SG2 + ks * 2048, KM_RT), id_q, acc);
           if constexpr (SCAN) {
             if (values) {
               const uint64_t pd = km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks;
-              tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SHI + ks * 2048, 16), id_f, acc);
-              tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SLO + ks * 2048, 16), id_f, 1u);
+              if (elect_one()) tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SHI + ks * 2048, 16), id_f, acc);
+              if (elect_one()) tc_mma(tmem + KM_TVA, pd, sdesc_mnmajor_sw128(st + L::SLO + ks * 2048, 16), id_f, 1u);
             }
           } else {
-            tc_mma(tmem + KM_TVA, km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks,
+            if (elect_one()) tc_mma(tmem + KM_TVA, km_sdesc_kmajor_sw64(w + 3 * KM_WT) + 2u * ks,
                    sdesc_mnmajor_sw128(st + L::SH + ks * 2048, 16), id_f, acc);
           }
         }
-        tc_commit(&w_empty[wb]);
-        tc_commit(&st_empty[svj % L::STAGES]);
+        if (elect_one()) tc_commit(&w_empty[wb]);
+        if (elect_one()) tc_commit(&st_empty[svj % L::STAGES]);
         return true;
       };
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
         const int kt = w / p.rows;
         int lo, hi;
         tiles_of(kt, lo, hi);
-        if (!mbar_wait(kv_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+        if (!mbar_wait_warp(kv_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
         // the accumulators are free once the previous item's epilogue has read them (S / C may start before)
-        auto acc_free = [&]() { return mbar_wait(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status); };
+        auto acc_free = [&]() { return mbar_wait_warp(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status); };
         // S / C of the tile with global index svj into buffer svj & 1 (free once the tile two back was read)
         auto scores = [&](int svj) {
           const int sl = svj % L::STAGES, b = svj & 1;
-          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(svj / L::STAGES) & 1u, p.status) ||
-              !mbar_wait(&s_empty[b], (static_cast<uint32_t>(svj >> 1) & 1u) ^ 1u, p.status))
+          if (!mbar_wait_warp(&st_full[sl], static_cast<uint32_t>(svj / L::STAGES) & 1u, p.status) ||
+              !mbar_wait_warp(&s_empty[b], (static_cast<uint32_t>(svj >> 1) & 1u) ^ 1u, p.status))
             return false;
           tc_fence_after();
           const uint32_t st = sbase + L::RING + sl * L::STAGE;
@@ -324,24 +324,26 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t ho = (k >> 2);
-              km_mma_tf32(ts, sdesc_kmajor_sw128(sbase + L::K + ho * KM_KT) + 2u * (k & 3),
+              if (elect_one()) km_mma_tf32(ts, sdesc_kmajor_sw128(sbase + L::K + ho * KM_KT) + 2u * (k & 3),
                           sdesc_kmajor_sw128(st + L::SQ + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
             }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t ho = (k >> 2);
-              km_mma_tf32(ts + 32, sdesc_kmajor_sw128(sbase + L::V + ho * KM_KT) + 2u * (k & 3),
+              if (elect_one()) km_mma_tf32(ts + 32, sdesc_kmajor_sw128(sbase + L::V + ho * KM_KT) + 2u * (k & 3),
                           sdesc_kmajor_sw128(st + L::SH + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
             }
           } else {
             const uint64_t kd = sdesc_kmajor_sw128(sbase + L::K), vd = sdesc_kmajor_sw128(sbase + L::V);
             const uint64_t qd = sdesc_kmajor_sw128(st + L::SQ), hd = sdesc_kmajor_sw128(st + L::SH);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tc_mma(ts, kd + 2u * k, qd + 2u * k, id_s, k > 0);
+            for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(ts, kd + 2u * k, qd + 2u * k, id_s, k > 0);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tc_mma(ts + 32, vd + 2u * k, hd + 2u * k, id_s, k > 0);
+            for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(ts + 32, vd + 2u * k, hd + 2u * k, id_s, k > 0);
           }
-          tc_commit(&s_full[b]);
+          if (elect_one()) tc_commit(&s_full[b]);
           return true;
         };
         // S / C run AHEAD tiles ahead of the moment MMAs, so a tile's moments issue as soon as its weights are
@@ -354,12 +356,12 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
           if (ok && j + L::AHEAD <= hi) ok = scores(sv + L::AHEAD);
         }
         if (ok) {
-          tc_commit(kv_empty);
-          tc_commit(acc_full);
+          if (elect_one()) tc_commit(kv_empty);
+          if (elect_one()) tc_commit(acc_full);
         }
       }
-      tc_commit(drain);
-      mbar_wait(drain, 0, p.status);
+      if (elect_one()) tc_commit(drain);
+      mbar_wait_warp(drain, 0, p.status);
     }
   } else {
     const int quarter = warp & 3, half = (warp - 2) >> 2;

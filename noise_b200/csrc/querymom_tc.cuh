@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         mbar_wait(&st_full[j % QM_STAGES], static_cast<uint32_t>(j / QM_STAGES) & 1u, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issuer; one elected lane issues the MMAs and commits
       constexpr uint32_t id_s = idesc_bf16(QM_B, QM_R);               // S, C: B = k / v rows (K-major)
       constexpr uint32_t id_n = idesc_bf16(QM_B, 160, false, true);   // N, D: B = fa | fb | fc (MN-major)
       constexpr uint32_t id_l = idesc_bf16(QM_B, 64, false, true);    // L, M: B = fa
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
       bool ok = true;
       auto moments = [&](int svj, bool first) {
         const int wb = svj & 1;
-        if (!mbar_wait(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
+        if (!mbar_wait_warp(&w_full[wb], static_cast<uint32_t>(svj >> 1) & 1u, p.status)) return false;
         tc_fence_after();
         const uint32_t st = sbase + QM_RING + (svj % QM_STAGES) * QM_STAGE;
         const uint32_t w = sbase + QM_W + wb * 4 * QM_WT;  // W, A, WL, AL
@@ -196,54 +196,56 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         for (int ks = 0; ks < QM_R / 16; ++ks) {
           const uint32_t acc = (first && ks == 0) ? 0u : 1u;
           const uint64_t fd = sdesc_mnmajor_sw128(st + QM_SFA + ks * 2048, QM_RT);
-          tc_mma(tmem + QM_TN, km_sdesc_kmajor_sw64(w) + 2u * ks, fd, id_n, acc);
-          tc_mma(tmem + QM_TD, km_sdesc_kmajor_sw64(w + QM_WT) + 2u * ks, fd, id_n, acc);
-          tc_mma(tmem + QM_TL, km_sdesc_kmajor_sw64(w + 2 * QM_WT) + 2u * ks, fd, id_l, acc);
-          tc_mma(tmem + QM_TM, km_sdesc_kmajor_sw64(w + 3 * QM_WT) + 2u * ks, fd, id_l, acc);
+          if (elect_one()) tc_mma(tmem + QM_TN, km_sdesc_kmajor_sw64(w) + 2u * ks, fd, id_n, acc);
+          if (elect_one()) tc_mma(tmem + QM_TD, km_sdesc_kmajor_sw64(w + QM_WT) + 2u * ks, fd, id_n, acc);
+          if (elect_one()) tc_mma(tmem + QM_TL, km_sdesc_kmajor_sw64(w + 2 * QM_WT) + 2u * ks, fd, id_l, acc);
+          if (elect_one()) tc_mma(tmem + QM_TM, km_sdesc_kmajor_sw64(w + 3 * QM_WT) + 2u * ks, fd, id_l, acc);
         }
-        tc_commit(&w_empty[wb]);
-        tc_commit(&st_empty[svj % QM_STAGES]);
+        if (elect_one()) tc_commit(&w_empty[wb]);
+        if (elect_one()) tc_commit(&st_empty[svj % QM_STAGES]);
         return true;
       };
       // S / C of the tile with global index svj (the single S / C buffer is free once the weight warps read the
       // previous tile's)
       auto scores = [&](int svj) {
         const int sl = svj % QM_STAGES;
-        if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(svj / QM_STAGES) & 1u, p.status) ||
-            !mbar_wait(s_empty, (static_cast<uint32_t>(svj) & 1u) ^ 1u, p.status))
+        if (!mbar_wait_warp(&st_full[sl], static_cast<uint32_t>(svj / QM_STAGES) & 1u, p.status) ||
+            !mbar_wait_warp(s_empty, (static_cast<uint32_t>(svj) & 1u) ^ 1u, p.status))
           return false;
         tc_fence_after();
         const uint32_t st = sbase + QM_RING + sl * QM_STAGE;
         const uint64_t qd = sdesc_kmajor_sw128(sbase + QM_Q), hd = sdesc_kmajor_sw128(sbase + QM_H);
         const uint64_t kd = sdesc_kmajor_sw128(st + QM_SK), vd = sdesc_kmajor_sw128(st + QM_SV);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(tmem + QM_TS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
+        for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(tmem + QM_TS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(tmem + QM_TC, hd + 2u * k, vd + 2u * k, id_s, k > 0);
-        tc_commit(&s_full[0]);
+        for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(tmem + QM_TC, hd + 2u * k, vd + 2u * k, id_s, k > 0);
+        if (elect_one()) tc_commit(&s_full[0]);
         return true;
       };
       for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
         const int qt = nqt - 1 - w / p.rows;
         int lo, hi;
         tiles_of(qt, lo, hi);
-        if (!mbar_wait(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+        if (!mbar_wait_warp(q_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
         ok = scores(sv);
         for (int j = lo; j <= hi && ok; ++j, ++sv) {
           if (j + 1 <= hi) ok = scores(sv + 1);
-          if (ok && j == lo) ok = mbar_wait(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status);
+          if (ok && j == lo) ok = mbar_wait_warp(acc_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status);
           if (ok) ok = moments(sv, j == lo);
         }
         if (ok) {
-          tc_commit(q_empty);
-          tc_commit(acc_full);
+          if (elect_one()) tc_commit(q_empty);
+          if (elect_one()) tc_commit(acc_full);
         }
       }
-      tc_commit(drain);
-      mbar_wait(drain, 0, p.status);
+      if (elect_one()) tc_commit(drain);
+      mbar_wait_warp(drain, 0, p.status);
     }
   } else {
     const int quarter = warp & 3, half = (warp - 2) >> 2;

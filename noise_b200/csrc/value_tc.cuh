@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
         mbar_wait(&st_full[j % TV_STAGES], static_cast<uint32_t>(j / TV_STAGES) & 1u, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {  // the whole warp runs the issuer; one elected lane issues the MMAs and commits
       constexpr uint32_t idesc_s = idesc_bf16(TV_B, TV_B);
       constexpr uint32_t idesc_pv = idesc_bf16(TV_B, 64, false, true);
       int sv = 0, nitem = 0;
@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
         int first_pv[2] = {1, 1};
         auto issue_pv = [&](int g, int svi) {  // O_g += P_g hi + P_g lo of the receiver tile in ring slot svi
           const int sl = svi % TV_STAGES;
-          if (!mbar_wait(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
+          if (!mbar_wait_warp(&p_full[g], static_cast<uint32_t>(pv_count[g]) & 1u, p.status)) return false;
           tc_fence_after();
           const uint32_t pbase = sbase + TV_P + g * 2 * TV_TILE;
           const uint32_t stage = sbase + TV_RING + sl * TV_STAGE;
@@ -205,56 +205,58 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
             for (int ks = 0; ks < TV_B / 16; ++ks) {
               const uint64_t ad = sdesc_kmajor_sw128(pbase + (ks >> 2) * TV_TILE) + 2u * (ks & 3);
               const uint64_t bd = sdesc_mnmajor_sw128(bbase + ks * 2048, 16);
-              tc_mma(tmem + 256 + ob * 128 + g * 64, ad, bd, idesc_pv, !(first_pv[g] && part == 0 && ks == 0));
+              if (elect_one())
+                tc_mma(tmem + 256 + ob * 128 + g * 64, ad, bd, idesc_pv, !(first_pv[g] && part == 0 && ks == 0));
             }
           }
           first_pv[g] = 0;
-          tc_commit(&p_empty[g]);
+          if (elect_one()) tc_commit(&p_empty[g]);
           ++pv_count[g];
           return true;
         };
-        if (!mbar_wait(&o_empty[ob], (static_cast<uint32_t>(nitem >> 1) & 1u) ^ 1u, p.status) ||
-            !mbar_wait(k_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+        if (!mbar_wait_warp(&o_empty[ob], (static_cast<uint32_t>(nitem >> 1) & 1u) ^ 1u, p.status) ||
+            !mbar_wait_warp(k_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
           ok = false;
           break;
         }
         const int sv0 = sv;
         for (int st = it.lo; st <= it.hi && ok; ++st, ++sv) {
           const int sl = sv % TV_STAGES;
-          if (!mbar_wait(&st_full[sl], static_cast<uint32_t>(sv / TV_STAGES) & 1u, p.status)) {
+          if (!mbar_wait_warp(&st_full[sl], static_cast<uint32_t>(sv / TV_STAGES) & 1u, p.status)) {
             ok = false;
             break;
           }
           const uint64_t qd = sdesc_kmajor_sw128(sbase + TV_RING + sl * TV_STAGE);
           for (int g = 0; g < 2 && ok; ++g) {
             if (!sees(g, st)) continue;
-            if (!mbar_wait(&s_empty[g], (static_cast<uint32_t>(s_count[g]) & 1u) ^ 1u, p.status)) {
+            if (!mbar_wait_warp(&s_empty[g], (static_cast<uint32_t>(s_count[g]) & 1u) ^ 1u, p.status)) {
               ok = false;
               break;
             }
             tc_fence_after();
             const uint64_t kd = sdesc_kmajor_sw128(sbase + TV_K + g * TV_TILE);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) tc_mma(tmem + g * TV_B, kd + 2u * k, qd + 2u * k, idesc_s, k > 0);
-            tc_commit(&s_full[g]);
+            for (int k = 0; k < 4; ++k)
+              if (elect_one()) tc_mma(tmem + g * TV_B, kd + 2u * k, qd + 2u * k, idesc_s, k > 0);
+            if (elect_one()) tc_commit(&s_full[g]);
             ++s_count[g];
           }
-          if (st == it.hi && ok) tc_commit(k_empty);  // the item's last S MMAs read K
+          if (st == it.hi && ok && elect_one()) tc_commit(k_empty);  // the item's last S MMAs read K
           if (st > it.lo && ok) {  // O MMAs of the previous receiver tile, then release its ring slot
             for (int g = 0; g < 2 && ok; ++g)
               if (sees(g, st - 1)) ok = issue_pv(g, sv - 1);
-            tc_commit(&st_empty[(sv - 1) % TV_STAGES]);
+            if (elect_one()) tc_commit(&st_empty[(sv - 1) % TV_STAGES]);
           }
         }
         if (ok) {
           for (int g = 0; g < 2 && ok; ++g)
             if (sees(g, it.hi)) ok = issue_pv(g, sv0 + (it.hi - it.lo));
-          tc_commit(&st_empty[(sv - 1) % TV_STAGES]);
-          tc_commit(&o_full[ob]);
+          if (elect_one()) tc_commit(&st_empty[(sv - 1) % TV_STAGES]);
+          if (elect_one()) tc_commit(&o_full[ob]);
         }
       }
-      tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
-      mbar_wait(drain, 0, p.status);
+      if (elect_one()) tc_commit(drain);  // every MMA of this CTA done before TMEM is freed
+      mbar_wait_warp(drain, 0, p.status);
     }
   } else {
     // groups: warps 2..5 -> key tile A, 6..9 -> B; thread = key row of the group's tile
