@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       const int tk = kt * KM_B + r;
       int lo, hi;
       tiles_of(kt, lo, hi);
-      float s1 = 0.f, s2 = 0.f;
+      float2 s1p = make_float2(0.f, 0.f), s2p = make_float2(0.f, 0.f);  // even / odd receivers' partial sums
       for (int j = lo; j <= hi && ok; ++j, ++sv) {
         const int b = sv & 1;
         if (!mbar_wait(&s_full[b], static_cast<uint32_t>(sv >> 1) & 1u, p.status)) {
@@ -401,30 +401,29 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         const int s0 = j * KM_R + half * 16;
         const bool full = s0 >= kt * KM_B + KM_B - 1 && s0 + 15 - kt * KM_B <= p.window;
         uint32_t pw1[8], pw2[8], pw2l[8], pp[8];
+        // receivers in pairs: packed fp32x2 arithmetic, two exponentials on the MUFU pipe
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          float x1v[2], x2v[2], x2lv[2], av[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float logit = s[e + u] * 0.125f;
-            float a = ex2_approx(fmaf(s[e + u], SL2, -lse[e + u] * L2E));
-            if (!full) {
-              const int sr = s0 + e + u;
-              if (sr < tk || sr - tk > p.window) a = 0.f;
-            }
-            const float cc = c[e + u] - ctr[e + u];
-            const float x1 = a * cc, x2 = (0.5f * a - a * a) * cc;
-            s1 += x1 * logit;
-            s2 += x2 * logit * logit;
-            x1v[u] = x1;
-            x2v[u] = x2;
-            x2lv[u] = x2 * logit;
-            av[u] = a;
+          const float2 sc = make_float2(s[e], s[e + 1]);
+          const float2 logit = __fmul2_rn(sc, make_float2(0.125f, 0.125f));
+          const float2 arg = __ffma2_rn(sc, make_float2(SL2, SL2), __fmul2_rn(make_float2(-lse[e], -lse[e + 1]),
+                                                                               make_float2(L2E, L2E)));
+          float2 a = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+          if (!full) {
+            if (s0 + e < tk || s0 + e - tk > p.window) a.x = 0.f;
+            if (s0 + e + 1 < tk || s0 + e + 1 - tk > p.window) a.y = 0.f;
           }
-          pw1[e / 2] = pack_bf16x2(x1v[0], x1v[1]);
-          pw2[e / 2] = pack_bf16x2(x2v[0], x2v[1]);
-          pw2l[e / 2] = pack_bf16x2(x2lv[0], x2lv[1]);
-          pp[e / 2] = pack_bf16x2(av[0], av[1]);
+          const float2 cc = __fadd2_rn(make_float2(c[e], c[e + 1]), make_float2(-ctr[e], -ctr[e + 1]));
+          const float2 x1 = __fmul2_rn(a, cc);
+          const float2 half_a = __fmul2_rn(make_float2(0.5f, 0.5f), a);
+          const float2 x2 = __fmul2_rn(__ffma2_rn(make_float2(-a.x, -a.y), a, half_a), cc);  // (a / 2 - a^2) c
+          const float2 x2l = __fmul2_rn(x2, logit);
+          s1p = __ffma2_rn(x1, logit, s1p);
+          s2p = __ffma2_rn(x2l, logit, s2p);
+          pw1[e / 2] = pack_bf16x2(x1.x, x1.y);
+          pw2[e / 2] = pack_bf16x2(x2.x, x2.y);
+          pw2l[e / 2] = pack_bf16x2(x2l.x, x2l.y);
+          pp[e / 2] = pack_bf16x2(a.x, a.y);
         }
         if (!mbar_wait(&w_empty[b], (static_cast<uint32_t>(sv >> 1) & 1u) ^ 1u, p.status)) {
           ok = false;
@@ -459,8 +458,8 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) rsq = fmaf(rv[i], rv[i], rsq);
       }
-      sums[(half * 3) * 128 + r] = s1;
-      sums[(half * 3 + 1) * 128 + r] = s2;
+      sums[(half * 3) * 128 + r] = s1p.x + s1p.y;
+      sums[(half * 3 + 1) * 128 + r] = s2p.x + s2p.y;
       sums[(half * 3 + 2) * 128 + r] = rsq;
       km_bar_sync();
       const float a1 = sums[r] + sums[3 * 128 + r], a2 = sums[128 + r] + sums[4 * 128 + r];

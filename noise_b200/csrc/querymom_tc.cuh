@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
       const float lse_r = p.lse[ti], hout_r = p.hub_out[ti];
       int lo, hi;
       tiles_of(qt, lo, hi);
-      float s1n = 0.f, s2n = 0.f, s1d = 0.f, s2d = 0.f;
+      // even / odd keys' partial sums
+      float2 s1n = make_float2(0.f, 0.f), s2n = s1n, s1d = s1n, s2d = s1n;
       for (int j = lo; j <= hi && ok; ++j, ++sv) {
         if (!mbar_wait(s_full, static_cast<uint32_t>(sv) & 1u, p.status)) {
           ok = false;
@@ -283,32 +284,28 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         const int t0 = j * QM_R + half * 16;
         const bool full = t0 + 15 <= qt * QM_B && qt * QM_B + QM_B - 1 - t0 <= p.window;
         uint32_t pw[8], pa[8], pwl[8], pal[8];
+        // keys in pairs: packed fp32x2 arithmetic, two exponentials on the MUFU pipe
+        const float2 nl = make_float2(-lse_r * L2E, -lse_r * L2E), nh = make_float2(-hout_r, -hout_r);
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          float wv[2], av[2], wlv[2], alv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float logit = s[e + u] * 0.125f;
-            float a = ex2_approx(fmaf(s[e + u], SL2, -lse_r * L2E));
-            if (!full) {
-              const int tk = t0 + e + u;
-              if (tk > sq || sq - tk > p.window) a = 0.f;
-            }
-            const float wn = a * (c[e + u] - hout_r);
-            const float wl = wn * logit, al = a * logit;
-            s1n += wl;
-            s2n += wl * logit;
-            s1d += al;
-            s2d += al * logit;
-            wv[u] = wn;
-            av[u] = a;
-            wlv[u] = wl;
-            alv[u] = al;
+          const float2 sc = make_float2(s[e], s[e + 1]);
+          const float2 logit = __fmul2_rn(sc, make_float2(0.125f, 0.125f));
+          const float2 arg = __ffma2_rn(sc, make_float2(SL2, SL2), nl);
+          float2 a = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));
+          if (!full) {
+            if (t0 + e > sq || sq - (t0 + e) > p.window) a.x = 0.f;
+            if (t0 + e + 1 > sq || sq - (t0 + e + 1) > p.window) a.y = 0.f;
           }
-          pw[e / 2] = pack_bf16x2(wv[0], wv[1]);
-          pa[e / 2] = pack_bf16x2(av[0], av[1]);
-          pwl[e / 2] = pack_bf16x2(wlv[0], wlv[1]);
-          pal[e / 2] = pack_bf16x2(alv[0], alv[1]);
+          const float2 wn = __fmul2_rn(a, __fadd2_rn(make_float2(c[e], c[e + 1]), nh));
+          const float2 wl = __fmul2_rn(wn, logit), al = __fmul2_rn(a, logit);
+          s1n = __fadd2_rn(s1n, wl);
+          s2n = __ffma2_rn(wl, logit, s2n);
+          s1d = __fadd2_rn(s1d, al);
+          s2d = __ffma2_rn(al, logit, s2d);
+          pw[e / 2] = pack_bf16x2(wn.x, wn.y);
+          pa[e / 2] = pack_bf16x2(a.x, a.y);
+          pwl[e / 2] = pack_bf16x2(wl.x, wl.y);
+          pal[e / 2] = pack_bf16x2(al.x, al.y);
         }
         const int b = sv & 1;
         if (!mbar_wait(&w_empty[b], (static_cast<uint32_t>(sv >> 1) & 1u) ^ 1u, p.status)) {
@@ -330,10 +327,10 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         if (lane == 0) mbar_arrive(&w_full[b]);
       }
       if (!ok) break;
-      sums[(half * 4) * 128 + r] = s1n;
-      sums[(half * 4 + 1) * 128 + r] = s2n;
-      sums[(half * 4 + 2) * 128 + r] = s1d;
-      sums[(half * 4 + 3) * 128 + r] = s2d;
+      sums[(half * 4) * 128 + r] = s1n.x + s1n.y;
+      sums[(half * 4 + 1) * 128 + r] = s2n.x + s2n.y;
+      sums[(half * 4 + 2) * 128 + r] = s1d.x + s1d.y;
+      sums[(half * 4 + 3) * 128 + r] = s2d.x + s2d.y;
       km_bar_sync();
       const float v1n = sums[r] + sums[4 * 128 + r], v2n = sums[128 + r] + sums[5 * 128 + r];
       const float v1d = sums[2 * 128 + r] + sums[6 * 128 + r], v2d = sums[3 * 128 + r] + sums[7 * 128 + r];
