@@ -242,12 +242,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           if (m == -INFINITY) continue;  // every logit so far masked
           const float off = -m * L2E;
+          // pairs: packed fp32x2 arithmetic into even / odd partial sums
+          float2 l2 = make_float2(0.f, 0.f), sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float pe = ex2_approx(fmaf(s[e], SL2, off));  // masked: 2^-inf = 0
-            l += pe;
-            sum = fmaf(pe, cc[e], sum);
+          for (int e = 0; e < 32; e += 2) {
+            const float2 arg = __ffma2_rn(make_float2(s[e], s[e + 1]), make_float2(SL2, SL2), make_float2(off, off));
+            const float2 pe = make_float2(ex2_approx(arg.x), ex2_approx(arg.y));  // masked: 2^-inf = 0
+            l2 = __fadd2_rn(l2, pe);
+            sum2 = __ffma2_rn(pe, make_float2(cc[e], cc[e + 1]), sum2);
           }
+          l += l2.x + l2.y;
+          sum += sum2.x + sum2.y;
         }
       };
       for (int kt = rg.lo; kt <= rg.hi && ok; ++kt, ++cnt) {

@@ -292,9 +292,15 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
           const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
           float pe[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            pe[e] = ex2_approx(fmaf(v[c + e], SL2, -lv[e] * L2E));
-            if constexpr (MASKED) {
+          for (int e = 0; e < 8; e += 2) {  // pairs: packed fp32x2 FMAs, the rounding of scalar ones
+            const float2 nl = __fmul2_rn(make_float2(-lv[e], -lv[e + 1]), make_float2(L2E, L2E));
+            const float2 arg = __ffma2_rn(make_float2(v[c + e], v[c + e + 1]), make_float2(SL2, SL2), nl);
+            pe[e] = ex2_approx(arg.x);
+            pe[e + 1] = ex2_approx(arg.y);
+          }
+          if constexpr (MASKED) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
               const int s = st * TV_B + c + e;
               if (s < tk || s - tk > p.window) pe[e] = 0.f;
             }
