@@ -402,7 +402,7 @@ struct EpiQKV {
 
 // x += bf16(acc) + sign bf16(sum of the row's partial dots) a  (c_proj and mlp.c_proj, eggroll.py:92-93).
 struct EpiResid {
-  static constexpr int CH = 32;
+  static constexpr int CH = 64;
   static constexpr bool PIPELINED = false;
   int T, nparts;
   const float* sign;
@@ -429,43 +429,52 @@ struct EpiResid {
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
-    // the linear's output for this thread's row (32 columns, 128 bytes) -> staging
-    const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
-    const int lane = threadIdx.x & 31;
-    const float2 coef2 = make_float2(coef, coef);
-    // columns in pairs: one packed bf16 conversion per rounding and fp32x2 FMAs, with the rounding of scalar ones
-#pragma unroll
-    for (int i = 0; i < CH / 4; ++i) {
-      const float4 av = a4[i];
-      float2 y0 = __ffma2_rn(coef2, make_float2(av.x, av.y), unpack_bf16x2(pack_bf16x2(acc[4 * i], acc[4 * i + 1])));
-      float2 y1 =
-          __ffma2_rn(coef2, make_float2(av.z, av.w), unpack_bf16x2(pack_bf16x2(acc[4 * i + 2], acc[4 * i + 3])));
-      if (jit) {
-        const float4 jv = *reinterpret_cast<const float4*>(jit + static_cast<int64_t>(row) * D + col + 4 * i);
-        y0 = __fadd2_rn(y0, make_float2(jv.x, jv.y));
-        y1 = __fadd2_rn(y1, make_float2(jv.z, jv.w));
-      }
-      sts128(stg_addr(stg, lane, i), make_uint4(__float_as_uint(y0.x), __float_as_uint(y0.y), __float_as_uint(y1.x),
-                                                __float_as_uint(y1.y)));
-    }
-    __syncwarp();
-    // x += y for rows row - lane .. + 31, 4 whole 128-byte rows per instruction
-    const int c = lane & 7;
+    const int lane = threadIdx.x & 31, c = lane & 7;
+    // x of rows row - lane .. + 31, columns col .. col + 63 (two 32-column halves, 4 whole 128-byte row segments per
+    // instruction): every load is issued first, so the warp has 8 KB of the residual stream in flight while it
+    // forms y (the epilogue is bound by the latency of these loads)
     float4* xr = reinterpret_cast<float4*>(x + static_cast<int64_t>(row - lane) * D + col) + c;
-    float4 xv[8];
+    float4 xv[16];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) xv[i] = xr[((lane >> 3) + 4 * i) * (D / 4)];  // all loads before any store
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = (lane >> 3) + 4 * i;
-      const uint4 yv = lds128(stg_addr(stg, r, c));
-      const float2 s0 =
-          __fadd2_rn(make_float2(xv[i].x, xv[i].y), make_float2(__uint_as_float(yv.x), __uint_as_float(yv.y)));
-      const float2 s1 =
-          __fadd2_rn(make_float2(xv[i].z, xv[i].w), make_float2(__uint_as_float(yv.z), __uint_as_float(yv.w)));
-      xr[r * (D / 4)] = make_float4(s0.x, s0.y, s1.x, s1.y);
+      for (int i = 0; i < 8; ++i) xv[8 * h + i] = xr[((lane >> 3) + 4 * i) * (D / 4) + 8 * h];
+    const float4* a4 = reinterpret_cast<const float4*>(scratch + (col - col0));
+    const float2 coef2 = make_float2(coef, coef);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      // the linear's output for this thread's row (32 columns, 128 bytes) -> staging; columns in pairs: one packed
+      // bf16 conversion per rounding and fp32x2 FMAs, with the rounding of scalar ones
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 av = a4[8 * h + i];
+        const float* ac = acc + 32 * h + 4 * i;
+        float2 y0 = __ffma2_rn(coef2, make_float2(av.x, av.y), unpack_bf16x2(pack_bf16x2(ac[0], ac[1])));
+        float2 y1 = __ffma2_rn(coef2, make_float2(av.z, av.w), unpack_bf16x2(pack_bf16x2(ac[2], ac[3])));
+        if (jit) {
+          const float4 jv =
+              *reinterpret_cast<const float4*>(jit + static_cast<int64_t>(row) * D + col + 32 * h + 4 * i);
+          y0 = __fadd2_rn(y0, make_float2(jv.x, jv.y));
+          y1 = __fadd2_rn(y1, make_float2(jv.z, jv.w));
+        }
+        sts128(stg_addr(stg, lane, i), make_uint4(__float_as_uint(y0.x), __float_as_uint(y0.y),
+                                                  __float_as_uint(y1.x), __float_as_uint(y1.y)));
+      }
+      __syncwarp();
+      // x += y for rows row - lane .. + 31
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = (lane >> 3) + 4 * i;
+        const uint4 yv = lds128(stg_addr(stg, r, c));
+        const float4 xo = xv[8 * h + i];
+        const float2 s0 =
+            __fadd2_rn(make_float2(xo.x, xo.y), make_float2(__uint_as_float(yv.x), __uint_as_float(yv.y)));
+        const float2 s1 =
+            __fadd2_rn(make_float2(xo.z, xo.w), make_float2(__uint_as_float(yv.z), __uint_as_float(yv.w)));
+        xr[r * (D / 4) + 8 * h] = make_float4(s0.x, s0.y, s1.x, s1.y);
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
 };
 
