@@ -292,6 +292,16 @@ def run_ours(a):
                     'peak_source': src + ' hbm_gbs', 'algorithmic_bytes_per_launch': nbytes}
     roofline['traffic'] = tr * m_launch * T if tr is not None else None
     roofline['step'] = {'achieved_tflops': round(step_tf, 1), 'frac': round(step_tf / tf_peak, 4)}
+    if dom == 'attention':
+        # attention's other roof: one exponential per visible pair on the MUFU pipe, at its nominal 16 a SM-cycle
+        # (not a measured peak) and the median SM clock sampled under load
+        mhz = (clk or {}).get('sm_mhz') or peaks.get('sm_max_mhz', 1965.0)
+        exp_rate = flops / 256.0 / per_launch_s
+        mufu_peak = 16 * 148 * mhz * 1e6
+        roofline['mufu'] = {'achieved_gexp_s': round(exp_rate / 1e9, 1),
+                            'nominal_peak_gexp_s': round(mufu_peak / 1e9, 1),
+                            'frac': round(exp_rate / mufu_peak, 4), 'sm_mhz': mhz,
+                            'basis': 'nominal 16 ex2 per SM-cycle x 148 SMs at the median SM clock under load'}
 
     line = {
         'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
