@@ -9,16 +9,17 @@
 // One CTA per (member x head, pair of 128-query tiles A = 2i, B = 2i + 1), 320 threads:
 //   warp 0      TMA: Q_A, Q_B once, then 128-key K / V tiles (the union of both tiles' key ranges) into a 3-stage
 //               ring (128-byte swizzle); both query tiles share every K / V load;
-//   warp 1      TMEM (512 columns: S_A, S_B 128 each, O_A, O_B 64 each, P_A, P_B 64 each) and one lane issuing,
-//               per key tile, S_w = Q_w K^T (M=128, N=128, K=64) for each tile w that sees it, then O_w += P_w V of
+//   warp 1      TMEM (512 columns: S_A, S_B 128 each, O_A, O_B 64 each, P_A, P_B 64 each); the whole warp runs
+//               the issue loop and an elect.sync lane issues, per key tile, S_w = Q_w K^T (M=128, N=128, K=64) for
+//               each tile w that sees it, then O_w += P_w V of
 //               the previous key tile (M=128, N=64, K=128; P the A operand read from tensor memory, V an MN-major
 //               shared-memory operand);
 //   warps 2..5  softmax group A, warps 6..9 group B: one query row per thread; S_w is read with one batched
 //               tcgen05.ld and released at once, P = exp2(s log2(e) / 8 - 8 log2(e)) goes as packed bf16 pairs into
 //               the group's P columns of tensor memory (tcgen05.st; the A operand of the next O MMA, so the MMAs read
-//               only V from shared memory), every exponential on the MUFU pipe (it is
-//               under half busy: moving a share to an FMA polynomial measured slower); at the end y = O / l (bf16)
-//               and the per-head partial dot y . b of the c_proj rank-1 term.
+//               only V from shared memory), every exponential on the MUFU pipe (moving a share to an FMA
+//               polynomial measured slower); at the end y = O / l (bf16) and the per-head partial dot y . b of the
+//               c_proj rank-1 term.
 // Only the diagonal key tile and the window's first tile take the masked path.
 #pragma once
 #include <type_traits>

@@ -17,8 +17,9 @@
 //   warp 0      TMA: K, V once per item; per receiver tile q, hub, f2, g2, xy (and hi, lo) and lse / center into
 //               a ring (5 stages IDENT, 2 SCAN);
 //   warp 1      TMEM (512 columns): S = K Q^T and C = V H^T (32 columns each, double-buffered), the accumulators
-//               P2 (64), R2 (64), Q2 | QXY (96: g2 and xy as one 96-wide B operand) and VA (64); one lane issues
-//               S / C of tile j + AHEAD ahead of the moment MMAs of tile j (M = 128 keys, K = 32 receivers);
+//               P2 (64), R2 (64), Q2 | QXY (96: g2 and xy as one 96-wide B operand) and VA (64); the whole warp
+//               runs the issue loop and an elect.sync lane issues S / C of tile j + AHEAD ahead of the moment MMAs of
+//               tile j (M = 128 keys, K = 32 receivers);
 //   warps 2..9  warp w: key rows of TMEM lane quarter w % 4, receivers half (w - 2) / 4 of each tile: the weights
 //               as bf16 into one of two 64-byte-swizzled shared buffers (the moment MMAs' A operands), so a tile's
 //               weights are written while the previous tile's moment MMAs run; at the item's end the response

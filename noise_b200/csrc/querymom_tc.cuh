@@ -15,8 +15,9 @@
 //               fc = (x y | 0) (32 rows each, adjacent: fa | fb | fc is one 160-wide MN-major operand) into a
 //               5-stage ring;
 //   warp 1      TMEM (512 columns): S = Q K^T, C = H V^T (32 columns each), the accumulators N = W (fa | fb | fc)
-//               (160), D = A (fa | fb | fc) (160), L = WL fa (64), M = AL fa (64); one lane issues S / C of tile
-//               j + 1 (once the weight warps have read tile j's) ahead of the moment MMAs of tile j;
+//               (160), D = A (fa | fb | fc) (160), L = WL fa (64), M = AL fa (64); the whole warp runs the issue
+//               loop and an elect.sync lane issues S / C of tile j + 1 (once the weight warps have read tile j's)
+//               ahead of the moment MMAs of tile j;
 //   warps 2..9  warp w: query rows of TMEM lane quarter w % 4, keys half (w - 2) / 4 of each tile: the four weights
 //               as bf16 into one of two 64-byte-swizzled buffers; at the item's end the response epilogue for its 16
 //               rotary pairs.

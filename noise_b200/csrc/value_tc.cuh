@@ -6,9 +6,9 @@
 // tiles A, B of one row sharing every 128-receiver tile; 320 threads, one CTA per SM, persistent:
 //   warp 0      TMA: K_A, K_B once, then per receiver tile its q rows, source hi / lo rows and lse values into a
 //               2-stage ring (128-byte swizzle for the bf16 tiles);
-//   warp 1      TMEM (S_A, S_B 128 columns each, O double-buffered 2 x (64 + 64)) and one lane issuing S_g = K_g Q^T
-//               (M=128 keys, N=128 receivers, K=64) and O_g += P_g hi + P_g lo (M=128, N=64, K=128; hi / lo
-//               MN-major operands);
+//   warp 1      TMEM (S_A, S_B 128 columns each, O double-buffered 2 x (64 + 64)); the whole warp runs the issue
+//               loop and an elect.sync lane issues S_g = K_g Q^T (M=128 keys, N=128 receivers, K=64) and
+//               O_g += P_g hi + P_g lo (M=128, N=64, K=128; hi / lo MN-major operands);
 //   warps 2..9  two groups of 4 warps (tile A, tile B), one key row per thread: P = exp2(s log2(e) / 8 - lse_s
 //               log2(e)) (<= 1), masked to 0 <= s - t <= window, as bf16 into swizzled shared memory; at the end O
 //               (fp32) to the output view.
