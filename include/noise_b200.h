@@ -23,7 +23,7 @@ extern "C" {
 #define NOISE_ERR_SHAPE 1       /* unsupported size (e.g. T not a multiple of 128, members < 1) */
 #define NOISE_ERR_ALIGN 2       /* a pointer or stride violates the 16-byte TMA / vector alignment rule */
 #define NOISE_ERR_WORKSPACE 3   /* workspace NULL or smaller than the *_workspace_bytes query */
-#define NOISE_ERR_ARGUMENT 4    /* NULL required pointer or bad enum value */
+#define NOISE_ERR_ARGUMENT 4    /* NULL required pointer, bad enum value, or a stream of another device */
 #define NOISE_ERR_CUDA 5        /* a CUDA runtime/driver call failed (launch, tensor-map encode, attributes) */
 #define NOISE_ERR_DEVICE 6      /* not an sm_100 device */
 #define NOISE_ERR_TOO_LARGE 7   /* size beyond the static scratch of noise_population_loss_noalloc */
@@ -591,13 +591,20 @@ int noise_head_loss(const float* x, const void* weight, const int64_t* targets, 
  * library routine. The first call on a device looks up the array's device address (cudaGetSymbolAddress, with
  * that device current); make that first call before any stream capture. All calls share the one array and it
  * keeps the last call's contents (the status word is cleared at the start of each call): calls that overlap on the
- * GPU (concurrent streams, or threads sharing a device) race on it, so serialise them. The device status word is the
- * array's first int and is not readable through noise_read_status (it has no host-visible workspace pointer). */
+ * GPU (concurrent streams, or threads sharing a device) race on it, so serialise them. `stream` must belong to the
+ * current device (the array used is the current device's): a stream of another device, or a current device index
+ * at or above NOISE_STATIC_MAX_DEVICES, returns NOISE_ERR_ARGUMENT. The device status word is the array's first int;
+ * read it with noise_read_static_status. */
 #define NOISE_STATIC_SCRATCH_BYTES (48u << 20)
 #define NOISE_STATIC_MAX_DEVICES 64
 int noise_population_loss_noalloc(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
                                   const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
                                   float* losses, void* stream);
+
+/* No counterpart in the reference: the device status word of noise_population_loss_noalloc's static scratch on the
+ * current device, copied to *status after `stream` (which must belong to the current device) is synchronised.
+ * NOISE_DEVICE_TIMEOUT there means a bounded wait of the last call gave up and its losses are not valid. */
+int noise_read_static_status(int* status, void* stream);
 
 /* D[m, n] (fp32, row-major) = A[m, k] . B[n, k]^T for bf16 row-major A and B, on the persistent tcgen05/TMA GEMM
  * that every linear layer of noise_population_loss runs on, with a plain store epilogue. Stands in for the cuBLAS

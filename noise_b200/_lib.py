@@ -96,6 +96,7 @@ SIGNATURES = [
     ('noise_population_loss_noalloc', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.POINTER(Slice), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_read_static_status', ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_void_p]),
     ('noise_gemm_bf16_tn', ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
       ctypes.c_void_p]),
@@ -203,6 +204,15 @@ def read_status(workspace):
     out = ctypes.c_int(0)
     check(lib().noise_read_status(workspace.data_ptr(), ctypes.byref(out), stream_handle(workspace.device)),
           'noise_read_status')
+    return out.value
+
+
+def read_static_status(device):
+    """Device status word of the no-allocation entry point's static scratch on ``device`` (synchronises the
+    device's current stream)."""
+    out = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        check(lib().noise_read_static_status(ctypes.byref(out), stream_handle(device)), 'noise_read_static_status')
     return out.value
 
 

@@ -1502,29 +1502,49 @@ static __device__ __align__(256) unsigned char g_static_scratch[NOISE_STATIC_SCR
 static void* g_static_scratch_addr[NOISE_STATIC_MAX_DEVICES];
 static std::mutex g_static_scratch_mutex;
 
+namespace noise {
+
+// Device address of the current device's copy of g_static_scratch, after checking that `stream` belongs to that
+// device (a stream of another device would run the kernels against the wrong GPU's array).
+static int static_scratch(cudaStream_t stream, void** out) {
+  int dev = 0, sdev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (dev < 0 || dev >= NOISE_STATIC_MAX_DEVICES) return NOISE_ERR_ARGUMENT;
+  if (cudaStreamGetDevice(stream, &sdev) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (sdev != dev) return NOISE_ERR_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (!g_static_scratch_addr[dev]) {  // first call on this device: resolve the array's device address
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_static_scratch) != cudaSuccess || !addr) return NOISE_ERR_CUDA;
+    g_static_scratch_addr[dev] = addr;
+  }
+  *out = g_static_scratch_addr[dev];
+  return NOISE_OK;
+}
+
+}  // namespace noise
+
 int noise_population_loss_noalloc(const noise_gpt_t* model, const noise_slice_t* noise, const float* sign,
                                   const int64_t* idx, const int64_t* targets, int members, int tokens, int reduction,
                                   float* losses, void* stream) {
   const size_t need = noise_population_workspace_bytes(members, tokens);
   if (need == 0) return NOISE_ERR_SHAPE;
   if (need > NOISE_STATIC_SCRATCH_BYTES) return NOISE_ERR_TOO_LARGE;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return NOISE_ERR_CUDA;
-  if (dev < 0 || dev >= NOISE_STATIC_MAX_DEVICES) return NOISE_ERR_DEVICE;
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
-    if (!g_static_scratch_addr[dev]) {  // first call on this device: resolve the array's device address
-      void* addr = nullptr;
-      if (cudaGetSymbolAddress(&addr, g_static_scratch) != cudaSuccess || !addr) return NOISE_ERR_CUDA;
-      g_static_scratch_addr[dev] = addr;
-    }
-    scratch = g_static_scratch_addr[dev];
-  }
+  const int rc = static_scratch(static_cast<cudaStream_t>(stream), &scratch);
+  if (rc) return rc;
   // The status word at the head of the scratch is cleared by noise_population_loss itself; every other buffer is
   // fully written before it is read, so stale contents of an earlier call never leak into this one.
   return noise_population_loss(model, noise, sign, idx, targets, members, tokens, reduction, losses, scratch,
                                NOISE_STATIC_SCRATCH_BYTES, stream);
+}
+
+int noise_read_static_status(int* status, void* stream) {
+  if (!status) return NOISE_ERR_ARGUMENT;
+  void* scratch = nullptr;
+  const int rc = static_scratch(static_cast<cudaStream_t>(stream), &scratch);
+  if (rc) return rc;
+  return noise_read_status(scratch, status, stream);
 }
 
 int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace,
@@ -1571,7 +1591,7 @@ const char* noise_status_string(int status) {
     case NOISE_ERR_SHAPE: return "unsupported shape";
     case NOISE_ERR_ALIGN: return "misaligned pointer or stride";
     case NOISE_ERR_WORKSPACE: return "workspace missing or too small";
-    case NOISE_ERR_ARGUMENT: return "invalid argument";
+    case NOISE_ERR_ARGUMENT: return "invalid argument (NULL pointer, bad enum value, or a stream or device index the entry point does not take)";
     case NOISE_ERR_CUDA: return "CUDA call failed";
     case NOISE_ERR_DEVICE: return "not an sm_100 device";
     case NOISE_ERR_TOO_LARGE: return "members x tokens exceed the static scratch of the no-allocation entry point";

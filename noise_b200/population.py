@@ -139,15 +139,23 @@ def _packed_for(model, p):
     return cached.refresh()
 
 
-def _run(packed, slices, keep, sign, idx, targets, reduction):
-    dev = packed.device
+def _row_args(sign, idx, targets, reduction):
+    """sign fp32 [m], idx / targets int64 [T] as contiguous CUDA tensors, after the checks every entry makes."""
     sign = sign.detach().float().contiguous()
     idx = idx.detach().long().contiguous()
     targets = targets.detach().long().contiguous()
     _lib.require_cuda(sign, idx, targets)
+    if sign.dim() != 1 or idx.dim() != 1 or targets.shape != idx.shape:
+        raise ValueError('sign must be [m]; idx and targets [T] of the same length')
+    if reduction not in _lib.REDUCTION:
+        raise ValueError(f'reduction must be one of {sorted(_lib.REDUCTION)}')
+    return sign, idx, targets
+
+
+def _run(packed, slices, keep, sign, idx, targets, reduction):
+    dev = packed.device
+    sign, idx, targets = _row_args(sign, idx, targets, reduction)
     m, length = sign.shape[0], idx.shape[0]
-    if targets.shape[0] != length:
-        raise ValueError('idx and targets must have the same length')
     L = _lib.lib()
     nbytes = L.noise_population_workspace_bytes(m, length)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
@@ -196,14 +204,15 @@ def member_offsets(offsets, directions):
     return offsets.index_select(1, directions.to(offsets.device)).contiguous()
 
 
-def population_loss_offsets(packed, buffer, member_off, sign, idx, targets, reduction='mean'):
-    """population_loss with every member's (a, b) read in place from the fixed noise buffer: member j of parameter P
-    uses a = buffer[off : off + out], b = buffer[off + out : off + out + in] with off = member_off[P, j]
-    (eggroll.py:122-128). member_off: int64 [60, m] device tensor (``member_offsets``)."""
-    packed = packed.refresh()
+def _offset_slices(packed, buffer, member_off, members):
+    """The 60 noise_slice_t of the in-place noise path (checked: fp32 CUDA buffer, int64 CUDA offsets [60, m])."""
     _lib.require_cuda(buffer, member_off)
-    if buffer.dtype != torch.float32 or member_off.dtype != torch.int64 or member_off.shape[0] != len(NAMES):
-        raise ValueError('buffer must be fp32 and member_off int64 [60, m]')
+    if buffer.dtype != torch.float32 or buffer.dim() != 1:
+        raise ValueError('buffer must be a 1-D fp32 tensor')
+    if member_off.dtype != torch.int64 or member_off.dim() != 2 or member_off.shape != (len(NAMES), members):
+        raise ValueError(f'member_off must be int64 [{len(NAMES)}, m] with m = len(sign)')
+    if buffer.device != packed.device or member_off.device != packed.device:
+        raise ValueError('buffer and member_off must be on the weights\' device')
     member_off = member_off.contiguous()
     base = buffer.data_ptr()
     slices = []
@@ -211,29 +220,36 @@ def population_loss_offsets(packed, buffer, member_off, sign, idx, targets, redu
         off = member_off[k].data_ptr()
         out = shape[0] if len(shape) == 2 else 0
         slices.append(_lib.Slice(base, base + 4 * out, off, 0, 0))
+    return slices, member_off
+
+
+def population_loss_offsets(packed, buffer, member_off, sign, idx, targets, reduction='mean'):
+    """population_loss with every member's (a, b) read in place from the fixed noise buffer: member j of parameter P
+    uses a = buffer[off : off + out], b = buffer[off + out : off + out + in] with off = member_off[P, j]
+    (eggroll.py:122-128). member_off: int64 [60, m] device tensor (``member_offsets``)."""
+    packed = packed.refresh()
+    slices, member_off = _offset_slices(packed, buffer, member_off, sign.shape[0])
     return _run(packed, slices, [member_off, buffer], sign, idx, targets, reduction)
 
 
 def population_loss_offsets_noalloc(packed, buffer, member_off, sign, idx, targets, reduction='mean'):
-    """``population_loss_offsets`` through ``noise_population_loss_noalloc``: for callers that cannot allocate device
-    memory, the C entry point takes no workspace and runs in the library's static device scratch (48 MiB per GPU:
-    members x tokens up to about 4,400 rows). Only the returned loss vector is allocated here, by torch. Calls that
-    overlap on the GPU race on the shared scratch."""
+    """``population_loss_offsets`` through ``noise_population_loss_noalloc``, for callers that cannot allocate device
+    memory while they evaluate: the C entry point takes no workspace and runs in the library's static device scratch
+    (48 MiB per GPU: members x tokens up to about 4,400 rows). Only the returned loss vector is allocated here, by
+    torch. The call runs with the weights' device current, on that device's current stream. Calls that overlap on the
+    GPU race on the shared scratch. Its device status word is read with ``_lib.read_static_status(device)``."""
     packed = packed.refresh()
-    _lib.require_cuda(buffer, member_off)
-    member_off = member_off.contiguous()
-    sign = sign.detach().float().contiguous()
-    idx = idx.detach().long().contiguous()
-    targets = targets.detach().long().contiguous()
-    base = buffer.data_ptr()
-    slices = [_lib.Slice(base, base + 4 * (shape[0] if len(shape) == 2 else 0), member_off[k].data_ptr(), 0, 0)
-              for k, (name, shape) in enumerate(PARAMS)]
+    slices, member_off = _offset_slices(packed, buffer, member_off, sign.shape[0])
+    sign, idx, targets = _row_args(sign, idx, targets, reduction)
     m, length = sign.shape[0], idx.shape[0]
-    losses = torch.empty((m, length) if reduction == 'none' else (m,), dtype=torch.float32, device=packed.device)
+    dev = packed.device
+    losses = torch.empty((m, length) if reduction == 'none' else (m,), dtype=torch.float32, device=dev)
     arr = (_lib.Slice * len(NAMES))(*slices)
-    rc = _lib.lib().noise_population_loss_noalloc(ctypes.byref(packed.struct), arr, sign.data_ptr(), idx.data_ptr(),
-                                                  targets.data_ptr(), m, length, _lib.REDUCTION[reduction],
-                                                  losses.data_ptr(), _lib.stream_handle(packed.device))
+    with torch.cuda.device(dev):
+        rc = _lib.lib().noise_population_loss_noalloc(ctypes.byref(packed.struct), arr, sign.data_ptr(),
+                                                      idx.data_ptr(), targets.data_ptr(), m, length,
+                                                      _lib.REDUCTION[reduction], losses.data_ptr(),
+                                                      _lib.stream_handle(dev))
     _lib.check(rc, 'noise_population_loss_noalloc')
     return losses
 

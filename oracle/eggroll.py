@@ -6,8 +6,9 @@ Two arithmetic modes:
 - ``autocast=True``: the rounding points of ``torch.autocast('cuda', torch.bfloat16)`` around the reference's
   matmuls (eggroll.py:144-145): every ``@`` takes bf16 operands, accumulates in fp32 and returns bf16; the rank-1
   correction's ``sign * (x @ b)`` then promotes back to fp32 and multiplies the fp32 ``a`` (eggroll.py:56-58), so a
-  perturbed linear returns fp32 = bf16(x W^T) + sign bf16(x b) a. Embeddings, norms, RoPE, attention and the
-  cross-entropy stay fp32 as in the reference.
+  perturbed linear returns fp32 = bf16(x W^T) + sign bf16(x b) a. Attention follows flex attention's autocast rule
+  (``gpt.attention_autocast``: q, k, v cast to bf16, fp32 softmax, bf16 probabilities and output). Embeddings, norms,
+  RoPE and the cross-entropy stay fp32 as in the reference.
 """
 import torch
 from torch.nn import functional as F
@@ -91,7 +92,8 @@ def population_loss(w, nz, sign, idx, targets, autocast=False, reduction='mean',
             gate = 2 * torch.sigmoid(linear('attn.ve_gate.weight', h[..., :gpt.VE_GATE_CHANNELS]))
             v = v + gate.unsqueeze(-1) * ve
         q, k = gpt.norm(gpt.apply_rotary_emb(q, cos, sin)), gpt.norm(gpt.apply_rotary_emb(k, cos, sin))
-        y = torch.cat([gpt.attention(q[j:j + 1], k[j:j + 1], v[j:j + 1], gpt.WINDOWS[i]) for j in range(m)])
+        attend = gpt.attention_autocast if autocast else gpt.attention
+        y = torch.cat([attend(q[j:j + 1], k[j:j + 1], v[j:j + 1], gpt.WINDOWS[i]) for j in range(m)])
         x = x + linear('attn.c_proj.weight', y.reshape(m, length, -1))
         x = x + linear('mlp.c_proj.weight', F.relu(linear('mlp.c_fc.weight', gpt.norm(x))).square())
     h = gpt.norm(x)

@@ -158,6 +158,18 @@ def attention(q, k, v, window):
     return (scores.softmax(-1) @ vh).transpose(1, 2)
 
 
+def attention_autocast(q, k, v, window):
+    """model.py:24-31 as it runs under ``torch.autocast(..., torch.bfloat16)``: flex attention's autocast rule
+    (torch._higher_order_ops.flex_attention, ``_flex_attention_autocast_impl`` in the torch of this build, 2.11)
+    casts q, k and v to bf16 before attending; the scores of the bf16 values are formed in fp32, softmax in fp32,
+    the probabilities rounded to bf16 for the product with v, and the output is bf16."""
+    qh, kh, vh = (z.transpose(1, 2).bfloat16() for z in (q, k, v))
+    scores = (qh.float() @ kh.float().transpose(-1, -2)) * HEAD_DIM ** -0.5
+    scores = scores.masked_fill(~window_allowed(q.shape[1], window, q.device), float('-inf'))
+    p = scores.softmax(-1).bfloat16()
+    return (p.float() @ vh.float()).bfloat16().float().transpose(1, 2)
+
+
 def forward(w, idx, targets=None, loss_reduction='mean', dtype=torch.float32):
     """GPT.forward (model.py:193-209) in ``dtype`` on the CPU. idx [B, T] int64."""
     B, T = idx.shape

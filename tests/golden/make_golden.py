@@ -15,6 +15,9 @@ Compiled flex attention does not lower on the CPU, so ``utils.model.flex`` is sw
 ``flex_attention`` (same function, no compilation). The noise buffer is shrunk from 2**28 to 2**20 values
 (``eggroll.NOISE``) and the chunk from 256 to 2 pairs (``eggroll.CHUNK``) so one step finishes in seconds.
 
+- ``utils/model.py`` and ``eggroll.py`` again on weights whose blocks are all active (``informative.pt``): GPT.forward
+  and population_loss (fp32 and CPU autocast) with oracle.gpt.informative_weights loaded by load_state_dict.
+
 - ``train/speedrun/run.py``: pack_heads_kernel, head_prep_fused and id_head_scores (the identity phase's head
   sharding) under the same patched interpreter, on tests/golden/heads_inputs.py's seeded inputs.
 
@@ -108,6 +111,54 @@ def golden_population(eggroll, length=2048, pairs=2, sigma=0.002):
                     directions=directions, tokens=tokens.short(), loss_fp32=fp32, loss_autocast=bf16.float(),
                     gathered=gathered, weights=checksums(es.params)), HERE / f'population_T{length}.pt')
     print(f'population T={length}: fp32', fp32.tolist(), 'autocast', bf16.float().tolist())
+
+
+def golden_informative(model, eggroll):
+    """The reference's GPT.forward and population_loss on weights whose every block matters: EGGROLL's make_model
+    weights with an active LM head, value-embedding gates and mixing scalars (oracle.gpt.informative_weights, the
+    parity tests' weights), loaded into the reference's own modules with load_state_dict (strict). At the reference's
+    initialisation the LM head (std 1e-3) puts every loss at ln 4096 and GPT(GPTConfig())'s zero c_proj makes every
+    block inert, so these fixtures are the ones that pin attention, MLP, norms and value embeddings.
+
+    - forward: GPT(GPTConfig()) fp32 eval forward, loss_reduction='none', on 2 Zipf rows x 2048 (seed 3).
+    - population_T256: 16 antithetic pairs (32 members), one Zipf row of 256 (seed 1), step 1 offsets.
+    - population_T2048: 4 pairs (8 members), one Zipf row of 2048 (seed 1), step 1 offsets.
+    Each population case runs fp32 (the CPU's native arithmetic) and under CPU bf16 autocast."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from oracle.gpt import informative_weights  # the input generator only; outputs come from the reference
+    w = informative_weights(0)
+    out = dict(weights=checksums(w))
+    torch.manual_seed(0)
+    gpt = model.GPT(model.GPTConfig())
+    gpt.load_state_dict(w, strict=True)
+    gpt.eval()
+    tokens = zipf(2, 2049, seed=3)
+    with torch.no_grad():
+        ce = gpt(tokens[:, :-1], tokens[:, 1:].contiguous(), loss_reduction='none').view(2, 2048)
+    out['forward'] = dict(tokens=tokens.short(), ce=ce.clone())
+    print('informative forward: mean CE', float(ce.mean()))
+    eggroll.NOISE = SMALL_NOISE
+    for length, pairs in ((256, 16), (2048, 4)):
+        net = eggroll.make_model(torch.device('cpu'), 0)
+        net.load_state_dict(w, strict=True)
+        es = eggroll.Eggroll(net, pairs)
+        offsets = es.offsets(step=1)
+        directions = torch.arange(2 * pairs) // 2
+        nz = es.noise(offsets, directions)
+        sign = torch.tensor([eggroll.SIGMA, -eggroll.SIGMA]).repeat(pairs)
+        row = zipf(1, length + 1, seed=1)[0]
+        idx, tgt = row[:-1], row[1:].contiguous()
+        with torch.no_grad():
+            fp32 = eggroll.population_loss(net, es.params, nz, sign, idx, tgt)
+            with torch.autocast('cpu', dtype=torch.bfloat16):
+                bf16 = eggroll.population_loss(net, es.params, nz, sign, idx, tgt).float()
+        out[f'population_T{length}'] = dict(length=length, pairs=pairs, sigma=eggroll.SIGMA, noise_size=SMALL_NOISE,
+                                             step=1, directions=directions, tokens=row.short(), loss_fp32=fp32,
+                                             loss_autocast=bf16)
+        fit32, fit16 = fp32[1::2] - fp32[0::2], bf16[1::2] - bf16[0::2]
+        print(f'informative population T={length}: mean loss {float(fp32.mean()):.4f}; autocast-vs-fp32 fitness '
+              f'gap {float((fit16 - fit32).abs().max() / fit32.std()):.4f} of the fitness std')
+    torch.save(out, HERE / 'informative.pt')
 
 
 def golden_step(eggroll, length=256, pairs=4, rows=2):
@@ -499,6 +550,8 @@ def main():
         golden_population(eggroll, length=2048)
     if want('step'):
         golden_step(eggroll)
+    if want('informative'):
+        golden_informative(model, eggroll)
     if want('implicit'):
         golden_implicit(root)
     if want('credit'):

@@ -178,3 +178,60 @@ def test_key_moment_oracle_matches_reference_kernel(golden):
     out, values = credit.moment_key_scores(b['qp'], b['kp'], b['values'], b['hub'], x['k_raw'], o['sq'], x['qp'],
                                            x['cos'], x['sin'], o['lse'], o['center'], o['steps'], emulate=True)
     assert _rel(out, o['out']) < 1e-4 and _rel(values, o['values']) < 1e-4
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# weights whose every block matters (tests/golden/informative.pt: the reference's modules loaded with
+# oracle.gpt.informative_weights), so attention, MLP, norms and value embeddings are pinned, not only the embedding
+# ------------------------------------------------------------------------------------------------------------------
+def informative_case(p):
+    """(noise, sign, idx, targets) of a population_T* entry of informative.pt."""
+    shapes = gpt.param_shapes()
+    buf = eggroll.make_buffer(p['noise_size'], seed=0)
+    offs = eggroll.offsets(shapes, p['pairs'], step=p['step'], n_noise=p['noise_size'])
+    nz = eggroll.noise(buf, offs, p['directions'], shapes)
+    sign = torch.tensor([p['sigma'], -p['sigma']]).repeat(p['pairs'])
+    tokens = p['tokens'].long()
+    return nz, sign, tokens[:-1], tokens[1:]
+
+
+def fitness_error(got, ref):
+    """(max |fitness error| / max |fitness|, rms fitness error / std of the fitness) of per-member losses against a
+    reference's, fitness = l(-) - l(+) per antithetic pair (eggroll.py:151); the std is what the update's z-scoring
+    divides by (eggroll.py:152)."""
+    fg, fr = got[1::2] - got[0::2], ref[1::2] - ref[0::2]
+    err = (fg.double() - fr.double())
+    return (err.abs().max() / fr.double().abs().max()).item(), (err.square().mean().sqrt() / fr.double().std()).item()
+
+
+def test_informative_weights_match_fixture(golden):
+    _check_weights(gpt.informative_weights(0), golden('informative.pt')['weights'])
+
+
+def test_forward_informative_matches_reference(golden):
+    """The oracle's dense-attention forward against the reference's GPT.forward, fp32, per token, on active weights
+    (one of the fixture's two rows, to keep the CPU suite short)."""
+    f = golden('informative.pt')['forward']
+    tokens = f['tokens'].long()[:1]
+    ce = gpt.forward(gpt.informative_weights(0), tokens[:, :-1], tokens[:, 1:], loss_reduction='none').view(1, -1)
+    torch.testing.assert_close(ce, f['ce'][:1], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize('autocast', [False, True])
+def test_population_informative_matches_reference(golden, autocast):
+    """The oracle's population_loss against the reference's on active weights, 16 antithetic pairs x 256 tokens.
+
+    fp32 against the reference's fp32 run: per-member losses within 2e-6 relative and the antithetic fitness within
+    1e-3 of its scale, i.e. the same arithmetic. The autocast rounding points against the reference's CPU bf16
+    autocast run: losses within 5e-4 relative and the fitness within 5% of its scale. That is the floor for any two
+    bf16 implementations that sum their products in different orders: the CPU's bf16 GEMMs round about 1 output in
+    10,000 to the other neighbouring bf16 value than an fp32-accumulated product does, and the same oracle with its
+    products summed in fp64 moves the fitness by 2.5-2.9% of its scale (the reference's own autocast-vs-fp32 gap on
+    these inputs is 2.7%)."""
+    p = golden('informative.pt')['population_T256']
+    nz, sign, idx, tgt = informative_case(p)
+    got = eggroll.population_loss(gpt.informative_weights(0), nz, sign, idx, tgt, autocast=autocast)
+    ref = p['loss_autocast'] if autocast else p['loss_fp32']
+    torch.testing.assert_close(got, ref, rtol=5e-4 if autocast else 2e-6, atol=0)
+    worst, rms = fitness_error(got, ref)
+    assert worst <= (5e-2 if autocast else 1e-3), (worst, rms)

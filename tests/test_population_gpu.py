@@ -1,11 +1,16 @@
 """Parity of the CUDA population-perturbed forward with the CPU oracle (bf16 autocast rounding points) and with the
-reference's own outputs (tests/golden/population_T*.pt).
+reference's own outputs (tests/golden/population_T*.pt at EGGROLL's initialisation, tests/golden/informative.pt on
+weights whose every block matters).
 
 The oracle comparisons use oracle.gpt.informative_weights: at EGGROLL's initialisation the LM head (std 1e-3) makes
 every loss ln 4096 whatever the body computes, which would hide errors anywhere before the head.
-Tolerances: per-member mean cross-entropy within RTOL relative of the oracle; the antithetic fitness l(-) - l(+)
-within FIT_TOL of the oracle's, relative to the fitness scale. The CUDA path rounds q, k, v to bf16 before attention
-where the reference attends in fp32; everything else follows the autocast rounding points."""
+Tolerances: per-member mean cross-entropy within RTOL relative of the oracle. The antithetic fitness
+l(-) - l(+) (eggroll.py:151) is checked on 16 pairs, where its scale means something: within FIT_TOL of its scale
+(max |error| / max |fitness|) and FIT_RMS of its std (what the update's z-scoring divides by). The floor for any two
+bf16 implementations that sum their GEMM products in different orders is 2.5-3.5% of the scale (the oracle with its
+products summed in fp64 moves the fitness that much; the reference's own autocast-vs-fp32 gap on these inputs is
+2.7%). Attention takes bf16 q, k, v and bf16 probabilities on both sides: flex attention's autocast rule casts q, k
+and v to bf16 (oracle.gpt.attention_autocast)."""
 import pytest
 import torch
 
@@ -13,8 +18,9 @@ from oracle import eggroll, gpt
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
-RTOL = 5e-4     # observed <= 2.2e-4; the reference's own autocast-vs-fp32 gap is 1.2-2.6e-4
-FIT_TOL = 0.12  # observed <= 8% of the fitness scale; the reference's own autocast-vs-fp32 gap is 1-4%
+RTOL = 5e-4      # per-member mean CE; observed <= 2.2e-4, the reference's own autocast-vs-fp32 gap is 1-3e-4
+FIT_TOL = 0.05   # of the fitness scale, on 16 pairs
+FIT_RMS = 0.05   # of the fitness std, on 16 pairs
 GOLDEN_RTOL = 1e-4
 
 
@@ -43,10 +49,12 @@ def _gpu(w, nz, sign, idx, tgt, reduction='mean'):
     return out.cpu()
 
 
-def _check_fitness(got, ref):
-    fr, fg = ref[1::2] - ref[0::2], got[1::2] - got[0::2]
-    scale = fr.abs().max().item()
-    assert (fg - fr).abs().max().item() <= FIT_TOL * scale, (fg, fr)
+def fitness_error(got, ref):
+    """(max |fitness error| / max |fitness|, rms fitness error / fitness std) of per-member losses against a
+    reference's, fitness = l(-) - l(+) per antithetic pair."""
+    fg, fr = got[1::2].double() - got[0::2].double(), ref[1::2].double() - ref[0::2].double()
+    err = fg - fr
+    return (err.abs().max() / fr.abs().max()).item(), (err.square().mean().sqrt() / fr.std()).item()
 
 
 @pytest.mark.parametrize('members,length', [(4, 128), (4, 256), (2, 384), (2, 1024)])
@@ -55,7 +63,6 @@ def test_matches_oracle_autocast(members, length):
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
     got = _gpu(w, nz, sign, idx, tgt)
     torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
-    _check_fitness(got, ref)
 
 
 def test_full_length_window_matches_oracle():
@@ -64,7 +71,6 @@ def test_full_length_window_matches_oracle():
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
     got = _gpu(w, nz, sign, idx, tgt)
     torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
-    _check_fitness(got, ref)
 
 
 @pytest.mark.parametrize('length', [256, 2048])
@@ -111,10 +117,34 @@ def test_members_are_independent():
     assert torch.equal(full[2:], part)
 
 
-def test_antithetic_fitness_tracks_oracle():
-    """The fitness l(-) - l(+) that drives the update agrees with the oracle's in sign and size."""
-    w, buf, offs, directions, nz, sign, idx, tgt = _case(16, 256, pairs=8)
+def test_antithetic_fitness_matches_oracle():
+    """The fitness that drives the update, 16 antithetic pairs x 256 tokens, against the autocast oracle."""
+    w, buf, offs, directions, nz, sign, idx, tgt = _case(32, 256, pairs=16)
     ref = eggroll.population_loss(w, nz, sign, idx, tgt, autocast=True)
     got = _gpu(w, nz, sign, idx, tgt)
-    fr, fg = ref[1::2] - ref[0::2], got[1::2] - got[0::2]
-    assert torch.corrcoef(torch.stack([fr, fg]))[0, 1] > 0.95
+    torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
+    worst, rms = fitness_error(got, ref)
+    print(f'fitness vs oracle: {worst:.4f} of scale, {rms:.4f} of std')
+    assert worst <= FIT_TOL and rms <= FIT_RMS, (worst, rms)
+
+
+@pytest.mark.parametrize('length', [256, 2048])
+def test_informative_matches_reference_golden(golden, length):
+    """Against the reference's own population_loss on active weights (tests/golden/informative.pt): 16 pairs x 256
+    tokens and 4 pairs x 2048 tokens, its CPU bf16 autocast run and its fp32 run. Per-member losses within RTOL; the
+    fitness within FIT_TOL of its scale (and FIT_RMS of its std on the 16 pairs)."""
+    import sys
+    from conftest import ROOT
+    sys.path.insert(0, str(ROOT / 'tests'))
+    from test_oracle_golden import informative_case
+    p = golden('informative.pt')[f'population_T{length}']
+    nz, sign, idx, tgt = informative_case(p)
+    got = _gpu(gpt.informative_weights(0), nz, sign, idx, tgt)
+    for key in ('loss_autocast', 'loss_fp32'):
+        ref = p[key]
+        torch.testing.assert_close(got, ref, rtol=RTOL, atol=0)
+        worst, rms = fitness_error(got, ref)
+        print(f'T={length} vs reference {key}: {worst:.4f} of scale, {rms:.4f} of std')
+        assert worst <= FIT_TOL, (key, worst, rms)
+        if p['pairs'] >= 16:
+            assert rms <= FIT_RMS, (key, worst, rms)

@@ -2,8 +2,9 @@
 
 Some callers cannot allocate device memory when they evaluate (a C/FFI host without its own CUDA allocator that must
 not call cudaMalloc on its hot path, or one whose memory pool is already fully reserved); the no-allocation entry point
-runs in the library's static device scratch instead. This file is collected last so that a failure here, under
-``-x``, comes after every other test has run. It passes alone in a fresh process and after the other tests."""
+runs in the library's static device scratch instead. Both entry points run the same kernels on the same inputs, so
+their results must be identical bit for bit. This file is collected last so that a failure here, under ``-x``, comes
+after every other test has run. It passes alone in a fresh process and after the other tests."""
 import ctypes
 
 import pytest
@@ -12,7 +13,6 @@ import torch
 from oracle import eggroll, gpt
 
 pytestmark = pytest.mark.gpu
-RTOL = 5e-4  # the tolerance of tests/test_population_gpu.py
 
 
 def _case(members, length, seed, device):
@@ -28,18 +28,22 @@ def _case(members, length, seed, device):
     return buf, off, sign, tok[:-1], tok[1:]
 
 
-def test_noalloc_matches_workspace_entry_point_twice_in_a_row():
+@pytest.mark.parametrize('reduction', ['mean', 'none'])
+def test_noalloc_matches_workspace_entry_point_twice_in_a_row(reduction):
     import noise_b200
     from noise_b200.population import PackedGPT, population_loss_offsets, population_loss_offsets_noalloc
     dev = torch.device('cuda', 0)
     packed = PackedGPT({k: v.to(dev) for k, v in gpt.informative_weights(0).items()})
     for members, length, seed in [(2, 2048, 11), (4, 1024, 12)]:  # two calls in a row, different sizes and inputs
         buf, off, sign, idx, tgt = _case(members, length, seed, dev)
-        got = population_loss_offsets_noalloc(packed, buf, off, sign, idx, tgt)
-        ref = population_loss_offsets(packed, buf, off, sign, idx, tgt)
+        got = population_loss_offsets_noalloc(packed, buf, off, sign, idx, tgt, reduction)
+        assert noise_b200._lib.read_static_status(dev) == 0, 'a bounded wait of the no-allocation call gave up'
+        ref = population_loss_offsets(packed, buf, off, sign, idx, tgt, reduction)
         torch.cuda.synchronize()
         assert noise_b200._lib.read_status(ref._noise_workspace) == 0
-        torch.testing.assert_close(got.cpu(), ref.cpu(), rtol=RTOL, atol=0)
+        assert got.shape == ref.shape == ((members, length) if reduction == 'none' else (members,))
+        assert torch.isfinite(got).all()
+        assert torch.equal(got, ref), (got - ref).abs().max().item()
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
