@@ -1,22 +1,24 @@
-"""Benchmark of the population-perturbed forward (BASELINE config 2 per GPU).
+"""Benchmark of Noise's forward-only training hot path on B200s (BASELINE.json's metric: train tokens/sec at
+population 24k on 1/2/4/8 B200; population forwards/sec/GPU).
 
-One step = one population evaluation on every rank: 512 antithetic members (256 pairs, sigma 1e-3) of the fixed
-37.7M GPT (random init of utils/model.py's architecture, EGGROLL's make_model), each member scoring 8 rows x 2048
-synthetic Zipf(1.1) tokens (summed cross-entropy = its fitness), the rank-1 noise read in place from EGGROLL's
-2**28-value N(0, 1) buffer at the step's offsets, then the NCCL all-gather of the fitness vector (N > 1). Ranks hold
-disjoint members of one population of 512 N (weak scaling). The unit of work is a population forward: one member
-over one 2048-token row ("population forwards/s").
+Default (--workload train): one step = one EGGROLL update at population 24,576 (12,288 antithetic
+pairs, sigma 2e-3) of the fixed 37.7M GPT (random init of utils/model.py's architecture, EGGROLL's make_model) on 8
+rows x 2048 synthetic Zipf(1.1) tokens: the population forward of this rank's members (rank-1 noise read in place
+from EGGROLL's 2**28-value N(0, 1) buffer at the step's offsets), the fitness all-gather, the seed-rebuilt update on
+this rank's pair shard with one NCCL all-reduce, and AdamW. The population is split over the ranks (strong scaling).
+Unit: train tokens/s (16,384 per update, all GPUs); the line's config also carries population forwards/s/GPU.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload population|credit|train]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload train|population|credit|aux|exchange]
 
---workload credit times the credit-readout kernels in isolation; --workload train one EGGROLL
-update at population 24,576 (configs 4 / 5: forward, fitness all-gather, rebuilt update all-reduce, AdamW);
+--workload population times the population forward alone (BASELINE config 2 per GPU: 512 members x 8 rows x 2048
+tokens, weak scaling, population forwards/s); --workload credit the credit-readout kernels in isolation (config 3);
 --workload aux the other entry points (un-perturbed forward, head loss, head sharding, readout scorers);
 --workload exchange the identity phase's head exchange (pack + heads-in + heads-out all_to_all) as the reference does
 it (pack kernel, NCCL all_to_all_single) and fused over peer memory (HeadExchange), N ranks under torchrun.
 
 --impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
-fp32, all host threads) on a bounded sample of the same workload, rank 0 only.
+fp32, all host threads) on a bounded sample of the same workload, rank 0 only, in the same unit.
 """
 import argparse
 import json
@@ -35,7 +37,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = 'train tokens/sec at pop 24k on 1/2/4/8 B200; population forwards/sec/GPU'
-UNIT = 'population forwards/s (one member x one 2048-token row, all GPUs)'
+UNIT = 'population forwards/s (one member x one 2048-token row, all GPUs)'  # the --workload population line
+POP_METRIC = 'population forwards/sec/GPU (BASELINE config 2: 512 members x 8 x 2048 tokens per GPU)'
 MEMBERS, ROWS, T, SIGMA = 512, 8, 2048, 1e-3
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per member-token row of each kernel kind, from one ncu
 # capture of a 64-member x 1-row call (bench.py --members 64 --rows 1), scaled by the rows of a launch
@@ -44,6 +47,10 @@ TRAFFIC_BYTES_PER_ROW = {'norm_mix': 4437.3, 'gemm_qkv': 3750.1, 'attention': 94
                          'gemm_head_ce': 1083.2, 'member_reduce': 16.2}
 FLOP_PER_MEMBER_TOKEN = 68.3e6  # algorithmic forward FLOPs per member-token (linears + attention)
 CPU_SAMPLE_MEMBERS, CPU_SAMPLE_T = 2, 2048
+TRAIN_PAIRS, TRAIN_ROWS = 12288, 8  # population 24,576, eggroll.py's BATCH of 8 rows
+TRAIN_UNIT = 'train tokens/s (all GPUs)'
+# one update = 24,576 population forwards (members x one 2048-token row) for 8 x 2048 train tokens
+TRAIN_FORWARDS, TRAIN_TOKENS = 2 * TRAIN_PAIRS, TRAIN_ROWS * T
 
 
 def args_():
@@ -52,7 +59,7 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='population', choices=['population', 'credit', 'train', 'aux', 'exchange'])
+    ap.add_argument('--workload', default='train', choices=['train', 'population', 'credit', 'aux', 'exchange'])
     # smaller population cases for profiling captures only; the benchmark line uses the defaults
     ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (population workload)')
     ap.add_argument('--rows', type=int, default=ROWS, help='2048-token rows per member (population workload)')
@@ -165,6 +172,8 @@ def cpu_reference_sample(threads):
 
 
 def run_reference(a):
+    """The reference arm: the reference's algorithm (the fp32 oracle port of eggroll.population_loss) on all the host
+    cores, rank 0 only, each step a bounded sample of the workload, reported in the unit of our arm's line."""
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
@@ -173,18 +182,87 @@ def run_reference(a):
     for _ in range(a.warmup):
         cpu_reference_sample(threads)
     times = [cpu_reference_sample(threads) for _ in range(a.steps)]
-    value = per * len(times) / sum(times)
+    fwd = per * len(times) / sum(times)
+    if a.workload == 'population':
+        value, unit, metric, scaling = fwd, UNIT, POP_METRIC, 'weak'
+        workload = 'population forward, BASELINE config 2 shape, bounded CPU sample'
+        conv = ''
+    else:
+        value, unit, metric, scaling = fwd * TRAIN_TOKENS / TRAIN_FORWARDS, TRAIN_UNIT, METRIC, 'strong'
+        workload = 'BASELINE config 4 update (population 24,576), bounded CPU sample of its population forward'
+        conv = '; x 16,384 train tokens per 24,576 population forwards of an update'
     sample = (f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of the fp32 population forward per step '
-              f'(oracle restatement of eggroll.population_loss, dense attention)')
+              f'(oracle restatement of eggroll.population_loss, dense attention){conv}')
     print(json.dumps({
-        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': a.gpus, 'steps': a.steps,
+        'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit, 'n_gpus': a.gpus, 'steps': a.steps,
         'warmup': a.warmup, 'ms_per_step': 1e3 * sum(times) / len(times), 'higher_is_better': True,
-        'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'population forward, BASELINE config 2 shape, bounded CPU sample',
-                   'members_per_step': CPU_SAMPLE_MEMBERS, 'seq_len': CPU_SAMPLE_T},
-        'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': threads, 'kind': 'port', 'sample': sample},
-        'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'scaling': scaling, 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+        'config': {'workload': workload, 'members_per_step': CPU_SAMPLE_MEMBERS, 'seq_len': CPU_SAMPLE_T,
+                   'population_forwards_per_s': fwd},
+        'cpu_baseline': {'value': value, 'unit': unit, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
+
+
+def kernel_roofline(prof, m_launch, clk, ms, forwards):
+    """{'roofline', 'kernels', 'clocks'} of a timed region: per kernel kind its launches, CUDA-event time per launch,
+    share and achieved rate; the roofline object of the dominant kind (algorithmic FLOPs or bytes of one launch on
+    m_launch members x T rows over its mean launch time, against MEASURED_PEAKS.json); ``step`` = the forward's
+    algorithmic FLOPs of ``forwards`` population forwards over the ``ms`` of the timed region."""
+    kinds = {}
+    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
+    tf_peak = peaks.get('bf16_tflops_sustained', 1400.0)
+    total = sum(prof.ms.values())
+    for k, kms in prof.ms.items():
+        n = prof.count[k]
+        flops, nbytes = kernel_work(k, m_launch, T)
+        per = kms / n
+        kinds[k] = {'launches': n, 'ms_per_launch': round(per, 4), 'share': round(kms / total, 4)}
+        if flops:
+            kinds[k]['tflops'] = round(flops / (per / 1e3) / 1e12, 1)
+        if nbytes:
+            kinds[k]['gbs'] = round(nbytes / (per / 1e3) / 1e9, 1)
+    dom = max(prof.ms, key=prof.ms.get)
+    flops, nbytes = kernel_work(dom, m_launch, T)
+    per_launch_s = prof.ms[dom] / prof.count[dom] / 1e3
+    tr = TRAFFIC_BYTES_PER_ROW.get(dom)
+    step_tf = forwards * T * FLOP_PER_MEMBER_TOKEN / (ms / 1e3) / 1e12
+    src = 'MEASURED_PEAKS.json (of measured)' if peaks else 'fallback'
+    if flops:
+        roofline = {'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1),
+                    'peak': tf_peak, 'unit': 'TFLOP/s', 'frac': round(flops / per_launch_s / 1e12 / tf_peak, 4),
+                    'peak_source': src + ' bf16_tflops_sustained', 'algorithmic_flops_per_launch': flops}
+    else:
+        hbm = peaks.get('hbm_gbs', 6650.0)
+        roofline = {'kernel': dom, 'bound': 'hbm', 'achieved': round(nbytes / per_launch_s / 1e9, 1), 'peak': hbm,
+                    'unit': 'GB/s', 'frac': round(nbytes / per_launch_s / 1e9 / hbm, 4),
+                    'peak_source': src + ' hbm_gbs', 'algorithmic_bytes_per_launch': nbytes}
+    roofline['traffic'] = tr * m_launch * T if tr is not None else None
+    roofline['step'] = {'achieved_tflops': round(step_tf, 1), 'frac': round(step_tf / tf_peak, 4)}
+    if dom == 'attention':
+        # attention's other roof: one exponential per visible pair on the MUFU pipe, at its nominal 16 a SM-cycle
+        # (not a measured peak) and the median SM clock sampled under load
+        mhz = (clk or {}).get('sm_mhz') or peaks.get('sm_max_mhz', 1965.0)
+        exp_rate = flops / 256.0 / per_launch_s
+        mufu_peak = 16 * 148 * mhz * 1e6
+        roofline['mufu'] = {'achieved_gexp_s': round(exp_rate / 1e9, 1),
+                            'nominal_peak_gexp_s': round(mufu_peak / 1e9, 1),
+                            'frac': round(exp_rate / mufu_peak, 4), 'sm_mhz': mhz,
+                            'basis': 'nominal 16 ex2 per SM-cycle x 148 SMs at the median SM clock under load'}
+    return {'roofline': roofline, 'kernels': kinds, 'clocks': clk}
+
+
+def cpu_baseline_train():
+    """The CPU baseline in train tokens/s: the population forward's fp32 oracle port timed on the host cores (a
+    bounded sample), scaled by the forwards an update needs (24,576 member rows for 8 x 2048 train tokens; the
+    update's rebuild and AdamW, under 2% of an update here, are left out)."""
+    threads = os.cpu_count() or 1
+    secs = [cpu_reference_sample(threads) for _ in range(2)]
+    fwd = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(secs)
+    return {'value': fwd * TRAIN_TOKENS / TRAIN_FORWARDS, 'unit': TRAIN_UNIT, 'cores': threads, 'kind': 'port',
+            'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of the fp32 oracle restatement of '
+                      f'eggroll.population_loss, median of 2 ({fwd:.3f} population forwards/s), x 16,384 train '
+                      f'tokens per 24,576 population forwards'}
 
 
 def run_ours(a):
@@ -261,50 +339,9 @@ def run_ours(a):
     e2e_value = work / (ms_e2e / 1e3)
 
     m_launch = min(pop.chunk, a.members)  # members per library call
-    # roofline of the dominant kernel kind (CUDA-event times of every launch in the timed region)
-    kinds = {}
-    peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
-    tf_peak = peaks.get('bf16_tflops_sustained', 1400.0)
-    total = sum(prof.ms.values())
-    for k, kms in prof.ms.items():
-        n = prof.count[k]
-        flops, nbytes = kernel_work(k, m_launch, T)
-        per = kms / n
-        kinds[k] = {'launches': n, 'ms_per_launch': round(per, 4), 'share': round(kms / total, 4)}
-        if flops:
-            kinds[k]['tflops'] = round(flops / (per / 1e3) / 1e12, 1)
-        if nbytes:
-            kinds[k]['gbs'] = round(nbytes / (per / 1e3) / 1e9, 1)
-    dom = max(prof.ms, key=prof.ms.get)
-    flops, nbytes = kernel_work(dom, m_launch, T)
-    per_launch_s = prof.ms[dom] / prof.count[dom] / 1e3
-    tr = TRAFFIC_BYTES_PER_ROW.get(dom)
-    step_tf = a.members * a.rows * T * FLOP_PER_MEMBER_TOKEN * a.steps / (ms / 1e3) / 1e12
-    src = 'MEASURED_PEAKS.json (of measured)' if peaks else 'fallback'
-    if flops:
-        roofline = {'kernel': dom, 'bound': 'tensor', 'achieved': round(flops / per_launch_s / 1e12, 1),
-                    'peak': tf_peak, 'unit': 'TFLOP/s', 'frac': round(flops / per_launch_s / 1e12 / tf_peak, 4),
-                    'peak_source': src + ' bf16_tflops_sustained', 'algorithmic_flops_per_launch': flops}
-    else:
-        hbm = peaks.get('hbm_gbs', 6650.0)
-        roofline = {'kernel': dom, 'bound': 'hbm', 'achieved': round(nbytes / per_launch_s / 1e9, 1), 'peak': hbm,
-                    'unit': 'GB/s', 'frac': round(nbytes / per_launch_s / 1e9 / hbm, 4),
-                    'peak_source': src + ' hbm_gbs', 'algorithmic_bytes_per_launch': nbytes}
-    roofline['traffic'] = tr * m_launch * T if tr is not None else None
-    roofline['step'] = {'achieved_tflops': round(step_tf, 1), 'frac': round(step_tf / tf_peak, 4)}
-    if dom == 'attention':
-        # attention's other roof: one exponential per visible pair on the MUFU pipe, at its nominal 16 a SM-cycle
-        # (not a measured peak) and the median SM clock sampled under load
-        mhz = (clk or {}).get('sm_mhz') or peaks.get('sm_max_mhz', 1965.0)
-        exp_rate = flops / 256.0 / per_launch_s
-        mufu_peak = 16 * 148 * mhz * 1e6
-        roofline['mufu'] = {'achieved_gexp_s': round(exp_rate / 1e9, 1),
-                            'nominal_peak_gexp_s': round(mufu_peak / 1e9, 1),
-                            'frac': round(exp_rate / mufu_peak, 4), 'sm_mhz': mhz,
-                            'basis': 'nominal 16 ex2 per SM-cycle x 148 SMs at the median SM clock under load'}
-
+    forwards = a.members * a.rows * a.steps  # this rank's population forwards in the timed region
     line = {
-        'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
+        'metric': POP_METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': a.steps, 'warmup': a.warmup,
         'ms_per_step': ms / a.steps, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
         'dtype': 'bf16',
         'data': 'synthetic: Zipf(1.1) token rows over vocab 4096; random-init weights of the utils/model.py GPT '
@@ -316,11 +353,11 @@ def run_ours(a):
                    'members_per_gpu': a.members, 'rows_per_member': a.rows, 'seq_len': T, 'sigma': SIGMA,
                    'member_tokens_per_s': value * T, 'train_tokens_per_step': a.rows * T,
                    'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}'},
-        'roofline': roofline, 'kernels': kinds, 'clocks': clk,
         'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': a.rows * (T + 1) * 8,
                 'd2h_bytes_per_step': a.members * world * 4},
         'gpu_launches': launches,
     }
+    line.update(kernel_roofline(prof, m_launch, clk, ms, forwards))
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
         secs = [cpu_reference_sample(threads) for _ in range(2)]
@@ -343,17 +380,31 @@ CREDIT_FLOP_PER_PAIR = {  # algorithmic FLOPs per visible (receiver, key) pair, 
     'moment_key_scores': 832}
 
 
-def run_credit(a):
-    """One line per window: every credit kernel on rows = 16 x 8 heads, T = 2048, d = 64 (q, k, v ~ N(0,1)/8, hub the
-    per-token error signal e[b, t] u_h with e ~ N(0, 1), u_h ~ N(0, 1)/8), CUDA-event timed over K launches after W
-    warm-ups; inputs (~0.5 GB) exceed L2."""
-    import noise_b200.moment_kernels as mk
-    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
-    torch.cuda.set_device(device)
-    g = torch.Generator(device).manual_seed(0)
+REFERENCE_MOMENT_KERNELS = ROOT / 'baseline' / '_ref' / 'train' / 'speedrun' / 'moment_kernels.py'
+
+
+def reference_moment_kernels():
+    """The reference's own Triton credit kernels (train/speedrun/moment_kernels.py, unmodified, from the reference
+    install in baseline/_ref) with KEY_IMPL = VALUE_IMPL = None: the B200 reference for BASELINE config 3 (the Gluon
+    versions need Hopper's wgmma). Raises FileNotFoundError when the install is absent."""
+    import importlib.util
+    if not REFERENCE_MOMENT_KERNELS.exists():
+        raise FileNotFoundError(f'{REFERENCE_MOMENT_KERNELS} is missing (the reference install in baseline/_ref)')
+    spec = importlib.util.spec_from_file_location('reference_moment_kernels', REFERENCE_MOMENT_KERNELS)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.KEY_IMPL is None and mod.VALUE_IMPL is None
+    return mod
+
+
+def credit_config3(device, seed=0):
+    """BASELINE config 3 inputs: rows = 16 x 8 heads, T = 2048, d = 64; q, k, v ~ N(0,1)/8 (bf16 copies feed the
+    bf16 kernels), hub the per-token error signal e[b, t] u_h with e ~ N(0, 1), u_h ~ N(0, 1)/8; raw queries / keys
+    N(0, 1); bf16-rounded RoPE tables; the query moments' step sizes 0.01 rms(raw)."""
+    g = torch.Generator(device).manual_seed(seed)
     B, H, t = 16, 8, 2048
     rows = B * H
-    rn = lambda *s: torch.randn(*s, device=device, generator=g)
+    rn = lambda *shape: torch.randn(*shape, device=device, generator=g)
     q, k, v = (rn(B, H, t, 64).div_(8).view(rows, t, 64) for _ in range(3))
     e = rn(B, 1, t, 1)
     u = rn(1, H, 1, 64) / 8
@@ -361,27 +412,67 @@ def run_credit(a):
     raw_q, raw_k = rn(rows, t, 64), rn(rows, t, 64)
     inv = 1.0 / 10000 ** (torch.arange(0, 64, 2, dtype=torch.float32, device=device) / 64)
     freqs = torch.outer(torch.arange(t, dtype=torch.float32, device=device), inv)
-    cos, sin = freqs.cos().bfloat16().float(), freqs.sin().bfloat16().float()
-    b16 = [z.bfloat16() for z in (q, k, v, hub)]
     sq = raw_q.square().sum(-1)
-    steps = 0.01 * (sq / 64).sqrt().clamp(min=1e-6)
+    return dict(rows=rows, t=t, q=q, k=k, v=v, hub=hub, raw_q=raw_q, raw_k=raw_k,
+                cos=freqs.cos().bfloat16().float(), sin=freqs.sin().bfloat16().float(),
+                b16=[z.bfloat16() for z in (q, k, v, hub)], sq=sq, steps=0.01 * (sq / 64).sqrt().clamp(min=1e-6))
+
+
+def credit_calls(mk, x, window, lse, center):
+    """name -> zero-argument call of each credit kernel through module mk's ops (ours, noise_b200.moment_kernels, or
+    the reference's: the same signatures), returning its outputs. lse, center: the key context the downstream
+    kernels read (the same tensors for both arms in a parity check)."""
+    dev, rows, t = x['q'].device, x['rows'], x['t']
+    b16 = x['b16']
+    qs = torch.empty(1, rows, t, 64, dtype=torch.bfloat16, device=dev)
+    ko, kv = torch.empty(1, rows, t, 64, device=dev), torch.empty(1, rows, t, 64, device=dev)
+
+    def query():
+        mk.moment_query_scores(*b16, x['raw_q'].unsqueeze(0), x['sq'], x['k'], x['cos'], x['sin'], lse, center,
+                               x['steps'], qs, 4, window)
+        return qs
+
+    def keys():
+        mk.moment_key_scores(*b16, x['raw_k'].unsqueeze(0), x['sq'], x['q'], x['cos'], x['sin'], lse, center,
+                             x['steps'], ko, kv, 2)
+        return ko, kv
+
+    calls = {
+        'implicit_key_context': lambda: mk.implicit_key_context_edges(*b16, window),
+        'value_pass': lambda: mk.raw_value_credits(b16[0], b16[1], lse, x['hub'], window),
+        'key_scan': lambda: mk.key_credits(x['q'], x['k'], x['raw_k'], lse, x['v'], x['hub'], center, x['cos'],
+                                           x['sin'], window, 0.003),
+        'moment_query_scores': query,
+    }
+    if window >= t:  # the identity phase's key moments are full-causal
+        calls['moment_key_scores'] = keys
+    return calls
+
+
+def run_credit(a):
+    """One line per window: every credit kernel on BASELINE config 3 (credit_config3), CUDA-event timed over K launches
+    after W warm-ups; inputs (~0.5 GB) exceed L2. ``--impl reference`` times the reference's Triton kernels
+    (reference_moment_kernels) on the same inputs and clocks; without the reference install it prints an
+    ``unavailable`` line."""
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    if a.impl == 'reference':
+        try:
+            mk = reference_moment_kernels()
+        except Exception as exc:  # noqa: BLE001 - reported, not hidden
+            print(json.dumps({'impl': 'reference', 'workload': 'credit', 'unavailable': repr(exc)}), flush=True)
+            return
+    else:
+        import noise_b200.moment_kernels as mk
+    x = credit_config3(device)
+    rows, t = x['rows'], x['t']
     peaks = json.loads((ROOT / 'MEASURED_PEAKS.json').read_text()) if (ROOT / 'MEASURED_PEAKS.json').exists() else {}
     tf_peak = peaks.get('bf16_tflops', 1590.0)
     for window in (2048, 1024):
         pairs = rows * visible_pairs(t, window)
-        lse, center = mk.implicit_key_context_edges(*b16, window)
-        qs = torch.empty(1, rows, t, 64, dtype=torch.bfloat16, device=device)
-        ko, kv = torch.empty(1, rows, t, 64, device=device), torch.empty(1, rows, t, 64, device=device)
-        calls = {
-            'implicit_key_context': lambda: mk.implicit_key_context_edges(*b16, window),
-            'value_pass': lambda: mk.raw_value_credits(b16[0], b16[1], lse, hub, window),
-            'key_scan': lambda: mk.key_credits(q, k, raw_k, lse, v, hub, center, cos, sin, window, 0.003),
-            'moment_query_scores': lambda: mk.moment_query_scores(*b16, raw_q.unsqueeze(0), sq, k, cos, sin, lse,
-                                                                  center, steps, qs, 4, window),
-        }
-        if window >= t:
-            calls['moment_key_scores'] = lambda: mk.moment_key_scores(*b16, raw_k.unsqueeze(0), sq, q, cos, sin, lse,
-                                                                      center, steps, ko, kv, 2)
+        lse, center = mk.implicit_key_context_edges(*x['b16'], window)
+        calls = credit_calls(mk, x, window, lse, center)
+        clocks = Clocks(device)
         res = {}
         for name, fn in calls.items():
             for _ in range(a.warmup):
@@ -399,8 +490,9 @@ def run_credit(a):
                          'frac_of_tensor_peak': round(flops / us / 1e6 / tf_peak, 4),
                          'mufu_floor_us': round(pairs / (16 * 148 * 1.965e9) * 1e6, 1)}
         print(json.dumps({'metric': 'credit-readout kernel time (BASELINE config 3)', 'unit': 'us per launch',
-                          'config': {'workload': 'credit kernels in isolation', 'B': B, 'H': H, 'T': t, 'd_head': 64,
-                                     'window': window, 'pairs': pairs},
+                          'impl': a.impl, 'clocks': clocks.stop(),
+                          'config': {'workload': 'credit kernels in isolation', 'B': 16, 'H': 8, 'T': t,
+                                     'd_head': 64, 'window': window, 'pairs': pairs},
                           'peak': {'bf16_tflops': tf_peak, 'source': 'MEASURED_PEAKS.json bf16_tflops (burst)'},
                           'kernels': res}), flush=True)
 
@@ -408,57 +500,102 @@ def run_credit(a):
 # ------------------------------------------------------------------------------------------------------------------
 # one EGGROLL training update at population 24,576 (BASELINE configs 4 / 5)
 # ------------------------------------------------------------------------------------------------------------------
-TRAIN_PAIRS, TRAIN_ROWS = 12288, 8
 
 
 def run_train(a):
-    """Train tokens/s: each update consumes 8 rows x 2048 Zipf tokens (eggroll.py's BATCH), evaluates 24,576
-    antithetic members (3,072 per row, split over the ranks), all-gathers their losses, rebuilds the update on each
-    rank's pair shard (tcgen05 GEMM, K = pairs) with one NCCL all-reduce, and applies AdamW."""
+    """BASELINE config 4, the headline: train tokens/s of EGGROLL updates at population 24,576. Each update consumes
+    8 rows x 2048 Zipf tokens (eggroll.py's BATCH), evaluates 24,576 antithetic members (3,072 per row, split evenly
+    over the ranks: strong scaling), all-gathers their losses, rebuilds the update on each rank's pair shard
+    (tcgen05 GEMM, K = pairs) with one NCCL all-reduce, and applies AdamW.
+
+    One timed loop of K updates serves both numbers: per update, the token rows go host -> device (pinned), the update
+    runs, and the mean loss comes back device -> host. ``value`` sums the device time of the updates alone (CUDA
+    events after the copy-in and before the copy-out), ``e2e`` the whole loop including the copies and the host's
+    wait for the loss. Both are max-reduced over the ranks."""
+    from noise_b200 import _lib
     from noise_b200.eggroll import make_params
-    from noise_b200.train import EggrollTrainer
+    from noise_b200.train import EggrollTrainer, phase_ms
 
     rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
     device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
     torch.cuda.set_device(device)
-    if world > 1:
-        torch.distributed.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=600))
+    dist = world > 1
+    if dist:
+        torch.distributed.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=300))
     tr = EggrollTrainer(make_params(device, 0), TRAIN_PAIRS, TRAIN_ROWS, sigma=SIGMA, lr=1e-3, rank=rank,
                         world=world)
-    rows = [zipf_rows(TRAIN_ROWS, T + 1, seed=100 + s).pin_memory() for s in range(a.warmup + a.steps)]
+    host_rows = [zipf_rows(TRAIN_ROWS, T + 1, seed=100 + s).pin_memory() for s in range(a.warmup + a.steps)]
+    loss_host = torch.empty(1, pin_memory=True)
     for i in range(a.warmup):
-        tr.step(rows[i].to(device, non_blocking=True), step=i + 1)
+        loss = tr.step(host_rows[i].to(device, non_blocking=True), step=i + 1)
+        loss_host.copy_(loss.view(1), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
     torch.cuda.synchronize()
-    if world > 1:
+    if dist:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.steps):
-        loss = tr.step(rows[a.warmup + i].to(device, non_blocking=True), step=a.warmup + i + 1)
-        loss_host = loss.item()
-    e1.record()
+
+    clocks = Clocks(device)
+    marks, timer, launches = [], [], 0
+    ev = lambda: torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
+    if dist:
+        torch.distributed.barrier()
+    with _lib.LaunchProfile() as prof:
+        for i in range(a.steps):
+            e_in, e_go, e_done, e_out = ev(), ev(), ev(), ev()
+            e_in.record()
+            tokens = host_rows[a.warmup + i].to(device, non_blocking=True)
+            e_go.record()
+            loss = tr.step(tokens, step=a.warmup + i + 1, timer=timer)
+            e_done.record()
+            loss_host.copy_(loss.view(1), non_blocking=True)
+            e_out.record()
+            torch.cuda.current_stream().synchronize()
+            launches += tr.launches
+            marks.append((e_in, e_go, e_done, e_out))
+        torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    clk = clocks.stop()
+    ms = sum(go.elapsed_time(done) for _, go, done, _ in marks)
+    ms_e2e = marks[0][0].elapsed_time(marks[-1][3])
+    phases = phase_ms(timer)
+    if dist:
+        names = list(EggrollTrainer.PHASES)
+        t = torch.tensor([ms, ms_e2e] + [phases.get(n, 0.0) for n in names], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = t.item()
-    tokens = TRAIN_ROWS * T * a.steps
+        vals = t.tolist()
+        ms, ms_e2e = vals[:2]
+        phases = dict(zip(names, vals[2:]))
+    value = TRAIN_TOKENS * a.steps / (ms / 1e3)
+    e2e_value = TRAIN_TOKENS * a.steps / (ms_e2e / 1e3)
+    per_rank_forwards = TRAIN_FORWARDS // world * a.steps
+    line = {
+        'metric': METRIC, 'value': value, 'unit': TRAIN_UNIT, 'n_gpus': world, 'steps': a.steps,
+        'warmup': a.warmup, 'ms_per_step': ms / a.steps, 'higher_is_better': True, 'scaling': 'strong',
+        'vs_baseline': None, 'dtype': 'bf16',
+        'data': 'synthetic: Zipf(1.1) token rows over vocab 4096; random-init weights of the utils/model.py GPT '
+                '(EGGROLL make_model); EGGROLL 2**28 N(0,1) noise buffer',
+        'config': {'workload': 'BASELINE config 4: one EGGROLL update per step at population 24,576 (12,288 '
+                               'antithetic pairs, sigma 2e-3), 8 rows x 2048 tokens per update, members split over '
+                               'the ranks; fitness all-gather, pair-sharded rebuilt update + NCCL all-reduce, AdamW',
+                   'population': 2 * TRAIN_PAIRS, 'members_per_gpu': 2 * TRAIN_PAIRS // world,
+                   'rows_per_update': TRAIN_ROWS, 'seq_len': T, 'train_tokens_per_step': TRAIN_TOKENS,
+                   'population_forwards_per_s_per_gpu': per_rank_forwards / (ms / 1e3),
+                   'member_tokens_per_s': TRAIN_FORWARDS * T * a.steps / (ms / 1e3),
+                   'phase_ms_per_step': {k: round(v / a.steps, 3) for k, v in phases.items()},
+                   'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}',
+                   'last_mean_loss': float(loss_host[0])},
+        'e2e': {'value': e2e_value, 'unit': TRAIN_UNIT, 'h2d_bytes_per_step': TRAIN_ROWS * (T + 1) * 8,
+                'd2h_bytes_per_step': 4},
+        'gpu_launches': launches,
+    }
+    line.update(kernel_roofline(prof, min(tr.pop.chunk, TRAIN_FORWARDS // world), clk, ms, per_rank_forwards))
+    if rank == 0 and world == 1:
+        line['cpu_baseline'] = cpu_baseline_train()
     if rank == 0:
-        print(json.dumps({
-            'metric': 'train tokens/sec at pop 24k (EGGROLL update: population forward + fitness all-gather + '
-                      'rebuilt update all-reduce + AdamW)',
-            'value': tokens / (ms / 1e3), 'unit': 'train tokens/s (all GPUs)', 'n_gpus': world, 'steps': a.steps,
-            'warmup': a.warmup, 'ms_per_step': ms / a.steps, 'higher_is_better': True, 'scaling': 'strong',
-            'dtype': 'bf16', 'data': 'synthetic Zipf(1.1) rows, random-init GPT (EGGROLL make_model)',
-            'config': {'workload': 'BASELINE config 4/5 update', 'population': 2 * TRAIN_PAIRS,
-                       'rows_per_update': TRAIN_ROWS, 'seq_len': T, 'members_per_row': 2 * TRAIN_PAIRS // TRAIN_ROWS,
-                       'member_tokens_per_s': 2 * TRAIN_PAIRS * T * a.steps / (ms / 1e3),
-                       'last_mean_loss': loss_host},
-            'e2e': {'value': tokens / (ms / 1e3), 'unit': 'train tokens/s', 'h2d_bytes_per_step': TRAIN_ROWS * (T + 1) * 8,
-                    'd2h_bytes_per_step': 4},
-        }), flush=True)
-    if world > 1:
+        print(json.dumps(line), flush=True)
+    if dist:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
@@ -675,10 +812,10 @@ def run_exchange(a):
 
 def main():
     a = args_()
-    if a.impl == 'reference':
-        run_reference(a)
-    elif a.workload == 'credit':
+    if a.workload == 'credit':
         run_credit(a)
+    elif a.impl == 'reference':
+        run_reference(a)
     elif a.workload == 'train':
         run_train(a)
     elif a.workload == 'aux':

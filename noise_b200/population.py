@@ -72,12 +72,15 @@ class PackedGPT:
         return tuple((t.data_ptr(), t._version) for t in (self.params[n] for n in NAMES))
 
     def _pack(self, dst, src):
+        self.packs += 1
         src = src.detach().float().contiguous()
         _lib.check(_lib.lib().noise_pack_bf16(src.data_ptr(), dst.data_ptr(), src.numel(),
                                               _lib.stream_handle(self.device)), 'noise_pack_bf16')
 
     def refresh(self):
+        """Re-pack if a source changed; ``packs`` = the pack kernels this call launched."""
         key = self._source_key()
+        self.packs = 0
         if key == self._key:
             return self
         p, dev = self.params, self.device

@@ -60,7 +60,8 @@ class FlatParams:
 
 def rebuild_update(buffer, offsets, weight, count, shard, grad_flat, fp):
     """Write into grad_flat (fp32, FlatParams layout) the update terms of the pairs shard = (start, stop):
-    G_P = -(1 / count) sum_j w_j a_j b_j^T. offsets: int64 [60, pairs]; weight: fp32 [pairs]."""
+    G_P = -(1 / count) sum_j w_j a_j b_j^T. offsets: int64 [60, pairs]; weight: fp32 [pairs].
+    Returns (device status word, number of the library's kernels enqueued)."""
     L = _lib.lib()
     stream = _lib.stream_handle(buffer.device)
     start, stop = shard
@@ -68,6 +69,7 @@ def rebuild_update(buffer, offsets, weight, count, shard, grad_flat, fp):
     scale = -1.0 / count
     status = torch.zeros(_lib.STATUS_BYTES // 4, dtype=torch.int32, device=buffer.device)
     w = weight[start:stop].float().contiguous()
+    launches = 0
     for k, (name, shape) in enumerate(PARAMS):
         g = grad_flat[fp.offsets[k]:fp.offsets[k] + math.prod(shape)]
         if n == 0:
@@ -85,12 +87,14 @@ def rebuild_update(buffer, offsets, weight, count, shard, grad_flat, fp):
                                               b.data_ptr(), stream), 'noise_rank1_operands')
             _lib.check(L.noise_gemm_bf16_tn(a.data_ptr(), b.data_ptr(), g.data_ptr(), out, inn, kp,
                                             status.data_ptr(), stream), 'noise_gemm_bf16_tn')
+            launches += 3
         else:
             one_d = len(shape) == 1
             n_out, n_in = (1, shape[0]) if one_d else shape
             _lib.check(L.noise_rank1_small(buffer.data_ptr(), off.data_ptr(), w.data_ptr(), scale, n_out, n_in,
                                            int(one_d), n, g.data_ptr(), stream), 'noise_rank1_small')
-    return status
+            launches += 1
+    return status, launches
 
 
 class AdamW:
@@ -130,15 +134,46 @@ class EggrollTrainer:
         if members % world:
             raise ValueError('every rank must evaluate the same number of members')
 
-    def step(self, tokens, step, lr=None):
-        """tokens: int64 [rows, T + 1] on the device. Returns the population's mean loss (a device scalar)."""
+    PHASES = ('forward', 'fitness', 'rebuild', 'all_reduce', 'adamw')
+
+    def step(self, tokens, step, lr=None, timer=None):
+        """tokens: int64 [rows, T + 1] on the device. Returns the population's mean loss (a device scalar).
+
+        timer: optional list; CUDA events recorded on the current stream at the start and after each phase are
+        appended to it as (phase, event) pairs (phases: PHASES; 'forward' includes the re-pack of the bf16 weights
+        after the previous update). ``launches`` holds the number of the library's kernels the step enqueued."""
+        def mark(name):
+            if timer is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                timer.append((name, ev))
+
+        mark('start')
         offsets = step_offsets(self.pairs, step, self.device, self.seed, self.buffer.numel())
+        packs = self.pop.packed.refresh().packs
         _, losses = self.pop.evaluate(tokens, step, offsets=offsets)
+        mark('forward')
         weight, count = fitness_weights(losses, self.pairs)
+        mark('fitness')
         shard = pair_shard(self.pairs, self.rank, self.world) if self.shard_update else (0, self.pairs)
-        self.status = rebuild_update(self.buffer, offsets, weight, count, shard, self.grad, self.fp)
+        self.status, rebuilt = rebuild_update(self.buffer, offsets, weight, count, shard, self.grad, self.fp)
+        mark('rebuild')
         if self.shard_update and self.world > 1:
             torch.distributed.all_reduce(self.grad)
+        mark('all_reduce')
         self.opt.step(self.grad, lr)
         self.pop.packed.invalidate()
+        mark('adamw')
+        self.launches = packs + self.pop.launches + rebuilt + 1
         return losses.mean()
+
+
+def phase_ms(timer):
+    """Milliseconds per phase from the (phase, event) list ``EggrollTrainer.step(timer=...)`` filled (after a
+    synchronize), summed over the steps it covers."""
+    out = {}
+    for (_, e0), (name, e1) in zip(timer, timer[1:]):
+        if name == 'start':
+            continue
+        out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+    return out

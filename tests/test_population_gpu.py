@@ -19,8 +19,8 @@ from oracle import eggroll, gpt
 pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
 RTOL = 5e-4      # per-member mean CE; observed <= 2.2e-4, the reference's own autocast-vs-fp32 gap is 1-3e-4
-FIT_TOL = 0.05   # of the fitness scale, on 16 pairs
-FIT_RMS = 0.05   # of the fitness std, on 16 pairs
+FIT_TOL = 0.04   # of the fitness scale, on 16 pairs; observed 3.5% vs the oracle, 1.5-2.2% vs the reference
+FIT_RMS = 0.04   # of the fitness std, on 16 pairs; observed 3.3% vs the oracle, 1.9-3.3% vs the reference
 GOLDEN_RTOL = 1e-4
 
 

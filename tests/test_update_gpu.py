@@ -26,7 +26,7 @@ def _rebuild_gpu(buf, offs, weight, count, shard=None):
     grad = torch.zeros_like(fp.flat)
     table = torch.stack([offs[n] for n, _ in PARAMS]).to(DEV)
     pairs = weight.shape[0]
-    st = train.rebuild_update(buf.to(DEV), table, weight.to(DEV), count, shard or (0, pairs), grad, fp)
+    st, _ = train.rebuild_update(buf.to(DEV), table, weight.to(DEV), count, shard or (0, pairs), grad, fp)
     torch.cuda.synchronize()
     assert int(st[0]) == 0
     return {n: grad[o:o + math.prod(s)].view(s).cpu() for (n, s), o in zip(PARAMS, fp.offsets)}
