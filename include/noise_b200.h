@@ -253,6 +253,11 @@ int noise_moment_query_scores_ws(const void* q, const void* k, const void* v, co
 int noise_rank1_operands(const float* buffer, const int64_t* offsets, const float* weight, float weight_scale,
                          int64_t shift, int n_elem, int pairs, int k_padded, void* dst, void* stream);
 
+/* noise_rank1_operands with fp32 output (dst float [n_elem, k_padded]): the operands of the tf32 update GEMM
+ * (noise_gemm_tf32_tn), for the reference's fp32 rebuild at 'high' precision (eggroll.py:159-160, :184). */
+int noise_rank1_operands_f32(const float* buffer, const int64_t* offsets, const float* weight, float weight_scale,
+                             int64_t shift, int n_elem, int pairs, int k_padded, float* dst, void* stream);
+
 /* out[o, i] = scale * sum_j weight[j] a_j[o] b_j[i] (fp32) for parameters too small for GEMM tiles: a_j =
  * buffer + offsets[j], b_j = a_j + n_out; with one_d != 0 the 1-D case out[i] = scale * sum_j weight[j] eps_j[i],
  * eps_j = buffer + offsets[j] (eggroll.py:162-163). */
@@ -608,9 +613,17 @@ int noise_read_static_status(int* status, void* stream);
 
 /* D[m, n] (fp32, row-major) = A[m, k] . B[n, k]^T for bf16 row-major A and B, on the persistent tcgen05/TMA GEMM
  * that every linear layer of noise_population_loss runs on, with a plain store epilogue. Stands in for the cuBLAS
- * GEMM autocast issues for `x @ weight.t()` (eggroll.py:58; utils/model.py:83-85). m % 128 == 0, n % 256 == 0,
- * k % 64 == 0; `workspace` holds at least NOISE_STATUS_BYTES (the device status word). */
+ * GEMM autocast issues for `x @ weight.t()` (eggroll.py:58; utils/model.py:83-85) and for the bf16 moment products
+ * of the readout cycle (train/speedrun/run.py:3681-3685). m >= 1, n % 32 == 0, k % 8 == 0 (partial tiles read zeros
+ * past the edges and store only inside D); A, B, D 16-byte aligned; `workspace` holds at least NOISE_STATUS_BYTES
+ * (the device status word). */
 int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace, void* stream);
+
+/* The same GEMM on fp32 A and B read as tf32 (tcgen05 kind::tf32, fp32 accumulation): an fp32 matmul at
+ * torch.set_float32_matmul_precision('high'), which the reference sets for its fp32 contractions — the seed-rebuilt
+ * update (archive/10M/train/val/eggroll.py:159-160, precision set at :184) and the readout cycle's x W, h W, x h^T,
+ * fg1 c^T and out h (train/speedrun/run.py:3673-3686, precision set at :4447). m >= 1, n % 32 == 0, k % 4 == 0. */
+int noise_gemm_tf32_tn(const float* a, const float* b, float* d, int m, int n, int k, void* workspace, void* stream);
 
 /* fp32 -> bf16 (round to nearest even) of n values; both pointers 16-byte aligned, n % 8 == 0.
  * Replaces autocast's per-call weight casts inside the reference's linears (eggroll.py:58 under

@@ -100,8 +100,12 @@ SIGNATURES = [
     ('noise_gemm_bf16_tn', ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
       ctypes.c_void_p]),
+    ('noise_gemm_tf32_tn', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+      ctypes.c_void_p]),
     ('noise_pack_bf16', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     ('noise_rank1_operands', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_rank1_operands_f32', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_rank1_small', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_adam_step', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
     ('noise_implicit_key_context', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
@@ -220,16 +224,31 @@ def launches():
     return lib().noise_last_launch_count()
 
 
-def gemm_bf16_tn(a, b):
-    """fp32 a @ b.T for bf16 a [m, k], b [n, k] on the tcgen05 GEMM core (m % 128, n % 256, k % 64 == 0)."""
+def _gemm(entry, dtype, a, b, out=None):
     require_cuda(a, b)
+    if a.dtype != dtype or b.dtype != dtype or a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f'{entry}: a [m, k] and b [n, k] of {dtype}')
     a, b = a.contiguous(), b.contiguous()
-    out = torch.empty((a.shape[0], b.shape[0]), dtype=torch.float32, device=a.device)
+    if out is None:
+        out = torch.empty((a.shape[0], b.shape[0]), dtype=torch.float32, device=a.device)
+    elif out.shape != (a.shape[0], b.shape[0]) or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError(f'{entry}: out must be contiguous fp32 [m, n]')
     ws = torch.empty(STATUS_BYTES, dtype=torch.uint8, device=a.device)
-    check(lib().noise_gemm_bf16_tn(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.shape[0], b.shape[0], a.shape[1],
-                                   ws.data_ptr(), stream_handle(a.device)), 'noise_gemm_bf16_tn')
+    check(getattr(lib(), entry)(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.shape[0], b.shape[0], a.shape[1],
+                                ws.data_ptr(), stream_handle(a.device)), entry)
     out._noise_workspace = ws
     return out
+
+
+def gemm_bf16_tn(a, b, out=None):
+    """fp32 a @ b.T for bf16 a [m, k], b [n, k] on the tcgen05 GEMM core (n % 32 == 0, k % 8 == 0)."""
+    return _gemm('noise_gemm_bf16_tn', torch.bfloat16, a, b, out)
+
+
+def gemm_tf32_tn(a, b, out=None):
+    """a @ b.T for fp32 a [m, k], b [n, k] at tf32 precision (torch's 'high') on the tcgen05 GEMM core (n % 32 == 0,
+    k % 4 == 0)."""
+    return _gemm('noise_gemm_tf32_tn', torch.float32, a, b, out)
 
 
 KINDS = ['norm_mix', 'gemm_qkv', 'attention', 'gemm_cproj', 'norm_mid', 'gemm_cfc', 'gemm_mproj', 'norm_final',

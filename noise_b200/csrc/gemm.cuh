@@ -1,6 +1,8 @@
-// Persistent, warp-specialised bf16 "TN" GEMM for sm_100a: D[M, N] = A[M, K] . B[N, K]^T with both operands
-// K-major in HBM (activations row-major, nn.Linear weights [out, in]), fp32 accumulation in tensor memory, and a
-// fused per-row epilogue supplied as a functor.
+// Persistent, warp-specialised "TN" GEMM for sm_100a: D[M, N] = A[M, K] . B[N, K]^T with both operands K-major in
+// HBM (activations row-major, nn.Linear weights [out, in]), fp32 accumulation in tensor memory, and a fused per-row
+// epilogue supplied as a functor. Operands are bf16 (kind::f16) or, with TF32, fp32 read as tf32 (kind::tf32: what
+// torch.set_float32_matmul_precision('high') gives an fp32 matmul). A shared-memory tile row is 128 bytes either way:
+// 64 bf16 or 32 fp32 values of K.
 //
 // Roles (320 threads, one CTA per SM):
 //   warp 0      one lane issues TMA tile loads (128-byte swizzle) into a STAGES-deep shared-memory ring;
@@ -78,7 +80,7 @@ struct GemmLayout {
 //   void chunk(int row, int col, float* v);           v[0..CH) = D[row, col .. col + CH) (may be modified in place)
 //   void tile_end(int row, int n_tile, int part);     after the last chunk of the thread's half of a tile
 //   void row_end(int row, int part);                  after the last N tile
-template <int BN, int STAGES, class Epi>
+template <int BN, int STAGES, class Epi, bool TF32 = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         int m_tiles, int n_tiles, int k_blocks, Epi epi, int* status) {
@@ -133,8 +135,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
             uint8_t* a = smem + stage * L::STAGE_BYTES;
             mbar_arrive_expect_tx(&full[stage], L::STAGE_BYTES);
-            tma_load_2d(a, &tmA, &full[stage], kb * GEMM_BK, mb * GEMM_BM);
-            tma_load_2d(a + L::A_BYTES, &tmB, &full[stage], kb * GEMM_BK, nb * BN);
+            constexpr int KE = TF32 ? GEMM_BK / 2 : GEMM_BK;  // K elements of a 128-byte tile row
+            tma_load_2d(a, &tmA, &full[stage], kb * KE, mb * GEMM_BM);
+            tma_load_2d(a + L::A_BYTES, &tmB, &full[stage], kb * KE, nb * BN);
             ++issued;
             if (++stage == STAGES) {
               stage = 0;
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(GEMM_BM, BN);
+      constexpr uint32_t idesc = TF32 ? idesc_tf32(GEMM_BM, BN) : idesc_bf16(GEMM_BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int t = 0;
@@ -176,8 +179,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t a = smem_u32(smem + stage * L::STAGE_BYTES);
             const uint64_t ad = sdesc_kmajor_sw128(a), bd = sdesc_kmajor_sw128(a + L::A_BYTES);
 #pragma unroll
-            for (int k = 0; k < GEMM_BK / 16; ++k)  // +32 bytes along K = +2 in the 16-byte address field
-              tc_mma(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0);
+            for (int k = 0; k < GEMM_BK / 16; ++k) {  // +32 bytes along K = +2 in the 16-byte address field
+              if constexpr (TF32)
+                tc_mma_tf32(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0);
+              else
+                tc_mma(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0);
+            }
             tc_commit(&empty[stage]);
             if (++stage == STAGES) {
               stage = 0;

@@ -70,22 +70,6 @@ __device__ __forceinline__ uint64_t km_sdesc_kmajor_sw64(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor of tcgen05.mma kind::tf32: tf32 A and B (fp32 in shared memory), fp32 D, M x N.
-__host__ __device__ constexpr uint32_t km_idesc_tf32(int M, int N) {
-  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
-         (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32 (K = 8 per instruction: 32 bytes of each row, as kind::f16's 16).
-__device__ __forceinline__ void km_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 struct KeyMomTcArgs {
   int T, window, rows;
   Rows raw;
@@ -267,7 +251,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
     }
   } else if (warp == 1) {
     {  // the whole warp runs the issuer; one elected lane issues the MMAs and commits
-      constexpr uint32_t id_s = SCAN ? km_idesc_tf32(KM_B, KM_R) : idesc_bf16(KM_B, KM_R);  // S, C (K-major B)
+      constexpr uint32_t id_s = SCAN ? idesc_tf32(KM_B, KM_R) : idesc_bf16(KM_B, KM_R);  // S, C (K-major B)
       constexpr uint32_t id_f = idesc_bf16(KM_B, 64, false, true);   // P2, R2, VA: B MN-major
       constexpr uint32_t id_q = idesc_bf16(KM_B, 96, false, true);   // Q2 | QXY
       int sv = 0, nitem = 0;
@@ -325,13 +309,13 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t ho = (k >> 2);
-              if (elect_one()) km_mma_tf32(ts, sdesc_kmajor_sw128(sbase + L::K + ho * KM_KT) + 2u * (k & 3),
+              if (elect_one()) tc_mma_tf32(ts, sdesc_kmajor_sw128(sbase + L::K + ho * KM_KT) + 2u * (k & 3),
                           sdesc_kmajor_sw128(st + L::SQ + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
             }
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const uint32_t ho = (k >> 2);
-              if (elect_one()) km_mma_tf32(ts + 32, sdesc_kmajor_sw128(sbase + L::V + ho * KM_KT) + 2u * (k & 3),
+              if (elect_one()) tc_mma_tf32(ts + 32, sdesc_kmajor_sw128(sbase + L::V + ho * KM_KT) + 2u * (k & 3),
                           sdesc_kmajor_sw128(st + L::SH + ho * KM_RT) + 2u * (k & 3), id_s, k > 0);
             }
           } else {

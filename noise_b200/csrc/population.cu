@@ -617,11 +617,13 @@ struct EpiHeadCE {
 };
 
 // Plain fp32 store of the accumulator: D[row, col] = acc (the tcgen05 core without any fused arithmetic).
+// Plain store of D (fp32, row-major, leading dimension ldd) for rows < m and columns < n: the M and N tails of a
+// GEMM whose last tiles reach past the operands (TMA fills those operand rows with zeros).
 struct EpiStore {
   static constexpr int CH = 32;
   static constexpr bool PIPELINED = false;
   float* d;
-  int ldd;
+  int ldd, m, n;
   float* scratch;
   uint32_t stg;
   __device__ __forceinline__ void stage(int, int, float*, int) {}
@@ -629,6 +631,7 @@ struct EpiStore {
   __device__ __forceinline__ void tile_end(int, int, int) {}
   __device__ __forceinline__ void row_end(int, int) {}
   __device__ __forceinline__ void chunk(int row, int col, float* acc) {
+    if (row >= m || col >= n) return;  // n % CH == 0: a chunk is wholly inside or outside
     float4* out = reinterpret_cast<float4*>(d + static_cast<int64_t>(row) * ldd + col);
 #pragma unroll
     for (int i = 0; i < CH / 4; ++i) out[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
@@ -915,16 +918,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 row-major [outer, inner] tensor, box [box_outer, 64] with 128-byte swizzle.
-static int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+// 2-D row-major [outer, inner] tensor of bf16 (or, f32, fp32) values, box [box_outer, 128 bytes] with 128-byte
+// swizzle; reads past the tensor's edge fill with zeros.
+static int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer,
+                    bool f32 = false) {
   auto fn = encode_fn();
   if (!fn) return NOISE_ERR_CUDA;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16) return NOISE_ERR_ALIGN;
+  const uint64_t es_bytes = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * es_bytes) % 16) return NOISE_ERR_ALIGN;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(GEMM_BK), box_outer};
+  cuuint64_t strides[1] = {inner * es_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es_bytes), box_outer};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
@@ -983,6 +990,32 @@ static int run_gemm(const void* A, int M, int K, const void* B, int N, const Epi
   const int grid = m_tiles < sms ? m_tiles : sms;
   launch_begin(s, kind);
   kern<<<grid, GEMM_THREADS, L::SMEM_BYTES, s>>>(ma, mb, m_tiles, N / GEMM_BN, K / GEMM_BK, epi, status);
+  launch_end(s);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+// D[m, n] = A[m, k] B[n, k]^T with a plain fp32 store, any m >= 1, n % 32 == 0 and k a whole number of 16 bytes:
+// the last M / N / K tiles read zeros past the operands' edges and store only rows < m, columns < n.
+template <bool TF32>
+static int run_gemm_plain(const void* A, int M, int K, const void* B, int N, float* D, int* status, cudaStream_t s) {
+  using L = GemmLayout<GEMM_BN, GEMM_STAGES>;
+  constexpr int KE = TF32 ? GEMM_BK / 2 : GEMM_BK;
+  if (M < 1 || N < 32 || N % 32 || K < 1) return NOISE_ERR_SHAPE;
+  CUtensorMap ma, mb;
+  int rc = make_map(&ma, A, K, M, GEMM_BM, TF32);
+  if (rc) return rc;
+  if ((rc = make_map(&mb, B, K, N, GEMM_BN, TF32))) return rc;
+  EpiStore e{D, N, M, N};
+  auto kern = gemm_bf16_tn_kernel<GEMM_BN, GEMM_STAGES, EpiStore, TF32>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES) != cudaSuccess)
+    return NOISE_ERR_CUDA;
+  const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+  int sms = sm_count();
+  if (sms <= 0) return NOISE_ERR_CUDA;
+  const int grid = m_tiles < sms ? m_tiles : sms;
+  launch_begin(s, K_GEMM_PLAIN);
+  kern<<<grid, GEMM_THREADS, L::SMEM_BYTES, s>>>(ma, mb, m_tiles, (N + GEMM_BN - 1) / GEMM_BN, (K + KE - 1) / KE, e,
+                                                 status);
   launch_end(s);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
@@ -1550,13 +1583,23 @@ int noise_read_static_status(int* status, void* stream) {
 int noise_gemm_bf16_tn(const void* a, const void* b, float* d, int m, int n, int k, void* workspace,
                        void* stream) {
   if (!a || !b || !d || !workspace) return NOISE_ERR_ARGUMENT;
-  if (m <= 0 || n <= 0 || k <= 0 || m % GEMM_BM || n % GEMM_BN || k % GEMM_BK) return NOISE_ERR_SHAPE;
+  if (m < 1 || n < 32 || n % 32 || k < 8 || k % 8) return NOISE_ERR_SHAPE;
   if (reinterpret_cast<uintptr_t>(d) & 15) return NOISE_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
   g_launches = 0;
-  EpiStore e{d, n};
-  return run_gemm(a, m, k, b, n, e, static_cast<int*>(workspace), s, K_GEMM_PLAIN);
+  return run_gemm_plain<false>(a, m, k, b, n, d, static_cast<int*>(workspace), s);
+}
+
+int noise_gemm_tf32_tn(const float* a, const float* b, float* d, int m, int n, int k, void* workspace,
+                       void* stream) {
+  if (!a || !b || !d || !workspace) return NOISE_ERR_ARGUMENT;
+  if (m < 1 || n < 32 || n % 32 || k < 4 || k % 4) return NOISE_ERR_SHAPE;
+  if (reinterpret_cast<uintptr_t>(d) & 15) return NOISE_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  g_launches = 0;
+  return run_gemm_plain<true>(a, m, k, b, n, d, static_cast<int*>(workspace), s);
 }
 
 int noise_pack_bf16(const float* src, void* dst, int64_t n, void* stream) {

@@ -162,6 +162,17 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32: fp32 operands in shared memory of which the tensor core reads the tf32
+// part (K = 8 per instruction: 32 bytes of each row, as kind::f16's 16 bf16 values).
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]^T (A operand read from tensor memory).
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
@@ -260,6 +271,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn_major 
          | (static_cast<uint32_t>(b_mn_major) << 16)
          | (static_cast<uint32_t>(N >> 3) << 17)
          | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor of tcgen05.mma kind::tf32: tf32 A and B (fp32 in shared memory), fp32 D, K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -2,9 +2,10 @@
 //
 // G_P = -(1 / count) sum_j w_j a_j b_j^T for every parameter P, where (a_j, b_j) is pair j's slice of the fixed noise
 // buffer at offsets[P, j] (a = first `out` values, b = next `in`), then AdamW. For matrices the sum over pairs is a GEMM
-// with K = pairs: rank1_operands_kernel builds A' [out, Kp] = -w_j a_j[o] / count and B' [in, Kp] = b_j[i] in bf16
-// (transposed through shared memory; columns j >= pairs are zero so Kp may be padded to the GEMM's K tile), and the
-// tcgen05 GEMM (noise_gemm_bf16_tn) computes G = A' B'^T. Parameters too small for GEMM tiles (the value-embedding gates
+// with K = pairs: rank1_operands_kernel builds A' [out, Kp] = -w_j a_j[o] / count and B' [in, Kp] = b_j[i] in fp32
+// (or bf16; transposed through shared memory; columns j >= pairs are zero so Kp may be padded), and the tcgen05 GEMM
+// computes G = A' B'^T at tf32 (noise_gemm_tf32_tn: the reference's fp32 matmul at 'high' precision, eggroll.py:184)
+// or bf16 (noise_gemm_bf16_tn). Parameters too small for GEMM tiles (the value-embedding gates
 // [8, 32], the mixing scalars [8]) use rank1_small_kernel directly. adam_kernel is torch.optim.AdamW's update
 // (weight_decay = 0) for one flat fp32 tensor.
 #include <cuda_bf16.h>
@@ -20,13 +21,17 @@ namespace update {
 constexpr int TJ = 64;  // pairs per tile
 constexpr int TE = 64;  // vector elements per tile
 
+__device__ __forceinline__ void store_operand(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void store_operand(float* p, float v) { *p = v; }
+
 // One block: pairs j0 .. j0 + 63, elements e0 .. e0 + 63 of the a (or b) vectors.
-// dst[e][j] = scale_j * buffer[off_j + shift + e] (bf16), zero for j >= pairs.
+// dst[e][j] = scale_j * buffer[off_j + shift + e] (bf16, or fp32 for the tf32 GEMM), zero for j >= pairs.
+template <class Out>
 __global__ void __launch_bounds__(256) rank1_operands_kernel(const float* __restrict__ buffer,
                                                              const int64_t* __restrict__ off,
                                                              const float* __restrict__ weight, float wscale,
                                                              int64_t shift, int n_elem, int pairs, int kp,
-                                                             __nv_bfloat16* __restrict__ dst) {
+                                                             Out* __restrict__ dst) {
   __shared__ float tile[TJ][TE + 1];
   const int j0 = blockIdx.x * TJ, e0 = blockIdx.y * TE;
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
@@ -42,7 +47,7 @@ __global__ void __launch_bounds__(256) rank1_operands_kernel(const float* __rest
   __syncthreads();
   for (int ee = ty; ee < TE; ee += 4) {
     const int e = e0 + ee, j = j0 + tx;
-    if (e < n_elem && j < kp) dst[static_cast<int64_t>(e) * kp + j] = __float2bfloat16_rn(tile[tx][ee]);
+    if (e < n_elem && j < kp) store_operand(dst + static_cast<int64_t>(e) * kp + j, tile[tx][ee]);
   }
 }
 
@@ -97,6 +102,16 @@ int noise_rank1_operands(const float* buffer, const int64_t* offsets, const floa
   dim3 grid((k_padded + TJ - 1) / TJ, (n_elem + TE - 1) / TE);
   rank1_operands_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       buffer, offsets, weight, weight_scale, shift, n_elem, pairs, k_padded, static_cast<__nv_bfloat16*>(dst));
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_rank1_operands_f32(const float* buffer, const int64_t* offsets, const float* weight, float weight_scale,
+                             int64_t shift, int n_elem, int pairs, int k_padded, float* dst, void* stream) {
+  if (!buffer || !offsets || !dst) return NOISE_ERR_ARGUMENT;
+  if (n_elem < 1 || pairs < 1 || k_padded < pairs || shift < 0) return NOISE_ERR_SHAPE;
+  dim3 grid((k_padded + TJ - 1) / TJ, (n_elem + TE - 1) / TE);
+  rank1_operands_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      buffer, offsets, weight, weight_scale, shift, n_elem, pairs, k_padded, dst);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

@@ -7,8 +7,9 @@ Same names, arguments and results as the reference's functions:
 - ``top_credit(model, x, y)`` -> [n, 512]: the readout cycle's credit of the final stream (run.py:3673-3686).
 
 The per-logit weights, the finish and coordinate_change are this library's kernels; the five bf16 moment GEMMs run on
-its tcgen05 GEMM; the fp32 contractions (x W, h W, x h^T, fg1 c^T and the final one with h) are cuBLAS matmuls, at
-the precision the caller set (the reference sets torch.set_float32_matmul_precision('high')).
+its tcgen05 GEMM, and the fp32 contractions (x W, h W, x h^T, fg1 c^T and the final one with h) on the same GEMM at
+tf32, the precision the reference runs them at (torch.set_float32_matmul_precision('high'), run.py:4447). The GEMM
+takes both operands K-major, so W and h are transposed once per call where they are the right-hand side.
 """
 import ctypes
 
@@ -72,7 +73,7 @@ def cycle_weights_fused(x, base, h):
     fg1, fast, rows, total, sq, _ = _weights(x, base, y)
     sq = sq[:, None]
     steps = SIGMA * torch.clamp(torch.sqrt(sq / D), min=1e-6)
-    dots = x @ h.T
+    dots = _lib.gemm_tf32_tn(x, h.detach().float())
     eps = torch.finfo(torch.float32).eps
     inv = torch.rsqrt((sq + 2 * steps * dots + steps * steps * D) / D + eps)
     inv0 = torch.rsqrt(sq / D + eps)
@@ -85,24 +86,21 @@ def top_credit(model, x, y):
     x = x.detach().float().contiguous()
     y = y.detach().long().contiguous()
     _lib.require_cuda(x, y)
-    h = model.H * step_signs(model.step_t, x.device)[None, :]
-    W = model.lm_head.float()
-    c = (h @ W).contiguous()
-    base = (x @ W).contiguous()
+    h = (model.H * step_signs(model.step_t, x.device)[None, :]).float().contiguous()
+    Wt = model.lm_head.float().t().contiguous()  # [4096, 512]: W as the K-major right-hand side
+    c = _lib.gemm_tf32_tn(h, Wt)                 # h W
+    base = _lib.gemm_tf32_tn(x, Wt)              # x W
     fg1, fast, rows, total, sq, base_y = _weights(x, base, y)
-    exact = (fg1 @ c.T).contiguous()
-    dots = (x @ h.T).contiguous()
+    exact = _lib.gemm_tf32_tn(fg1, c)            # fg1 c^T
+    dots = _lib.gemm_tf32_tn(x, h)               # x h^T
     n, R = x.shape[0], c.shape[0]
     powers = (c.bfloat16(), (c * c).bfloat16(), (c * c * c).bfloat16())
     prods = torch.empty(5, n, R, device=x.device)
     for k, p in enumerate((0, 0, 1, 1, 2)):  # fast_k against c, c, c^2, c^2, c^3 (run.py:3681-3685)
-        if n % 128 == 0 and R % 256 == 0:
-            prods[k] = _lib.gemm_bf16_tn(fast[k], powers[p])
-        else:
-            prods[k] = (fast[k] @ powers[p].T).float()
+        _lib.gemm_bf16_tn(fast[k], powers[p], prods[k])
     out = torch.empty(n, R, device=x.device)
     _lib.check(_lib.lib().noise_cycle_finish(dots.data_ptr(), sq.data_ptr(), exact.data_ptr(), prods.data_ptr(),
                                              rows.data_ptr(), total.data_ptr(), base_y.data_ptr(), c.data_ptr(),
                                              y.data_ptr(), n, R, SIGMA, out.data_ptr(), _lib.stream_handle(x.device)),
                'noise_cycle_finish')
-    return out @ h / D
+    return _lib.gemm_tf32_tn(out, h.t().contiguous()).div_(D)  # out h / D

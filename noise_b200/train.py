@@ -4,7 +4,8 @@
 1. offsets of the step (eggroll.py:117-120) and this rank's share of the population forward (``Population``);
 2. NCCL all-gather of the losses, fitness l(-) - l(+) z-scored and summed per pair (eggroll.py:147-154);
 3. the seed-rebuilt update G_P = -(1 / count) sum_j w_j a_j b_j^T over this rank's shard of the pairs: a GEMM with
-   K = pairs on the tcgen05 core for every matrix, a direct kernel for the small ones (eggroll.py:155-163); the
+   K = pairs on the tcgen05 core at tf32 (the reference's fp32 matmul at 'high' precision, eggroll.py:184) for every
+   matrix, a direct kernel for the small ones (eggroll.py:155-163); the
    partial updates are summed with one NCCL all-reduce of the flat gradient (the reference rebuilds the whole update
    on every rank instead; ``shard_update=False`` does that);
 4. AdamW on the flat fp32 parameters (eggroll.py:164-167) and a re-pack of the bf16 weights.
@@ -18,7 +19,8 @@ from . import _lib
 from .eggroll import NOISE, SIGMA, Population, member_layout, noise_buffer, step_offsets
 from .population import PARAMS
 
-GEMM_M, GEMM_N, GEMM_K = 128, 256, 64
+GEMM_N = 32  # the GEMM's N granularity (columns of a stored chunk)
+GEMM_MIN_ROWS = 128  # smaller matrices (the [8, 32] value-embedding gates) take the direct kernel
 
 
 def fitness_weights(losses, pairs):
@@ -76,17 +78,17 @@ def rebuild_update(buffer, offsets, weight, count, shard, grad_flat, fp):
             g.zero_()
             continue
         off = offsets[k, start:stop].contiguous()
-        if len(shape) == 2 and shape[0] % GEMM_M == 0 and shape[1] % GEMM_N == 0:
+        if len(shape) == 2 and shape[0] >= GEMM_MIN_ROWS and shape[1] % GEMM_N == 0:
             out, inn = shape
-            kp = -(-n // GEMM_K) * GEMM_K
-            a = torch.empty((out, kp), dtype=torch.bfloat16, device=buffer.device)
-            b = torch.empty((inn, kp), dtype=torch.bfloat16, device=buffer.device)
-            _lib.check(L.noise_rank1_operands(buffer.data_ptr(), off.data_ptr(), w.data_ptr(), scale, 0, out, n, kp,
-                                              a.data_ptr(), stream), 'noise_rank1_operands')
-            _lib.check(L.noise_rank1_operands(buffer.data_ptr(), off.data_ptr(), None, 1.0, out, inn, n, kp,
-                                              b.data_ptr(), stream), 'noise_rank1_operands')
-            _lib.check(L.noise_gemm_bf16_tn(a.data_ptr(), b.data_ptr(), g.data_ptr(), out, inn, kp,
-                                            status.data_ptr(), stream), 'noise_gemm_bf16_tn')
+            kp = -(-n // 4) * 4  # whole 16-byte rows of fp32; the GEMM reads zeros past them
+            a = torch.empty((out, kp), dtype=torch.float32, device=buffer.device)
+            b = torch.empty((inn, kp), dtype=torch.float32, device=buffer.device)
+            _lib.check(L.noise_rank1_operands_f32(buffer.data_ptr(), off.data_ptr(), w.data_ptr(), scale, 0, out, n,
+                                                  kp, a.data_ptr(), stream), 'noise_rank1_operands_f32')
+            _lib.check(L.noise_rank1_operands_f32(buffer.data_ptr(), off.data_ptr(), None, 1.0, out, inn, n, kp,
+                                                  b.data_ptr(), stream), 'noise_rank1_operands_f32')
+            _lib.check(L.noise_gemm_tf32_tn(a.data_ptr(), b.data_ptr(), g.data_ptr(), out, inn, kp,
+                                            status.data_ptr(), stream), 'noise_gemm_tf32_tn')
             launches += 3
         else:
             one_d = len(shape) == 1

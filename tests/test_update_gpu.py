@@ -1,7 +1,9 @@
 """The seed-rebuilt update and AdamW on the GPU against the CPU oracle, the reference's golden step and torch.
 
-Tolerance of the rebuilt update: relative to the largest |G| of each parameter, 2e-2 (the GEMM takes bf16 operands;
-the reference multiplies fp32 / tf32)."""
+Tolerance of the rebuilt update: relative to the largest |G| of each parameter, 4e-3. The GEMM reads its fp32
+operands as tf32, as the reference's fp32 matmul does at torch.set_float32_matmul_precision('high') (eggroll.py:184):
+each product carries a relative error below 2^-9 and the sum over pairs about 2^-9 sqrt(pairs) of the term scale,
+against a largest |G| of a few sqrt(pairs) term scales."""
 import math
 
 import pytest
@@ -11,7 +13,7 @@ from oracle import eggroll as oe, gpt
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device('cuda', 0) if torch.cuda.is_available() else None
-GTOL = 2e-2
+GTOL = 4e-3
 
 
 def _rel(a, r):
