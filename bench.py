@@ -15,7 +15,8 @@ Unit: train tokens/s (16,384 per update, all GPUs); the line's config also carri
 tokens, weak scaling, population forwards/s); --workload credit the credit-readout kernels in isolation (config 3);
 --workload aux the other entry points (un-perturbed forward, head loss, head sharding, readout scorers);
 --workload exchange the identity phase's head exchange (pack + heads-in + heads-out all_to_all) as the reference does
-it (pack kernel, NCCL all_to_all_single) and fused over peer memory (HeadExchange), N ranks under torchrun.
+it (pack kernel, NCCL all_to_all_single) and fused over peer memory (HeadExchange), N ranks under torchrun;
+--workload epoch the first --updates updates of a one-epoch run with its projected wall time.
 
 --impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
 fp32, all host threads) on a bounded sample of the same workload, rank 0 only, in the same unit.
@@ -59,7 +60,9 @@ def args_():
     ap.add_argument('--steps', type=int, default=5)
     ap.add_argument('--warmup', type=int, default=3)
     ap.add_argument('--impl', default='ours', choices=['ours', 'reference'])
-    ap.add_argument('--workload', default='train', choices=['train', 'population', 'credit', 'aux', 'exchange'])
+    ap.add_argument('--workload', default='train',
+                    choices=['train', 'population', 'credit', 'aux', 'exchange', 'epoch'])
+    ap.add_argument('--updates', type=int, default=100, help='timed updates of the bounded epoch run (--workload epoch)')
     # smaller population cases for profiling captures only; the benchmark line uses the defaults
     ap.add_argument('--members', type=int, default=MEMBERS, help='members per GPU (population workload)')
     ap.add_argument('--rows', type=int, default=ROWS, help='2048-token rows per member (population workload)')
@@ -600,6 +603,70 @@ def run_train(a):
         torch.distributed.destroy_process_group()
 
 
+EPOCH_ROWS = 14648  # utils/prepare_data.py's TRAIN_ROWS: rows of 2,049 tokens, one update per 8 rows
+
+
+def run_epoch(a):
+    """BASELINE config 5, bounded: the first --updates updates (default 100) of one epoch over 14,648 synthetic
+    Zipf(1.1) rows of 2,049 tokens (seed 0), 8 rows per update (1,831 updates an epoch), population 24,576 split over
+    the ranks, EGGROLL with AdamW as in run_train. Prints the timed updates' train tokens/s (max over ranks of the
+    CUDA-event time), the host wall time, the projected wall time of the whole epoch (1,831 x the mean update time)
+    and the mean loss of the first and last timed updates. The reference's own run (eggroll.py) trains on FineWeb;
+    synthetic rows stand in for it here."""
+    from noise_b200.eggroll import make_params
+    from noise_b200.train import EggrollTrainer
+
+    rank, world = int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', 0)))
+    torch.cuda.set_device(device)
+    dist = world > 1
+    if dist:
+        torch.distributed.init_process_group('nccl', device_id=device, timeout=timedelta(seconds=300))
+    rows = zipf_rows(EPOCH_ROWS, T + 1, seed=0)
+    n_updates = EPOCH_ROWS // TRAIN_ROWS
+    updates = min(a.updates, n_updates - a.warmup)
+    tr = EggrollTrainer(make_params(device, 0), TRAIN_PAIRS, TRAIN_ROWS, sigma=SIGMA, lr=1e-3, rank=rank,
+                        world=world)
+    batch = lambda u: rows[u * TRAIN_ROWS:(u + 1) * TRAIN_ROWS].pin_memory().to(device, non_blocking=True)
+    for u in range(a.warmup):
+        tr.step(batch(u), step=u + 1)
+    torch.cuda.synchronize()
+    if dist:
+        torch.distributed.barrier()
+    losses = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for u in range(a.warmup, a.warmup + updates):
+        losses.append(tr.step(batch(u), step=u + 1))
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms, wall * 1e3], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, wall = t[0].item(), t[1].item() / 1e3
+    per_update = ms / 1e3 / updates
+    if rank == 0:
+        loss = torch.stack(losses).float().cpu()
+        print(json.dumps({
+            'metric': 'one-epoch-equivalent training (BASELINE config 5), bounded to the first updates',
+            'value': TRAIN_TOKENS * updates / (ms / 1e3), 'unit': TRAIN_UNIT, 'n_gpus': world,
+            'updates_timed': updates, 'warmup': a.warmup, 'ms_per_update': per_update * 1e3,
+            'host_wall_s': wall, 'epoch_updates': n_updates, 'epoch_train_tokens': n_updates * TRAIN_TOKENS,
+            'projected_epoch_wall_s': per_update * n_updates,
+            'mean_loss_first': float(loss[:5].mean()), 'mean_loss_last': float(loss[-5:].mean()),
+            'scaling': 'strong', 'dtype': 'bf16',
+            'data': 'synthetic: 14,648 Zipf(1.1) rows of 2,049 tokens (seed 0), 8 rows per update',
+            'config': {'workload': 'BASELINE config 5 (EGGROLL updates at population 24,576, one row feeds one '
+                                   'update)', 'population': 2 * TRAIN_PAIRS, 'parallelism': f'members x{world}'}}),
+              flush=True)
+    if dist:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def _timed(fn, steps, warmup):
     """Microseconds per call of fn, CUDA events on the current stream after warm-up calls."""
     for _ in range(warmup):
@@ -822,6 +889,8 @@ def main():
         run_aux(a)
     elif a.workload == 'exchange':
         run_exchange(a)
+    elif a.workload == 'epoch':
+        run_epoch(a)
     else:
         run_ours(a)
 
