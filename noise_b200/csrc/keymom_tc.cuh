@@ -126,8 +126,19 @@ __global__ void __launch_bounds__(256) tf32_round_kernel(Tf32Job job, int64_t n4
 __device__ __forceinline__ void km_st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-__device__ __forceinline__ void km_bar_sync() {  // named barrier 1 over the 256 weight / epilogue threads
-  asm volatile("bar.sync 1, 256;" ::: "memory");
+// Named barrier 1 over the NT weight / epilogue threads of the calling kernel, returning the AND of their
+// predicates (a warp whose bounded wait gave up still arrives, with false, so every warp leaves together).
+template <int NT>
+__device__ __forceinline__ bool km_bar_and(bool pred) {
+  static_assert(NT % 32 == 0, "whole warps");
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(NT)
+      : "memory");
+  return r != 0;
 }
 
 struct KeyMomMaps {
@@ -428,7 +439,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&w_full[b]);
       }
-      if (!ok) break;
+      ok = __all_sync(0xffffffffu, ok);
       // the two halves' s1 / s2 of each key row
       // this thread's 32 raw coordinates d = half * 16 + i and 32 + half * 16 + i (and SCAN: their square sum)
       const int64_t ro = p.raw.at(row, tk, p.T);
@@ -446,13 +457,14 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       sums[(half * 3) * 128 + r] = s1p.x + s1p.y;
       sums[(half * 3 + 1) * 128 + r] = s2p.x + s2p.y;
       sums[(half * 3 + 2) * 128 + r] = rsq;
-      km_bar_sync();
-      const float a1 = sums[r] + sums[3 * 128 + r], a2 = sums[128 + r] + sums[4 * 128 + r];
-      const float rsq_all = sums[2 * 128 + r] + sums[5 * 128 + r];
-      if (!mbar_wait(acc_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
+      if (!km_bar_and<KM_THREADS - 64>(ok)) {
         ok = false;
         break;
       }
+      const float a1 = sums[r] + sums[3 * 128 + r], a2 = sums[128 + r] + sums[4 * 128 + r];
+      const float rsq_all = sums[2 * 128 + r] + sums[5 * 128 + r];
+      // a thread whose wait gives up skips the epilogue but still reaches the item's closing barrier
+      const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full, static_cast<uint32_t>(nitem) & 1u, p.status));
       tc_fence_after();
       // response per raw coordinate d = P and P + 32 of this half's pairs P = half * 16 + g * 8 + i, 8 pairs at a time
       float stepv, den;
@@ -469,7 +481,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       const float ka = 2.f * stepv * inv, kb = stepv * stepv * inv, cbk = stepv * rsqrtf(den), rstep = 1.f / stepv;
       const int64_t oo = p.out.at(row, tk, p.T);
 #pragma unroll 1
-      for (int g8 = 0; g8 < 2; ++g8) {
+      for (int g8 = 0; g8 < (got ? 2 : 0); ++g8) {
         float p2[16], r2[16], q2[16], xy[16];
         tmem_ld16(trow + KM_TP2 + half * 32 + g8 * 16, p2);
         tmem_ld16(trow + KM_TR2 + half * 32 + g8 * 16, r2);
@@ -519,7 +531,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       }
       // value sums: 32 columns of VA
       float va[32];
-      if (values) {
+      if (values && got) {
         tmem_ld32(trow + KM_TVA + half * 32, va);
         tc_wait_ld();
         reg_fence<32>(va);
@@ -527,8 +539,11 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
-      if (!values) {
-        km_bar_sync();  // both halves have read sums before the next item overwrites them
+      if (!values || !got) {
+        if (!km_bar_and<KM_THREADS - 64>(got)) {  // both halves have read sums before the next item overwrites them
+          ok = false;
+          break;
+        }
         continue;
       }
       const int64_t vo = p.vout.at(row, tk, p.T) + half * 32;
@@ -544,7 +559,10 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         for (int q = 0; q < 8; ++q)
           dst[q] = make_float4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
       }
-      km_bar_sync();  // both halves have read sums before the next item overwrites them
+      if (!km_bar_and<KM_THREADS - 64>(true)) {  // both halves have read sums before the next item overwrites them
+        ok = false;
+        break;
+      }
     }
   }
   __syncwarp();

@@ -327,12 +327,15 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&w_full[b]);
       }
-      if (!ok) break;
+      ok = __all_sync(0xffffffffu, ok);
       sums[(half * 4) * 128 + r] = s1n.x + s1n.y;
       sums[(half * 4 + 1) * 128 + r] = s2n.x + s2n.y;
       sums[(half * 4 + 2) * 128 + r] = s1d.x + s1d.y;
       sums[(half * 4 + 3) * 128 + r] = s2d.x + s2d.y;
-      km_bar_sync();
+      if (!km_bar_and<QM_THREADS - 64>(ok)) {
+        ok = false;
+        break;
+      }
       const float v1n = sums[r] + sums[4 * 128 + r], v2n = sums[128 + r] + sums[5 * 128 + r];
       const float v1d = sums[2 * 128 + r] + sums[6 * 128 + r], v2d = sums[3 * 128 + r] + sums[7 * 128 + r];
       // per query: ratio = (2 step raw + step^2) / 64 / den = ka raw + kb, z = bf16(zn / (1 + zd) / step)
@@ -342,13 +345,11 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
       const float ka = 2.f * stepv * inv, kb = stepv * stepv * inv, cbk = stepv * rsqrtf(den), rstep = 1.f / stepv;
       const int64_t ro = p.raw.at(row, sq, p.T);
       const int64_t oo = p.out.at(row, sq, p.T);
-      if (!mbar_wait(acc_full, static_cast<uint32_t>(nitem) & 1u, p.status)) {
-        ok = false;
-        break;
-      }
+      // a thread whose wait gives up skips the epilogue but still reaches the item's closing barrier
+      const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full, static_cast<uint32_t>(nitem) & 1u, p.status));
       tc_fence_after();
 #pragma unroll 1
-      for (int g8 = 0; g8 < 2; ++g8) {
+      for (int g8 = 0; g8 < (got ? 2 : 0); ++g8) {
         const int P0 = half * 16 + g8 * 8;  // this chunk's 8 rotary pairs
         float nx[8], ny[8], nxx[8], nyy[8], nxy[8], dx[8], dy[8], dxx[8], dyy[8], dxy[8], lx[8], ly[8], mx[8], my[8];
         qm_tmem_ld8(trow + QM_TN + P0, nx);
@@ -423,7 +424,11 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
           }
         }
       }
-      km_bar_sync();  // both halves have read sums before the next item overwrites them
+      // both halves have read sums before the next item overwrites them
+      if (!km_bar_and<QM_THREADS - 64>(got)) {
+        ok = false;
+        break;
+      }
     }
   }
   __syncwarp();
