@@ -156,22 +156,60 @@ class Clocks:
                 'reasons': sorted(reasons), 'samples': len(self.samples)}
 
 
-def cpu_reference_sample(threads):
-    """Seconds for the oracle restatement of eggroll.population_loss (fp32, CPU) on CPU_SAMPLE_MEMBERS members x
-    CPU_SAMPLE_T tokens."""
-    from oracle import eggroll as oe, gpt as og  # the CPU baseline leg only
+REFERENCE_ROOT = ROOT / 'baseline' / '_ref'
+_CPU_CASE = {}
+
+
+def _cpu_case(threads):
+    """The CPU baseline's prepared case: ('reference', call) running the reference's own eggroll.population_loss from
+    its install in baseline/_ref (eager flex attention: compiled flex attention does not lower on the CPU; the noise
+    buffer shrunk from 2**28 to 2**20 values, which changes which values a member reads, not the work), else ('port',
+    call) running the oracle's restatement. Either way fp32 on CPU_SAMPLE_MEMBERS members x CPU_SAMPLE_T tokens of
+    EGGROLL's make_model weights."""
+    if threads in _CPU_CASE:
+        return _CPU_CASE[threads]
     torch.set_num_threads(threads)
-    w = og.init_weights(0, eggroll=True)
-    buf = oe.make_buffer(2 ** 20, seed=0)
-    shapes = og.param_shapes()
-    offs = oe.offsets(shapes, 1, step=1, n_noise=2 ** 20)
-    nz = oe.noise(buf, offs, torch.tensor([0, 0]), shapes)
-    sign = torch.tensor([SIGMA, -SIGMA])
     tok = zipf_rows(1, CPU_SAMPLE_T + 1, seed=0)[0]
+    idx, tgt = tok[:-1], tok[1:].contiguous()
+    sign = torch.tensor([SIGMA, -SIGMA])
+    path = REFERENCE_ROOT / 'archive' / '10M' / 'train' / 'val' / 'eggroll.py'
+    case = None
+    if path.exists():
+        try:
+            import importlib.util
+            sys.path.insert(0, str(REFERENCE_ROOT))
+            import utils.model as model
+            from torch.nn.attention.flex_attention import flex_attention
+            model.flex = flex_attention
+            spec = importlib.util.spec_from_file_location('reference_eggroll', path)
+            eg = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(eg)
+            eg.NOISE = 2 ** 20
+            net = eg.make_model(torch.device('cpu'), 0)
+            es = eg.Eggroll(net, 1)
+            nz = es.noise(es.offsets(step=1), torch.tensor([0, 0]))
+            case = ('reference', lambda: eg.population_loss(net, es.params, nz, sign, idx, tgt))
+        except Exception as exc:  # noqa: BLE001 - the port below is the documented fallback
+            print(f'cpu baseline: the reference install did not load ({exc!r}); timing the oracle port', flush=True)
+    if case is None:
+        from oracle import eggroll as oe, gpt as og  # the CPU baseline leg only
+        w = og.init_weights(0, eggroll=True)
+        buf = oe.make_buffer(2 ** 20, seed=0)
+        shapes = og.param_shapes()
+        nz = oe.noise(buf, oe.offsets(shapes, 1, step=1, n_noise=2 ** 20), torch.tensor([0, 0]), shapes)
+        case = ('port', lambda: oe.population_loss(w, nz, sign, idx, tgt))
+    _CPU_CASE[threads] = case
+    return case
+
+
+def cpu_reference_sample(threads):
+    """(seconds of one CPU population forward of CPU_SAMPLE_MEMBERS members x CPU_SAMPLE_T tokens, its kind)."""
+    kind, call = _cpu_case(threads)
+    torch.set_num_threads(threads)
     t0 = time.perf_counter()
     with torch.no_grad():
-        oe.population_loss(w, nz, sign, tok[:-1], tok[1:], reduction='sum')
-    return time.perf_counter() - t0
+        call()
+    return time.perf_counter() - t0, kind
 
 
 def run_reference(a):
@@ -182,10 +220,12 @@ def run_reference(a):
         return
     threads = os.cpu_count() or 1
     per = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048  # population forwards per sample
-    for _ in range(a.warmup):
-        cpu_reference_sample(threads)
-    times = [cpu_reference_sample(threads) for _ in range(a.steps)]
+    for _ in range(max(a.warmup, 1)):
+        _, kind = cpu_reference_sample(threads)
+    times = [cpu_reference_sample(threads)[0] for _ in range(a.steps)]
     fwd = per * len(times) / sum(times)
+    what = ("the reference's own eggroll.population_loss (baseline/_ref, eager flex attention)" if kind == 'reference'
+            else 'oracle restatement of eggroll.population_loss, dense attention')
     if a.workload == 'population':
         value, unit, metric, scaling = fwd, UNIT, POP_METRIC, 'weak'
         workload = 'population forward, BASELINE config 2 shape, bounded CPU sample'
@@ -195,14 +235,14 @@ def run_reference(a):
         workload = 'BASELINE config 4 update (population 24,576), bounded CPU sample of its population forward'
         conv = '; x 16,384 train tokens per 24,576 population forwards of an update'
     sample = (f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of the fp32 population forward per step '
-              f'(oracle restatement of eggroll.population_loss, dense attention){conv}')
+              f'({what}){conv}')
     print(json.dumps({
         'impl': 'reference', 'metric': metric, 'value': value, 'unit': unit, 'n_gpus': a.gpus, 'steps': a.steps,
         'warmup': a.warmup, 'ms_per_step': 1e3 * sum(times) / len(times), 'higher_is_better': True,
         'scaling': scaling, 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
         'config': {'workload': workload, 'members_per_step': CPU_SAMPLE_MEMBERS, 'seq_len': CPU_SAMPLE_T,
                    'population_forwards_per_s': fwd},
-        'cpu_baseline': {'value': value, 'unit': unit, 'cores': threads, 'kind': 'port', 'sample': sample},
+        'cpu_baseline': {'value': value, 'unit': unit, 'cores': threads, 'kind': kind, 'sample': sample},
         'e2e': {'value': value, 'unit': unit, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }), flush=True)
 
@@ -260,12 +300,15 @@ def cpu_baseline_train():
     bounded sample), scaled by the forwards an update needs (24,576 member rows for 8 x 2048 train tokens; the
     update's rebuild and AdamW, under 2% of an update here, are left out)."""
     threads = os.cpu_count() or 1
-    secs = [cpu_reference_sample(threads) for _ in range(2)]
-    fwd = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(secs)
-    return {'value': fwd * TRAIN_TOKENS / TRAIN_FORWARDS, 'unit': TRAIN_UNIT, 'cores': threads, 'kind': 'port',
-            'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of the fp32 oracle restatement of '
-                      f'eggroll.population_loss, median of 2 ({fwd:.3f} population forwards/s), x 16,384 train '
-                      f'tokens per 24,576 population forwards'}
+    cpu_reference_sample(threads)  # warm-up
+    runs = [cpu_reference_sample(threads) for _ in range(2)]
+    kind = runs[0][1]
+    fwd = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(r[0] for r in runs)
+    what = "the reference's own eggroll.population_loss (eager flex)" if kind == 'reference' else \
+        'the oracle restatement of eggroll.population_loss'
+    return {'value': fwd * TRAIN_TOKENS / TRAIN_FORWARDS, 'unit': TRAIN_UNIT, 'cores': threads, 'kind': kind,
+            'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens of {what}, fp32, median of 2 '
+                      f'({fwd:.3f} population forwards/s), x 16,384 train tokens per 24,576 population forwards'}
 
 
 def run_ours(a):
@@ -363,11 +406,12 @@ def run_ours(a):
     line.update(kernel_roofline(prof, m_launch, clk, ms, forwards))
     if rank == 0 and world == 1:
         threads = os.cpu_count() or 1
-        secs = [cpu_reference_sample(threads) for _ in range(2)]
-        cv = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(secs)
-        line['cpu_baseline'] = {'value': cv, 'unit': UNIT, 'cores': threads, 'kind': 'port',
-                                'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens, fp32 oracle '
-                                          f'restatement of eggroll.population_loss, median of 2'}
+        cpu_reference_sample(threads)  # warm-up
+        runs = [cpu_reference_sample(threads) for _ in range(2)]
+        cv = CPU_SAMPLE_MEMBERS * CPU_SAMPLE_T / 2048 / statistics.median(r[0] for r in runs)
+        line['cpu_baseline'] = {'value': cv, 'unit': UNIT, 'cores': threads, 'kind': runs[0][1],
+                                'sample': f'{CPU_SAMPLE_MEMBERS} members x {CPU_SAMPLE_T} tokens, fp32 '
+                                          f'eggroll.population_loss ({runs[0][1]}), median of 2'}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:

@@ -125,11 +125,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&s_empty[b], 4);  // one arrival per softmax warp of the group (after its __syncwarp)
+      mbar_init(&p_full[b], 4);
       mbar_init(&p_empty[b], 1);
       mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 128);
+      mbar_init(&o_empty[b], 4);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -283,7 +283,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         for (int c = 0; c < TA_BK; c += 32) tmem_ld32(s_addr + c, v + c);
         tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_empty[g]);  // S is in registers: the next S MMA may overwrite it
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[g]);  // S is in registers: the next S MMA may overwrite it
         uint32_t pk[TA_BK / 2];
         // packed fp32x2 FMA / add (one instruction for two keys; the same rounding as two scalar ones)
         float2 rs2 = make_float2(0.f, 0.f);
@@ -318,7 +319,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         for (int c = 0; c < TA_BK / 2; c += 16) tmem_st16(p_addr + c, pk + c);
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[g]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g]);
         l += rs;
         return true;
       };
@@ -352,7 +354,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       tmem_ld32(o_addr + 32, o + 32);
       tc_wait_ld();
       tc_fence_before();
-      mbar_arrive(&o_empty[g]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[g]);
       if (active) {
         const int j = it.bh / NOISE_N_HEAD, hh = it.bh % NOISE_N_HEAD;
         const int64_t row = static_cast<int64_t>(j) * p.T + tq;

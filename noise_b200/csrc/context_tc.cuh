@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int g = 0; g < 2; ++g) {
       mbar_init(&s_full[g], 1);
-      mbar_init(&s_empty[g], 128);
+      mbar_init(&s_empty[g], 4);  // one arrival per warp of the group (after its __syncwarp)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -221,7 +221,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           reg_fence<32>(cc);
           if (c + 32 == TC_B) {  // the tile's last chunk is in registers: TMEM may take the next tile
             tc_fence_before();
-            mbar_arrive(&s_empty[g]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[g]);
           }
           if constexpr (MASKED) {
 #pragma unroll

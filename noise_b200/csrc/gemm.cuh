@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 32 * GEMM_EPI_WARPS);
+      mbar_init(&acce[b], GEMM_EPI_WARPS);  // one arrival per epilogue warp (after its __syncwarp)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -263,7 +263,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           e.tile_end(row, nb, part);
         }
         tc_fence_before();
-        mbar_arrive(&acce[buf]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[buf]);
         if (!ok) break;
       }
       if (ok) e.row_end(row, part);

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(THREADS, 1) idgemm_kernel(const __grid_constan
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 32 * EPI_WARPS);
+      mbar_init(&acce[b], EPI_WARPS);  // one arrival per epilogue warp (after its __syncwarp)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(THREADS, 1) idgemm_kernel(const __grid_constan
                          pack2(v[8 * i + 4], v[8 * i + 5]), pack2(v[8 * i + 6], v[8 * i + 7]));
       }
       tc_fence_before();
-      mbar_arrive(&acce[buf]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
     }
   }
   __syncwarp();

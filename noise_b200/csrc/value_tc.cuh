@@ -123,11 +123,11 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&s_empty[b], 4);  // one arrival per warp (after its __syncwarp)
+      mbar_init(&p_full[b], 4);
       mbar_init(&p_empty[b], 1);
       mbar_init(&o_full[b], 1);
-      mbar_init(&o_empty[b], 256);
+      mbar_init(&o_empty[b], 8);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
         for (int c = 0; c < TV_B; c += 32) tmem_ld32(s_addr + c, v + c);
         tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(&s_empty[g]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[g]);
         const float* lse = reinterpret_cast<const float*>(smem + TV_RING + (svi % TV_STAGES) * TV_STAGE + 3 * TV_TILE);
 #pragma unroll
         for (int c = 0; c < TV_B; c += 8) {
@@ -311,7 +312,8 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
                        pack_bf16x2(pe[2], pe[3]), pack_bf16x2(pe[4], pe[5]), pack_bf16x2(pe[6], pe[7]));
         }
         fence_proxy_async_smem();
-        mbar_arrive(&p_full[g]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g]);
         return true;
       };
       // the item's receiver tiles run through ring slots sv .. sv + (hi - lo); this group's start at lo_g
@@ -338,7 +340,8 @@ __global__ void __launch_bounds__(TV_THREADS, 1)
       tmem_ld32(o_addr + 32, o + 32);
       tc_wait_ld();
       tc_fence_before();
-      mbar_arrive(&o_empty[ob]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[ob]);
       if (active) {
         float* out = static_cast<float*>(p.out.data) + p.out.base(it.row) + static_cast<int64_t>(tk) * p.out.token_stride;
 #pragma unroll

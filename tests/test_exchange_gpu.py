@@ -3,8 +3,9 @@ all_to_all, the heads-out all_to_all, the epoch-flag waits).
 
 On one GPU (world 1, every send lands in the rank's own buffer): got equals pack_heads_kernel's send buffer and got2
 equals back bit for bit over several epochs, calls out of the step order raise, and a wait for an epoch nobody sends
-gives up after its limit with the timeout status (the context stays usable). On two GPUs (tests/exchange_ranks.py
-under torchrun, skipped with fewer): got and got2 equal NCCL's all_to_all_single of the same buffers bit for bit."""
+gives up after its limit with the timeout status (the context stays usable). On 2, 4 and 8 GPUs
+(tests/exchange_ranks.py under torchrun, each skipped with fewer GPUs): got and got2 equal NCCL's all_to_all_single of
+the same buffers bit for bit."""
 import ctypes
 import os
 import subprocess
@@ -65,12 +66,15 @@ def test_wait_gives_up_with_timeout_status():
         ex.close()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason='needs 2 GPUs')
-def test_two_ranks_match_nccl_all_to_all():
+@pytest.mark.parametrize('world', [2, 4, 8])
+def test_ranks_match_nccl_all_to_all(world):
+    """world ranks (one GPU each; skipped when the box has fewer): the exchange against all_to_all_single."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f'needs {world} GPUs')
     env = dict(os.environ, NCCL_NVLS_ENABLE='0', PYTHONPATH=str(ROOT))
     cmd = ['timeout', '-k', '30', '240', sys.executable, '-m', 'torch.distributed.run', '--nnodes=1',
-           '--nproc-per-node', '2', '--master-addr', '127.0.0.1', '--master-port', '29531',
+           '--nproc-per-node', str(world), '--master-addr', '127.0.0.1', '--master-port', str(29530 + world),
            str(ROOT / 'tests' / 'exchange_ranks.py')]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    assert r.stdout.count('exchange ok') == 2, r.stdout
+    assert r.stdout.count('exchange ok') == world, r.stdout
