@@ -164,15 +164,14 @@ int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const f
                    int window, float sigma, const noise_rows_t* key_out, const noise_rows_t* value_out, void* stream);
 
 /* Bytes of the caller's workspace for noise_key_scan_ws: a 256-byte status block, the receivers' pair features and
- * the hub's bf16 hi / lo halves (bf16 [rows, T, 64] x 5), then tf32-rounded copies of qp, kp, values and hub (fp32
- * [rows, T, 64] x 4: the MMAs see the operands rounded as the warp kernels round them). 0 for rows < 1 or
- * tokens < 1. */
+ * the hub's bf16 hi / lo halves (bf16 [rows, T, 64] x 5). 0 for rows < 1 or tokens < 1. */
 size_t noise_key_scan_workspace_bytes(int rows, int tokens);
 
 /* noise_key_scan with a caller workspace (256-byte aligned): T % 128 == 0 with 16-byte-aligned, non-blocked key_out /
- * value_out views runs on tcgen05 (the logits and scores as kind::tf32 MMAs on the fp32 operands, the moment sums as
- * bf16 MMAs, the same kernel as noise_moment_key_scores_ws); anything else falls through to noise_key_scan. Same
- * results (moment_kernels.py:467-607). */
+ * value_out views runs on tcgen05 (the logits and scores as kind::tf32 MMAs reading the fp32 operands as they are,
+ * which is how the reference's Triton tf32 dots run on this GPU; the moment sums as bf16 MMAs; the same kernel as
+ * noise_moment_key_scores_ws); anything else falls through to noise_key_scan (tf32 operands rounded to nearest).
+ * Same results (moment_kernels.py:467-607). */
 int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, const float* lse, const float* values,
                       const float* hub, const float* center, const float* cos, const float* sin, int rows, int tokens,
                       int window, float sigma, const noise_rows_t* key_out, const noise_rows_t* value_out,

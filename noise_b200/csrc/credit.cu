@@ -1116,8 +1116,7 @@ int noise_key_scan(const float* qp, const float* kp, const float* k_raw, const f
 
 size_t noise_key_scan_workspace_bytes(int rows, int tokens) {
   if (rows < 1 || tokens < 1) return 0;
-  return 256 + 5 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16) +
-         4 * static_cast<size_t>(rows) * tokens * D * sizeof(float);
+  return 256 + 5 * static_cast<size_t>(rows) * tokens * D * sizeof(__nv_bfloat16);
 }
 
 int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, const float* lse, const float* values,
@@ -1147,14 +1146,12 @@ int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, cons
   __nv_bfloat16* xy = g2 + n * D;
   __nv_bfloat16* hi = xy + n * D;
   __nv_bfloat16* lo = hi + n * D;
-  float* qt = reinterpret_cast<float*>(lo + n * D);  // tf32-rounded qp, kp, values, hub
-  float* kt = qt + n * D;
-  float* vt = kt + n * D;
-  float* ht = vt + n * D;
   KeyMomMaps m;
   int rc;
-  if ((rc = km_map_rows(&m.k, kt, false, n, 32, KM_B)) || (rc = km_map_rows(&m.v, vt, false, n, 32, KM_B)) ||
-      (rc = km_map_rows(&m.q, qt, false, n, 32, KM_R)) || (rc = km_map_rows(&m.h, ht, false, n, 32, KM_R)) ||
+  // the logits' and scores' operands go to the kind::tf32 MMAs as they are: the tensor core reads the tf32 part of
+  // each fp32 value, as the reference's Triton kernel's tf32 dots do on this GPU (no rounding pass)
+  if ((rc = km_map_rows(&m.k, kp, false, n, 32, KM_B)) || (rc = km_map_rows(&m.v, values, false, n, 32, KM_B)) ||
+      (rc = km_map_rows(&m.q, qp, false, n, 32, KM_R)) || (rc = km_map_rows(&m.h, hub, false, n, 32, KM_R)) ||
       (rc = km_map(&m.f2, f2, n)) || (rc = km_map(&m.g2, g2, n)) || (rc = km_map(&m.xy, xy, n)) ||
       (rc = km_map(&m.hi, hi, n)) || (rc = km_map(&m.lo, lo, n)) || (rc = km_map_f32(&m.lse, lse, tokens, rows)) ||
       (rc = km_map_f32(&m.ctr, center, tokens, rows)))
@@ -1163,18 +1160,6 @@ int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, cons
   const int64_t n_pairs = n * 32;
   keymom_features_kernel<<<static_cast<int>(std::min<int64_t>((n_pairs + 255) / 256, static_cast<int64_t>(sms) * 8)),
                            256, 0, s>>>(qp, n_pairs, f2, g2, xy);
-  {
-    Tf32Job job;
-    const float* src[4] = {qp, kp, values, hub};
-    float* dst[4] = {qt, kt, vt, ht};
-    for (int t = 0; t < 4; ++t) {
-      job.src[t] = reinterpret_cast<const float4*>(src[t]);
-      job.dst[t] = reinterpret_cast<float4*>(dst[t]);
-    }
-    const int64_t n4 = n * (D / 4);
-    tf32_round_kernel<<<static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(sms) * 8)), 256, 0,
-                        s>>>(job, n4);
-  }
   if (with_values) {
     const Rows hub_rows = stacked_rows(hub, tokens);
     const int64_t n4 = n * (D / 4);

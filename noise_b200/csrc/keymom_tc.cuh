@@ -99,30 +99,6 @@ __global__ void __launch_bounds__(256) keymom_features_kernel(const float* __res
   }
 }
 
-// fp32 -> tf32 (round to nearest, ties away from zero) of up to four [n] fp32 arrays into copies: the key scan's
-// operands as the warp kernels and the lse / center pass round them, so the tcgen05 kind::tf32 MMAs (which read the
-// top 19 bits of each fp32 operand) see the same values.
-struct Tf32Job {
-  const float4* src[4];
-  float4* dst[4];
-};
-__global__ void __launch_bounds__(256) tf32_round_kernel(Tf32Job job, int64_t n4) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const float4 v = job.src[t][i];
-      uint32_t r[4];
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[0]) : "f"(v.x));
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[1]) : "f"(v.y));
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[2]) : "f"(v.z));
-      asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r[3]) : "f"(v.w));
-      job.dst[t][i] = make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]),
-                                  __uint_as_float(r[3]));
-    }
-  }
-}
-
 __device__ __forceinline__ void km_st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }

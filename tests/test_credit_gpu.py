@@ -3,7 +3,10 @@ by running moment_kernels.py under the Triton interpreter) and with the dense CP
 
 Stated tolerances (relative to the largest |reference| of the output): lse / center 1e-5; value credits 2e-3 (bf16
 probabilities, hi + lo source); key credits and key moments 5e-3; query credits 1e-2 (bf16 operands and a bf16-rounded
-output, so single elements differ by a bf16 ulp)."""
+output, so single elements differ by a bf16 ulp). The key scan's raw value credits 4e-3: the interpreter evaluates the
+reference's tf32 logit dots exactly, while on the GPU the kind::tf32 MMAs read the tf32 part of each fp32 operand, as
+the reference's own Triton kernel does there (the tcgen05 key scan is within 2e-4 of that kernel at config 3,
+tests/test_credit_triton_gpu.py); against the exact dots that moves these sums by up to 2.7e-3."""
 import sys
 
 import pytest
@@ -56,7 +59,7 @@ def test_against_reference_kernels(mk, fixture, window):
     assert rel(key, o['key']) < 5e-3
     key_v, raw_v = mk.key_and_raw_value_credits(d['qp'], d['kp'], d['k_raw'], lse_r, d['values'], d['hub'], ctr_r,
                                                 d['cos'], d['sin'], window, 0.003)
-    assert rel(key_v, o['key_v']) < 5e-3 and rel(raw_v, o['raw_v']) < 2e-3
+    assert rel(key_v, o['key_v']) < 5e-3 and rel(raw_v, o['raw_v']) < 4e-3
     qs = torch.empty(1, g['rows'], g['length'], 64, dtype=torch.bfloat16, device=DEV)
     mk.moment_query_scores(b['qp'], b['kp'], b['values'], b['hub'], d['q_raw'].unsqueeze(0), o['sq'].to(DEV),
                            d['kp'], d['cos'], d['sin'], lse_r, ctr_r, o['steps'].to(DEV), qs, 4, window)
