@@ -15,17 +15,21 @@
 namespace noise {
 namespace xch {
 
-// Chunk p (n16 16-byte words) of send into rank p's buffer at dst_offset + rank * chunk, grid-stride, then the flag.
+// Chunk p (n16 16-byte words) of send into rank p's buffer at dst_offset + rank * chunk, then the flag. The grid walks
+// 4 KB tiles (one block's stores) with the destination varying fastest and staggered by this rank, so the blocks,
+// and the ranks at any moment, write to different destinations instead of every sender to one at a time.
 __global__ void __launch_bounds__(256) alltoall_peer_kernel(const uint4* __restrict__ send, int64_t n16,
                                                             const __grid_constant__ Peers peers, int64_t dst_offset,
                                                             int slot, uint32_t epoch) {
-  const int64_t total = n16 * peers.world;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int p = static_cast<int>(i / n16);
-    const int64_t j = i - p * n16;
-    uint4* dst = reinterpret_cast<uint4*>(peers.base[p] + dst_offset) + peers.rank * n16 + j;
-    *dst = send[i];
+  const int W = peers.world;
+  const int64_t tiles = (n16 + blockDim.x - 1) / blockDim.x * W;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int p = static_cast<int>((t % W + peers.rank) % W);
+    const int64_t j = (t / W) * blockDim.x + threadIdx.x;
+    if (j < n16) {
+      uint4* dst = reinterpret_cast<uint4*>(peers.base[p] + dst_offset) + peers.rank * n16 + j;
+      *dst = send[p * n16 + j];
+    }
   }
   send_done(peers, slot, epoch);
 }

@@ -83,9 +83,12 @@ __global__ void __launch_bounds__(256) pack_heads_peer_kernel(const __grid_const
   uint32_t* st = stage[warp];
   for (int64_t gi = static_cast<int64_t>(blockIdx.x) * WARPS + warp; gi < groups;
        gi += static_cast<int64_t>(gridDim.x) * WARPS) {
-    const int tok0 = static_cast<int>(gi % groups_per_hl) * GROUP;
-    const int hl = static_cast<int>(gi / groups_per_hl);
-    const int l = hl % a.L, h = hl / a.L;
+    // the head varies fastest and starts at this rank's own heads: the warps of a block, and the ranks at any moment,
+    // write to different destinations, so no destination's NVLink ingress is shared by every sender at once
+    const int h = static_cast<int>((gi % H + static_cast<int64_t>(peers.rank) * hp) % H);
+    const int64_t rest = gi / H;
+    const int l = static_cast<int>(rest % a.L);
+    const int tok0 = static_cast<int>(rest / a.L) * GROUP;
 #pragma unroll
     for (int r = 0; r < GROUP; ++r) pack_row(a, h, l, tok0 + r, st + r * (PACK / 2), lane);
     __syncwarp();
