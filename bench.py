@@ -634,7 +634,8 @@ def run_train(a):
                    'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}',
                    'last_mean_loss': float(loss_host[0])},
         'e2e': {'value': e2e_value, 'unit': TRAIN_UNIT, 'h2d_bytes_per_step': TRAIN_ROWS * (T + 1) * 8,
-                'd2h_bytes_per_step': 4},
+                'd2h_bytes_per_step': 4, 'ms_per_step': ms_e2e / a.steps,
+                'copy_and_host_wait_ms_per_step': (ms_e2e - ms) / a.steps},
         'gpu_launches': launches,
     }
     line.update(kernel_roofline(prof, min(tr.pop.chunk, TRAIN_FORWARDS // world), clk, ms, per_rank_forwards))
