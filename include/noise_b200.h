@@ -435,6 +435,25 @@ int noise_query_response(const float* dq, const noise_view3_t* keys, const noise
                          const noise_view3_t* probabilities, const noise_view3_t* base, int tokens, int probes,
                          int heads, int keys_len, float* out, void* stream);
 
+/* The library's own fp32 e^x - 1 (the one the tcgen05 query_response evaluates: Cody-Waite reduction by ln2, degree-8
+ * Taylor polynomial, no MUFU) over n device values; a numerics check against CUDA's expm1f. */
+int noise_expm1_f32(const float* x, float* out, int64_t n, void* stream);
+
+/* Bytes of the caller's workspace for noise_query_response_ws: a 256-byte status block, the keys and the transposed
+ * values as tf32 hi / lo planes (fp32 [heads, Tp, 64] each, Tp = keys_len rounded up to 64) and one live flag per
+ * (head, token, 64-key tile). 0 for any argument < 1. */
+size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, int keys_len);
+
+/* noise_query_response on tcgen05 with a caller workspace (256-byte aligned, noise_query_response_workspace_bytes
+ * large; dq and out 16-byte aligned): both dots at the reference kernel's tf32x3 precision (run.py:1808,1813), one
+ * CTA per 128 (token, probe) rows of a head, S and change V as kind::tf32 MMAs with the change in tensor memory.
+ * keys_len > 32,768 falls through to noise_query_response. Same result definition. The workspace's first int32 is
+ * the device status after the call completes: 0, or 1 if a pipeline wait gave up (the output is then incomplete). */
+int noise_query_response_ws(const float* dq, const noise_view3_t* keys, const noise_view3_t* values,
+                            const noise_view3_t* probabilities, const noise_view3_t* base, int tokens, int probes,
+                            int heads, int keys_len, float* out, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* noise_record::routed_response (run.py:604-619, kernel :548-569): out[m, p, h] = bf16(w V) + (e^-dlse - 1) rest,
  * w = bf16(p_k (e^(ds - dlse) - 1)), ds = bf16(dq . k) / 8, dlse = log1p(sum_k p_k (e^ds - 1)). dq bf16
  * [M, P, H, 64], keys, values bf16 [M, H, K, 64], probabilities fp32 [M, H, K], rest fp32 [M, H, 64], all

@@ -102,21 +102,6 @@ __global__ void __launch_bounds__(256) keymom_features_kernel(const float* __res
 __device__ __forceinline__ void km_st_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
-// Named barrier 1 over the NT weight / epilogue threads of the calling kernel, returning the AND of their
-// predicates (a warp whose bounded wait gave up still arrives, with false, so every warp leaves together).
-template <int NT>
-__device__ __forceinline__ bool km_bar_and(bool pred) {
-  static_assert(NT % 32 == 0, "whole warps");
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
-      "bar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "n"(NT)
-      : "memory");
-  return r != 0;
-}
-
 struct KeyMomMaps {
   CUtensorMap k, v;                // [rows * T, 64]: bf16 128 x 64 boxes (IDENT) or fp32 128 x 32 boxes (SCAN)
   CUtensorMap q, h;                // [rows * T, 64]: bf16 32 x 64 boxes or fp32 32 x 32 boxes
@@ -433,7 +418,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       sums[(half * 3) * 128 + r] = s1p.x + s1p.y;
       sums[(half * 3 + 1) * 128 + r] = s2p.x + s2p.y;
       sums[(half * 3 + 2) * 128 + r] = rsq;
-      if (!km_bar_and<KM_THREADS - 64>(ok)) {
+      if (!bar_and<KM_THREADS - 64>(ok)) {
         ok = false;
         break;
       }
@@ -516,7 +501,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       if (!values || !got) {
-        if (!km_bar_and<KM_THREADS - 64>(got)) {  // both halves have read sums before the next item overwrites them
+        if (!bar_and<KM_THREADS - 64>(got)) {  // both halves have read sums before the next item overwrites them
           ok = false;
           break;
         }
@@ -535,7 +520,7 @@ __global__ void __launch_bounds__(KM_THREADS, 1)
         for (int q = 0; q < 8; ++q)
           dst[q] = make_float4(va[4 * q], va[4 * q + 1], va[4 * q + 2], va[4 * q + 3]);
       }
-      if (!km_bar_and<KM_THREADS - 64>(true)) {  // both halves have read sums before the next item overwrites them
+      if (!bar_and<KM_THREADS - 64>(true)) {  // both halves have read sums before the next item overwrites them
         ok = false;
         break;
       }

@@ -116,6 +116,21 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Named barrier 1 over the NT consumer (weight / epilogue) threads of the calling kernel, returning the AND of their
+// predicates (a warp whose bounded wait gave up still arrives, with false, so every warp leaves together).
+template <int NT>
+__device__ __forceinline__ bool bar_and(bool pred) {
+  static_assert(NT % 32 == 0, "whole warps");
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(NT)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), no multicast
 // ---------------------------------------------------------------------------------------------------------------
@@ -179,6 +194,17 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// kind::tf32 with A read from tensor memory: one fp32 element per 32-bit column (K = 8 per instruction: 8
+// columns), K-major.
+__device__ __forceinline__ void tc_mma_ts_tf32(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -291,6 +317,44 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 __device__ __forceinline__ float bf16_round_alu(float x) {
   const uint32_t u = __float_as_uint(x);
   return __uint_as_float((u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u);
+}
+
+// The tf32 part of x, rounded to nearest on the 13 dropped mantissa bits (ties away from zero): exactly
+// representable in tf32, |x - tf32_hi(x)| <= 2^-11 |x| and exact in fp32, so a tf32x3 product a b ~ a_hi b_hi +
+// a_hi b_lo + a_lo b_hi misses only a_lo b_lo and the tf32 part of the lo terms: about 2^-22 of |a b|. Finite x.
+__device__ __forceinline__ float tf32_hi(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+
+// e^x - 1 for two fp32 values on the FMA / ALU pipes (no MUFU), with the relative accuracy near 0 that e^x - 1
+// loses: Cody-Waite reduction x = k ln2 + r, |r| <= ln2 / 2 (ln2 split into a 17-bit head and its tail, so k ln2_hi
+// is exact), the Taylor polynomial of e^r - 1 to degree 8 (truncation below 2e-10 of |r|), and e^x - 1 =
+// 2^k (e^r - 1) + (2^k - 1), with 2^128 applied as 2^127 * 2. x is clamped below at -87 (e^x - 1 is -1 to fp32
+// precision below -17); x above ln(FLT_MAX) gives +inf, as e^x - 1 overflows there, and NaN stays NaN.
+__device__ __forceinline__ float2 expm1_f2(float2 x) {
+  constexpr float L2E = 1.4426950408889634f, LN2_HI = 0.693145751953125f, LN2_LO = 1.4286068203094172e-06f;
+  constexpr float MAGIC = 12582912.f;        // 1.5 * 2^23: t = x / ln2 + MAGIC holds round(x / ln2) in its low bits
+  constexpr float XMAX = 88.72283172607422f;  // the largest fp32 with e^x finite
+  const float2 xc = make_float2(fminf(fmaxf(x.x, -87.f), XMAX), fminf(fmaxf(x.y, -87.f), XMAX));
+  const float2 t = __ffma2_rn(xc, make_float2(L2E, L2E), make_float2(MAGIC, MAGIC));
+  const float2 k = __fadd2_rn(t, make_float2(-MAGIC, -MAGIC));
+  float2 r = __ffma2_rn(k, make_float2(-LN2_HI, -LN2_HI), xc);
+  r = __ffma2_rn(k, make_float2(-LN2_LO, -LN2_LO), r);
+  float2 q = __ffma2_rn(r, make_float2(1.f / 40320.f, 1.f / 40320.f), make_float2(1.f / 5040.f, 1.f / 5040.f));
+  q = __ffma2_rn(q, r, make_float2(1.f / 720.f, 1.f / 720.f));
+  q = __ffma2_rn(q, r, make_float2(1.f / 120.f, 1.f / 120.f));
+  q = __ffma2_rn(q, r, make_float2(1.f / 24.f, 1.f / 24.f));
+  q = __ffma2_rn(q, r, make_float2(1.f / 6.f, 1.f / 6.f));
+  q = __ffma2_rn(q, r, make_float2(0.5f, 0.5f));
+  const float2 p = __ffma2_rn(__fmul2_rn(r, r), q, r);  // e^r - 1
+  const int kx = __float_as_int(t.x) - __float_as_int(MAGIC), ky = __float_as_int(t.y) - __float_as_int(MAGIC);
+  const float2 s = make_float2(__int_as_float((min(kx, 127) + 127) << 23), __int_as_float((min(ky, 127) + 127) << 23));
+  float2 e = __ffma2_rn(s, p, __fadd2_rn(s, make_float2(-1.f, -1.f)));
+  if (kx > 127) e.x *= 2.f;  // k = 128 (x within ln2 / 2 of the overflow): 2^k (e^r - 1) + 2^k - 1 ~ 2 (2^127 e^r)
+  if (ky > 127) e.y *= 2.f;
+  if (!(x.x <= XMAX)) e.x = x.x > 0.f ? __int_as_float(0x7F800000) : x.x;  // overflow to +inf; NaN stays NaN
+  if (!(x.y <= XMAX)) e.y = x.y > 0.f ? __int_as_float(0x7F800000) : x.y;
+  return e;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {

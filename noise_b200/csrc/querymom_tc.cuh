@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
       sums[(half * 4 + 1) * 128 + r] = s2n.x + s2n.y;
       sums[(half * 4 + 2) * 128 + r] = s1d.x + s1d.y;
       sums[(half * 4 + 3) * 128 + r] = s2d.x + s2d.y;
-      if (!km_bar_and<QM_THREADS - 64>(ok)) {
+      if (!bar_and<QM_THREADS - 64>(ok)) {
         ok = false;
         break;
       }
@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1)
         }
       }
       // both halves have read sums before the next item overwrites them
-      if (!km_bar_and<QM_THREADS - 64>(got)) {
+      if (!bar_and<QM_THREADS - 64>(got)) {
         ok = false;
         break;
       }

@@ -15,10 +15,14 @@
 //                  ds = bf16(dq . k) / 8, dlse = log1p(sum_k p (e^ds - 1)) over the routed keys.
 // Each keeps its per-column (or per-probe) state in registers, stages the other side's tiles in shared memory, and
 // never materialises a [receiver x column] tensor.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "noise_b200.h"
 
@@ -312,6 +316,61 @@ static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) ==
 }  // namespace readout
 }  // namespace noise
 
+#include "query_tc.cuh"
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 qt_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// fp32 [outer, inner] rows, 64-row x 32-column boxes (128 bytes), 128-byte swizzle
+int qt_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer) {
+  auto fn = qt_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 4};
+  cuuint32_t box[2] = {32, 64};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, el,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+// e^x - 1 of the library's own (expm1_f2) over n values, two per thread: the numerics check of the scorers' exponential
+__global__ void __launch_bounds__(256) expm1_check_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                                          int64_t n) {
+  for (int64_t i = 2 * (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x); i < n;
+       i += 2 * static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float2 e = noise::expm1_f2(make_float2(x[i], i + 1 < n ? x[i + 1] : 0.f));
+    out[i] = e.x;
+    if (i + 1 < n) out[i + 1] = e.y;
+  }
+}
+
+// workspace: 256-byte status block, keys hi / lo and values^T hi / lo (fp32, H * Tp * 64 each), live flags
+struct QtWorkspace {
+  int64_t nt, tp, plane, live_bytes;
+  QtWorkspace(int tokens, int heads, int keys_len)
+      : nt((keys_len + noise::readout::QT_KEYS - 1) / noise::readout::QT_KEYS), tp(nt * noise::readout::QT_KEYS),
+        plane(static_cast<int64_t>(heads) * tp * noise::readout::D * 4),
+        live_bytes((static_cast<int64_t>(heads) * tokens * nt + 255) / 256 * 256) {}
+  size_t bytes() const { return static_cast<size_t>(256 + 4 * plane + live_bytes); }
+};
+
+}  // namespace
+
 using namespace noise::readout;
 
 extern "C" {
@@ -356,6 +415,65 @@ int noise_query_response(const float* dq, const noise_view3_t* keys, const noise
   dim3 grid((probes + QP - 1) / QP, tokens * heads);
   query_response_kernel<<<grid, 256, QUERY_SMEM, static_cast<cudaStream_t>(stream)>>>(
       dq, view(*keys), view(*values), view(*probabilities), view(*base), tokens, probes, heads, keys_len, out);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_expm1_f32(const float* x, float* out, int64_t n, void* stream) {
+  if (!x || !out) return NOISE_ERR_ARGUMENT;
+  if (n < 0) return NOISE_ERR_SHAPE;
+  if (n == 0) return NOISE_OK;
+  const int64_t blocks = std::min<int64_t>((n + 511) / 512, 4096);
+  expm1_check_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, n);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, int keys_len) {
+  if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1) return 0;
+  return QtWorkspace(tokens, heads, keys_len).bytes();
+}
+
+int noise_query_response_ws(const float* dq, const noise_view3_t* keys, const noise_view3_t* values,
+                            const noise_view3_t* probabilities, const noise_view3_t* base, int tokens, int probes,
+                            int heads, int keys_len, float* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (!dq || !keys || !values || !probabilities || !base || !out || !keys->data || !values->data ||
+      !probabilities->data || !base->data)
+    return NOISE_ERR_ARGUMENT;
+  if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1) return NOISE_ERR_SHAPE;
+  if (keys_len > QT_MAX_TILES * QT_KEYS)  // longer than the live-tile list holds: the CUDA-core kernel
+    return noise_query_response(dq, keys, values, probabilities, base, tokens, probes, heads, keys_len, out, stream);
+  const QtWorkspace w(tokens, heads, keys_len);
+  if (!workspace || workspace_bytes < w.bytes()) return NOISE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !a16(dq) || !a16(out)) return NOISE_ERR_ALIGN;
+  const int64_t rows = static_cast<int64_t>(tokens) * probes;
+  const int64_t items = (rows + QT_ROWS - 1) / QT_ROWS * heads;
+  if (items > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  float* khi = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  float* klo = khi + w.plane / 4;
+  float* vhi = klo + w.plane / 4;
+  float* vlo = vhi + w.plane / 4;
+  uint8_t* live = reinterpret_cast<uint8_t*>(vlo + w.plane / 4);
+  QtMaps maps;
+  int rc;
+  const uint64_t krows = static_cast<uint64_t>(heads) * w.tp, vrows = static_cast<uint64_t>(heads) * D;
+  if ((rc = qt_map(&maps.khi, khi, D, krows)) || (rc = qt_map(&maps.klo, klo, D, krows)) ||
+      (rc = qt_map(&maps.vhi, vhi, w.tp, vrows)) || (rc = qt_map(&maps.vlo, vlo, w.tp, vrows)))
+    return rc;
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  qr_split_kernel<<<dim3(static_cast<unsigned>(w.nt), heads), 256, 0, s>>>(view(*keys), view(*values), keys_len,
+                                                                           static_cast<int>(w.tp), khi, klo, vhi, vlo);
+  const int64_t warps = static_cast<int64_t>(heads) * tokens * w.nt;
+  qr_live_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(
+      view(*probabilities), heads, tokens, keys_len, static_cast<int>(w.nt), live);
+  if (cudaFuncSetAttribute(query_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, QT_SMEM))
+    return NOISE_ERR_CUDA;
+  const noise_view3_t& pv = *probabilities;
+  const int vec = pv.stride2 == 1 && pv.stride1 % 4 == 0 && pv.stride0 % 4 == 0 && a16(pv.data);
+  QtArgs a{dq, view(pv), view(*base), live, out, tokens, probes, heads, keys_len, static_cast<int>(w.nt),
+           static_cast<int>(w.tp), vec, status};
+  query_tc_kernel<<<static_cast<unsigned>(items), QT_THREADS, QT_SMEM, s>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

@@ -10,7 +10,8 @@ Same names, arguments and results as the reference's custom ops:
 Each is also registered as a ``torch.library.custom_op`` (namespace ``noise_b200``) with a fake. ``install(R)``
 registers these implementations as the CUDA kernels of the record module's own ops, the seam the reference's
 ``fast_kernels.install`` uses (``op.register_kernel('cuda', impl)``, run.py:3440-3453), so R's callers run them
-unchanged. head_dim 64; fp32 arithmetic (the reference's tf32x3 dots are fp32-accurate).
+unchanged. head_dim 64. query_response runs its two dots on tcgen05 at the reference's tf32x3 precision; the others
+use fp32 CUDA-core arithmetic (at least as accurate as tf32x3).
 """
 import ctypes
 
@@ -73,7 +74,9 @@ def key_response_impl(q, dk, A, C, source_start, query_start, window):
     return out
 
 
-def query_response_impl(dq, keys, values, probabilities, base):
+def query_response_impl(dq, keys, values, probabilities, base, tc=True):
+    """tc=True: the tcgen05 kernel at the reference's tf32x3 precision (its workspace, whose first int is the device
+    status, rides on the output as ``_noise_workspace``); tc=False: the fp32 CUDA-core kernel, for comparison."""
     m, p, h, d = dq.shape
     if d != HD:
         raise ValueError('head_dim 64 only')
@@ -82,9 +85,17 @@ def query_response_impl(dq, keys, values, probabilities, base):
     (kv, keys), (vv, values), (pv, probabilities), (bv, base) = (_view(z) for z in (keys, values, probabilities,
                                                                                    base))
     out = torch.empty((m, p, h, d), device=dq.device, dtype=torch.float32)
-    _check(_lib.lib().noise_query_response(dq.data_ptr(), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(pv),
-                                           ctypes.byref(bv), m, p, h, keys.shape[1], out.data_ptr(), _stream(dq)),
-           'noise_query_response')
+    L, t = _lib.lib(), keys.shape[1]
+    if not tc:
+        _check(L.noise_query_response(dq.data_ptr(), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(pv),
+                                      ctypes.byref(bv), m, p, h, t, out.data_ptr(), _stream(dq)), 'noise_query_response')
+        return out
+    nbytes = L.noise_query_response_workspace_bytes(m, p, h, t)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dq.device)
+    _check(L.noise_query_response_ws(dq.data_ptr(), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(pv),
+                                     ctypes.byref(bv), m, p, h, t, out.data_ptr(), ws.data_ptr(), nbytes, _stream(dq)),
+           'noise_query_response_ws')
+    out._noise_workspace = ws
     return out
 
 

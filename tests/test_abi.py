@@ -120,6 +120,16 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_future_scores(r, r, fake + 4, fake, r, r, 2, 64, 2, 2, 0, 8, fake, None) == 2  # dk alignment
     assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
+    qn = L.noise_query_response_workspace_bytes(256, 64, 8, 2048)
+    assert qn == 256 + 4 * 8 * 2048 * 64 * 4 + 8 * 256 * 32                                   # planes + live flags
+    assert L.noise_query_response_workspace_bytes(3, 5, 2, 100) == 256 + 4 * 2 * 128 * 64 * 4 + 256  # keys to 128
+    assert L.noise_query_response_workspace_bytes(0, 64, 8, 2048) == 0
+    assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 8, 2048, fake, fake, qn - 1, None) == 3  # workspace
+    assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 8, 2048, fake, fake + 16, qn, None) == 2  # alignment
+    assert L.noise_query_response_ws(fake + 4, r, r, r, r, 256, 64, 8, 2048, fake, fake, qn, None) == 2  # dq alignment
+    assert L.noise_query_response_ws(fake, None, r, r, r, 256, 64, 8, 2048, fake, fake, qn, None) == 4
+    assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 0, 2048, fake, fake, qn, None) == 1     # no heads
+    assert L.noise_expm1_f32(None, fake, 4, None) == 4
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
     # Dust block rerun
     jit = _lib.Jitter()

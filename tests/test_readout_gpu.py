@@ -83,6 +83,110 @@ def test_query_response_larger():
     assert _rel(_query(_dev(q)), ref) < REL
 
 
+def _query_case(m, p, h, t, window, seed, dead=None):
+    """query_response inputs with token positions spread over the keys (sorted, as a row block's tokens are adjacent),
+    a strided (T, H, 64) keys buffer seen as [H, T, 64], and optionally a band of keys with zero probability."""
+    g = torch.Generator().manual_seed(seed)
+    dq = torch.randn(m, p, h, 64, generator=g) * 0.3
+    keys = torch.randn(t, h, 64, generator=g).permute(1, 0, 2)
+    values = torch.randn(h, t, 64, generator=g)
+    pos = torch.sort(torch.randint(0, t, (m,), generator=g)).values
+    lag = pos[:, None] - torch.arange(t)[None]
+    prob = torch.rand(h, m, t, generator=g) * ((lag >= 0) & (lag <= window))
+    if dead is not None:
+        prob[..., dead[0]:dead[1]] = 0
+    prob = prob / prob.sum(-1, keepdim=True).clamp_min(1e-6)
+    base = torch.randn(h, m, 64, generator=g)
+    return dict(dq=dq, keys=keys, values=values, probabilities=prob, base=base)
+
+
+def _query_tc(q, tc=True):
+    from noise_b200 import readout
+    return readout.query_response_impl(q['dq'], q['keys'], q['values'], q['probabilities'], q['base'], tc=tc)
+
+
+def _query_status(out):
+    from noise_b200 import _lib
+    return _lib.read_status(out._noise_workspace)
+
+
+@pytest.mark.parametrize('m,p,t,dead', [(5, 72, 1000, None), (3, 128, 64, None), (9, 16, 333, (100, 230)),
+                                        (2, 200, 700, (64, 300))])
+def test_query_response_tc_shapes(m, p, t, dead):
+    """The tcgen05 kernel's 128-row blocks spanning 1 to 9 tokens (or part of one), key counts off the 64-key tile,
+    live tiles with dead ones between them, and a strided keys view, against the fp64 oracle."""
+    q = _query_case(m, p, 3, t, t // 2, seed=31 + m, dead=dead)
+    ref = oracle.query_response(q['dq'], q['keys'], q['values'], q['probabilities'], q['base'])
+    assert ref.abs().max() > 0
+    out = _query_tc(_dev(q))
+    assert _query_status(out) == 0
+    assert _rel(out, ref) < REL
+
+
+def test_query_response_tc_skips_dead_tiles_exactly():
+    """A token whose probabilities are all zero gets exactly 0, even where e^(dq . k / 8) overflows (the reference
+    skips its tiles; the dense form would give 0 * inf = nan), while the other token of its 128-row block is live."""
+    q = _query_case(2, 64, 2, 256, 200, seed=5)
+    q['probabilities'][:, 0] = 0
+    q['dq'][0] *= 2000.0
+    out = _query_tc(_dev(q)).cpu()
+    assert torch.equal(out[0], torch.zeros_like(out[0]))
+    ref = oracle.query_response(q['dq'][1:], q['keys'], q['values'], q['probabilities'][:, 1:], q['base'][:, 1:])
+    assert _rel(out[1:], ref) < REL
+    zero = dict(q, probabilities=torch.zeros_like(q['probabilities']))
+    assert torch.equal(_query_tc(_dev(zero)).cpu(), torch.zeros(2, 64, 2, 64))
+
+
+def test_query_response_tc_bench_shape():
+    """The bench's shape (256 tokens x 64 probes x 8 heads over 2,048 keys, window 1,024; 1,024 CTAs, several waves):
+    the tcgen05 kernel against the fp32 CUDA-core kernel over the whole output, and against the fp64 oracle on a sample
+    of tokens. The probabilities are normalised per token, as attention's are: with unnormalised ones some tokens'
+    1 + partition comes near zero and amplifies any rounding difference."""
+    g = torch.Generator().manual_seed(9)
+    mq, pq, h, t = 256, 64, 8, 2048
+    dq, keys, vals = torch.randn(mq, pq, h, 64, generator=g) * 0.3, torch.randn(h, t, 64, generator=g), \
+        torch.randn(h, t, 64, generator=g)
+    pos = torch.arange(mq) * (t // mq) + t // mq - 1
+    lag = pos[:, None] - torch.arange(t)[None]
+    prob = torch.rand(h, mq, t, generator=g) * ((lag >= 0) & (lag <= 1024))
+    prob = (prob / prob.sum(-1, keepdim=True)).contiguous()
+    base = torch.randn(h, mq, 64, generator=g)
+    q = dict(dq=dq, keys=keys, values=vals, probabilities=prob, base=base)
+    qd = _dev(q)
+    out = _query_tc(qd)
+    assert _query_status(out) == 0
+    assert _rel(out, _query_tc(qd, tc=False)) < REL
+    pick = torch.tensor([0, 1, 127, 200, 255])
+    ref = oracle.query_response(dq[pick], keys, vals, prob[:, pick], base[:, pick])
+    assert _rel(out[pick.to(DEV)], ref) < REL
+
+
+def test_expm1_against_fp64_and_cuda():
+    """The scorers' own e^x - 1 (noise_expm1_f32: Cody-Waite reduction, degree-8 Taylor polynomial) over [-87,
+    ln(FLT_MAX)] and tiny arguments of both signs: within 3.5e-7 relative of fp64 (about 3 ulp; CUDA's expm1f,
+    torch.expm1 on the device, is held to the same bound here), +inf past the overflow, -1 far below, NaN kept."""
+    from noise_b200 import _lib
+
+    def run(xs):
+        x = xs.float().to(DEV)
+        out = torch.empty_like(x)
+        _lib.check(_lib.lib().noise_expm1_f32(x.data_ptr(), out.data_ptr(), x.numel(), _lib.stream_handle(DEV)),
+                   'noise_expm1_f32')
+        return x, out
+
+    tiny = torch.logspace(-30, 0, 300_001)
+    xs = torch.cat([torch.linspace(-87, 88.7228, 4_000_001), tiny, -tiny, torch.tensor([0.0, 88.72283172607422])])
+    x, out = run(xs)
+    ref = torch.expm1(x.double().cpu())
+    scale = ref.abs().clamp_min(1e-300)
+    assert ((out.double().cpu() - ref).abs() / scale).max() < 3.5e-7
+    assert ((torch.expm1(x).double().cpu() - ref).abs() / scale).max() < 3.5e-7
+    assert torch.isfinite(out).all()
+    _, sp = run(torch.tensor([88.72284, 100.0, float('inf'), -100.0, float('-inf'), float('nan')]))
+    sp = sp.cpu()
+    assert sp[:3].tolist() == [float('inf')] * 3 and sp[3:5].tolist() == [-1.0, -1.0] and sp[5].isnan()
+
+
 @pytest.mark.parametrize('k', [16, 100, 256])
 def test_routed_response_sizes(k):
     r = routed_inputs(m=6, p=70, h=8, k=k, seed=11)
