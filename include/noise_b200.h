@@ -462,6 +462,15 @@ int noise_routed_response(const void* dq, const void* keys, const void* values, 
                           const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
                           void* stream);
 
+/* noise_routed_response on tcgen05 with a workspace of at least NOISE_STATUS_BYTES (256-byte aligned; its first int32
+ * is the device status after the call: 0, or 1 if a pipeline wait gave up and the output is incomplete); out 16-byte
+ * aligned; keys_len <= 256. Both dots are kind::f16 MMAs (fp32 accumulation, outputs rounded to bf16 as the
+ * reference kernel's tl.dot outputs are, run.py:561,565): two (token, head) items share the 128 MMA rows when
+ * keys_len padded to 32 is at most 128, their weights block-diagonal in tensor memory. Same result definition. */
+int noise_routed_response_ws(const void* dq, const void* keys, const void* values, const float* probabilities,
+                             const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* The true-path readout's scorer (reference train/val/run.py, `readout` section :5900-6040): width 512, 8 heads of
  * 64. Moment tables of one block, per (global token, head): U, W fp32 [T, 8, 64]; M1, M2 bf16 [T, 8, 64, 64] (16-byte
  * aligned); QD, GD fp32 [T, 8, 64]; AD, CD fp32 [T, 8]; VT, OT fp32 [T, 8, 64] (the self-edge only). */

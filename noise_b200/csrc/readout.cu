@@ -317,6 +317,7 @@ static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) ==
 }  // namespace noise
 
 #include "query_tc.cuh"
+#include "routed_tc.cuh"
 
 namespace {
 
@@ -343,6 +344,23 @@ int qt_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer) 
   cuuint32_t box[2] = {32, 64};
   cuuint32_t el[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, el,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+// bf16 rows of 64 (128 bytes): a 2-D [outer, 64] map with 64 x box_rows boxes, or (heads > 0) the 3-D (64, heads,
+// outer) view of a [outer, heads, 64] buffer with 64 x 1 x box_rows boxes; 128-byte swizzle
+int rt_map(CUtensorMap* map, const void* base, uint64_t outer, int heads, uint32_t box_rows) {
+  auto fn = qt_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  const uint32_t rank = heads > 0 ? 3 : 2;
+  cuuint64_t dims[3] = {64, heads > 0 ? static_cast<cuuint64_t>(heads) : outer, outer};
+  cuuint64_t strides[2] = {128, heads > 0 ? static_cast<cuuint64_t>(heads) * 128 : 0};
+  cuuint32_t box[3] = {64, heads > 0 ? 1u : box_rows, box_rows};
+  cuuint32_t el[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, el,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
@@ -424,6 +442,48 @@ int noise_expm1_f32(const float* x, float* out, int64_t n, void* stream) {
   if (n == 0) return NOISE_OK;
   const int64_t blocks = std::min<int64_t>((n + 511) / 512, 4096);
   expm1_check_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, n);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_routed_response_ws(const void* dq, const void* keys, const void* values, const float* probabilities,
+                             const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (!dq || !keys || !values || !probabilities || !rest || !out) return NOISE_ERR_ARGUMENT;
+  if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1 || keys_len > RK) return NOISE_ERR_SHAPE;
+  if (!workspace || workspace_bytes < NOISE_STATUS_BYTES) return NOISE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !a16(out)) return NOISE_ERR_ALIGN;
+  RtArgs a{};
+  a.prob = probabilities;
+  a.rest = rest;
+  a.out = out;
+  a.M = tokens;
+  a.P = probes;
+  a.H = heads;
+  a.K = keys_len;
+  a.Kp = (keys_len + 31) / 32 * 32;
+  a.G = 2 * a.Kp <= 256 ? 2 : 1;
+  a.PB = (probes + 63) / 64;
+  const int64_t items = static_cast<int64_t>(tokens) * heads * a.PB;
+  if (items > 0x7FFFFFFF - 1) return NOISE_ERR_SHAPE;
+  a.items = static_cast<int>(items);
+  a.tiles = (a.items + a.G - 1) / a.G;
+  a.status = static_cast<int*>(workspace);
+  RtMaps maps;
+  int rc;
+  const uint64_t kv_rows = static_cast<uint64_t>(tokens) * heads * keys_len;
+  if ((rc = rt_map(&maps.q, dq, static_cast<uint64_t>(tokens) * probes, heads, 64)) ||
+      (rc = rt_map(&maps.kv, keys, kv_rows, 0, static_cast<uint32_t>(a.Kp))) ||
+      (rc = rt_map(&maps.v, values, kv_rows, 0, static_cast<uint32_t>(a.Kp))))
+    return rc;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return NOISE_ERR_CUDA;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(a.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  if (cudaFuncSetAttribute(routed_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM))
+    return NOISE_ERR_CUDA;
+  routed_tc_kernel<<<std::min(a.tiles, sms), RT_THREADS, RT_SMEM, s>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

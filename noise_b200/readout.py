@@ -10,8 +10,9 @@ Same names, arguments and results as the reference's custom ops:
 Each is also registered as a ``torch.library.custom_op`` (namespace ``noise_b200``) with a fake. ``install(R)``
 registers these implementations as the CUDA kernels of the record module's own ops, the seam the reference's
 ``fast_kernels.install`` uses (``op.register_kernel('cuda', impl)``, run.py:3440-3453), so R's callers run them
-unchanged. head_dim 64. query_response runs its two dots on tcgen05 at the reference's tf32x3 precision; the others
-use fp32 CUDA-core arithmetic (at least as accurate as tf32x3).
+unchanged. head_dim 64. query_response runs its two dots on tcgen05 at the reference's tf32x3 precision and
+routed_response its bf16 dots as kind::f16 MMAs; future_scores and key_response use fp32 CUDA-core arithmetic (at
+least as accurate as tf32x3).
 """
 import ctypes
 
@@ -99,7 +100,9 @@ def query_response_impl(dq, keys, values, probabilities, base, tc=True):
     return out
 
 
-def routed_response_impl(dq, keys, values, probabilities, rest):
+def routed_response_impl(dq, keys, values, probabilities, rest, tc=True):
+    """tc=True: the tcgen05 kernel (its status workspace rides on the output as ``_noise_workspace``); tc=False:
+    the CUDA-core kernel, for comparison."""
     m, probes, heads, width = dq.shape
     if width != HD:
         raise ValueError('head_dim 64 only')
@@ -108,9 +111,15 @@ def routed_response_impl(dq, keys, values, probabilities, rest):
     dq, keys, values = (z.detach().to(torch.bfloat16).contiguous() for z in (dq, keys, values))
     probabilities, rest = _f32c(probabilities), _f32c(rest)
     out = torch.empty((m, probes, heads, width), device=dq.device, dtype=torch.float32)
-    _check(_lib.lib().noise_routed_response(dq.data_ptr(), keys.data_ptr(), values.data_ptr(),
-                                            probabilities.data_ptr(), rest.data_ptr(), m, probes, heads, count,
-                                            out.data_ptr(), _stream(dq)), 'noise_routed_response')
+    args = (dq.data_ptr(), keys.data_ptr(), values.data_ptr(), probabilities.data_ptr(), rest.data_ptr(), m, probes,
+            heads, count, out.data_ptr())
+    if not tc:
+        _check(_lib.lib().noise_routed_response(*args, _stream(dq)), 'noise_routed_response')
+        return out
+    ws = torch.empty(_lib.STATUS_BYTES, dtype=torch.uint8, device=dq.device)
+    _check(_lib.lib().noise_routed_response_ws(*args, ws.data_ptr(), _lib.STATUS_BYTES, _stream(dq)),
+           'noise_routed_response_ws')
+    out._noise_workspace = ws
     return out
 
 

@@ -131,6 +131,10 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 0, 2048, fake, fake, qn, None) == 1     # no heads
     assert L.noise_expm1_f32(None, fake, 4, None) == 4
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
+    assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, fake, 256, None) == 1  # K
+    assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 64, fake, fake, 16, None) == 3   # ws
+    assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 64, fake + 4, fake, 256, None) == 2
+    assert L.noise_routed_response_ws(None, fake, fake, fake, fake, 2, 2, 2, 64, fake, fake, 256, None) == 4
     # Dust block rerun
     jit = _lib.Jitter()
     assert L.noise_block_forward(ctypes.byref(gpt), 0, fake, None, ctypes.byref(jit), 2, 256, 128, fake, 1 << 30,

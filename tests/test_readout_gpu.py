@@ -187,6 +187,22 @@ def test_expm1_against_fp64_and_cuda():
     assert sp[:3].tolist() == [float('inf')] * 3 and sp[3:5].tolist() == [-1.0, -1.0] and sp[5].isnan()
 
 
+@pytest.mark.parametrize('m,p,k', [(6, 70, 16), (5, 40, 100), (3, 64, 128), (4, 130, 129), (3, 20, 256), (1, 64, 32)])
+def test_routed_response_tc(m, p, k):
+    """The tcgen05 kernel: two items per 128-row tile (keys padded to 32 at most 128) or one (129..256 keys), an odd
+    item count (the last tile's second slot repeats a real item), probe blocks of 64 with a partial last block,
+    against the bf16-rounding oracle and the CUDA-core kernel."""
+    from noise_b200 import _lib, readout
+    r = routed_inputs(m=m, p=p, h=3, k=k, seed=13 + k)
+    ref = oracle.routed_response(r['dq'], r['keys'], r['values'], r['probabilities'], r['rest'])
+    d = _dev(r)
+    out = readout.routed_response_impl(d['dq'], d['keys'], d['values'], d['probabilities'], d['rest'], tc=True)
+    assert _lib.read_status(out._noise_workspace) == 0
+    assert _routed_ok(out, ref)
+    cc = readout.routed_response_impl(d['dq'], d['keys'], d['values'], d['probabilities'], d['rest'], tc=False)
+    assert _routed_ok(out, cc)
+
+
 @pytest.mark.parametrize('k', [16, 100, 256])
 def test_routed_response_sizes(k):
     r = routed_inputs(m=6, p=70, h=8, k=k, seed=11)
