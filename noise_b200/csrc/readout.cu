@@ -481,9 +481,9 @@ int noise_routed_response_ws(const void* dq, const void* keys, const void* value
     return NOISE_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(a.status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
-  if (cudaFuncSetAttribute(routed_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM))
-    return NOISE_ERR_CUDA;
-  routed_tc_kernel<<<std::min(a.tiles, sms), RT_THREADS, RT_SMEM, s>>>(maps, a);
+  const auto kernel = a.Kp <= 128 ? routed_tc_kernel<1> : routed_tc_kernel<2>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM)) return NOISE_ERR_CUDA;
+  kernel<<<std::min(a.tiles, sms), RT_THREADS, RT_SMEM, s>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

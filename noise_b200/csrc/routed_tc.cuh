@@ -14,11 +14,13 @@
 // Persistent CTAs (one per SM), 576 threads:
 //   warp 0      TMA: per tile the G items' probe rows (a 3-D map over dq's (row, head, dim)), keys and values into
 //               one of 2 stages (80 KB each);
-//   warp 1      TMEM (512 columns: S 256, W 128, O 64) and the MMAs: S (4 per tile), then, once the epilogue has
-//               written W, O (G Kp / 16);
-//   warps 2..17 warp w: rows of TMEM lane quarter w % 4, 32-key pieces (w - 2) / 4 and + 4 of its item: e^ds - 1
-//               sums, dlse (the 4 warps of a row exchange partial sums in shared memory), W into TMEM, then
-//               dims 16 ((w - 2) / 4) .. + 15 of O and the output.
+//   warp 1      TMEM (512 columns: S 256, W 128, O 64) and the MMAs: S of tile t + 1 (4) as soon as the epilogue
+//               has read S(t), then O(t) (G Kp / 16) once it has written W(t);
+//   warps 2..17 warp w: rows of TMEM lane quarter w % 4, 32-key pieces (w - 2) / 4 and + 4 of its item. First pass:
+//               e = e^ds - 1 (kept in registers) and its p-weighted sum; the 4 warps of a row exchange partial sums
+//               in shared memory for sigma; second pass: W = bf16(p (e - sigma) / (1 + sigma)) into TMEM; then
+//               dims 16 ((w - 2) / 4) .. + 15 of O and the output. The first pass of tile t + 1 runs before O(t) is
+//               read, so the O MMAs overlap it. The probabilities are staged in shared memory two tiles ahead.
 #pragma once
 #include "ptx.cuh"
 
@@ -30,7 +32,8 @@ constexpr int RT_Q = 64 * 128;             // one item's 64 probe rows, 128 byte
 constexpr int RT_KV = 256 * 128;           // keys (or values) of a tile: G Kp <= 256 rows
 constexpr int RT_STAGE = 2 * RT_Q + 2 * RT_KV;  // Q0, Q1, K, V
 constexpr int RT_SUMS = 2 * RT_STAGE;      // [2 tiles][4 pieces][128 rows] fp32
-constexpr int RT_BAR = RT_SUMS + 2 * 4 * 128 * 4;
+constexpr int RT_PROB = RT_SUMS + 2 * 4 * 128 * 4;  // [3 tiles][256] fp32: a tile's probabilities, slot-major
+constexpr int RT_BAR = RT_PROB + 3 * 256 * 4;
 constexpr int RT_SMEM = RT_BAR + 256 + 1024;
 static_assert(RT_SMEM <= 227 * 1024, "shared memory per CTA");
 constexpr uint32_t RT_TS = 0, RT_TW = 256, RT_TO = 384;
@@ -49,6 +52,8 @@ struct RtMaps {
   CUtensorMap v;   // bf16 values, same
 };
 
+// NP: 32-key pieces per epilogue warp and row, ceil(Kp / 128) (1 up to 128 keys, 2 up to 256)
+template <int NP>
 __global__ void __launch_bounds__(RT_THREADS, 1)
     routed_tc_kernel(const __grid_constant__ RtMaps m, const __grid_constant__ RtArgs p) {
   extern __shared__ uint8_t smem_raw[];
@@ -61,7 +66,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
   uint64_t* o_full = bar + 6;
   uint64_t* acc_free = bar + 7;
   uint64_t* drain = bar + 8;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 9);
+  uint64_t* s_free = bar + 9;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bar + 10);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NS = p.G * p.Kp;  // S columns = O's K extent
 
@@ -75,6 +81,7 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
     mbar_init(o_full, 1);
     mbar_init(acc_free, RT_EPI);
     mbar_init(drain, 1);
+    mbar_init(s_free, RT_EPI);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -119,17 +126,12 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
   } else if (warp == 1) {
     const uint32_t id_s = idesc_bf16(128, NS);
     constexpr uint32_t id_o = idesc_bf16(128, 64, false, true);  // V as the MN-major B operand
-    int lt = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x, ++lt) {
+    // S(lt): the stage's operands have landed and the epilogue's first pass has read S(lt - 1)
+    auto scores = [&](int lt) {
       const int s = lt & 1;
-      const uint32_t par = static_cast<uint32_t>(lt) & 1u;
-      // S: the stage's operands have landed and the previous tile's epilogue has read S and O
       if (!mbar_wait_warp(&st_full[s], static_cast<uint32_t>(lt >> 1) & 1u, p.status) ||
-          !mbar_wait_warp(acc_free, par ^ 1u, p.status)) {
-        ok = false;
-        break;
-      }
+          (lt > 0 && !mbar_wait_warp(s_free, static_cast<uint32_t>(lt - 1) & 1u, p.status)))
+        return false;
       tc_fence_after();
       const uint32_t st = sbase + s * RT_STAGE;
 #pragma unroll
@@ -137,18 +139,28 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         if (elect_one())
           tc_mma(tmem + RT_TS, sdesc_kmajor_sw128(st) + 2u * k, sdesc_kmajor_sw128(st + 2 * RT_Q) + 2u * k, id_s, k > 0);
       if (elect_one()) tc_commit(s_full);
-      // O = W V once the epilogue has written W
-      if (!mbar_wait_warp(w_full, par, p.status)) {
-        ok = false;
-        break;
-      }
+      return true;
+    };
+    // O(lt) = W V: the epilogue has written W(lt) and read O(lt - 1)
+    auto values = [&](int lt) {
+      const uint32_t par = static_cast<uint32_t>(lt) & 1u;
+      if (!mbar_wait_warp(w_full, par, p.status) || !mbar_wait_warp(acc_free, par ^ 1u, p.status)) return false;
       tc_fence_after();
+      const uint32_t st = sbase + (lt & 1) * RT_STAGE;
       for (int ks = 0; ks < NS / 16; ++ks)
         if (elect_one())
           tc_mma_ts(tmem + RT_TO, tmem + RT_TW + ks * 8, sdesc_mnmajor_sw128(st + 2 * RT_Q + RT_KV + ks * 2048, 16),
                     id_o, ks > 0);
       if (elect_one()) tc_commit(o_full);
-      if (elect_one()) tc_commit(&st_empty[s]);
+      if (elect_one()) tc_commit(&st_empty[lt & 1]);
+      return true;
+    };
+    // S of the next tile goes in as soon as the epilogue has read this tile's S, ahead of this tile's O
+    const int nt = (p.tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x;
+    bool ok = nt > 0 && scores(0);
+    for (int lt = 0; lt < nt && ok; ++lt) {
+      if (lt + 1 < nt) ok = scores(lt + 1);
+      if (ok) ok = values(lt);
     }
     if (elect_one()) tc_commit(drain);
     mbar_wait_warp(drain, 0, p.status);
@@ -157,7 +169,22 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
     const int r = quarter * 32 + lane, g = r >> 6;  // MMA row; its tile slot (warp-uniform)
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     float* sums = reinterpret_cast<float*>(smem + RT_SUMS);
+    float* probs = reinterpret_cast<float*>(smem + RT_PROB);
     const int pieces = p.Kp / 32;
+    const int et = threadIdx.x - 64;  // 0 .. 511
+    const int nt = (p.tiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x;
+    auto tile_of = [&](int lt) { return static_cast<int>(blockIdx.x) + lt * static_cast<int>(gridDim.x); };
+    // local tile lt's probabilities into buffer lt % 3: slot g's keys at g Kp .. g Kp + Kp - 1, zero past K. A buffer
+    // is written two barriers before its first read and after the last read of its previous tile
+    auto stage_probs = [&](int lt) {
+      if (lt < nt && et < p.G * p.Kp) {
+        const int sg = et / p.Kp, k = et % p.Kp;
+        const int mh = item_of(tile_of(lt), sg) / p.PB;
+        probs[(lt % 3) * 256 + et] = k < p.K ? p.prob[static_cast<int64_t>(mh) * p.K + k] : 0.f;
+      }
+    };
+    stage_probs(0);
+    stage_probs(1);
     // W starts zero: a row's weights are only ever written in its own item's columns (block-diagonal)
     {
       uint32_t z[16];
@@ -167,88 +194,120 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
       tc_wait_st();
     }
     tc_fence_before();
-    // every epilogue warp reaches the named barrier once per tile, whatever happened: a warp whose bounded wait gave
-    // up arrives with false, all of them see the AND, and from then on they only keep the barrier count
+    // every epilogue warp reaches the named barrier the same number of times, whatever happened: a warp whose bounded
+    // wait gave up arrives with false, all of them see the AND, and from then on they only keep the count
     bool ok = bar_and<RT_THREADS - 64>(true);
     tc_fence_after();
-    int lt = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x, ++lt) {
-      const uint32_t par = static_cast<uint32_t>(lt) & 1u;
-      const bool slot = g < p.G && t * p.G + g < p.items;  // this row's tile slot holds a real item
-      const int it = item_of(t, g);
-      const int pb = it % p.PB, mh = it / p.PB, tok = mh / p.H, hd = mh % p.H;
-      const int probe = pb * 64 + (r & 63);
-      const bool row_ok = slot && probe < p.P;
-      const float* pk = p.prob + static_cast<int64_t>(mh) * p.K;
-      bool got = ok && mbar_wait_warp(s_full, par, p.status);
-      if (got) tc_fence_after();
-      // pass 1: sum_k p_k (e^ds_k - 1) over this warp's pieces of the row's own keys
+    float e[NP][32];  // e^ds - 1 of this warp's pieces of the row's own keys, from the first pass to the second
+    // first pass of local tile lt: e and its p-weighted partial sum into sums[lt & 1]; then S may be overwritten
+    auto pass1 = [&](int lt) {
+      const bool got = ok && mbar_wait_warp(s_full, static_cast<uint32_t>(lt) & 1u, p.status);
+      const float* pk = probs + (lt % 3) * 256 + g * p.Kp;
       float2 acc = make_float2(0.f, 0.f);
-      if (got && g < p.G) {
-        for (int pc = cg; pc < pieces; pc += 4) {
-          float sv[32];
-          tmem_ld32(trow + RT_TS + g * p.Kp + pc * 32, sv);
-          tc_wait_ld();
-          reg_fence<32>(sv);
+      if (got) {
+        tc_fence_after();
+        if (g < p.G) {
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const int k = pc * 32 + c;
-            const float2 ds = make_float2(bf16_round(sv[c]) * SCALE, bf16_round(sv[c + 1]) * SCALE);
-            const float2 e = expm1_f2(ds);
-            if (k < p.K) acc.x = fmaf(pk[k], e.x, acc.x);
-            if (k + 1 < p.K) acc.y = fmaf(pk[k + 1], e.y, acc.y);
+          for (int i = 0; i < NP; ++i) {
+            const int pc = cg + 4 * i;
+            if (pc < pieces) {
+              float sv[32];
+              tmem_ld32(trow + RT_TS + g * p.Kp + pc * 32, sv);
+              tc_wait_ld();
+              reg_fence<32>(sv);
+#pragma unroll
+              for (int c = 0; c < 32; c += 2) {
+                const int k = pc * 32 + c;
+                const float2 ev = expm1_f2(
+                    make_float2(bf16_round_alu(sv[c]) * SCALE, bf16_round_alu(sv[c + 1]) * SCALE));
+                e[i][c] = ev.x, e[i][c + 1] = ev.y;
+                if (k < p.K) acc.x = fmaf(pk[k], ev.x, acc.x);
+                if (k + 1 < p.K) acc.y = fmaf(pk[k + 1], ev.y, acc.y);
+              }
+            }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_free);
       }
-      float* sb = sums + (lt & 1) * 4 * 128;
-      sb[cg * 128 + r] = acc.x + acc.y;
-      ok = bar_and<RT_THREADS - 64>(got);
-      if (!ok) continue;
-      const float dlse = log1pf((sb[r] + sb[128 + r]) + (sb[256 + r] + sb[384 + r]));
-      // pass 2: w_k = bf16(p_k (e^(ds_k - dlse) - 1)) into W (bf16 pairs, the TS operand's K-major packing)
+      sums[(lt & 1) * 512 + cg * 128 + r] = acc.x + acc.y;
+      return got;
+    };
+    // second pass (after the barrier): e^(ds - dlse) - 1 = (e - sigma) / (1 + sigma), as 1 + sigma = e^dlse, so
+    // w_k = bf16(p_k (e_k - sigma) / (1 + sigma)) into W (bf16 pairs, the TS operand's K-major packing); returns
+    // dlse. 1 + sigma <= 0 makes dlse, and the reference's weights with it, NaN: so here too
+    auto pass2 = [&](int lt) {
+      const float* sb = sums + (lt & 1) * 512;
+      const float sigma = (sb[r] + sb[128 + r]) + (sb[256 + r] + sb[384 + r]);
+      const float inv = 1.f + sigma > 0.f ? 1.f / (1.f + sigma) : __int_as_float(0x7FC00000);
+      const float* pk = probs + (lt % 3) * 256 + g * p.Kp;
       if (g < p.G) {
-        for (int pc = cg; pc < pieces; pc += 4) {
-          float sv[32];
-          tmem_ld32(trow + RT_TS + g * p.Kp + pc * 32, sv);
-          tc_wait_ld();
-          reg_fence<32>(sv);
-          uint32_t wv[16];
 #pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const int k = pc * 32 + c;
-            const float2 ds = make_float2(bf16_round(sv[c]) * SCALE - dlse, bf16_round(sv[c + 1]) * SCALE - dlse);
-            const float2 e = expm1_f2(ds);
-            const float w0 = k < p.K ? pk[k] * e.x : 0.f, w1 = k + 1 < p.K ? pk[k + 1] * e.y : 0.f;
-            wv[c / 2] = pack_bf16x2(w0, w1);
+        for (int i = 0; i < NP; ++i) {
+          const int pc = cg + 4 * i;
+          if (pc < pieces) {
+            uint32_t wv[16];
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+              const int k = pc * 32 + c;
+              const float2 d = __fmul2_rn(__fadd2_rn(make_float2(e[i][c], e[i][c + 1]), make_float2(-sigma, -sigma)),
+                                          make_float2(inv, inv));
+              const float w0 = k < p.K ? pk[k] * d.x : 0.f, w1 = k + 1 < p.K ? pk[k + 1] * d.y : 0.f;
+              wv[c / 2] = pack_bf16x2(w0, w1);
+            }
+            tmem_st16(trow + RT_TW + (g * p.Kp + pc * 32) / 2, wv);
           }
-          tmem_st16(trow + RT_TW + (g * p.Kp + pc * 32) / 2, wv);
         }
         tc_wait_st();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(w_full);
-      if (!mbar_wait_warp(o_full, par, p.status)) {
-        ok = false;  // the next tile's barrier tells the other warps
-        continue;
-      }
-      tc_fence_after();
-      float o[16];
-      tmem_ld16(trow + RT_TO + cg * 16, o);
-      tc_wait_ld();
-      reg_fence<16>(o);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_free);
-      if (row_ok) {
-        const float em = expm1f(-dlse);
-        const float* rs = p.rest + static_cast<int64_t>(mh) * 64 + cg * 16;
-        float4* dst = reinterpret_cast<float4*>(
-            p.out + ((static_cast<int64_t>(tok) * p.P + probe) * p.H + hd) * 64 + cg * 16);
+      return log1pf(sigma);
+    };
+    // software pipeline over the CTA's tiles: pass 1 of tile lt + 1 runs while O(lt) is on the tensor pipe
+    float dlse = 0.f;
+    if (nt > 0) {
+      const bool got = pass1(0);
+      ok = bar_and<RT_THREADS - 64>(got);
+      stage_probs(2);
+      if (ok) dlse = pass2(0);
+    }
+    for (int lt = 0; lt < nt; ++lt) {
+      const bool got1 = lt + 1 < nt ? pass1(lt + 1) : true;
+      // O(lt): read, release, finish and store
+      const bool have = ok && mbar_wait_warp(o_full, static_cast<uint32_t>(lt) & 1u, p.status);
+      if (have) {
+        tc_fence_after();
+        float o[16];
+        tmem_ld16(trow + RT_TO + cg * 16, o);
+        tc_wait_ld();
+        reg_fence<16>(o);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_free);
+        const int t = tile_of(lt);
+        const int it = item_of(t, g);
+        const int pb = it % p.PB, mh = it / p.PB, tok = mh / p.H, hd = mh % p.H;
+        const int probe = pb * 64 + (r & 63);
+        if (g < p.G && t * p.G + g < p.items && probe < p.P) {
+          const float em = expm1f(-dlse);
+          const float* rs = p.rest + static_cast<int64_t>(mh) * 64 + cg * 16;
+          float4* dst = reinterpret_cast<float4*>(
+              p.out + ((static_cast<int64_t>(tok) * p.P + probe) * p.H + hd) * 64 + cg * 16);
 #pragma unroll
-        for (int c = 0; c < 16; c += 4)
-          dst[c / 4] = make_float4(bf16_round(o[c]) + em * rs[c], bf16_round(o[c + 1]) + em * rs[c + 1],
-                                   bf16_round(o[c + 2]) + em * rs[c + 2], bf16_round(o[c + 3]) + em * rs[c + 3]);
+          for (int c = 0; c < 16; c += 4)
+            dst[c / 4] = make_float4(bf16_round_alu(o[c]) + em * rs[c], bf16_round_alu(o[c + 1]) + em * rs[c + 1],
+                                     bf16_round_alu(o[c + 2]) + em * rs[c + 2],
+                                     bf16_round_alu(o[c + 3]) + em * rs[c + 3]);
+        }
+      }
+      ok = ok && have;
+      if (lt + 1 < nt) {
+        ok = bar_and<RT_THREADS - 64>(ok && got1);
+        stage_probs(lt + 3);
+        if (ok) dlse = pass2(lt + 1);
       }
     }
   }
