@@ -841,7 +841,7 @@ def run_aux(a):
     xc, yc = rn(nc_, 512), torch.randint(0, 4096, (nc_,), device=device, generator=g)
     us = _timed(lambda: cycle.top_credit(model, xc, yc), a.steps, a.warmup)
     rate('top_credit', us, flops=nc_ * (7 * 2 * 4096 * 512 + 2 * 512 * 512), tokens=nc_,
-         matmul_precision=torch.get_float32_matmul_precision())
+         fp32_contractions='tf32 tcgen05 GEMM (the reference\'s high precision)')
     raw = rn(nc_, 4096, scale=3)
     us = _timed(lambda: cycle.coordinate_change(raw, yc), a.steps, a.warmup)
     rate('coordinate_change', us, nbytes=nc_ * 4096 * 8)
