@@ -427,6 +427,26 @@ int noise_key_response(const noise_view3_t* q, const float* dk, const noise_view
                        int heads, int tokens, int probes, int sources, int source_start, int query_start, int window,
                        float* out, void* stream);
 
+/* Bytes of the caller's workspace for noise_future_scores_ws / noise_key_response_ws: a 256-byte status block, then q
+ * (and, for future_scores, target) as tf32 hi / lo planes, fp32 [heads, Tp, 64] each (Tp = tokens rounded up to 64).
+ * 0 for an argument < 1. */
+size_t noise_future_scores_workspace_bytes(int heads, int tokens);
+size_t noise_key_response_workspace_bytes(int heads, int tokens);
+
+/* noise_future_scores / noise_key_response on tcgen05 with a caller workspace (256-byte aligned, the *_workspace_bytes
+ * query large; dk, dv 16-byte aligned): both dots at the reference kernels' tf32x3 precision (run.py:1714-1715, :585)
+ * as kind::tf32 MMAs with the (probe, source) columns as the 128 MMA rows, so each column's sum over its receivers
+ * stays in one thread; receivers stream in 32-row tiles over the union of a block's windows, each column masked to its
+ * own. Same result definitions. The workspace's first int32 is the device status after the call completes: 0, or 1 if
+ * a pipeline wait gave up (the output is then incomplete). */
+int noise_future_scores_ws(const noise_view3_t* q, const noise_view3_t* target, const float* dk, const float* dv,
+                           const noise_view3_t* a, const noise_view3_t* contrast, int heads, int tokens, int probes,
+                           int sources, int source_start, int window, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int noise_key_response_ws(const noise_view3_t* q, const float* dk, const noise_view3_t* a, const noise_view3_t* c,
+                          int heads, int tokens, int probes, int sources, int source_start, int query_start,
+                          int window, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* noise_record::future_query_response (run.py:1818-1834, kernel :1780-1815): out[m, p, h] (fp32 [M, P, H, 64]) =
  * (sum_k change v_k - (sum_k change) base[h, m]) / (1 + sum_k change), change = probabilities[h, m, k]
  * (e^(dq[m, p, h] . k_k / 8) - 1). dq contiguous fp32 [M, P, H, 64]; keys, values (H, T, 64), probabilities (H, M, T),

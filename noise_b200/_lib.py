@@ -147,6 +147,10 @@ SIGNATURES = [
     ('noise_square_credit_grads', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_future_scores', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_key_response', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_future_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 2),
+    ('noise_key_response_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 2),
+    ('noise_future_scores_ws', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_key_response_ws', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_query_response', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_expm1_f32', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     ('noise_query_response_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 4),

@@ -318,6 +318,7 @@ static bool a16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) ==
 
 #include "query_tc.cuh"
 #include "routed_tc.cuh"
+#include "column_tc.cuh"
 
 namespace {
 
@@ -334,14 +335,14 @@ PFN_cuTensorMapEncodeTiled_v12000 qt_encode() {
   return fn;
 }
 
-// fp32 [outer, inner] rows, 64-row x 32-column boxes (128 bytes), 128-byte swizzle
-int qt_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer) {
+// fp32 [outer, inner] rows, box_rows x 32-column boxes (128 bytes), 128-byte swizzle
+int qt_map(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint32_t box_rows = 64) {
   auto fn = qt_encode();
   if (!fn) return NOISE_ERR_CUDA;
   if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {inner * 4};
-  cuuint32_t box[2] = {32, 64};
+  cuuint32_t box[2] = {32, box_rows};
   cuuint32_t el[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, el,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -375,6 +376,50 @@ __global__ void __launch_bounds__(256) expm1_check_kernel(const float* __restric
     out[i] = e.x;
     if (i + 1 < n) out[i + 1] = e.y;
   }
+}
+
+// future_scores / key_response on tcgen05: 256-byte status block, then q (and target) as tf32 hi / lo planes
+size_t ct_plane_bytes(int heads, int tokens) {
+  return static_cast<size_t>(heads) * ((tokens + 63) / 64 * 64) * noise::readout::D * 4;
+}
+
+template <bool VALUES>
+int column_ws(const noise_view3_t* q, const noise_view3_t* target, const float* dk, const float* dv,
+              const noise_view3_t* a, const noise_view3_t* c, int heads, int tokens, int probes, int sources,
+              int first_off, int span, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace noise::readout;
+  using L = CtLayout<VALUES>;
+  const size_t plane = ct_plane_bytes(heads, tokens);
+  if (!workspace || workspace_bytes < 256 + (VALUES ? 4 : 2) * plane) return NOISE_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !a16(dk) || (VALUES && !a16(dv))) return NOISE_ERR_ALIGN;
+  const int64_t cols = static_cast<int64_t>(probes) * sources;
+  if (cols > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
+  const int tp = (tokens + 63) / 64 * 64;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  float* qhi = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);
+  float* qlo = qhi + plane / 4;
+  float* ghi = qlo + plane / 4;
+  float* glo = ghi + plane / 4;
+  CtMaps maps;
+  int rc;
+  const uint64_t rows = static_cast<uint64_t>(heads) * tp;
+  if ((rc = qt_map(&maps.qhi, qhi, D, rows, CT_RECV)) || (rc = qt_map(&maps.qlo, qlo, D, rows, CT_RECV))) return rc;
+  if (VALUES) {
+    if ((rc = qt_map(&maps.ghi, ghi, D, rows, CT_RECV)) || (rc = qt_map(&maps.glo, glo, D, rows, CT_RECV))) return rc;
+  } else {
+    maps.ghi = maps.qhi;
+    maps.glo = maps.qlo;
+  }
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  col_split_kernel<<<dim3(tp / 64, heads), 256, 0, s>>>(view(*q), tokens, tp, qhi, qlo);
+  if (VALUES) col_split_kernel<<<dim3(tp / 64, heads), 256, 0, s>>>(view(*target), tokens, tp, ghi, glo);
+  if (cudaFuncSetAttribute(column_tc_kernel<VALUES>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM))
+    return NOISE_ERR_CUDA;
+  CtArgs args{dk, dv, view(*a), view(*c), out, tokens, sources, probes, heads, tp, first_off, span, status};
+  column_tc_kernel<VALUES><<<dim3(static_cast<unsigned>((cols + CT_COLS - 1) / CT_COLS), heads), CT_THREADS, L::SMEM,
+                             s>>>(maps, args);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
 // workspace: 256-byte status block, keys hi / lo and values^T hi / lo (fp32, H * Tp * 64 each), live flags
@@ -485,6 +530,37 @@ int noise_routed_response_ws(const void* dq, const void* keys, const void* value
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, RT_SMEM)) return NOISE_ERR_CUDA;
   kernel<<<std::min(a.tiles, sms), RT_THREADS, RT_SMEM, s>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+size_t noise_future_scores_workspace_bytes(int heads, int tokens) {
+  return heads < 1 || tokens < 1 ? 0 : 256 + 4 * ct_plane_bytes(heads, tokens);
+}
+
+size_t noise_key_response_workspace_bytes(int heads, int tokens) {
+  return heads < 1 || tokens < 1 ? 0 : 256 + 2 * ct_plane_bytes(heads, tokens);
+}
+
+int noise_future_scores_ws(const noise_view3_t* q, const noise_view3_t* target, const float* dk, const float* dv,
+                           const noise_view3_t* a, const noise_view3_t* contrast, int heads, int tokens, int probes,
+                           int sources, int source_start, int window, float* out, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!q || !target || !dk || !dv || !a || !contrast || !out || !q->data || !target->data || !a->data ||
+      !contrast->data)
+    return NOISE_ERR_ARGUMENT;
+  if (heads < 1 || tokens < 1 || probes < 1 || sources < 1 || window < 0) return NOISE_ERR_SHAPE;
+  // receivers 0 < s - (start + m) <= window: s in [start + m + 1, start + m + window]
+  return column_ws<true>(q, target, dk, dv, a, contrast, heads, tokens, probes, sources, source_start + 1, window - 1,
+                         out, workspace, workspace_bytes, stream);
+}
+
+int noise_key_response_ws(const noise_view3_t* q, const float* dk, const noise_view3_t* a, const noise_view3_t* c,
+                          int heads, int tokens, int probes, int sources, int source_start, int query_start,
+                          int window, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !dk || !a || !c || !out || !q->data || !a->data || !c->data) return NOISE_ERR_ARGUMENT;
+  if (heads < 1 || tokens < 1 || probes < 1 || sources < 1 || window < 0) return NOISE_ERR_SHAPE;
+  // query index s with query_start + s in [source_start + m, source_start + m + window]
+  return column_ws<false>(q, q, dk, dk, a, c, heads, tokens, probes, sources, source_start - query_start, window, out,
+                          workspace, workspace_bytes, stream);
 }
 
 size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, int keys_len) {

@@ -10,9 +10,8 @@ Same names, arguments and results as the reference's custom ops:
 Each is also registered as a ``torch.library.custom_op`` (namespace ``noise_b200``) with a fake. ``install(R)``
 registers these implementations as the CUDA kernels of the record module's own ops, the seam the reference's
 ``fast_kernels.install`` uses (``op.register_kernel('cuda', impl)``, run.py:3440-3453), so R's callers run them
-unchanged. head_dim 64. query_response runs its two dots on tcgen05 at the reference's tf32x3 precision and
-routed_response its bf16 dots as kind::f16 MMAs; future_scores and key_response use fp32 CUDA-core arithmetic (at
-least as accurate as tf32x3).
+unchanged. head_dim 64. future_scores, key_response and query_response run their dots on tcgen05 at the reference's
+tf32x3 precision, routed_response its bf16 dots as kind::f16 MMAs; each keeps its fp32 CUDA-core form as tc=False.
 """
 import ctypes
 
@@ -47,7 +46,9 @@ def _stream(t):
     return _lib.stream_handle(t.device)
 
 
-def future_scores_impl(q, target, dk, dv, a, contrast, source_start, window):
+def future_scores_impl(q, target, dk, dv, a, contrast, source_start, window, tc=True):
+    """tc=True: the tcgen05 kernel at the reference's tf32x3 precision (its workspace, whose first int is the device
+    status, rides on the output as ``_noise_workspace``); tc=False: the fp32 CUDA-core kernel, for comparison."""
     h, p, m, d = dk.shape
     if d != HD:
         raise ValueError('head_dim 64 only')
@@ -55,13 +56,22 @@ def future_scores_impl(q, target, dk, dv, a, contrast, source_start, window):
     (qv, q), (gv, target), (av, a), (cv, contrast) = _view(q), _view(target), _view(a), _view(contrast)
     dk, dv = _f32c(dk), _f32c(dv)
     out = torch.empty((h, p, m), device=q.device, dtype=torch.float32)
-    _check(_lib.lib().noise_future_scores(ctypes.byref(qv), ctypes.byref(gv), dk.data_ptr(), dv.data_ptr(),
-                                          ctypes.byref(av), ctypes.byref(cv), h, q.shape[1], p, m, int(source_start),
-                                          int(window), out.data_ptr(), _stream(q)), 'noise_future_scores')
+    L, t = _lib.lib(), q.shape[1]
+    args = (ctypes.byref(qv), ctypes.byref(gv), dk.data_ptr(), dv.data_ptr(), ctypes.byref(av), ctypes.byref(cv), h, t,
+            p, m, int(source_start), int(window), out.data_ptr())
+    if not tc:
+        _check(L.noise_future_scores(*args, _stream(q)), 'noise_future_scores')
+        return out
+    nbytes = L.noise_future_scores_workspace_bytes(h, t)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    _check(L.noise_future_scores_ws(*args, ws.data_ptr(), nbytes, _stream(q)), 'noise_future_scores_ws')
+    out._noise_workspace = ws
     return out
 
 
-def key_response_impl(q, dk, A, C, source_start, query_start, window):
+def key_response_impl(q, dk, A, C, source_start, query_start, window, tc=True):
+    """tc=True: the tcgen05 kernel at the reference's tf32x3 precision (workspace on ``_noise_workspace``); tc=False:
+    the fp32 CUDA-core kernel, for comparison."""
     heads, probes, sources, width = dk.shape
     if width != HD:
         raise ValueError('head_dim 64 only')
@@ -69,9 +79,16 @@ def key_response_impl(q, dk, A, C, source_start, query_start, window):
     (qv, q), (av, A), (cv, C) = _view(q), _view(A), _view(C)
     dk = _f32c(dk)
     out = torch.empty((heads, probes, sources), device=q.device, dtype=torch.float32)
-    _check(_lib.lib().noise_key_response(ctypes.byref(qv), dk.data_ptr(), ctypes.byref(av), ctypes.byref(cv), heads,
-                                         q.shape[1], probes, sources, int(source_start), int(query_start),
-                                         int(window), out.data_ptr(), _stream(q)), 'noise_key_response')
+    L, t = _lib.lib(), q.shape[1]
+    args = (ctypes.byref(qv), dk.data_ptr(), ctypes.byref(av), ctypes.byref(cv), heads, t, probes, sources,
+            int(source_start), int(query_start), int(window), out.data_ptr())
+    if not tc:
+        _check(L.noise_key_response(*args, _stream(q)), 'noise_key_response')
+        return out
+    nbytes = L.noise_key_response_workspace_bytes(heads, t)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    _check(L.noise_key_response_ws(*args, ws.data_ptr(), nbytes, _stream(q)), 'noise_key_response_ws')
+    out._noise_workspace = ws
     return out
 
 

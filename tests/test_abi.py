@@ -119,6 +119,15 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_future_scores(r, r, fake, fake, r, r, 0, 64, 2, 2, 0, 8, fake, None) == 1   # no heads
     assert L.noise_future_scores(r, r, fake + 4, fake, r, r, 2, 64, 2, 2, 0, 8, fake, None) == 2  # dk alignment
     assert L.noise_key_response(None, fake, r, r, 2, 64, 2, 2, 0, 0, 8, fake, None) == 4
+    fn = L.noise_future_scores_workspace_bytes(8, 2000)
+    assert fn == 256 + 4 * 8 * 2048 * 64 * 4 and L.noise_key_response_workspace_bytes(8, 2000) == 256 + 2 * 8 * 2048 * 256
+    assert L.noise_future_scores_workspace_bytes(0, 64) == 0
+    fs = (r, r, fake, fake, r, r, 8, 2000, 2, 2, 0, 8, fake)
+    assert L.noise_future_scores_ws(*fs, fake, fn - 1, None) == 3                               # workspace
+    assert L.noise_future_scores_ws(*fs, fake + 16, fn, None) == 2                              # workspace alignment
+    assert L.noise_future_scores_ws(r, r, fake + 4, fake, r, r, 8, 2000, 2, 2, 0, 8, fake, fake, fn, None) == 2  # dk
+    assert L.noise_key_response_ws(r, fake, r, r, 8, 2000, 2, 2, 0, 0, -1, fake, fake, fn, None) == 1  # window < 0
+    assert L.noise_key_response_ws(None, fake, r, r, 8, 2000, 2, 2, 0, 0, 8, fake, fake, fn, None) == 4
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
     qn = L.noise_query_response_workspace_bytes(256, 64, 8, 2048)
     assert qn == 256 + 4 * 8 * 2048 * 64 * 4 + 8 * 256 * 32                                   # planes + live flags

@@ -83,6 +83,33 @@ def test_query_response_larger():
     assert _rel(_query(_dev(q)), ref) < REL
 
 
+@pytest.mark.parametrize('h,t,p,m,start,window', [(3, 300, 5, 100, 40, 96), (2, 1000, 3, 200, 0, 1000),
+                                                   (2, 257, 1, 129, 250, 64), (1, 64, 2, 17, 10, 0)])
+def test_column_scores_tc(h, t, p, m, start, window):
+    """future_scores and key_response on tcgen05: column blocks of 128 spanning probes, sources past T, windows
+    wider than T, an empty window, receivers off the 32-row tile; against the fp64 oracle and the CUDA-core kernels."""
+    from noise_b200 import _lib, readout
+    f = future_inputs(h=h, t=t, p=p, m=m, source_start=start, window=window, seed=41 + t)
+    ref = oracle.future_scores(f['q'], f['target'], f['dk'], f['dv'], f['a'], f['contrast'], f['source_start'],
+                               f['window'])
+    d = _dev(f)
+    args = (d['q'], d['target'], d['dk'], d['dv'], d['a'], d['contrast'], start, window)
+    out = readout.future_scores_impl(*args, tc=True)
+    assert _lib.read_status(out._noise_workspace) == 0
+    scale = max(ref.abs().max().item(), 1e-30)
+    assert (out.double().cpu() - ref).abs().max().item() <= REL * scale
+    assert torch.allclose(out, readout.future_scores_impl(*args, tc=False), rtol=0, atol=REL * scale)
+    k = key_inputs(h=h, t=t, p=p, m=m, source_start=start + 8, query_start=start, window=window, seed=43 + t)
+    kref = oracle.key_response(k['q'], k['dk'], k['A'], k['C'], k['source_start'], k['query_start'], k['window'])
+    e = _dev(k)
+    kargs = (e['q'], e['dk'], e['A'], e['C'], start + 8, start, window)
+    kout = readout.key_response_impl(*kargs, tc=True)
+    assert _lib.read_status(kout._noise_workspace) == 0
+    kscale = max(kref.abs().max().item(), 1e-30)
+    assert (kout.double().cpu() - kref).abs().max().item() <= REL * kscale
+    assert torch.allclose(kout, readout.key_response_impl(*kargs, tc=False), rtol=0, atol=REL * kscale)
+
+
 def _query_case(m, p, h, t, window, seed, dead=None):
     """query_response inputs with token positions spread over the keys (sorted, as a row block's tokens are adjacent),
     a strided (T, H, 64) keys buffer seen as [H, T, 64], and optionally a band of keys with zero probability."""
