@@ -13,7 +13,7 @@
 // 64, zero rows past T), K-major and TMA-loadable. One CTA per 128 consecutive columns of a head; its receivers are
 // the union of its columns' windows, in 32-receiver tiles. 320 threads:
 //   warp 0      TMA: per receiver tile q hi / lo (and target hi / lo) into a ring of 2 stages (4 for key_response);
-//   warp 1      TMEM (128 columns: S and VS, 32 each, double-buffered) and the MMAs: S^T (and VS^T) of a tile, 24
+//   warp 1      TMEM (256 columns: S and VS, 32 each, 4 buffers) and the MMAs: S^T (and VS^T) of a tile, 24
 //               kind::tf32 MMAs 128 x 32 x 8 each (hi.hi + hi.lo + lo.hi per K-step), A = dk (dv) from shared
 //               memory;
 //   warps 2..9  warp w: columns of TMEM lane quarter w % 4, receivers 16 ((w - 2) / 4) .. + 15 of each tile; a and
@@ -26,6 +26,7 @@ namespace noise {
 namespace readout {
 
 constexpr int CT_COLS = 128, CT_RECV = 32, CT_THREADS = 320, CT_EPI = 8;
+constexpr int CT_SB = 4;  // S (and VS) buffers in TMEM: the MMAs run up to CT_SB - 1 tiles ahead of the epilogue
 constexpr int CT_HALF = CT_COLS * 128;    // 128 rows x 32 fp32 (one K-major half of 64 dims): 16 KB
 constexpr int CT_OP = CT_RECV * 128;      // 32 receivers x 32 fp32: 4 KB
 constexpr int CT_B = 4 * CT_OP;           // hi half 0, hi half 1, lo half 0, lo half 1 of q (or target): 16 KB
@@ -80,9 +81,9 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::BAR);
   uint64_t* full = bar;                  // STAGES
   uint64_t* empty = full + L::STAGES;    // STAGES
-  uint64_t* s_full = empty + L::STAGES;  // 2
-  uint64_t* s_empty = s_full + 2;        // 2
-  uint64_t* drain = s_empty + 2;
+  uint64_t* s_full = empty + L::STAGES;  // CT_SB
+  uint64_t* s_empty = s_full + CT_SB;    // CT_SB
+  uint64_t* drain = s_empty + CT_SB;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       mbar_init(&full[b], 1);
       mbar_init(&empty[b], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < CT_SB; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], CT_EPI);  // one arrival per epilogue warp
     }
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, 128);
+    tmem_alloc(tmem_holder, 64 * CT_SB);
     tmem_relinquish();
   }
   // dk (dv) rows of the block as tf32 hi / lo: float4 q of a row = 16-byte chunk q % 8 of half q / 8, swizzled
@@ -187,9 +188,9 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
       }
     };
     for (int j = 0; j < n; ++j) {
-      const int b = j % L::STAGES, sb = j & 1;
+      const int b = j % L::STAGES, sb = j % CT_SB;
       if (!mbar_wait_warp(&full[b], static_cast<uint32_t>(j / L::STAGES) & 1u, p.status) ||
-          !mbar_wait_warp(&s_empty[sb], (static_cast<uint32_t>(j >> 1) & 1u) ^ 1u, p.status))
+          !mbar_wait_warp(&s_empty[sb], (static_cast<uint32_t>(j / CT_SB) & 1u) ^ 1u, p.status))
         break;
       tc_fence_after();
       const uint32_t st = sbase + L::RING + b * L::STAGE;
@@ -209,25 +210,32 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
     const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     // a and c of this column for receivers s0 + 16 half .. + 15 of tile jj, a tile ahead of their use
     float an[16], cn[16];
+    // this column's a and c rows (receiver stride s1): one base pointer each, stepped per receiver
+    const float* acol = p.a.p + h * p.a.s0 + mc * p.a.s2;
+    const float* ccol = p.c.p + h * p.c.s0 + mc * p.c.s2;
     auto fetch = [&](int jj) {
       const int s0 = (t_first + jj) * CT_RECV + half * 16;
+      const float* ap = acol + s0 * p.a.s1;
+      const float* cp = ccol + s0 * p.c.s1;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const bool in = valid && s0 + i < p.T;
-        an[i] = in ? p.a.at(h, s0 + i, mc) : 0.f;
-        cn[i] = in ? p.c.at(h, s0 + i, mc) : 0.f;
+        an[i] = in ? *ap : 0.f;
+        cn[i] = in ? *cp : 0.f;
+        ap += p.a.s1;
+        cp += p.c.s1;
       }
     };
     float acc = 0.f;
     bool ok = true;
     if (n > 0) fetch(0);
     for (int j = 0; j < n; ++j) {
-      const int sb = j & 1;
+      const int sb = j % CT_SB;
       float av[16], cv[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) av[i] = an[i], cv[i] = cn[i];
       if (j + 1 < n) fetch(j + 1);
-      if (!mbar_wait_warp(&s_full[sb], static_cast<uint32_t>(j >> 1) & 1u, p.status)) {
+      if (!mbar_wait_warp(&s_full[sb], static_cast<uint32_t>(j / CT_SB) & 1u, p.status)) {
         ok = false;
         break;
       }
@@ -251,10 +259,11 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
           const float ev = u ? e.y : e.x;
           const float ch = av[i + u] * ev;
           float term;
+          // fast division (2 ulp for a denominator in the normal range, as Triton's default fp32 division)
           if constexpr (VALUES)
-            term = (ch * cv[i + u] + (av[i + u] + ch) * vv[i + u]) / (1.f + ch);
+            term = __fdividef(ch * cv[i + u] + (av[i + u] + ch) * vv[i + u], 1.f + ch);
           else
-            term = ch / (1.f + ch) * cv[i + u];
+            term = __fdividef(ch, 1.f + ch) * cv[i + u];
           if (valid && s >= lo_s && s <= hi_s && s < p.T) acc += term;
         }
       }
@@ -270,7 +279,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 64 * CT_SB);
   }
 }
 
