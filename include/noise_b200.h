@@ -523,6 +523,16 @@ int noise_readout_staged(const void* up, const float* st, const float* r0, const
                          float* out, void* se, int start, int n, int se_rows, int tokens, int nc, int diag,
                          void* stream);
 
+/* noise_readout_staged with the moment-table terms on tcgen05 and a workspace of at least NOISE_STATUS_BYTES
+ * (256-byte aligned; its first int32 is the device status after the call: 0, or 1 if a bounded wait gave up and out is
+ * incomplete): per head bf16(dk) M1 and bf16(dk) M2 for 128 rows of a token as kind::f16 MMAs (the reference's
+ * tl.dot of the same bf16 operands, run.py:6032-6033), each row's dot with its fp32 dk / dv one thread's sum over a
+ * TMEM row; the rest as noise_readout_staged. Same arguments and results. */
+int noise_readout_staged_ws(const void* up, const float* st, const float* r0, const float* vc, const float* gz,
+                            const float* ve, const float* cs, const float* sn, const noise_scorer_tables_t* tab,
+                            float* out, void* se, int start, int n, int se_rows, int tokens, int nc, int diag,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* readout_kernel (:5906-5965): the same score from the projected change pj fp32 [tokens, probes, 2, 8, 64] (key and
  * value parts), r0 fp32 [tokens, 8, 64], cos / sin rows of the chunk's tokens (strided: token, pair), gc fp32
  * [tokens, probes, 8] and ve fp32 [tokens, 8, 64] (both NULL: ungated): out fp32 [tokens, probes]; se bf16

@@ -10,12 +10,16 @@
 // Layout: one warp per row; lane l owns the features l and l + 32 (a rotary pair: each is the other's RoPE partner).
 // A block is 64 rows of one token; per head the token's M1, M2 (bf16 64 x 64) are staged in shared memory once for
 // all of them.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "noise_b200.h"
+#include "ptx.cuh"
 
 namespace noise {
 namespace scorer {
@@ -96,17 +100,19 @@ struct DirectArgs {
   int start, P, diag;
 };
 
-// One head of one row: dr, dv (the lane's two features), the clean rotated key r0 -> the scores against the tables
-// of (token, head); returns the row's score part (every lane holds it) and writes the self-edge.
+// One head of one row: dr, dv (the lane's two features), the clean rotated key r0 -> the change dk of the rotated,
+// RMS-normed key (the lane's features in dk0, dk1) and the row's score part without the moment tables: the exact
+// receiver s = t (DIAG), the self-edge (SELF, written) and dk . U / 8 + dv . W (every lane holds the sum).
 template <bool SELF>
-__device__ __forceinline__ float score_head(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
-                                            const Tables& tb, int64_t row, int lane, const __nv_bfloat16* sm1,
-                                            const __nv_bfloat16* sm2, float* sdk, int diag, __nv_bfloat16* se_row) {
+__device__ __forceinline__ float head_change(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
+                                             const Tables& tb, int64_t row, int lane, int diag,
+                                             __nv_bfloat16* se_row, float& dk0, float& dk1) {
   const float square = warp_sum(r00 * r00 + r01 * r01);
   const float grow = warp_sum(2.f * (r00 * dr0 + r01 * dr1) + dr0 * dr0 + dr1 * dr1) / D;
   const float inverse = rsqrtf(square / D + NEPS), moved = rsqrtf(square / D + grow + NEPS);
   const float shrink = grow * (inverse * moved) * (inverse * moved) / (inverse + moved);
-  const float dk0 = dr0 * moved - r00 * shrink, dk1 = dr1 * moved - r01 * shrink;
+  dk0 = dr0 * moved - r00 * shrink;
+  dk1 = dr1 * moved - r01 * shrink;
   const int64_t v = row * D;
   float total = 0.f;
   if (diag || SELF) {  // the receiver s = t, exactly
@@ -119,7 +125,19 @@ __device__ __forceinline__ float score_head(float dr0, float dr1, float dv0, flo
       se_row[lane + 32] = __float2bfloat16_rn(gain * (tb.VT[v + lane + 32] - tb.OT[v + lane + 32]) + vgain * dv1);
     }
   }
-  // bf16(dk) M1 dk / 64 + bf16(dk) M2 dv / 8: the lane forms columns lane, lane + 32 of bf16(dk) M
+  total += warp_sum((dk0 * tb.U[v + lane] + dk1 * tb.U[v + lane + 32]) * 0.125f + dv0 * tb.WV[v + lane] +
+                    dv1 * tb.WV[v + lane + 32]);
+  return total;
+}
+
+// head_change plus the moment tables on the CUDA cores: bf16(dk) M1 dk / 64 + bf16(dk) M2 dv / 8, the lane forming
+// columns lane, lane + 32 of bf16(dk) M from the tables staged in shared memory
+template <bool SELF>
+__device__ __forceinline__ float score_head(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
+                                            const Tables& tb, int64_t row, int lane, const __nv_bfloat16* sm1,
+                                            const __nv_bfloat16* sm2, float* sdk, int diag, __nv_bfloat16* se_row) {
+  float dk0, dk1;
+  float total = head_change<SELF>(dr0, dr1, dv0, dv1, r00, r01, tb, row, lane, diag, se_row, dk0, dk1);
   sdk[lane] = bf16r(dk0);
   sdk[lane + 32] = bf16r(dk1);
   __syncwarp();
@@ -133,9 +151,7 @@ __device__ __forceinline__ float score_head(float dr0, float dr1, float dv0, flo
     c21 = fmaf(k, __bfloat162float(sm2[i * D + lane + 32]), c21);
   }
   __syncwarp();
-  total += warp_sum((dk0 * tb.U[v + lane] + dk1 * tb.U[v + lane + 32]) * 0.125f + dv0 * tb.WV[v + lane] +
-                    dv1 * tb.WV[v + lane + 32] + (c10 * dk0 + c11 * dk1) * (1.f / D) +
-                    (c20 * dv0 + c21 * dv1) * 0.125f);
+  total += warp_sum((c10 * dk0 + c11 * dk1) * (1.f / D) + (c20 * dv0 + c21 * dv1) * 0.125f);
   return total;
 }
 
@@ -276,7 +292,41 @@ static bool tables_ok(const noise_scorer_tables_t& t, bool self) {
 }  // namespace scorer
 }  // namespace noise
 
+#include "staged_tc.cuh"
+
 using namespace noise::scorer;
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 stc_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 moment tables [rows, 64] (rows = tokens x 8 heads x 64), 64 x 64 boxes, 128-byte swizzle
+int stc_map(CUtensorMap* map, const void* base, uint64_t rows) {
+  auto fn = stc_encode();
+  if (!fn) return NOISE_ERR_CUDA;
+  if (reinterpret_cast<uintptr_t>(base) & 15) return NOISE_ERR_ALIGN;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), rows};
+  cuuint64_t strides[1] = {D * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D), static_cast<cuuint32_t>(D)};
+  cuuint32_t el[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, el,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -311,6 +361,34 @@ int noise_readout_staged(const void* up, const float* st, const float* r0, const
   else if (gated) staged_kernel<true, false><<<grid, 256, 0, s>>>(a);
   else if (self) staged_kernel<false, true><<<grid, 256, 0, s>>>(a);
   else staged_kernel<false, false><<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_readout_staged_ws(const void* up, const float* st, const float* r0, const float* vc, const float* gz,
+                            const float* ve, const float* cs, const float* sn, const noise_scorer_tables_t* tab,
+                            float* out, void* se, int start, int n, int se_rows, int tokens, int nc, int diag,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (!up || !st || !r0 || !vc || !cs || !sn || !tab || !out) return NOISE_ERR_ARGUMENT;
+  const bool gated = gz != nullptr, self = se != nullptr;
+  if ((gated && !ve) || !tables_ok(*tab, self)) return NOISE_ERR_ARGUMENT;
+  if (n < 0 || tokens < 0 || start < 0 || nc < 2 * W + (gated ? 16 : 0) || (self && se_rows < n))
+    return NOISE_ERR_SHAPE;
+  if (!workspace || workspace_bytes < NOISE_STATUS_BYTES) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  if (n == 0 || tokens == 0) return NOISE_OK;
+  StagedArgs a{static_cast<const __nv_bfloat16*>(up), st, r0, vc, gz, ve, cs, sn, tables(*tab), out,
+               static_cast<__nv_bfloat16*>(se), start, n, se_rows, nc, diag};
+  StcMaps maps;
+  const uint64_t rows = static_cast<uint64_t>(start + tokens) * H * D;
+  int rc;
+  if ((rc = stc_map(&maps.m1, tab->M1, rows)) || (rc = stc_map(&maps.m2, tab->M2, rows))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  auto kernel = gated ? (self ? staged_tc_kernel<true, true> : staged_tc_kernel<true, false>)
+                      : (self ? staged_tc_kernel<false, true> : staged_tc_kernel<false, false>);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, STC_SMEM)) return NOISE_ERR_CUDA;
+  kernel<<<dim3((n + STC_ROWS - 1) / STC_ROWS, tokens), STC_THREADS, STC_SMEM, s>>>(maps, a, status);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

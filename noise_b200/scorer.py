@@ -48,15 +48,22 @@ def stats_kernel(delta, X, SQX, DB, ST, start, n, d_rows, eps):
 
 
 def staged_kernel(UP, ST, R0, VC, GZ, VE, CS, SN, U, W, M1, M2, QD, GD, AD, CD, VT, OT, out, SE, start, n, se_rows,
-                  gated, diag, self_edge, nc):
-    """out [m, n] (and SE [m, se_rows, 512] bf16 with self_edge), written in place; m = out.shape[0]."""
+                  gated, diag, self_edge, nc, tc=True):
+    """out [m, n] (and SE [m, se_rows, 512] bf16 with self_edge), written in place; m = out.shape[0]. tc=True: the
+    moment-table terms on tcgen05 (returns the workspace, whose first int is the device status); tc=False: all on
+    the CUDA cores (returns None)."""
     tab = _tables(U, W, M1, M2, QD, GD, AD, CD, VT if self_edge else None, OT if self_edge else None)
     _lib.require_cuda(UP, ST, R0, VC, CS, SN, out)
-    _lib.check(_lib.lib().noise_readout_staged(
-        UP.data_ptr(), ST.data_ptr(), R0.data_ptr(), VC.data_ptr(), _p(GZ) if gated else None,
-        _p(VE) if gated else None, CS.data_ptr(), SN.data_ptr(), ctypes.byref(tab), out.data_ptr(),
-        _p(SE) if self_edge else None, int(start), int(n), int(se_rows), out.shape[0], int(nc), int(bool(diag)),
-        _lib.stream_handle(out.device)), 'noise_readout_staged')
+    args = (UP.data_ptr(), ST.data_ptr(), R0.data_ptr(), VC.data_ptr(), _p(GZ) if gated else None,
+            _p(VE) if gated else None, CS.data_ptr(), SN.data_ptr(), ctypes.byref(tab), out.data_ptr(),
+            _p(SE) if self_edge else None, int(start), int(n), int(se_rows), out.shape[0], int(nc), int(bool(diag)))
+    if not tc:
+        _lib.check(_lib.lib().noise_readout_staged(*args, _lib.stream_handle(out.device)), 'noise_readout_staged')
+        return None
+    ws = torch.empty(_lib.STATUS_BYTES, dtype=torch.uint8, device=out.device)
+    _lib.check(_lib.lib().noise_readout_staged_ws(*args, ws.data_ptr(), _lib.STATUS_BYTES,
+                                                  _lib.stream_handle(out.device)), 'noise_readout_staged_ws')
+    return ws
 
 
 def readout_kernel(PJ, R0, CS, SN, GC, VE, U, W, M1, M2, QD, GD, AD, CD, VT, OT, out, SE, start, probes, gated, diag,

@@ -79,3 +79,29 @@ def test_variants_against_oracle(gated, diag, self_edge):
         assert _se_ok(se_s[:, :x['n']], ref_se.float().bfloat16()) and _se_ok(se_d, ref_dse.float().bfloat16())
     else:
         assert not se_s.float().abs().sum() and not se_d.float().abs().sum()  # nothing written
+
+
+@pytest.mark.parametrize('gated,diag,self_edge', [(True, True, True), (False, False, False)])
+def test_staged_tc_matches_cuda_cores(gated, diag, self_edge):
+    """The tcgen05 staged kernel (bf16(dk) M1 / M2 as MMAs over 128 rows of a token) against the all-CUDA-core one on
+    three blocks a token, the last partial; the self-edge comes from the same arithmetic, so within one rounding."""
+    from noise_b200 import _lib, scorer
+    x = scorer_inputs(T=64, start=5, m=4, n=300, d_rows=300, seed=9)
+    m, n, start, nc = x['m'], x['n'], x['start'], x['nc']
+    d = _dev(x)
+    db = torch.empty(m, n, 512, dtype=torch.bfloat16, device=DEV)
+    st = torch.empty(m, n, 2, device=DEV)
+    scorer.stats_kernel(d['delta'], d['X'], d['SQX'], db, st, start, n, x['d_rows'], x['eps'])
+    outs, ses = [], []
+    for tc in (True, False):
+        out = torch.full((m, n), float('nan'), device=DEV)
+        se = torch.zeros(m, n, 512, dtype=torch.bfloat16, device=DEV)
+        ws = scorer.staged_kernel(d['UP'], st, d['R0'], d['VC'], d['GZ'], d['VE'], d['CS'], d['SN'], *tables(d), out,
+                                  se, start, n, n, gated, diag, self_edge, nc, tc=tc)
+        if tc:
+            assert _lib.read_status(ws) == 0
+        outs.append(out.cpu())
+        ses.append(se.cpu())
+    assert torch.isfinite(outs[0]).all()
+    assert _rel(outs[0], outs[1]) < REL
+    assert _se_ok(ses[0], ses[1]) if self_edge else not ses[0].float().abs().sum()
