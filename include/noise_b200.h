@@ -542,6 +542,15 @@ int noise_readout_direct(const float* pj, const float* r0, const float* cs, int6
                          const float* gc, const float* ve, const noise_scorer_tables_t* tab, float* out, void* se,
                          int start, int probes, int tokens, int diag, void* stream);
 
+/* noise_readout_direct with the moment-table terms on tcgen05 (as noise_readout_staged_ws: bf16(dk) M1 / M2 as
+ * kind::f16 MMAs over 128 probes of a token, run.py:5952-5953) and a workspace of at least NOISE_STATUS_BYTES
+ * (256-byte aligned; first int32 the device status). Same arguments and results. */
+int noise_readout_direct_ws(const float* pj, const float* r0, const float* cs, int64_t cs_token_stride,
+                            int64_t cs_pair_stride, const float* sn, int64_t sn_token_stride, int64_t sn_pair_stride,
+                            const float* gc, const float* ve, const noise_scorer_tables_t* tab, float* out, void* se,
+                            int start, int probes, int tokens, int diag, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * The identity phase's readout cycle (reference train/speedrun/run.py:3569-3686), width 512, vocabulary 4096,
  * softcap 15. The GEMMs between these kernels (x W, h W, x h^T, fg1 c^T in fp32; fast_k c^p^T in bf16; the final

@@ -385,10 +385,38 @@ int noise_readout_staged_ws(const void* up, const float* st, const float* r0, co
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = static_cast<int*>(workspace);
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
-  auto kernel = gated ? (self ? staged_tc_kernel<true, true> : staged_tc_kernel<true, false>)
-                      : (self ? staged_tc_kernel<false, true> : staged_tc_kernel<false, false>);
+  auto kernel = gated ? (self ? staged_tc_kernel<true, true, StagedArgs> : staged_tc_kernel<true, false, StagedArgs>)
+                      : (self ? staged_tc_kernel<false, true, StagedArgs> : staged_tc_kernel<false, false, StagedArgs>);
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, STC_SMEM)) return NOISE_ERR_CUDA;
   kernel<<<dim3((n + STC_ROWS - 1) / STC_ROWS, tokens), STC_THREADS, STC_SMEM, s>>>(maps, a, status);
+  return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
+}
+
+int noise_readout_direct_ws(const float* pj, const float* r0, const float* cs, int64_t cs_token_stride,
+                            int64_t cs_pair_stride, const float* sn, int64_t sn_token_stride, int64_t sn_pair_stride,
+                            const float* gc, const float* ve, const noise_scorer_tables_t* tab, float* out, void* se,
+                            int start, int probes, int tokens, int diag, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (!pj || !r0 || !cs || !sn || !tab || !out) return NOISE_ERR_ARGUMENT;
+  const bool gated = gc != nullptr, self = se != nullptr;
+  if ((gated && !ve) || !tables_ok(*tab, self)) return NOISE_ERR_ARGUMENT;
+  if (probes < 0 || tokens < 0 || start < 0) return NOISE_ERR_SHAPE;
+  if (!workspace || workspace_bytes < NOISE_STATUS_BYTES) return NOISE_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return NOISE_ERR_ALIGN;
+  if (probes == 0 || tokens == 0) return NOISE_OK;
+  DirectArgs a{pj, r0, cs, sn, cs_token_stride, cs_pair_stride, sn_token_stride, sn_pair_stride, gc, ve, tables(*tab),
+               out, static_cast<__nv_bfloat16*>(se), start, probes, diag};
+  StcMaps maps;
+  const uint64_t rows = static_cast<uint64_t>(start + tokens) * H * D;
+  int rc;
+  if ((rc = stc_map(&maps.m1, tab->M1, rows)) || (rc = stc_map(&maps.m2, tab->M2, rows))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  auto kernel = gated ? (self ? staged_tc_kernel<true, true, DirectArgs> : staged_tc_kernel<true, false, DirectArgs>)
+                      : (self ? staged_tc_kernel<false, true, DirectArgs> : staged_tc_kernel<false, false, DirectArgs>);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, STC_SMEM)) return NOISE_ERR_CUDA;
+  kernel<<<dim3((probes + STC_ROWS - 1) / STC_ROWS, tokens), STC_THREADS, STC_SMEM, s>>>(maps, a, status);
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 

@@ -1,16 +1,17 @@
-// The true-path readout scorer's staged_kernel (reference train/val/run.py :5985-6040) with its moment-table terms on
-// tcgen05: per head, bf16(dk) M1 and bf16(dk) M2 for a block's 128 rows are kind::f16 MMAs (M = 128 rows, N = 64,
+// The true-path readout scorer's staged_kernel (reference train/val/run.py :5985-6040) and readout_kernel
+// (:5906-5965) with their moment-table terms on tcgen05: per head, bf16(dk) M1 and bf16(dk) M2 for a block's 128 rows are kind::f16 MMAs (M = 128 rows, N = 64,
 // K = 64; the reference's tl.dot of the same bf16 operands, fp32 accumulation), and each row's dot of those rows with
 // its fp32 dk / dv is one thread's sum over a TMEM row. Everything else (dk, dv from the bf16 projection, the RMS norm
 // and RoPE, the exact receiver, the self-edge, dk . U / 8 + dv . W) stays head_change's warp-per-row arithmetic.
 //
-// A block is 128 rows of one token (two blocks per SM), 8 warps. Per head h:
+// A block is 128 rows (moves or probes) of one token (two blocks per SM), 8 warps. Per head h:
 //   warp phase   warp w takes rows w, w + 8, ..: head_change, then bf16(dk) into the 128-byte-swizzled K-major A tile
-//                and fp32 dk, dv into padded rows of shared memory (zero for rows past n);
+//                and fp32 dk, dv into padded rows of shared memory (zero for rows past the token's count);
 //   MMAs         thread 0: D1 = A M1, D2 = A M2 into TMEM (tables M1, M2 of (t, h) by TMA as the MN-major B
 //                operands), committed to an mbarrier; then the next head's tables;
 //   TMEM phase   warp w: TMEM lane quarter w % 4; warps 0..3 sum D1 . dk, warps 4..7 D2 . dv over their rows.
 #pragma once
+#include <type_traits>
 
 namespace noise {
 namespace scorer {
@@ -29,9 +30,12 @@ struct StcMaps {
   CUtensorMap m1, m2;  // bf16 [T * H * 64, 64], 64 x 64 boxes, 128-byte swizzle
 };
 
-template <bool GATED, bool SELF>
+// Args = StagedArgs (staged_kernel: the change from the bf16 projection of the raw move and the stats pass) or
+// DirectArgs (readout_kernel, run.py:5906-5965: from the projected change itself, per-chunk r0 / ve / cos / sin rows)
+template <bool GATED, bool SELF, class Args>
 __global__ void __launch_bounds__(STC_THREADS, 2)
-    staged_tc_kernel(const __grid_constant__ StcMaps maps, const __grid_constant__ StagedArgs a, int* status) {
+    staged_tc_kernel(const __grid_constant__ StcMaps maps, const __grid_constant__ Args a, int* status) {
+  constexpr bool DIRECT = std::is_same<Args, DirectArgs>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* sdk = reinterpret_cast<float*>(smem + STC_DK);
@@ -49,6 +53,9 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
   const int t = blockIdx.y, p0 = blockIdx.x * STC_ROWS;
   const int tok = a.start + t;
   const uint32_t sbase = smem_u32(smem);
+  int nrows;
+  if constexpr (DIRECT) nrows = a.P;
+  else nrows = a.n;
 
   if (threadIdx.x == 0) {
     mbar_init(tb_full, 1);
@@ -59,23 +66,25 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
     tmem_alloc(tmem_holder, 128);
     tmem_relinquish();
   }
-  // per row: the stats pass's inverse RMS and coefficient, the gate change per head (GATED)
+  // per row (staged): the stats pass's inverse RMS and coefficient, the gate change per head (GATED)
   for (int k = 0; k < STC_ROWS / 8; ++k) {
     const int rl = wib + 8 * k, p = p0 + rl;
-    const bool live = p < a.n;
-    const float iv = live ? a.st[(static_cast<int64_t>(t) * a.n + p) * 2] : 1.f;
-    const float cf = live ? a.st[(static_cast<int64_t>(t) * a.n + p) * 2 + 1] : 0.f;
-    if (lane == 0) {
-      sinv[rl] = iv;
-      scoef[rl] = cf;
-      stot[rl] = 0.f;
-    }
-    if constexpr (GATED) {  // gate change per head: 2 (sigmoid(gz + inv ug + coef gz) - sigmoid(gz))
-      if (lane < H) {
-        const float gz = a.gz[static_cast<int64_t>(tok) * H + lane];
-        const float ug = live ? bf(a.up, (static_cast<int64_t>(t) * a.n + p) * a.nc + 2 * W + lane) : 0.f;
-        const float z = gz + iv * ug + cf * gz;
-        sgc[rl * H + lane] = 2.f * (1.f / (1.f + __expf(-z)) - 1.f / (1.f + __expf(-gz)));
+    if (lane == 0) stot[rl] = 0.f;
+    if constexpr (!DIRECT) {
+      const bool live = p < a.n;
+      const float iv = live ? a.st[(static_cast<int64_t>(t) * a.n + p) * 2] : 1.f;
+      const float cf = live ? a.st[(static_cast<int64_t>(t) * a.n + p) * 2 + 1] : 0.f;
+      if (lane == 0) {
+        sinv[rl] = iv;
+        scoef[rl] = cf;
+      }
+      if constexpr (GATED) {  // gate change per head: 2 (sigmoid(gz + inv ug + coef gz) - sigmoid(gz))
+        if (lane < H) {
+          const float gz = a.gz[static_cast<int64_t>(tok) * H + lane];
+          const float ug = live ? bf(a.up, (static_cast<int64_t>(t) * a.n + p) * a.nc + 2 * W + lane) : 0.f;
+          const float z = gz + iv * ug + cf * gz;
+          sgc[rl * H + lane] = 2.f * (1.f / (1.f + __expf(-z)) - 1.f / (1.f + __expf(-gz)));
+        }
       }
     }
   }
@@ -92,38 +101,63 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
     tma_load_2d(smem + STC_TB, &maps.m1, tb_full, 0, tok * H * D);
     tma_load_2d(smem + STC_TB + D * D * 2, &maps.m2, tb_full, 0, tok * H * D);
   }
-  const float c = a.cs[static_cast<int64_t>(tok) * (D / 2) + lane], s = a.sn[static_cast<int64_t>(tok) * (D / 2) + lane];
+  float c, s;
+  if constexpr (DIRECT) {
+    c = a.cs[t * a.csm + lane * a.csf];
+    s = a.sn[t * a.snm + lane * a.snf];
+  } else {
+    c = a.cs[static_cast<int64_t>(tok) * (D / 2) + lane];
+    s = a.sn[static_cast<int64_t>(tok) * (D / 2) + lane];
+  }
   bool ok = true;
   for (int h = 0; h < H; ++h) {
     const int64_t row = static_cast<int64_t>(tok) * H + h;
-    const float r00 = a.r0[row * D + lane], r01 = a.r0[row * D + lane + 32];
-    const float vc0 = a.vc[static_cast<int64_t>(tok) * W + h * D + lane];
-    const float vc1 = a.vc[static_cast<int64_t>(tok) * W + h * D + lane + 32];
+    // the clean rotated key (and, gated, the value embedding): global token rows (staged) or chunk rows (direct)
+    const int64_t kr = DIRECT ? (static_cast<int64_t>(t) * H + h) * D : row * D;
+    const float r00 = a.r0[kr + lane], r01 = a.r0[kr + lane + 32];
+    float vc0 = 0.f, vc1 = 0.f;
+    if constexpr (!DIRECT) {
+      vc0 = a.vc[static_cast<int64_t>(tok) * W + h * D + lane];
+      vc1 = a.vc[static_cast<int64_t>(tok) * W + h * D + lane + 32];
+    }
     float ve0 = 0.f, ve1 = 0.f;
     if constexpr (GATED) {
-      ve0 = a.ve[row * D + lane];
-      ve1 = a.ve[row * D + lane + 32];
+      ve0 = a.ve[kr + lane];
+      ve1 = a.ve[kr + lane + 32];
     }
     // warp phase: head_change per row, bf16(dk) into A (element (r, f) at r * 128 + ((f / 8) ^ (r % 8)) * 16 + (f % 8) * 2)
 #pragma unroll 1
     for (int k = 0; k < STC_ROWS / 8; ++k) {
       const int rl = wib + 8 * k, p = p0 + rl;
       float dk0 = 0.f, dk1 = 0.f, dv0 = 0.f, dv1 = 0.f;
-      if (p < a.n) {
-        const float iv = sinv[rl], cf = scoef[rl];
-        const int64_t ur = (static_cast<int64_t>(t) * a.n + p) * a.nc;
-        const float uk0 = bf(a.up, ur + h * D + lane), uk1 = bf(a.up, ur + h * D + lane + 32);
-        const float uv0 = bf(a.up, ur + W + h * D + lane), uv1 = bf(a.up, ur + W + h * D + lane + 32);
-        const float dr0 = iv * (uk0 * c + uk1 * s) + cf * r00;
-        const float dr1 = iv * (uk1 * c - uk0 * s) + cf * r01;
-        dv0 = iv * uv0 + cf * vc0;
-        dv1 = iv * uv1 + cf * vc1;
+      if (p < nrows) {
+        float dr0, dr1, gc = 0.f;
+        __nv_bfloat16* se_row = nullptr;
+        if constexpr (DIRECT) {
+          const int64_t base = ((static_cast<int64_t>(t) * a.P + p) * 2 * H + h) * D;
+          const float pk0 = a.pj[base + lane], pk1 = a.pj[base + lane + 32];
+          dr0 = pk0 * c + pk1 * s;
+          dr1 = -pk0 * s + pk1 * c;
+          dv0 = a.pj[base + H * D + lane];
+          dv1 = a.pj[base + H * D + lane + 32];
+          if constexpr (GATED) gc = a.gc[(static_cast<int64_t>(t) * a.P + p) * H + h];
+          if constexpr (SELF) se_row = a.se + (static_cast<int64_t>(t) * a.P + p) * W + h * D;
+        } else {
+          const float iv = sinv[rl], cf = scoef[rl];
+          const int64_t ur = (static_cast<int64_t>(t) * a.n + p) * a.nc;
+          const float uk0 = bf(a.up, ur + h * D + lane), uk1 = bf(a.up, ur + h * D + lane + 32);
+          const float uv0 = bf(a.up, ur + W + h * D + lane), uv1 = bf(a.up, ur + W + h * D + lane + 32);
+          dr0 = iv * (uk0 * c + uk1 * s) + cf * r00;
+          dr1 = iv * (uk1 * c - uk0 * s) + cf * r01;
+          dv0 = iv * uv0 + cf * vc0;
+          dv1 = iv * uv1 + cf * vc1;
+          if constexpr (GATED) gc = sgc[rl * H + h];
+          if constexpr (SELF) se_row = a.se + (static_cast<int64_t>(t) * a.se_rows + p) * W + h * D;
+        }
         if constexpr (GATED) {
-          const float gc = sgc[rl * H + h];
           dv0 += gc * ve0;
           dv1 += gc * ve1;
         }
-        __nv_bfloat16* se_row = SELF ? a.se + (static_cast<int64_t>(t) * a.se_rows + p) * W + h * D : nullptr;
         const float part = head_change<SELF>(dr0, dr1, dv0, dv1, r00, r01, a.tab, row, lane, a.diag, se_row, dk0, dk1);
         if (lane == 0) stot[rl] += part;
       }
@@ -193,8 +227,9 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
   }
   if (threadIdx.x < STC_ROWS && ok) {
     const int p = p0 + threadIdx.x;
-    if (p < a.n)
-      a.out[static_cast<int64_t>(t) * a.n + p] = stot[threadIdx.x] + sq1[threadIdx.x] * (1.f / D) + sq2[threadIdx.x] * 0.125f;
+    if (p < nrows)
+      a.out[static_cast<int64_t>(t) * nrows + p] =
+          stot[threadIdx.x] + sq1[threadIdx.x] * (1.f / D) + sq2[threadIdx.x] * 0.125f;
   }
   __syncthreads();
   if (wib == 0) {

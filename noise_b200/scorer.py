@@ -67,13 +67,21 @@ def staged_kernel(UP, ST, R0, VC, GZ, VE, CS, SN, U, W, M1, M2, QD, GD, AD, CD, 
 
 
 def readout_kernel(PJ, R0, CS, SN, GC, VE, U, W, M1, M2, QD, GD, AD, CD, VT, OT, out, SE, start, probes, gated, diag,
-                   self_edge):
-    """out [m, probes] (and SE [m, probes, 512] bf16 with self_edge), written in place; m = out.shape[0]."""
+                   self_edge, tc=True):
+    """out [m, probes] (and SE [m, probes, 512] bf16 with self_edge), written in place; m = out.shape[0]. tc=True: the
+    moment-table terms on tcgen05 (returns the workspace, whose first int is the device status); tc=False: all on the
+    CUDA cores (returns None)."""
     tab = _tables(U, W, M1, M2, QD, GD, AD, CD, VT if self_edge else None, OT if self_edge else None)
     PJ, R0 = PJ.contiguous(), R0.contiguous()
     _lib.require_cuda(PJ, R0, CS, SN, out)
-    _lib.check(_lib.lib().noise_readout_direct(
-        PJ.data_ptr(), R0.data_ptr(), CS.data_ptr(), CS.stride(0), CS.stride(1), SN.data_ptr(), SN.stride(0),
-        SN.stride(1), _p(GC.contiguous()) if gated else None, _p(VE.contiguous()) if gated else None,
-        ctypes.byref(tab), out.data_ptr(), _p(SE) if self_edge else None, int(start), int(probes), out.shape[0],
-        int(bool(diag)), _lib.stream_handle(out.device)), 'noise_readout_direct')
+    args = (PJ.data_ptr(), R0.data_ptr(), CS.data_ptr(), CS.stride(0), CS.stride(1), SN.data_ptr(), SN.stride(0),
+            SN.stride(1), _p(GC.contiguous()) if gated else None, _p(VE.contiguous()) if gated else None,
+            ctypes.byref(tab), out.data_ptr(), _p(SE) if self_edge else None, int(start), int(probes), out.shape[0],
+            int(bool(diag)))
+    if not tc:
+        _lib.check(_lib.lib().noise_readout_direct(*args, _lib.stream_handle(out.device)), 'noise_readout_direct')
+        return None
+    ws = torch.empty(_lib.STATUS_BYTES, dtype=torch.uint8, device=out.device)
+    _lib.check(_lib.lib().noise_readout_direct_ws(*args, ws.data_ptr(), _lib.STATUS_BYTES,
+                                                  _lib.stream_handle(out.device)), 'noise_readout_direct_ws')
+    return ws

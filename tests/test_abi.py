@@ -162,6 +162,8 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_readout_stats(fake, fake, fake, fake, fake, 0, 8, 4, 2, 1e-7, None) == 1    # d_rows < n
     assert L.noise_readout_stats(fake + 4, fake, fake, fake, fake, 0, 8, 8, 2, 1e-7, None) == 2
     assert L.noise_readout_staged_ws(*([fake] * 8), None, fake, None, 0, 4, 4, 2, 1040, 1, fake, 256, None) == 4
+    assert L.noise_readout_direct_ws(fake, fake, fake, 1, 1, fake, 1, 1, None, None, None, fake, None, 0, 4, 2, 1, fake,
+                                     256, None) == 4
     tab = _lib.ScorerTables()
     assert L.noise_readout_staged(fake, fake, fake, fake, None, None, fake, fake, ctypes.byref(tab), fake, None,
                                   0, 8, 8, 2, 1040, 1, None) == 4                              # tables missing

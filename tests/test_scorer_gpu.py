@@ -105,3 +105,26 @@ def test_staged_tc_matches_cuda_cores(gated, diag, self_edge):
     assert torch.isfinite(outs[0]).all()
     assert _rel(outs[0], outs[1]) < REL
     assert _se_ok(ses[0], ses[1]) if self_edge else not ses[0].float().abs().sum()
+
+
+@pytest.mark.parametrize('gated,diag,self_edge', [(True, True, True), (False, True, False)])
+def test_direct_tc_matches_cuda_cores(gated, diag, self_edge):
+    """The tcgen05 direct (readout_kernel) path against the all-CUDA-core one on three 128-probe blocks a token."""
+    from noise_b200 import _lib, scorer
+    x = scorer_inputs(T=64, start=5, m=4, n=300, d_rows=300, seed=19)
+    m, n, start = x['m'], x['n'], x['start']
+    d = _dev(x)
+    tok = slice(start, start + m)
+    outs, ses = [], []
+    for tc in (True, False):
+        out = torch.full((m, n), float('nan'), device=DEV)
+        se = torch.zeros(m, n, 512, dtype=torch.bfloat16, device=DEV)
+        ws = scorer.readout_kernel(d['PJ'], d['R0'][tok], d['CS'][tok], d['SN'][tok], d['GC'], d['VE'][tok],
+                                   *tables(d), out, se, start, n, gated, diag, self_edge, tc=tc)
+        if tc:
+            assert _lib.read_status(ws) == 0
+        outs.append(out.cpu())
+        ses.append(se.cpu())
+    assert torch.isfinite(outs[0]).all()
+    assert _rel(outs[0], outs[1]) < REL
+    assert _se_ok(ses[0], ses[1]) if self_edge else not ses[0].float().abs().sum()
