@@ -100,34 +100,60 @@ struct DirectArgs {
   int start, P, diag;
 };
 
+// A lane's values of the per-(token, head) tables that every row of the token reads: its two features of QD, GD, U,
+// W (and, SELF, VT - OT) and the scalars AD, CD.
+struct HeadVals {
+  float qd0, qd1, gd0, gd1, u0, u1, w0, w1, vo0, vo1, ad, cd;
+};
+
+template <bool SELF>
+__device__ __forceinline__ HeadVals head_vals(const Tables& tb, int64_t row, int lane) {
+  const int64_t v = row * D;
+  HeadVals hv;
+  hv.qd0 = tb.QD[v + lane], hv.qd1 = tb.QD[v + lane + 32];
+  hv.gd0 = tb.GD[v + lane], hv.gd1 = tb.GD[v + lane + 32];
+  hv.u0 = tb.U[v + lane], hv.u1 = tb.U[v + lane + 32];
+  hv.w0 = tb.WV[v + lane], hv.w1 = tb.WV[v + lane + 32];
+  hv.vo0 = SELF ? tb.VT[v + lane] - tb.OT[v + lane] : 0.f;
+  hv.vo1 = SELF ? tb.VT[v + lane + 32] - tb.OT[v + lane + 32] : 0.f;
+  hv.ad = tb.AD[row], hv.cd = tb.CD[row];
+  return hv;
+}
+
 // One head of one row: dr, dv (the lane's two features), the clean rotated key r0 -> the change dk of the rotated,
 // RMS-normed key (the lane's features in dk0, dk1) and the row's score part without the moment tables: the exact
 // receiver s = t (DIAG), the self-edge (SELF, written) and dk . U / 8 + dv . W (every lane holds the sum).
 template <bool SELF>
-__device__ __forceinline__ float head_change(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
-                                             const Tables& tb, int64_t row, int lane, int diag,
-                                             __nv_bfloat16* se_row, float& dk0, float& dk1) {
+__device__ __forceinline__ float head_change_v(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
+                                               const HeadVals& hv, int lane, int diag, __nv_bfloat16* se_row,
+                                               float& dk0, float& dk1) {
   const float square = warp_sum(r00 * r00 + r01 * r01);
   const float grow = warp_sum(2.f * (r00 * dr0 + r01 * dr1) + dr0 * dr0 + dr1 * dr1) / D;
   const float inverse = rsqrtf(square / D + NEPS), moved = rsqrtf(square / D + grow + NEPS);
   const float shrink = grow * (inverse * moved) * (inverse * moved) / (inverse + moved);
   dk0 = dr0 * moved - r00 * shrink;
   dk1 = dr1 * moved - r01 * shrink;
-  const int64_t v = row * D;
   float total = 0.f;
   if (diag || SELF) {  // the receiver s = t, exactly
-    const float x = warp_sum(dk0 * tb.QD[v + lane] + dk1 * tb.QD[v + lane + 32]) * 0.125f;
-    const float a = tb.AD[row], e = expm1f(x);
+    const float x = warp_sum(dk0 * hv.qd0 + dk1 * hv.qd1) * 0.125f;
+    const float a = hv.ad, e = expm1f(x);
     const float gain = a * e / (1.f + a * e), vgain = (a + a * e) / (1.f + a * e);
-    if (diag) total += gain * tb.CD[row] + vgain * warp_sum(dv0 * tb.GD[v + lane] + dv1 * tb.GD[v + lane + 32]);
+    if (diag) total += gain * hv.cd + vgain * warp_sum(dv0 * hv.gd0 + dv1 * hv.gd1);
     if (SELF) {
-      se_row[lane] = __float2bfloat16_rn(gain * (tb.VT[v + lane] - tb.OT[v + lane]) + vgain * dv0);
-      se_row[lane + 32] = __float2bfloat16_rn(gain * (tb.VT[v + lane + 32] - tb.OT[v + lane + 32]) + vgain * dv1);
+      se_row[lane] = __float2bfloat16_rn(gain * hv.vo0 + vgain * dv0);
+      se_row[lane + 32] = __float2bfloat16_rn(gain * hv.vo1 + vgain * dv1);
     }
   }
-  total += warp_sum((dk0 * tb.U[v + lane] + dk1 * tb.U[v + lane + 32]) * 0.125f + dv0 * tb.WV[v + lane] +
-                    dv1 * tb.WV[v + lane + 32]);
+  total += warp_sum((dk0 * hv.u0 + dk1 * hv.u1) * 0.125f + dv0 * hv.w0 + dv1 * hv.w1);
   return total;
+}
+
+template <bool SELF>
+__device__ __forceinline__ float head_change(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
+                                             const Tables& tb, int64_t row, int lane, int diag,
+                                             __nv_bfloat16* se_row, float& dk0, float& dk1) {
+  return head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, head_vals<SELF>(tb, row, lane), lane, diag, se_row, dk0,
+                             dk1);
 }
 
 // head_change plus the moment tables on the CUDA cores: bf16(dk) M1 dk / 64 + bf16(dk) M2 dv / 8, the lane forming

@@ -125,32 +125,46 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
       ve0 = a.ve[kr + lane];
       ve1 = a.ve[kr + lane + 32];
     }
+    const HeadVals hv = head_vals<SELF>(a.tab, row, lane);  // the head's table values, once for all its rows
     // warp phase: head_change per row, bf16(dk) into A (element (r, f) at r * 128 + ((f / 8) ^ (r % 8)) * 16 + (f % 8) * 2)
+    // a row's four raw inputs (the lane's key and value features), loaded one row ahead of their use
+    float in0 = 0.f, in1 = 0.f, in2 = 0.f, in3 = 0.f;
+    auto load_in = [&](int k) {
+      const int p = p0 + wib + 8 * k;
+      if (p >= nrows) return;
+      if constexpr (DIRECT) {
+        const int64_t base = ((static_cast<int64_t>(t) * a.P + p) * 2 * H + h) * D;
+        in0 = a.pj[base + lane], in1 = a.pj[base + lane + 32];
+        in2 = a.pj[base + H * D + lane], in3 = a.pj[base + H * D + lane + 32];
+      } else {
+        const int64_t ur = (static_cast<int64_t>(t) * a.n + p) * a.nc;
+        in0 = bf(a.up, ur + h * D + lane), in1 = bf(a.up, ur + h * D + lane + 32);
+        in2 = bf(a.up, ur + W + h * D + lane), in3 = bf(a.up, ur + W + h * D + lane + 32);
+      }
+    };
+    load_in(0);
 #pragma unroll 1
     for (int k = 0; k < STC_ROWS / 8; ++k) {
       const int rl = wib + 8 * k, p = p0 + rl;
+      const float x0 = in0, x1 = in1, x2 = in2, x3 = in3;
+      if (k + 1 < STC_ROWS / 8) load_in(k + 1);
       float dk0 = 0.f, dk1 = 0.f, dv0 = 0.f, dv1 = 0.f;
       if (p < nrows) {
         float dr0, dr1, gc = 0.f;
         __nv_bfloat16* se_row = nullptr;
         if constexpr (DIRECT) {
-          const int64_t base = ((static_cast<int64_t>(t) * a.P + p) * 2 * H + h) * D;
-          const float pk0 = a.pj[base + lane], pk1 = a.pj[base + lane + 32];
-          dr0 = pk0 * c + pk1 * s;
-          dr1 = -pk0 * s + pk1 * c;
-          dv0 = a.pj[base + H * D + lane];
-          dv1 = a.pj[base + H * D + lane + 32];
+          dr0 = x0 * c + x1 * s;
+          dr1 = -x0 * s + x1 * c;
+          dv0 = x2;
+          dv1 = x3;
           if constexpr (GATED) gc = a.gc[(static_cast<int64_t>(t) * a.P + p) * H + h];
           if constexpr (SELF) se_row = a.se + (static_cast<int64_t>(t) * a.P + p) * W + h * D;
         } else {
           const float iv = sinv[rl], cf = scoef[rl];
-          const int64_t ur = (static_cast<int64_t>(t) * a.n + p) * a.nc;
-          const float uk0 = bf(a.up, ur + h * D + lane), uk1 = bf(a.up, ur + h * D + lane + 32);
-          const float uv0 = bf(a.up, ur + W + h * D + lane), uv1 = bf(a.up, ur + W + h * D + lane + 32);
-          dr0 = iv * (uk0 * c + uk1 * s) + cf * r00;
-          dr1 = iv * (uk1 * c - uk0 * s) + cf * r01;
-          dv0 = iv * uv0 + cf * vc0;
-          dv1 = iv * uv1 + cf * vc1;
+          dr0 = iv * (x0 * c + x1 * s) + cf * r00;
+          dr1 = iv * (x1 * c - x0 * s) + cf * r01;
+          dv0 = iv * x2 + cf * vc0;
+          dv1 = iv * x3 + cf * vc1;
           if constexpr (GATED) gc = sgc[rl * H + h];
           if constexpr (SELF) se_row = a.se + (static_cast<int64_t>(t) * a.se_rows + p) * W + h * D;
         }
@@ -158,7 +172,7 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
           dv0 += gc * ve0;
           dv1 += gc * ve1;
         }
-        const float part = head_change<SELF>(dr0, dr1, dv0, dv1, r00, r01, a.tab, row, lane, a.diag, se_row, dk0, dk1);
+        const float part = head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, hv, lane, a.diag, se_row, dk0, dk1);
         if (lane == 0) stot[rl] += part;
       }
       const uint32_t arow = sbase + STC_A + rl * 128 + (lane & 7) * 2;
