@@ -461,7 +461,7 @@ int noise_expm1_f32(const float* x, float* out, int64_t n, void* stream);
 
 /* Bytes of the caller's workspace for noise_query_response_ws: a 256-byte status block, the keys and the transposed
  * values as tf32 hi / lo planes (fp32 [heads, Tp, 64] each, Tp = keys_len rounded up to 64) and one live flag per
- * (head, token, 64-key tile). 0 for any argument < 1. */
+ * (head, token, 64-key tile); 256 (the status block) when keys_len > 32,768. 0 for any argument < 1. */
 size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, int keys_len);
 
 /* noise_query_response on tcgen05 with a caller workspace (256-byte aligned, noise_query_response_workspace_bytes

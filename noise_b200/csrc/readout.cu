@@ -565,6 +565,7 @@ int noise_key_response_ws(const noise_view3_t* q, const float* dk, const noise_v
 
 size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, int keys_len) {
   if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1) return 0;
+  if (keys_len > QT_MAX_TILES * QT_KEYS) return 256;  // the CUDA-core kernel: the status word only
   return QtWorkspace(tokens, heads, keys_len).bytes();
 }
 
@@ -576,11 +577,15 @@ int noise_query_response_ws(const float* dq, const noise_view3_t* keys, const no
       !probabilities->data || !base->data)
     return NOISE_ERR_ARGUMENT;
   if (tokens < 1 || probes < 1 || heads < 1 || keys_len < 1) return NOISE_ERR_SHAPE;
-  if (keys_len > QT_MAX_TILES * QT_KEYS)  // longer than the live-tile list holds: the CUDA-core kernel
-    return noise_query_response(dq, keys, values, probabilities, base, tokens, probes, heads, keys_len, out, stream);
   const QtWorkspace w(tokens, heads, keys_len);
-  if (!workspace || workspace_bytes < w.bytes()) return NOISE_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < noise_query_response_workspace_bytes(tokens, probes, heads, keys_len))
+    return NOISE_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !a16(dq) || !a16(out)) return NOISE_ERR_ALIGN;
+  if (keys_len > QT_MAX_TILES * QT_KEYS) {  // longer than the live-tile list holds: the CUDA-core kernel
+    if (cudaMemsetAsync(workspace, 0, sizeof(int), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return NOISE_ERR_CUDA;  // its status word reads 0: that kernel has no waits to give up
+    return noise_query_response(dq, keys, values, probabilities, base, tokens, probes, heads, keys_len, out, stream);
+  }
   const int64_t rows = static_cast<int64_t>(tokens) * probes;
   const int64_t items = (rows + QT_ROWS - 1) / QT_ROWS * heads;
   if (items > 0x7FFFFFFF) return NOISE_ERR_SHAPE;

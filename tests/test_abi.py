@@ -133,6 +133,7 @@ def test_rejects_bad_shapes_before_launch(L):
     assert qn == 256 + 4 * 8 * 2048 * 64 * 4 + 8 * 256 * 32                                   # planes + live flags
     assert L.noise_query_response_workspace_bytes(3, 5, 2, 100) == 256 + 4 * 2 * 128 * 64 * 4 + 256  # keys to 128
     assert L.noise_query_response_workspace_bytes(0, 64, 8, 2048) == 0
+    assert L.noise_query_response_workspace_bytes(2, 8, 2, 40000) == 256                     # CUDA-core fall-through
     assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 8, 2048, fake, fake, qn - 1, None) == 3  # workspace
     assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 8, 2048, fake, fake + 16, qn, None) == 2  # alignment
     assert L.noise_query_response_ws(fake + 4, r, r, r, r, 256, 64, 8, 2048, fake, fake, qn, None) == 2  # dq alignment

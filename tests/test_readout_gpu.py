@@ -150,6 +150,18 @@ def test_query_response_tc_shapes(m, p, t, dead):
     assert _rel(out, ref) < REL
 
 
+def test_query_response_ws_falls_through_past_32k_keys():
+    """More keys than the tcgen05 kernel's live-tile list holds: the _ws entry runs the CUDA-core kernel, with its
+    status word cleared and a status-only workspace."""
+    from noise_b200 import _lib
+    q = _query_case(2, 8, 1, 33000, 500, seed=77)
+    assert _lib.lib().noise_query_response_workspace_bytes(2, 8, 1, 33000) == 256
+    ref = oracle.query_response(q['dq'], q['keys'], q['values'], q['probabilities'], q['base'])
+    out = _query_tc(_dev(q))
+    assert _query_status(out) == 0
+    assert _rel(out, ref) < REL
+
+
 def test_query_response_tc_skips_dead_tiles_exactly():
     """A token whose probabilities are all zero gets exactly 0, even where e^(dq . k / 8) overflows (the reference
     skips its tiles; the dense form would give 0 * inf = nan), while the other token of its 128-row block is live."""
