@@ -889,6 +889,14 @@ using namespace noise::credit;
 
 namespace {
 
+// A _ws entry point that falls through to a kernel without bounded waits still leaves the caller's status word
+// reading 0, as its contract says.
+int fall_through_status(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < sizeof(int) || (reinterpret_cast<uintptr_t>(workspace) & 3)) return NOISE_OK;
+  return cudaMemsetAsync(workspace, 0, sizeof(int), static_cast<cudaStream_t>(stream)) == cudaSuccess ? NOISE_OK
+                                                                                                   : NOISE_ERR_CUDA;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 tv_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1001,8 +1009,10 @@ int noise_implicit_key_context_ws(const void* q, const void* k, const void* valu
                                   size_t workspace_bytes, void* stream) {
   if (!q || !k || !values || !hub || !lse || !center) return NOISE_ERR_ARGUMENT;
   if (dtype != NOISE_DTYPE_F32 && dtype != NOISE_DTYPE_BF16) return NOISE_ERR_ARGUMENT;
-  if (dtype != NOISE_DTYPE_BF16 || tokens % TC_B)  // fp32 operands (tf32 dots) or T % 128 != 0: the warp-MMA kernel
+  if (dtype != NOISE_DTYPE_BF16 || tokens % TC_B) {  // fp32 operands (tf32 dots) or T % 128 != 0: the warp-MMA kernel
+    if (const int rc = fall_through_status(workspace, workspace_bytes, stream)) return rc;
     return noise_implicit_key_context(q, k, values, hub, dtype, rows, tokens, window, lse, center, stream);
+  }
   if (rows < 1 || window < 0 || window % 64) return NOISE_ERR_SHAPE;
   if (!a16(q) || !a16(k) || !a16(values) || !a16(hub)) return NOISE_ERR_ALIGN;
   if (!workspace || workspace_bytes < NOISE_STATUS_BYTES) return NOISE_ERR_WORKSPACE;
@@ -1057,8 +1067,10 @@ int noise_value_pass_ws(const void* q, const void* k, int dtype, const float* ls
                         size_t workspace_bytes, void* stream) {
   if (!q || !k || !lse || !source || !out) return NOISE_ERR_ARGUMENT;
   if (dtype != NOISE_DTYPE_F32 && dtype != NOISE_DTYPE_BF16) return NOISE_ERR_ARGUMENT;
-  if (dtype != NOISE_DTYPE_BF16 || tokens % TV_B)  // fp32 operands or T % 128 != 0: the warp-MMA kernel
+  if (dtype != NOISE_DTYPE_BF16 || tokens % TV_B) {  // fp32 operands or T % 128 != 0: the warp-MMA kernel
+    if (const int rc = fall_through_status(workspace, workspace_bytes, stream)) return rc;
     return noise_value_pass(q, k, dtype, lse, source, out, rows, tokens, window, stream);
+  }
   if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
   if (!a16(q) || !a16(k) || !a16(lse) || !rows_ok(*source, true) || !rows_ok(*out, true)) return NOISE_ERR_ALIGN;
   if (!workspace || workspace_bytes < noise_value_pass_workspace_bytes(rows, tokens)) return NOISE_ERR_WORKSPACE;
@@ -1129,9 +1141,11 @@ int noise_key_scan_ws(const float* qp, const float* kp, const float* k_raw, cons
     return r.data && rows_ok(r, true) && r.block_rows == 0;
   };
   if (tokens % KM_B || !vec_ok(*key_out) || (with_values && !vec_ok(*value_out)) || !a16(cos) || !a16(sin) ||
-      !a16(lse) || !a16(center))
+      !a16(lse) || !a16(center)) {
+    if (const int rc = fall_through_status(workspace, workspace_bytes, stream)) return rc;
     return noise_key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, rows, tokens, window, sigma, key_out,
                           value_out, stream);
+  }
   if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
   if (!a16(qp) || !a16(kp) || !a16(values) || !a16(hub)) return NOISE_ERR_ALIGN;
   if (!workspace || workspace_bytes < noise_key_scan_workspace_bytes(rows, tokens)) return NOISE_ERR_WORKSPACE;
@@ -1253,9 +1267,11 @@ int noise_moment_key_scores_ws(const void* q, const void* k, const void* v, cons
     return r.data && a16(r.data) && (r.layer_stride * es) % 16 == 0 && (r.token_stride * es) % 16 == 0 &&
            (r.block_rows == 0 || (r.gpu_stride * es) % 16 == 0);
   };
-  if (tokens % KM_B || !vec_ok(*out) || !vec_ok(*values_out) || !a16(cos) || !a16(sin))
+  if (tokens % KM_B || !vec_ok(*out) || !vec_ok(*values_out) || !a16(cos) || !a16(sin)) {
+    if (const int rc = fall_through_status(workspace, workspace_bytes, stream)) return rc;
     return noise_moment_key_scores_v(q, k, v, hub, raw, raw_dtype, sq, side, cos, sin, lse, hub_out, steps, rows,
                                      tokens, out, values_out, out_dtype, stream);
+  }
   if (rows < 1) return NOISE_ERR_SHAPE;
   if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) || !a16(lse) || !a16(hub_out) ||
       !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) || !view_ok(*out, ob, false) ||
@@ -1374,9 +1390,11 @@ int noise_moment_query_scores_ws(const void* q, const void* k, const void* v, co
     return r.data && a16(r.data) && (r.layer_stride * es) % 16 == 0 && (r.token_stride * es) % 16 == 0 &&
            (r.block_rows == 0 || (r.gpu_stride * es) % 16 == 0);
   };
-  if (tokens % QM_B || !vec_ok(*out) || !a16(cos) || !a16(sin))
+  if (tokens % QM_B || !vec_ok(*out) || !a16(cos) || !a16(sin)) {
+    if (const int rc = fall_through_status(workspace, workspace_bytes, stream)) return rc;
     return noise_moment_query_scores_v(q, k, v, hub, raw, raw_dtype, sq, side, cos, sin, lse, hub_out, steps, rows,
                                        tokens, window, out, out_dtype, stream);
+  }
   if (rows < 1 || window < 0) return NOISE_ERR_SHAPE;
   if (!a16(q) || !a16(k) || !a16(v) || !a16(hub) || !a16(side) ||
       !view_ok(*raw, raw_dtype == NOISE_DTYPE_BF16, false) || !view_ok(*out, ob, false))

@@ -278,3 +278,21 @@ def test_query_moments_full_size(mk):
     from noise_b200 import _lib
     assert _lib.read_status(ws) == 0
     assert rel(out, wout) < 1e-2
+
+
+def test_ws_fall_through_leaves_status_zero():
+    """A _ws entry point that falls through to its warp-MMA kernel (here fp32 operands) still leaves its workspace's
+    status word 0, as the header promises: the word starts as 0xFFFFFFFF."""
+    import ctypes
+    from noise_b200 import _lib
+    dev = torch.device('cuda', 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    q, k, v, hub = (torch.randn(2, 128, 64, device=dev, generator=g) for _ in range(4))
+    lse, center = torch.empty(2, 128, device=dev), torch.empty(2, 128, device=dev)
+    ws = torch.full((_lib.STATUS_BYTES,), 255, dtype=torch.uint8, device=dev)
+    rc = _lib.lib().noise_implicit_key_context_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), hub.data_ptr(), 0, 2, 128,
+                                                  64, lse.data_ptr(), center.data_ptr(), ws.data_ptr(),
+                                                  ctypes.c_size_t(_lib.STATUS_BYTES), _lib.stream_handle(dev))
+    assert rc == 0
+    assert _lib.read_status(ws) == 0
+    assert torch.isfinite(lse).all() and torch.isfinite(center).all()
