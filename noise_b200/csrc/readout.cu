@@ -2,8 +2,10 @@
 // :1633-1750, noise_record::key_response and noise_record::routed_response :541-637, noise_record::
 // future_query_response :1780-1835) on sm_100a.
 //
-// All four are attention-like reductions of a finite change of one side of a softmax over head_dim 64, in fp32 (the
-// reference's tf32x3 dots are fp32-accurate; routed_response's dots are bf16 with bf16-rounded outputs, as there):
+// All four are attention-like reductions of a finite change of one side of a softmax over head_dim 64. Each has a
+// tcgen05 form (the *_ws entry points: query_tc.cuh, column_tc.cuh for future_scores / key_response, routed_tc.cuh;
+// the reference's tf32x3 dots as kind::tf32 MMAs, routed_response's bf16 dots as kind::f16 with bf16-rounded
+// outputs) and the fp32 CUDA-core form in this file (the entry points without a workspace):
 //   future_scores  out[h, p, m] = sum over receivers s with 0 < s - (start + m) <= window of
 //                  (a (e^x - 1) c + (a + a (e^x - 1)) g . dv) / (1 + a (e^x - 1)),  x = q_s . dk_pm / 8,
 //                  a = A[h, s, m], c = C[h, s, m], g = target_s;
@@ -13,8 +15,8 @@
 //                  change = P[h, m, k] (e^(dq_mph . k_k / 8) - 1);
 //   routed_response out[m, p, h] = bf16(w V) + (e^-dlse - 1) rest, w = bf16(p (e^(ds - dlse) - 1)),
 //                  ds = bf16(dq . k) / 8, dlse = log1p(sum_k p (e^ds - 1)) over the routed keys.
-// Each keeps its per-column (or per-probe) state in registers, stages the other side's tiles in shared memory, and
-// never materialises a [receiver x column] tensor.
+// The CUDA-core kernels keep their per-column (or per-probe) state in registers, stage the other side's tiles in
+// shared memory, and never materialise a [receiver x column] tensor.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

@@ -9,7 +9,7 @@
 // the exact receiver s = t, and (SELF) the token's own output change written as bf16.
 // Layout: one warp per row; lane l owns the features l and l + 32 (a rotary pair: each is the other's RoPE partner).
 // A block is 64 rows of one token; per head the token's M1, M2 (bf16 64 x 64) are staged in shared memory once for
-// all of them.
+// all of them. The *_ws entry points run the M1 / M2 terms on tcgen05 instead (staged_tc.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
