@@ -120,31 +120,54 @@ __device__ __forceinline__ HeadVals head_vals(const Tables& tb, int64_t row, int
   return hv;
 }
 
-// One head of one row: dr, dv (the lane's two features), the clean rotated key r0 -> the change dk of the rotated,
-// RMS-normed key (the lane's features in dk0, dk1) and the row's score part without the moment tables: the exact
-// receiver s = t (DIAG), the self-edge (SELF, written) and dk . U / 8 + dv . W (every lane holds the sum).
+// Three (or two) independent butterfly sums at once: the same sums as warp_sum, their shuffle chains interleaved.
+__device__ __forceinline__ void warp_sum3(float& a, float& b, float& c) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+  }
+}
+__device__ __forceinline__ void warp_sum2(float& a, float& b) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+}
+
+// One head of one row: dr, dv (the lane's two features), the clean rotated key r0 (and its square sum over the head,
+// the same for every row of the head) -> the change dk of the rotated, RMS-normed key (the lane's features in dk0,
+// dk1) and the row's score part without the moment tables: the exact receiver s = t (DIAG), the self-edge (SELF,
+// written) and dk . U / 8 + dv . W (every lane holds the sum). Two rounds of reductions: the growth and both dv dots
+// together, then both dk dots.
 template <bool SELF>
 __device__ __forceinline__ float head_change_v(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
-                                               const HeadVals& hv, int lane, int diag, __nv_bfloat16* se_row,
-                                               float& dk0, float& dk1) {
-  const float square = warp_sum(r00 * r00 + r01 * r01);
-  const float grow = warp_sum(2.f * (r00 * dr0 + r01 * dr1) + dr0 * dr0 + dr1 * dr1) / D;
+                                               float square, const HeadVals& hv, int lane, int diag,
+                                               __nv_bfloat16* se_row, float& dk0, float& dk1) {
+  float grow = 2.f * (r00 * dr0 + r01 * dr1) + dr0 * dr0 + dr1 * dr1;
+  float gdot = dv0 * hv.gd0 + dv1 * hv.gd1, wdot = dv0 * hv.w0 + dv1 * hv.w1;
+  warp_sum3(grow, gdot, wdot);
+  grow /= D;
   const float inverse = rsqrtf(square / D + NEPS), moved = rsqrtf(square / D + grow + NEPS);
   const float shrink = grow * (inverse * moved) * (inverse * moved) / (inverse + moved);
   dk0 = dr0 * moved - r00 * shrink;
   dk1 = dr1 * moved - r01 * shrink;
+  float xq = dk0 * hv.qd0 + dk1 * hv.qd1, udot = dk0 * hv.u0 + dk1 * hv.u1;
+  warp_sum2(xq, udot);
   float total = 0.f;
   if (diag || SELF) {  // the receiver s = t, exactly
-    const float x = warp_sum(dk0 * hv.qd0 + dk1 * hv.qd1) * 0.125f;
+    const float x = xq * 0.125f;
     const float a = hv.ad, e = expm1f(x);
     const float gain = a * e / (1.f + a * e), vgain = (a + a * e) / (1.f + a * e);
-    if (diag) total += gain * hv.cd + vgain * warp_sum(dv0 * hv.gd0 + dv1 * hv.gd1);
+    if (diag) total += gain * hv.cd + vgain * gdot;
     if (SELF) {
       se_row[lane] = __float2bfloat16_rn(gain * hv.vo0 + vgain * dv0);
       se_row[lane + 32] = __float2bfloat16_rn(gain * hv.vo1 + vgain * dv1);
     }
   }
-  total += warp_sum((dk0 * hv.u0 + dk1 * hv.u1) * 0.125f + dv0 * hv.w0 + dv1 * hv.w1);
+  total += udot * 0.125f + wdot;
   return total;
 }
 
@@ -152,8 +175,8 @@ template <bool SELF>
 __device__ __forceinline__ float head_change(float dr0, float dr1, float dv0, float dv1, float r00, float r01,
                                              const Tables& tb, int64_t row, int lane, int diag,
                                              __nv_bfloat16* se_row, float& dk0, float& dk1) {
-  return head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, head_vals<SELF>(tb, row, lane), lane, diag, se_row, dk0,
-                             dk1);
+  return head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, warp_sum(r00 * r00 + r01 * r01),
+                             head_vals<SELF>(tb, row, lane), lane, diag, se_row, dk0, dk1);
 }
 
 // head_change plus the moment tables on the CUDA cores: bf16(dk) M1 dk / 64 + bf16(dk) M2 dv / 8, the lane forming

@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
       ve1 = a.ve[kr + lane + 32];
     }
     const HeadVals hv = head_vals<SELF>(a.tab, row, lane);  // the head's table values, once for all its rows
+    const float square = warp_sum(r00 * r00 + r01 * r01);   // |r0|^2 of the head, the same for all its rows
     // warp phase: head_change per row, bf16(dk) into A (element (r, f) at r * 128 + ((f / 8) ^ (r % 8)) * 16 + (f % 8) * 2)
     // a row's four raw inputs (the lane's key and value features), loaded one row ahead of their use
     float in0 = 0.f, in1 = 0.f, in2 = 0.f, in3 = 0.f;
@@ -172,7 +173,8 @@ __global__ void __launch_bounds__(STC_THREADS, 2)
           dv0 += gc * ve0;
           dv1 += gc * ve1;
         }
-        const float part = head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, hv, lane, a.diag, se_row, dk0, dk1);
+        const float part =
+            head_change_v<SELF>(dr0, dr1, dv0, dv1, r00, r01, square, hv, lane, a.diag, se_row, dk0, dk1);
         if (lane == 0) stot[rl] += part;
       }
       const uint32_t arow = sbase + STC_A + rl * 128 + (lane & 7) * 2;
