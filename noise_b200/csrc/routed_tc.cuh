@@ -218,8 +218,9 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
 #pragma unroll
               for (int c = 0; c < 32; c += 2) {
                 const int k = pc * 32 + c;
-                const float2 ev = expm1_f2(
-                    make_float2(bf16_round_alu(sv[c]) * SCALE, bf16_round_alu(sv[c + 1]) * SCALE));
+                // the dot's bf16 output: one packed conversion (round to nearest even) and its exact widening
+                const float2 ev = expm1_f2(__fmul2_rn(unpack_bf16x2(pack_bf16x2(sv[c], sv[c + 1])),
+                                                      make_float2(SCALE, SCALE)));
                 e[i][c] = ev.x, e[i][c + 1] = ev.y;
                 if (k < p.K) acc.x = fmaf(pk[k], ev.x, acc.x);
                 if (k + 1 < p.K) acc.y = fmaf(pk[k + 1], ev.y, acc.y);
@@ -297,10 +298,12 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
           float4* dst = reinterpret_cast<float4*>(
               p.out + ((static_cast<int64_t>(tok) * p.P + probe) * p.H + hd) * 64 + cg * 16);
 #pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            dst[c / 4] = make_float4(bf16_round_alu(o[c]) + em * rs[c], bf16_round_alu(o[c + 1]) + em * rs[c + 1],
-                                     bf16_round_alu(o[c + 2]) + em * rs[c + 2],
-                                     bf16_round_alu(o[c + 3]) + em * rs[c + 3]);
+          for (int c = 0; c < 16; c += 4) {
+            const float2 o01 = unpack_bf16x2(pack_bf16x2(o[c], o[c + 1]));
+            const float2 o23 = unpack_bf16x2(pack_bf16x2(o[c + 2], o[c + 3]));
+            dst[c / 4] = make_float4(o01.x + em * rs[c], o01.y + em * rs[c + 1], o23.x + em * rs[c + 2],
+                                     o23.y + em * rs[c + 3]);
+          }
         }
       }
       ok = ok && have;
