@@ -438,7 +438,8 @@ size_t noise_key_response_workspace_bytes(int heads, int tokens);
  * as kind::tf32 MMAs with the (probe, source) columns as the 128 MMA rows, so each column's sum over its receivers
  * stays in one thread; receivers stream in 32-row tiles over the union of a block's windows, each column masked to its
  * own. Same result definitions. The workspace's first int32 is the device status after the call completes: 0, or 1 if
- * a pipeline wait gave up (the output is then incomplete). */
+ * a pipeline wait gave up (the output is then incomplete). heads x tokens (rounded up to 64) below 2^31 (int32 TMA row
+ * coordinates; NOISE_ERR_SHAPE otherwise). */
 int noise_future_scores_ws(const noise_view3_t* q, const noise_view3_t* target, const float* dk, const float* dv,
                            const noise_view3_t* a, const noise_view3_t* contrast, int heads, int tokens, int probes,
                            int sources, int source_start, int window, float* out, void* workspace,
@@ -468,7 +469,8 @@ size_t noise_query_response_workspace_bytes(int tokens, int probes, int heads, i
  * large; dq and out 16-byte aligned): both dots at the reference kernel's tf32x3 precision (run.py:1808,1813), one
  * CTA per 128 (token, probe) rows of a head, S and change V as kind::tf32 MMAs with the change in tensor memory.
  * keys_len > 32,768 falls through to noise_query_response. Same result definition. The workspace's first int32 is
- * the device status after the call completes: 0, or 1 if a pipeline wait gave up (the output is then incomplete). */
+ * the device status after the call completes: 0, or 1 if a pipeline wait gave up (the output is then incomplete).
+ * heads x Tp below 2^31 (int32 TMA row coordinates; NOISE_ERR_SHAPE otherwise). */
 int noise_query_response_ws(const float* dq, const noise_view3_t* keys, const noise_view3_t* values,
                             const noise_view3_t* probabilities, const noise_view3_t* base, int tokens, int probes,
                             int heads, int keys_len, float* out, void* workspace, size_t workspace_bytes,
@@ -484,7 +486,8 @@ int noise_routed_response(const void* dq, const void* keys, const void* values, 
 
 /* noise_routed_response on tcgen05 with a workspace of at least NOISE_STATUS_BYTES (256-byte aligned; its first int32
  * is the device status after the call: 0, or 1 if a pipeline wait gave up and the output is incomplete); out 16-byte
- * aligned; keys_len <= 256. Both dots are kind::f16 MMAs (fp32 accumulation, outputs rounded to bf16 as the
+ * aligned; keys_len <= 256; tokens x probes and tokens x heads x keys_len below 2^31 (the kernel's TMA row coordinates
+ * are int32; NOISE_ERR_SHAPE otherwise). Both dots are kind::f16 MMAs (fp32 accumulation, outputs rounded to bf16 as the
  * reference kernel's tl.dot outputs are, run.py:561,565): two (token, head) items share the 128 MMA rows when
  * keys_len padded to 32 is at most 128, their weights block-diagonal in tensor memory. Same result definition. */
 int noise_routed_response_ws(const void* dq, const void* keys, const void* values, const float* probabilities,
@@ -527,7 +530,8 @@ int noise_readout_staged(const void* up, const float* st, const float* r0, const
  * (256-byte aligned; its first int32 is the device status after the call: 0, or 1 if a bounded wait gave up and out is
  * incomplete): per head bf16(dk) M1 and bf16(dk) M2 for 128 rows of a token as kind::f16 MMAs (the reference's
  * tl.dot of the same bf16 operands, run.py:6032-6033), each row's dot with its fp32 dk / dv one thread's sum over a
- * TMEM row; the rest as noise_readout_staged. Same arguments and results. */
+ * TMEM row; the rest as noise_readout_staged. Same arguments and results. (start + tokens) x 512 moment-table rows
+ * below 2^31 (int32 TMA row coordinates; NOISE_ERR_SHAPE otherwise; noise_readout_direct_ws likewise). */
 int noise_readout_staged_ws(const void* up, const float* st, const float* r0, const float* vc, const float* gz,
                             const float* ve, const float* cs, const float* sn, const noise_scorer_tables_t* tab,
                             float* out, void* se, int start, int n, int se_rows, int tokens, int nc, int diag,

@@ -396,6 +396,8 @@ int column_ws(const noise_view3_t* q, const noise_view3_t* target, const float* 
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) || !a16(dk) || (VALUES && !a16(dv))) return NOISE_ERR_ALIGN;
   const int64_t cols = static_cast<int64_t>(probes) * sources;
   if (cols > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
+  // the kernel's TMA row coordinates (head h's rows at h Tp) are int32
+  if (static_cast<int64_t>(heads) * ((tokens + 63) / 64 * 64) > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
   const int tp = (tokens + 63) / 64 * 64;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = static_cast<int*>(workspace);
@@ -512,6 +514,10 @@ int noise_routed_response_ws(const void* dq, const void* keys, const void* value
   a.PB = (probes + 63) / 64;
   const int64_t items = static_cast<int64_t>(tokens) * heads * a.PB;
   if (items > 0x7FFFFFFF - 1) return NOISE_ERR_SHAPE;
+  // the kernel's TMA row coordinates are int32: a probe block's first row tok P + 64 pb, an item's first key mh K
+  if (static_cast<int64_t>(tokens) * probes + 64 > 0x7FFFFFFF ||
+      static_cast<int64_t>(tokens) * heads * keys_len + a.Kp > 0x7FFFFFFF)
+    return NOISE_ERR_SHAPE;
   a.items = static_cast<int>(items);
   a.tiles = (a.items + a.G - 1) / a.G;
   a.status = static_cast<int*>(workspace);
@@ -590,7 +596,7 @@ int noise_query_response_ws(const float* dq, const noise_view3_t* keys, const no
   }
   const int64_t rows = static_cast<int64_t>(tokens) * probes;
   const int64_t items = (rows + QT_ROWS - 1) / QT_ROWS * heads;
-  if (items > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
+  if (items > 0x7FFFFFFF || heads * w.tp > 0x7FFFFFFF) return NOISE_ERR_SHAPE;  // int32 TMA rows h Tp + k
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = static_cast<int*>(workspace);
   float* khi = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + 256);

@@ -427,8 +427,10 @@ int noise_readout_staged_ws(const void* up, const float* st, const float* r0, co
   if (n == 0 || tokens == 0) return NOISE_OK;
   StagedArgs a{static_cast<const __nv_bfloat16*>(up), st, r0, vc, gz, ve, cs, sn, tables(*tab), out,
                static_cast<__nv_bfloat16*>(se), start, n, se_rows, nc, diag};
+  // the kernel's TMA row coordinate tok H D is int32
+  if ((static_cast<int64_t>(start) + tokens) * H * D > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
   StcMaps maps;
-  const uint64_t rows = static_cast<uint64_t>(start + tokens) * H * D;
+  const uint64_t rows = (static_cast<uint64_t>(start) + tokens) * H * D;
   int rc;
   if ((rc = stc_map(&maps.m1, tab->M1, rows)) || (rc = stc_map(&maps.m2, tab->M2, rows))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -455,8 +457,10 @@ int noise_readout_direct_ws(const float* pj, const float* r0, const float* cs, i
   if (probes == 0 || tokens == 0) return NOISE_OK;
   DirectArgs a{pj, r0, cs, sn, cs_token_stride, cs_pair_stride, sn_token_stride, sn_pair_stride, gc, ve, tables(*tab),
                out, static_cast<__nv_bfloat16*>(se), start, probes, diag};
+  // the kernel's TMA row coordinate tok H D is int32
+  if ((static_cast<int64_t>(start) + tokens) * H * D > 0x7FFFFFFF) return NOISE_ERR_SHAPE;
   StcMaps maps;
-  const uint64_t rows = static_cast<uint64_t>(start + tokens) * H * D;
+  const uint64_t rows = (static_cast<uint64_t>(start) + tokens) * H * D;
   int rc;
   if ((rc = stc_map(&maps.m1, tab->M1, rows)) || (rc = stc_map(&maps.m2, tab->M2, rows))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -128,6 +128,8 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_future_scores_ws(r, r, fake + 4, fake, r, r, 8, 2000, 2, 2, 0, 8, fake, fake, fn, None) == 2  # dk
     assert L.noise_key_response_ws(r, fake, r, r, 8, 2000, 2, 2, 0, 0, -1, fake, fake, fn, None) == 1  # window < 0
     assert L.noise_key_response_ws(None, fake, r, r, 8, 2000, 2, 2, 0, 0, 8, fake, fake, fn, None) == 4
+    # int32 TMA row coordinates: heads x tokens padded to 64
+    assert L.noise_key_response_ws(r, fake, r, r, 1 << 16, 1 << 15, 2, 2, 0, 0, 8, fake, fake, 1 << 42, None) == 1
     assert L.noise_query_response(fake, r, r, r, r, 2, 0, 2, 64, fake, None) == 1
     qn = L.noise_query_response_workspace_bytes(256, 64, 8, 2048)
     assert qn == 256 + 4 * 8 * 2048 * 64 * 4 + 8 * 256 * 32                                   # planes + live flags
@@ -139,12 +141,17 @@ def test_rejects_bad_shapes_before_launch(L):
     assert L.noise_query_response_ws(fake + 4, r, r, r, r, 256, 64, 8, 2048, fake, fake, qn, None) == 2  # dq alignment
     assert L.noise_query_response_ws(fake, None, r, r, r, 256, 64, 8, 2048, fake, fake, qn, None) == 4
     assert L.noise_query_response_ws(fake, r, r, r, r, 256, 64, 0, 2048, fake, fake, qn, None) == 1     # no heads
+    assert L.noise_query_response_ws(fake, r, r, r, r, 1, 1, 1 << 16, 1 << 15, fake, fake, 1 << 45, None) == 1  # h Tp
     assert L.noise_expm1_f32(None, fake, 4, None) == 4
     assert L.noise_routed_response(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, None) == 1  # K > 256
     assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 257, fake, fake, 256, None) == 1  # K
     assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 64, fake, fake, 16, None) == 3   # ws
     assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 2, 2, 2, 64, fake + 4, fake, 256, None) == 2
     assert L.noise_routed_response_ws(None, fake, fake, fake, fake, 2, 2, 2, 64, fake, fake, 256, None) == 4
+    # int32 TMA row coordinates: tokens x probes rows, tokens x heads x keys key rows
+    assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 1 << 20, 1 << 11, 1, 64, fake, fake, 256,
+                                      None) == 1
+    assert L.noise_routed_response_ws(fake, fake, fake, fake, fake, 1 << 20, 1, 16, 256, fake, fake, 256, None) == 1
     # Dust block rerun
     jit = _lib.Jitter()
     assert L.noise_block_forward(ctypes.byref(gpt), 0, fake, None, ctypes.byref(jit), 2, 256, 128, fake, 1 << 30,
@@ -173,6 +180,11 @@ def test_rejects_bad_shapes_before_launch(L):
                                   0, 8, 8, 2, 1000, 1, None) == 1                              # nc < 1024
     assert L.noise_readout_direct(fake, fake, fake, 32, 1, fake, 32, 1, fake, None, ctypes.byref(tab), fake, None,
                                   0, 8, 2, 1, None) == 4                                       # gated without ve
+    # int32 TMA row coordinates: (start + tokens) x 8 heads x 64 moment-table rows
+    assert L.noise_readout_staged_ws(fake, fake, fake, fake, None, None, fake, fake, ctypes.byref(tab), fake, None,
+                                     (1 << 22) - 1, 8, 8, 2, 1040, 1, fake, 256, None) == 1
+    assert L.noise_readout_direct_ws(fake, fake, fake, 32, 1, fake, 32, 1, None, None, ctypes.byref(tab), fake, None,
+                                     1 << 22, 8, 1, 1, fake, 256, None) == 1
 
 
 def test_product_path_has_no_oracle_import():
