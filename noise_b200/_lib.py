@@ -81,6 +81,7 @@ _lib = None
 # (name, restype, argtypes) of every exported entry point; tests check each one is present.
 SIGNATURES = [
     ('noise_param_index', ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    ('noise_attention_item', ctypes.c_int, [ctypes.c_int] * 5 + [ctypes.POINTER(ctypes.c_int)] * 2),
     ('noise_population_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_population_loss', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.POINTER(Slice), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,

@@ -46,6 +46,7 @@ struct TAttnArgs {
   Slice nproj;       // c_proj noise: b used
   int* status;
   const float* jit;  // [M, 512] fp32 added to the attention output before c_proj, or NULL (Dust's o jitter site)
+  int order;         // attention_item's order
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -58,6 +59,28 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
 }
 __device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+// Work item w of a launch over bh head rows (member x head), npairs pairs of 128-query tiles each, dealt round-robin
+// to `grid` persistent CTAs (CTA c takes w = c, c + grid, ...): its pair index pi and head row.
+//   order 0: heaviest pair first over the whole launch, head rows inner, so each round of the grid takes one pair
+//            level (equal cost); a head row's pairs are 1 / npairs of the launch apart, so its keys and values come
+//            from HBM once per pair.
+//   order 1: blocks of `grid` head rows, each block heaviest pair first: CTA c takes every pair of head row
+//            blk grid + c in turn, so the row's keys and values come from HBM once and then from L2, while each round
+//            still takes one pair level. The rows past the last whole block are dealt heaviest first over all CTAs.
+// Both are bijections of [0, npairs bh) onto (pair, row).
+__host__ __device__ inline void attention_item(int order, int w, int bh, int npairs, int grid, int& pi, int& row) {
+  const int per = grid * npairs, full = order == 1 ? bh / grid : 0;
+  if (w < full * per) {
+    const int r = w % per;
+    pi = npairs - 1 - r / grid;
+    row = w / per * grid + r % grid;
+  } else {
+    const int rest = bh - full * grid, r = w - full * per;
+    pi = npairs - 1 - r / rest;
+    row = full * grid + r % rest;
+  }
 }
 
 // Key-tile range [lo, hi] of query tile qt and whether its first tile is cut by the window.
@@ -96,7 +119,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   const int npairs = (nq + 1) / 2;
   const int items = npairs * p.bh;
 
-  // work item w: pair pi (heaviest first, so every wave of CTAs takes equal-cost items) of head-row bh
+  // work item w: pair pi of head-row bh (attention_item: every round of CTAs takes equal-cost items)
   struct Item {
     int bh, qa, qb, lo, hi;
     bool has_b;
@@ -104,8 +127,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   };
   auto item = [&](int w) {
     Item it;
-    const int pi = npairs - 1 - w / p.bh;
-    it.bh = w % p.bh;
+    int pi;
+    attention_item(p.order, w, p.bh, npairs, static_cast<int>(gridDim.x), pi, it.bh);
     it.qa = 2 * pi;
     it.qb = 2 * pi + 1;
     it.has_b = it.qb < nq;

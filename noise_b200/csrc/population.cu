@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -1020,6 +1021,16 @@ static int run_gemm_plain(const void* A, int M, int K, const void* B, int N, flo
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
+// attention_item's order for every attention launch: 1 when NOISE_B200_ATTN_ORDER is "1" (head rows in per-CTA
+// blocks), else 0 (the launch-wide heaviest-first order)
+static int attention_order() {
+  static const int order = [] {
+    const char* e = getenv("NOISE_B200_ATTN_ORDER");
+    return e && e[0] == '1' && e[1] == '\0' ? 1 : 0;
+  }();
+  return order;
+}
+
 static int run_attention(const void* q, const void* k, const void* v, int M, int T, int members,
                          const TAttnArgs& args, cudaStream_t s) {
   CUtensorMap mq, mk, mv;
@@ -1036,6 +1047,7 @@ static int run_attention(const void* q, const void* k, const void* v, int M, int
   if (sms <= 0) return NOISE_ERR_CUDA;
   TAttnArgs a = args;
   a.bh = members * H;
+  a.order = attention_order();
   const int items = (T / TA_BQ + 1) / 2 * a.bh;
   kern<<<items < sms ? items : sms, TA_THREADS, TA_SMEM, s>>>(mq, mk, mv, a);
   launch_end(s);
@@ -1112,6 +1124,15 @@ static Workspace carve_head(void* ws, int64_t rows) {
 using namespace noise;
 
 extern "C" {
+
+int noise_attention_item(int order, int item, int head_rows, int pairs, int grid, int* pair, int* head_row) {
+  if (!pair || !head_row || order < 0 || order > 1) return NOISE_ERR_ARGUMENT;
+  const int64_t items = static_cast<int64_t>(head_rows) * pairs;
+  if (head_rows < 1 || pairs < 1 || items > 0x7FFFFFFF || grid < 1 || grid > items || item < 0 || item >= items)
+    return NOISE_ERR_SHAPE;
+  attention_item(order, item, head_rows, pairs, grid, *pair, *head_row);
+  return NOISE_OK;
+}
 
 int noise_param_index(int block, int which) {
   if (block < 0 || block >= NOISE_N_LAYER) return -1;

@@ -1,0 +1,89 @@
+"""The attention kernel's work schedule through the C ABI (noise_attention_item, host code shared with the kernel):
+both orders are bijections of the launch's items onto (pair, head row); order 0 is the launch-wide heaviest-first
+order; order 1 gives each persistent CTA every pair of one head row in turn while every round of the grid still takes
+one pair level, so per-CTA work stays as balanced as order 0's at the bench's launch (512 members x 8 heads, T 2048,
+148 CTAs)."""
+import ctypes
+
+import pytest
+
+TQ = 128  # query / key tile
+
+
+@pytest.fixture(scope='module')
+def item():
+    from noise_b200 import _lib
+    L = _lib.lib()
+    pair, row = ctypes.c_int(), ctypes.c_int()
+
+    def call(order, w, bh, npairs, grid):
+        assert L.noise_attention_item(order, w, bh, npairs, grid, ctypes.byref(pair), ctypes.byref(row)) == 0
+        return pair.value, row.value
+    return call
+
+
+def key_tiles(pi, tokens, window):
+    """Key tiles one item streams: the union of its two query tiles' ranges (tile_range in attention_tc.cuh)."""
+    nq = tokens // TQ
+
+    def lo_hi(qt):
+        q0 = qt * TQ
+        return ((q0 - window) // TQ if q0 - window >= 0 else 0), q0 // TQ
+    lo, hi = lo_hi(2 * pi)
+    if 2 * pi + 1 < nq:
+        hi = lo_hi(2 * pi + 1)[1]
+    return hi - lo + 1
+
+
+def schedule(item, order, bh, npairs, grid):
+    return [item(order, w, bh, npairs, grid) for w in range(bh * npairs)]
+
+
+@pytest.mark.parametrize('bh,npairs,grid', [(3, 1, 3), (10, 8, 80), (148, 8, 148), (300, 8, 148), (4096, 8, 148),
+                                            (37, 5, 100)])
+def test_orders_are_bijections(item, bh, npairs, grid):
+    for order in (0, 1):
+        got = schedule(item, order, bh, npairs, grid)
+        assert sorted(got) == [(p, r) for p in range(npairs) for r in range(bh)], order
+
+
+def test_order_zero_is_heaviest_first(item):
+    bh, npairs = 300, 8
+    assert schedule(item, 0, bh, npairs, 148) == [(npairs - 1 - w // bh, w % bh) for w in range(bh * npairs)]
+
+
+def test_order_one_keeps_rows_on_their_cta(item):
+    bh, npairs, grid = 4096, 8, 148
+    full = bh // grid
+    for c in range(grid):
+        mine = [item(1, w, bh, npairs, grid) for w in range(c, full * grid * npairs, grid)]
+        for blk in range(full):
+            run = mine[blk * npairs:(blk + 1) * npairs]
+            assert [p for p, _ in run] == list(range(npairs - 1, -1, -1))  # heaviest pair first
+            assert {r for _, r in run} == {blk * grid + c}                  # one head row per block
+    for k in range(full * npairs):  # every round of whole blocks takes one pair level
+        assert len({item(1, w, bh, npairs, grid)[0] for w in range(k * grid, (k + 1) * grid)}) == 1
+
+
+@pytest.mark.parametrize('window', [1024, 2048])
+def test_order_one_balance_at_bench_launch(item, window):
+    bh, tokens, grid = 4096, 2048, 148
+    npairs = (tokens // TQ + 1) // 2
+    spread = {}
+    for order in (0, 1):
+        load = [0] * grid
+        for w in range(bh * npairs):
+            load[w % grid] += key_tiles(item(order, w, bh, npairs, grid)[0], tokens, window)
+        spread[order] = max(load) / (sum(load) / grid)
+    assert spread[1] <= spread[0] + 0.01, spread
+    assert spread[1] < 1.03, spread
+
+
+def test_rejects_bad_arguments():
+    from noise_b200 import _lib
+    L = _lib.lib()
+    a, b = ctypes.c_int(), ctypes.c_int()
+    assert L.noise_attention_item(2, 0, 8, 8, 8, ctypes.byref(a), ctypes.byref(b)) == 4   # order
+    assert L.noise_attention_item(1, 64, 8, 8, 8, ctypes.byref(a), ctypes.byref(b)) == 1  # item past the launch
+    assert L.noise_attention_item(1, 0, 8, 8, 65, ctypes.byref(a), ctypes.byref(b)) == 1  # grid above the items
+    assert L.noise_attention_item(1, 0, 8, 8, 8, None, ctypes.byref(b)) == 4
