@@ -85,6 +85,11 @@ def visible_pairs(length, window):
 WINDOWS = [1024, 1024, 1024, 2048, 1024, 1024, 1024, 2048]
 
 
+def attention_order():
+    """The attention kernel's work order this run uses (the library reads NOISE_B200_ATTN_ORDER: "1" or default 0)."""
+    return 1 if os.environ.get('NOISE_B200_ATTN_ORDER') == '1' else 0
+
+
 def kernel_work(kind, members, length):
     """(algorithmic FLOPs, algorithmic HBM bytes) of ONE launch of a kernel kind on members x length rows."""
     M = members * length
@@ -398,7 +403,8 @@ def run_ours(a):
                                 f'profiling case (not the benchmark config): {a.members} members x {a.rows} rows'),
                    'members_per_gpu': a.members, 'rows_per_member': a.rows, 'seq_len': T, 'sigma': SIGMA,
                    'member_tokens_per_s': value * T, 'train_tokens_per_step': a.rows * T,
-                   'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}'},
+                   'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}',
+                   'attention_order': attention_order()},
         'e2e': {'value': e2e_value, 'unit': UNIT, 'h2d_bytes_per_step': a.rows * (T + 1) * 8,
                 'd2h_bytes_per_step': a.members * world * 4},
         'gpu_launches': launches,
@@ -632,7 +638,7 @@ def run_train(a):
                    'member_tokens_per_s': TRAIN_FORWARDS * T * a.steps / (ms / 1e3),
                    'phase_ms_per_step': {k: round(v / a.steps, 3) for k, v in phases.items()},
                    'l2': 'inputs larger than L2 (per-call activations ~11 GB)', 'parallelism': f'members x{world}',
-                   'last_mean_loss': float(loss_host[0])},
+                   'last_mean_loss': float(loss_host[0]), 'attention_order': attention_order()},
         'e2e': {'value': e2e_value, 'unit': TRAIN_UNIT, 'h2d_bytes_per_step': TRAIN_ROWS * (T + 1) * 8,
                 'd2h_bytes_per_step': 4, 'ms_per_step': ms_e2e / a.steps,
                 'copy_and_host_wait_ms_per_step': (ms_e2e - ms) / a.steps},
