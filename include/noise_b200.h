@@ -486,10 +486,11 @@ int noise_routed_response(const void* dq, const void* keys, const void* values, 
 
 /* noise_routed_response on tcgen05 with a workspace of at least NOISE_STATUS_BYTES (256-byte aligned; its first int32
  * is the device status after the call: 0, or 1 if a pipeline wait gave up and the output is incomplete); out 16-byte
- * aligned; keys_len <= 256; tokens x probes and tokens x heads x keys_len below 2^31 (the kernel's TMA row coordinates
- * are int32; NOISE_ERR_SHAPE otherwise). Both dots are kind::f16 MMAs (fp32 accumulation, outputs rounded to bf16 as the
- * reference kernel's tl.dot outputs are, run.py:561,565): two (token, head) items share the 128 MMA rows when
- * keys_len padded to 32 is at most 128, their weights block-diagonal in tensor memory. Same result definition. */
+ * aligned; keys_len <= 256; tokens x probes and tokens x heads x keys_len below 2^31 (the kernel's TMA row
+ * coordinates are int32; NOISE_ERR_SHAPE otherwise). Both dots are kind::f16 MMAs (fp32 accumulation, outputs rounded
+ * to bf16 as the reference kernel's tl.dot outputs are, run.py:561,565): two (token, head) items share the 128 MMA
+ * rows when keys_len padded to 32 is at most 128, their weights block-diagonal in tensor memory. Same result
+ * definition. */
 int noise_routed_response_ws(const void* dq, const void* keys, const void* values, const float* probabilities,
                              const float* rest, int tokens, int probes, int heads, int keys_len, float* out,
                              void* workspace, size_t workspace_bytes, void* stream);

@@ -42,6 +42,14 @@ def _check(rc, what):
     _lib.check(rc, what)
 
 
+def _shapes(**named):
+    """Each keyword is (tensor, expected shape): a mismatch raises before any pointer reaches a kernel, which would
+    otherwise read past a smaller operand's end."""
+    for name, (t, want) in named.items():
+        if tuple(t.shape) != tuple(want):
+            raise ValueError(f'{name}: shape {tuple(t.shape)}, expected {tuple(want)}')
+
+
 def _stream(t):
     return _lib.stream_handle(t.device)
 
@@ -52,11 +60,14 @@ def future_scores_impl(q, target, dk, dv, a, contrast, source_start, window, tc=
     h, p, m, d = dk.shape
     if d != HD:
         raise ValueError('head_dim 64 only')
+    t = q.shape[1]
+    _shapes(q=(q, (h, t, d)), target=(target, (h, t, d)), dv=(dv, (h, p, m, d)), a=(a, (h, t, m)),
+            contrast=(contrast, (h, t, m)))
     _lib.require_cuda(q, target, dk, dv, a, contrast)
     (qv, q), (gv, target), (av, a), (cv, contrast) = _view(q), _view(target), _view(a), _view(contrast)
     dk, dv = _f32c(dk), _f32c(dv)
     out = torch.empty((h, p, m), device=q.device, dtype=torch.float32)
-    L, t = _lib.lib(), q.shape[1]
+    L = _lib.lib()
     args = (ctypes.byref(qv), ctypes.byref(gv), dk.data_ptr(), dv.data_ptr(), ctypes.byref(av), ctypes.byref(cv), h, t,
             p, m, int(source_start), int(window), out.data_ptr())
     if not tc:
@@ -75,11 +86,13 @@ def key_response_impl(q, dk, A, C, source_start, query_start, window, tc=True):
     heads, probes, sources, width = dk.shape
     if width != HD:
         raise ValueError('head_dim 64 only')
+    t = q.shape[1]
+    _shapes(q=(q, (heads, t, width)), A=(A, (heads, t, sources)), C=(C, (heads, t, sources)))
     _lib.require_cuda(q, dk, A, C)
     (qv, q), (av, A), (cv, C) = _view(q), _view(A), _view(C)
     dk = _f32c(dk)
     out = torch.empty((heads, probes, sources), device=q.device, dtype=torch.float32)
-    L, t = _lib.lib(), q.shape[1]
+    L = _lib.lib()
     args = (ctypes.byref(qv), dk.data_ptr(), ctypes.byref(av), ctypes.byref(cv), heads, t, probes, sources,
             int(source_start), int(query_start), int(window), out.data_ptr())
     if not tc:
@@ -98,12 +111,15 @@ def query_response_impl(dq, keys, values, probabilities, base, tc=True):
     m, p, h, d = dq.shape
     if d != HD:
         raise ValueError('head_dim 64 only')
+    t = keys.shape[1]
+    _shapes(keys=(keys, (h, t, d)), values=(values, (h, t, d)), probabilities=(probabilities, (h, m, t)),
+            base=(base, (h, m, d)))
     _lib.require_cuda(dq, keys, values, probabilities, base)
     dq = _f32c(dq)
     (kv, keys), (vv, values), (pv, probabilities), (bv, base) = (_view(z) for z in (keys, values, probabilities,
                                                                                    base))
     out = torch.empty((m, p, h, d), device=dq.device, dtype=torch.float32)
-    L, t = _lib.lib(), keys.shape[1]
+    L = _lib.lib()
     if not tc:
         _check(L.noise_query_response(dq.data_ptr(), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(pv),
                                       ctypes.byref(bv), m, p, h, t, out.data_ptr(), _stream(dq)), 'noise_query_response')
@@ -124,6 +140,8 @@ def routed_response_impl(dq, keys, values, probabilities, rest, tc=True):
     if width != HD:
         raise ValueError('head_dim 64 only')
     count = keys.shape[2]
+    _shapes(keys=(keys, (m, heads, count, width)), values=(values, (m, heads, count, width)),
+            probabilities=(probabilities, (m, heads, count)), rest=(rest, (m, heads, width)))
     _lib.require_cuda(dq, keys, values, probabilities, rest)
     dq, keys, values = (z.detach().to(torch.bfloat16).contiguous() for z in (dq, keys, values))
     probabilities, rest = _f32c(probabilities), _f32c(rest)

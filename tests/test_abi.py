@@ -190,3 +190,29 @@ def test_rejects_bad_shapes_before_launch(L):
 def test_product_path_has_no_oracle_import():
     for path in (ROOT / 'noise_b200').rglob('*.py'):
         assert 'oracle' not in path.read_text(), path
+
+
+def test_readout_wrappers_refuse_mismatched_operands():
+    """The scorer wrappers check every operand's shape against the dimensions they pass to the kernel (a smaller one
+    would be read past its end), then refuse CPU tensors: no CPU fallback."""
+    import sys
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from readout_inputs import future_inputs, key_inputs, query_inputs, routed_inputs
+    from noise_b200 import _lib, readout
+    f, k, q, r = future_inputs(), key_inputs(), query_inputs(), routed_inputs()
+    bad = [
+        lambda: readout.future_scores_impl(f['q'], f['target'], f['dk'], f['dv'], f['a'][:, :-1], f['contrast'], 48,
+                                           64),
+        lambda: readout.future_scores_impl(f['q'], f['target'][:1], f['dk'], f['dv'], f['a'], f['contrast'], 48, 64),
+        lambda: readout.key_response_impl(k['q'], k['dk'], k['A'], k['C'][..., :-1], 32, 24, 64),
+        lambda: readout.query_response_impl(q['dq'], q['keys'], q['values'], q['probabilities'][:, :-1], q['base']),
+        lambda: readout.query_response_impl(q['dq'], q['keys'], q['values'][:, :-1], q['probabilities'], q['base']),
+        lambda: readout.routed_response_impl(r['dq'], r['keys'], r['values'], r['probabilities'], r['rest'][:-1]),
+        lambda: readout.routed_response_impl(r['dq'], r['keys'], r['values'][:, :, :-1], r['probabilities'],
+                                             r['rest']),
+    ]
+    for call in bad:
+        with pytest.raises(ValueError):
+            call()
+    with pytest.raises(_lib.NoiseError):
+        readout.routed_response_impl(r['dq'], r['keys'], r['values'], r['probabilities'], r['rest'])
