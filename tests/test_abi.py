@@ -216,3 +216,39 @@ def test_readout_wrappers_refuse_mismatched_operands():
             call()
     with pytest.raises(_lib.NoiseError):
         readout.routed_response_impl(r['dq'], r['keys'], r['values'], r['probabilities'], r['rest'])
+
+
+def test_scorer_wrappers_refuse_mismatched_operands():
+    """The readout scorer's wrappers check each operand's dtype, layout and shape (the moment tables must cover the
+    chunk's global tokens) before any pointer reaches a kernel, then refuse CPU tensors."""
+    import sys
+    import torch
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from scorer_inputs import scorer_inputs, tables
+    from noise_b200 import _lib, scorer
+    x = scorer_inputs()
+    m, n, start, nc = x['m'], x['n'], x['start'], x['nc']
+    tok = slice(start, start + m)
+
+    def staged(**bad):
+        y = dict(x, **bad)
+        scorer.staged_kernel(y['UP'], torch.empty(m, n, 2), y['R0'], y['VC'], y['GZ'], y['VE'], y['CS'], y['SN'],
+                             *tables(y), torch.empty(m, n), None, start, n, n, True, True, False, nc)
+
+    def direct(**bad):
+        y = dict(x, **bad)
+        scorer.readout_kernel(y['PJ'], y['R0'][tok], y['CS'][tok], y['SN'][tok], y['GC'], y['VE'][tok], *tables(y),
+                              torch.empty(m, n), None, start, n, True, True, False)
+    for call, bad in ((staged, dict(U=x['U'][:start])), (staged, dict(M1=x['M1'].float())),
+                      (staged, dict(UP=x['UP'][:-1])), (staged, dict(VC=x['VC'][:, :256])),
+                      (direct, dict(PJ=x['PJ'][:, :-1])), (direct, dict(GC=x['GC'][..., :4])),
+                      (direct, dict(AD=x['AD'][:start + 1]))):
+        with pytest.raises(ValueError):
+            call(**bad)
+    with pytest.raises(ValueError):  # DB rows a token must be n
+        scorer.stats_kernel(x['delta'], x['X'], x['SQX'], torch.empty(m, n + 1, 512, dtype=torch.bfloat16),
+                            torch.empty(m, n, 2), start, n, x['d_rows'], x['eps'])
+    with pytest.raises(_lib.NoiseError):
+        staged()
+    with pytest.raises(_lib.NoiseError):
+        direct()
