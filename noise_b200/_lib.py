@@ -236,7 +236,7 @@ def launches():
 
 
 def _gemm(entry, dtype, a, b, out=None):
-    require_cuda(a, b)
+    require_cuda(a, b, *(() if out is None else (out,)))
     if a.dtype != dtype or b.dtype != dtype or a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
         raise ValueError(f'{entry}: a [m, k] and b [n, k] of {dtype}')
     a, b = a.contiguous(), b.contiguous()

@@ -53,6 +53,12 @@ def coordinate_change(raw, targets):
 
 def _weights(x, base, y):
     n = x.shape[0]
+    if (tuple(x.shape) != (n, D) or tuple(base.shape) != (n, VOCAB) or tuple(y.shape) != (n,)
+            or x.dtype != torch.float32 or base.dtype != torch.float32 or y.dtype != torch.int64
+            or not (x.is_contiguous() and base.is_contiguous() and y.is_contiguous())):
+        raise ValueError(f'x fp32 [n, {D}], base fp32 [n, {VOCAB}] and y int64 [n], contiguous: got '
+                         f'{tuple(x.shape)}, {tuple(base.shape)}, {tuple(y.shape)}')
+    _lib.require_cuda(x, base, y)
     dev = x.device
     fg1 = torch.empty(n, VOCAB, device=dev)
     fast = torch.empty(5, n, VOCAB, device=dev, dtype=torch.bfloat16)
@@ -68,7 +74,6 @@ def cycle_weights_fused(x, base, h):
     """The readout cycle's weights (run.py:3636-3647): fg1 [n, V], fast bf16 [5, n, V], rows [n, 3], total [n, 1] and
     cycle_scales' steps, inv, inv0, delta, sigma."""
     x, base = x.detach().float().contiguous(), base.detach().float().contiguous()
-    _lib.require_cuda(x, base)
     y = torch.zeros(x.shape[0], dtype=torch.int64, device=x.device)
     fg1, fast, rows, total, sq, _ = _weights(x, base, y)
     sq = sq[:, None]
@@ -85,6 +90,8 @@ def top_credit(model, x, y):
     model carries H (the 512 x 512 Hadamard basis), step_t and lm_head [512, 4096] fp32."""
     x = x.detach().float().contiguous()
     y = y.detach().long().contiguous()
+    if x.dim() != 2 or x.shape[1] != D or tuple(y.shape) != (x.shape[0],):
+        raise ValueError(f'x [n, {D}] and y [n]: got {tuple(x.shape)}, {tuple(y.shape)}')
     _lib.require_cuda(x, y)
     h = (model.H * step_signs(model.step_t, x.device)[None, :]).float().contiguous()
     Wt = model.lm_head.float().t().contiguous()  # [4096, 512]: W as the K-major right-hand side

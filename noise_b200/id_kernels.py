@@ -32,14 +32,16 @@ def hidden_credits_fused(us, steps, credb, w_out_t, config=None):
     layers, m, k = credb.shape
     n = w_out_t.shape[-1]
     assert credb.is_contiguous() and w_out_t.is_contiguous() and steps.is_contiguous()
-    assert all(u.numel() == m * n for u in us)
+    assert len(us) == layers and all(u.numel() == m * n for u in us)
     assert m % 128 == 0 and n % 128 == 0 and k % 64 == 0
+    assert tuple(w_out_t.shape) == (layers, k, n)
     us = [u.detach() for u in us]
     u_ptrs = _ptrs(us, 'us')
     _ptrs([credb, w_out_t], 'credb, w_out_t')
     steps = steps.detach()
-    if steps.dtype != torch.float32:
-        raise ValueError('steps: fp32')
+    if steps.dtype != torch.float32 or tuple(steps.shape) != (layers, m):
+        raise ValueError(f'steps: fp32 ({layers}, {m}), got {steps.dtype} {tuple(steps.shape)}')
+    _lib.require_cuda(steps)
     out = torch.empty((layers, m, n), device=credb.device, dtype=torch.bfloat16)
     ws = _status(credb.device)
     _lib.check(_lib.lib().noise_hidden_credits(u_ptrs, steps.data_ptr(), credb.data_ptr(), w_out_t.data_ptr(), layers,
@@ -56,6 +58,7 @@ def square_credit_grads(n1s, got2, out, config=None):
     world, _, three, _, hd = got2.shape
     assert three == 3 and world * hd == d and out.shape == (3 * layers, d, d) and out.is_contiguous()
     assert got2.is_contiguous() and m % 64 == 0 and d % 128 == 0
+    assert all(tuple(x.shape) == (m, d) for x in n1s) and got2.shape[1] == layers and got2.shape[3] == m
     if hd != 64:
         raise ValueError('square_credit_grads: head_dim 64')
     a = _ptrs([x.detach() for x in n1s], 'n1s')
@@ -74,6 +77,7 @@ def at_b_layers(As, Bs, out, config=None):
     p, q = As[0].shape[-1], Bs[0].shape[-1]
     k = As[0].numel() // p
     assert out.shape == (8, p, q) and out.is_contiguous() and all(b.numel() == k * q for b in Bs)
+    assert len(As) == len(Bs) == out.shape[0]
     assert all(a.numel() == k * p for a in As) and k % 64 == 0 and p % 128 == 0 and q % 128 == 0
     a = _ptrs([x.detach() for x in As], 'As')
     b = _ptrs([x.detach() for x in Bs], 'Bs')

@@ -252,3 +252,27 @@ def test_scorer_wrappers_refuse_mismatched_operands():
         staged()
     with pytest.raises(_lib.NoiseError):
         direct()
+
+
+def test_gemm_wrappers_refuse_short_operand_lists():
+    """The identity-phase GEMMs and the readout cycle check their operand lists and shapes before any pointer array
+    reaches the library (a short list would hand a kernel an undefined pointer)."""
+    import sys
+    import torch
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from id_inputs import at_b_inputs, hidden_inputs, square_inputs
+    from noise_b200 import cycle, id_kernels
+    us, steps, credb, w_out_t = hidden_inputs()
+    with pytest.raises(AssertionError):
+        id_kernels.hidden_credits_fused(us[:7], steps, credb, w_out_t)
+    with pytest.raises(AssertionError):
+        id_kernels.hidden_credits_fused(us, steps, credb, w_out_t[:, :, :128])
+    As, Bs = at_b_inputs()
+    with pytest.raises(AssertionError):
+        id_kernels.at_b_layers(As, Bs[:7], torch.empty(8, 128, 256, dtype=torch.bfloat16))
+    n1s, got2 = square_inputs()
+    with pytest.raises(AssertionError):
+        id_kernels.square_credit_grads(n1s, got2[:, :7], torch.empty(24, 128, 128, dtype=torch.bfloat16))
+    x = torch.randn(4, 512)
+    with pytest.raises(ValueError):
+        cycle.cycle_weights_fused(x, torch.randn(4, 2048), torch.randn(512, 512))
