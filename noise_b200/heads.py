@@ -30,13 +30,24 @@ def _pieces(qs, ks, vals, outs, targets, lses):
     tensors to keep alive, n, t, layers)."""
     n, t = qs[0].shape[0], lses[0].shape[-1]
     layers = len(qs)
-    pieces = (_lib.HeadPieces * layers)()
-    keep = []
+    if not len(ks) == len(vals) == len(outs) == len(targets) == len(lses) == layers:
+        raise ValueError('q, k, v, o, target and lse: one piece of each per layer')
+    if t < 1 or n % t:
+        raise ValueError(f'{n} tokens are not whole sequences of lse\'s {t}')
+    checked = []
     for i, group in enumerate(zip(qs, ks, vals, outs, targets, lses)):
         *mats, lse = group
         mats = [_two_byte(m.detach(), 'q, k, v, o, target') for m in mats]
+        if any(tuple(m.shape) != (n, H * HD) for m in mats):
+            raise ValueError(f'layer {i}: q, k, v, o, target must be ({n}, {H * HD})')
         lse = lse.detach().float().contiguous()
-        _lib.require_cuda(*mats, lse)
+        if tuple(lse.shape) != (n // t, H, t):
+            raise ValueError(f'layer {i}: lse {tuple(lse.shape)}, expected {(n // t, H, t)}')
+        checked.append((mats, lse))
+    _lib.require_cuda(*(z for mats, lse in checked for z in mats + [lse]))
+    pieces = (_lib.HeadPieces * layers)()
+    keep = []
+    for i, (mats, lse) in enumerate(checked):
         keep += mats + [lse]
         p = pieces[i]
         p.q, p.k, p.v, p.o, p.target = (m.data_ptr() for m in mats)
@@ -87,13 +98,23 @@ def _got(got, b, t):
     return got
 
 
+def _rope(cos, sin, t):
+    """fp32 contiguous RoPE tables with at least t rows of HD / 2 on the device (the kernels read rows 0 .. t - 1)."""
+    cos, sin = (z.detach().float().contiguous() for z in (cos, sin))
+    for z in (cos, sin):
+        if z.dim() != 2 or z.shape[0] < t or z.shape[1] != HD // 2:
+            raise ValueError(f'cos / sin: ({t} or more, {HD // 2}), got {tuple(z.shape)}')
+    _lib.require_cuda(cos, sin)
+    return cos, sin
+
+
 def head_prep_fused(got, cos, sin, b: int, t: int):
     """The received heads' RoPE'd queries and keys, values, hubs, lse and square norms and steps from got (W, L, N,
     PACK), in one kernel pass (run.py:3781-3796). Returns (q16, k16, v16, hub16, q32, (f2, f4, xy), lse, hub_out,
     sq_q, sq_k, steps_q, steps_k)."""
     got = _got(got, b, t)
     w, layers, n, _ = got.shape
-    cos, sin = (z.detach().float().contiguous() for z in (cos, sin))
+    cos, sin = _rope(cos, sin, t)
     s, result, _ = _prep_struct(got, b, t, keep_k32=False)
     _lib.check(_lib.lib().noise_head_prep(got.data_ptr(), w, layers, n, cos.data_ptr(), sin.data_ptr(), t, KEY_SIGMA,
                                           NORM_EPS, ctypes.byref(s), _lib.stream_handle(got.device)),
@@ -108,7 +129,8 @@ def id_head_scores(got, rope32, back, b, t):
     w, layers, n, _ = got.shape
     if back.dtype != torch.bfloat16 or tuple(back.shape) != (w, layers, 3, n, HD) or not back.is_contiguous():
         raise ValueError('back: contiguous bf16 (W, L, 3, N, 64)')
-    cos, sin = (z.detach().float().contiguous() for z in rope32)
+    cos, sin = _rope(*rope32, t)
+    _lib.require_cuda(back)
     L = _lib.lib()
     nbytes = L.noise_id_head_scores_workspace_bytes(w, layers, n)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=got.device)

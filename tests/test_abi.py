@@ -276,3 +276,18 @@ def test_gemm_wrappers_refuse_short_operand_lists():
     x = torch.randn(4, 512)
     with pytest.raises(ValueError):
         cycle.cycle_weights_fused(x, torch.randn(4, 2048), torch.randn(512, 512))
+
+
+def test_pack_heads_refuses_mismatched_pieces():
+    """pack_heads_kernel checks that every layer has all six pieces, each (n, 512), and an lse of whole sequences, before
+    a pointer reaches the library."""
+    import sys
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from heads_inputs import pack_inputs
+    from noise_b200 import heads
+    p = pack_inputs()
+    names = ('qs', 'ks', 'vals', 'outs', 'targets', 'lses')
+    for bad in (dict(ks=p['ks'][:1]), dict(vals=[p['vals'][0], p['vals'][1][:-1]]),
+                dict(lses=[p['lses'][0], p['lses'][1][:, :4]])):
+        with pytest.raises(ValueError):
+            heads.pack_heads_kernel(*(dict(p, **bad)[k] for k in names))
