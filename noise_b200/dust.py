@@ -33,12 +33,19 @@ class _Packed:
         key = (layer, T, cos.data_ptr(), sin.data_ptr()) + tuple(
             (w[n].data_ptr(), w[n]._version) if w.get(n) is not None else None for n in names)
         if key != self.key:
+            shapes = dict(q=(D, D), k=(D, D), v=(D, D), proj=(D, D), fc=(4 * D, D), out=(D, 4 * D), gate=(8, 32))
+            for n in names:
+                if w.get(n) is not None and tuple(w[n].shape) != shapes[n]:
+                    raise ValueError(f'{n}: shape {tuple(w[n].shape)}, expected {shapes[n]}')
             bf = lambda t: t.detach().to(torch.bfloat16).contiguous()
             qkv = torch.cat([bf(w['q']), bf(w['k']), bf(w['v'])]).contiguous()
             proj, fc, out = bf(w['proj']), bf(w['fc']), bf(w['out'])
             gate = w['gate'].detach().float().contiguous() if w.get('gate') is not None else None
             c = cos.detach().reshape(-1, HD // 2)[:T].to(torch.bfloat16).contiguous()
             s = sin.detach().reshape(-1, HD // 2)[:T].to(torch.bfloat16).contiguous()
+            if c.shape[0] < T or s.shape[0] < T:
+                raise ValueError(f'cos / sin: {T} positions of {HD // 2} values needed')
+            _lib.require_cuda(*(z for z in (qkv, proj, fc, out, gate, c, s) if z is not None))
             st = _lib.GPT()
             st.wqkv[layer], st.wproj[layer], st.wfc[layer], st.wmproj[layer] = (z.data_ptr() for z in (qkv, proj, fc,
                                                                                                        out))
@@ -73,7 +80,7 @@ def block_forward(x, w, ve, cos, sin, window, o=None, attn=None, fc=None, mlp=No
         return t.data_ptr()
     ve_p = rows(ve, D)
     jit = _lib.Jitter(rows(o, D), rows(attn, D), rows(fc, 4 * D), rows(mlp, D))
-    _lib.require_cuda(out)
+    _lib.require_cuda(out, *keep)
     L = _lib.lib()
     nbytes = L.noise_block_workspace_bytes(B, T)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=out.device)
@@ -98,6 +105,9 @@ def head_error(raw, y, clean_loss, draws, sigma=0.1, nrep=16, noise=None, vocab=
     if vocab != 4096:
         raise ValueError('vocab must be 4096')
     b, t = y.shape
+    if tuple(raw.shape) != (b, t, vocab) or tuple(clean_loss.shape) != (b, t):
+        raise ValueError(f'raw [b, t, {vocab}] and clean_loss [b, t] for y [b, t]: got {tuple(raw.shape)}, '
+                         f'{tuple(clean_loss.shape)}, {tuple(y.shape)}')
     n = chunk_size(draws, nrep)
     slabs = vocab // SLAB
     raw2 = raw.detach()
@@ -117,6 +127,9 @@ def head_error(raw, y, clean_loss, draws, sigma=0.1, nrep=16, noise=None, vocab=
                                        total.data_ptr(), clean_t.data_ptr(), stream), 'noise_head_error_prep')
     for chunk in range(draws // n):
         a = noise(n * b, t, SLAB).to(torch.bfloat16).contiguous()
+        if tuple(a.shape) != (n * b, t, SLAB):
+            raise ValueError(f'noise drew {tuple(a.shape)}, expected {(n * b, t, SLAB)}')
+        _lib.require_cuda(a)
         _lib.check(L.noise_head_error_chunk(raw2.data_ptr(), dt, raw2.stride(0), a.data_ptr(), y2.data_ptr(),
                                             cl.data_ptr(), sums.data_ptr(), total.data_ptr(), clean_t.data_ptr(), b,
                                             t, n, chunk % slabs, float(sigma), error.data_ptr(), stream),

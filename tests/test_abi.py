@@ -291,3 +291,23 @@ def test_pack_heads_refuses_mismatched_pieces():
                 dict(lses=[p['lses'][0], p['lses'][1][:, :4]])):
         with pytest.raises(ValueError):
             heads.pack_heads_kernel(*(dict(p, **bad)[k] for k in names))
+
+
+def test_dust_wrappers_refuse_mismatched_operands():
+    """Dust's block rerun checks every weight's shape and the RoPE positions, and head_error the logits' vocabulary and
+    the clean losses, before any pointer reaches the library."""
+    import sys
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from dust_inputs import dust_inputs, head_error_inputs
+    from noise_b200 import dust
+    x = dust_inputs()
+    for w, cos, sin in ((dict(x['w'], fc=x['w']['fc'][:1024]), x['cos'], x['sin']),
+                        (dict(x['w'], gate=x['w']['gate'][:4]), x['cos'], x['sin']),
+                        (x['w'], x['cos'][:100], x['sin'][:100])):
+        with pytest.raises(ValueError):
+            dust.block_forward(x['x'], w, x['ve'], cos, sin, 128)
+    h = head_error_inputs()
+    with pytest.raises(ValueError):
+        dust.head_error(h['raw'][..., :2048], h['y'], h['clean_loss'], h['draws'], 0.1, h['nrep'], h['noise'])
+    with pytest.raises(ValueError):
+        dust.head_error(h['raw'], h['y'], h['clean_loss'][:, :-1], h['draws'], 0.1, h['nrep'], h['noise'])
