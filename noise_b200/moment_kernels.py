@@ -44,8 +44,34 @@ def _check(rc, what):
     _lib.check(rc, what)
 
 
-def _rope(cos, sin):
-    return _c(cos, torch.float32), _c(sin, torch.float32)
+def _rope(cos, sin, t):
+    """fp32 contiguous RoPE tables holding 32 values for each of the t positions the kernels read."""
+    cos, sin = _c(cos, torch.float32), _c(sin, torch.float32)
+    for name, z in (('cos', cos), ('sin', sin)):
+        if z.shape[-1] != 32 or z.numel() < 32 * t:
+            raise ValueError(f'{name}: 32 values for each of {t} positions, got {tuple(z.shape)}')
+    return cos, sin
+
+
+def _shapes(**named):
+    """Each keyword is (tensor, expected shape; None where any extent goes, (None, n) for at least n): a mismatch
+    raises before a pointer reaches a kernel, which would otherwise read past a smaller operand's end."""
+    for name, (t, want) in named.items():
+        ok = t.dim() == len(want)
+        for got, w in zip(t.shape, want):
+            ok = ok and (w is None or (got >= w[1] if isinstance(w, tuple) else got == w))
+        if not ok:
+            raise ValueError(f'{name}: shape {tuple(t.shape)}, expected {want}')
+
+
+def _on_device(*ts):
+    _lib.require_cuda(*(z for z in ts if z is not None))
+
+
+def _layer_map(layers, groups):
+    """The int32 layer map of a by-token output: one entry per row group, on the device."""
+    if layers is not None and (layers.dtype != torch.int32 or layers.numel() < groups):
+        raise ValueError(f'layers: int32 with at least {groups} entries')
 
 
 # --- lse and center -----------------------------------------------------------------------------------------------
@@ -54,9 +80,10 @@ def implicit_key_context_edges_impl(q, k, values, hub, window, tc=True):
     """(lse, center); bf16 operands with T % 128 == 0 on the tcgen05 kernel (``tc=False``: the warp-MMA kernel, for
     comparison), the workspace's status word riding on lse."""
     h, t, _ = q.shape
+    _shapes(q=(q, (h, t, 64)), k=(k, (h, t, 64)), values=(values, (h, t, 64)), hub=(hub, (h, t, 64)))
     dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, values, hub = (_c(z, dt) for z in (q, k, values, hub))
-    _lib.require_cuda(q)
+    _on_device(q, k, values, hub)
     lse = torch.empty((h, t), device=q.device, dtype=torch.float32)
     center = torch.empty_like(lse)
     if tc and dt == torch.bfloat16 and t % 128 == 0:
@@ -81,16 +108,24 @@ def value_pass(q, k, lse, source, window, in_heads=1, out_heads=1, out=None, lay
     The signature of the reference's VALUE_IMPL plug-in. bf16 q / k with T % 128 == 0 run on the tcgen05 kernel
     (``tc=False``: the warp-MMA kernel, for comparison); the workspace's status word rides on ``out``."""
     h, t, _ = q.shape
+    _shapes(q=(q, (h, t, 64)), k=(k, (h, t, 64)), lse=(lse, (h, t)))
+    if h % in_heads or h % out_heads:
+        raise ValueError(f'{h} rows do not split into groups of {in_heads} / {out_heads} heads')
     dt = torch.bfloat16 if q.dtype == torch.bfloat16 else torch.float32
     q, k, lse = _c(q, dt), _c(k, dt), _c(lse, torch.float32)
-    _lib.require_cuda(q)
     if source.dtype != torch.float32 or source.stride(-1) != 1:
         source = source.float().contiguous()
     channels = source.shape[-1] // in_heads
     if channels != 64:
         raise ValueError('the value pass runs 64 channels per head')
+    _shapes(source=(source, ((None, h // in_heads), (None, t), in_heads * 64)))
     if out is None:
         out = source.new_empty((h // out_heads, t, out_heads * channels), dtype=torch.float32)
+    _shapes(out=(out, (None if layers is not None else (None, h // out_heads), (None, t), out_heads * 64)))
+    if out.dtype != torch.float32:
+        raise ValueError('out: fp32')
+    _layer_map(layers, h // out_heads)
+    _on_device(q, k, lse, source, out, layers)
     src_rows = _rows(source, in_heads)
     out_rows = _rows(out, out_heads, layers)
     if tc and dt == torch.bfloat16 and t % 128 == 0:
@@ -117,12 +152,21 @@ def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, w
     runs on the tcgen05 kernel (``tc=False``: the warp-MMA kernel, for comparison); its workspace rides on the key
     output as ``_noise_workspace``."""
     h, t, d = k_raw.shape
+    full = (h, t, 64)
+    _shapes(k_raw=(k_raw, full), qp=(qp, full), kp=(kp, full), values=(values, full), hub=(hub, full),
+            lse=(lse, (h, t)), center=(center, (h, t)))
+    if h % out_heads:
+        raise ValueError(f'{h} rows do not split into groups of {out_heads} heads')
     qp, kp, k_raw, values, hub = (_c(z, torch.float32) for z in (qp, kp, k_raw, values, hub))
     lse, center = _c(lse, torch.float32), _c(center, torch.float32)
-    cos, sin = _rope(cos, sin)
-    _lib.require_cuda(qp)
+    cos, sin = _rope(cos, sin, t)
     shape = (h // out_heads, t, out_heads * d)
     key = qp.new_empty(shape) if key is None else key
+    _shapes(key=(key, (None if layers is not None else (None, h // out_heads), (None, t), out_heads * d)))
+    if key.dtype != torch.float32:
+        raise ValueError('key: fp32')
+    _layer_map(layers, h // out_heads)
+    _on_device(qp, kp, k_raw, lse, values, hub, center, cos, sin, key, layers)
     raw_value = qp.new_empty(shape) if with_values else None
     key_rows = _rows(key, out_heads, layers)
     val_rows = _rows(raw_value, out_heads, layers) if with_values else _lib.Rows()
@@ -150,7 +194,7 @@ def key_scan(qp, kp, k_raw, lse, values, hub, center, cos, sin, window, sigma, w
 
 # --- query and key moments ------------------------------------------------------------------------------------------
 
-def _blocked(t, rows, m, blocks):
+def _blocked(t, rows, m, blocks, tokens):
     """noise_rows_t of one of the reference's strided 4-D raw / out arguments (G, blocks, M, >= 64): row r, token s
     at (r // (rows // blocks)) * stride(1) + (n // m) * stride(0) + (n % m) * stride(2), n = (r % (rows // blocks)) *
     T + s (moment_kernels.py:200-220: RAW_BLK, RAW_GPU, RAW_STRIDE, M). (1, rows, T, 64) is the stacked layout; the
@@ -159,6 +203,9 @@ def _blocked(t, rows, m, blocks):
         raise ValueError('raw / out: 4-D with a unit last stride')
     if rows % blocks:
         raise ValueError('rows must split evenly over raw.shape[1] blocks')
+    if t.shape[1] < blocks or t.shape[2] < m or t.shape[3] < 64 or t.shape[0] * m < rows // blocks * tokens:
+        raise ValueError(f'raw / out {tuple(t.shape)}: too small for {rows} rows x {tokens} tokens in {blocks} blocks '
+                         f'of {m} tokens a GPU')
     v = _lib.Rows()
     v.data = t.data_ptr()
     v.heads = 1
@@ -187,19 +234,29 @@ def moment_query_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out
         raise ValueError('head_dim 64 only (the reference asserts it)')
     if side is None:
         raise ValueError("side (the keys' fp32 pair-feature source) is required")
+    full = (rows, t, 64)
+    _shapes(k=(k, full), v=(v, full), hub=(hub, full), side=(side, full), sq=(sq, (rows, t)), steps=(steps, (rows, t)),
+            lse=(lse, (rows, t)), hub_out=(hub_out, (rows, t)))
     q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
     raw = _raw4(raw, rows, t)
     side = _c(side, torch.float32)
     sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
-    cos, sin = _rope(cos, sin)
+    cos, sin = _rope(cos, sin, t)
     window = t if window is None else min(window, t)
     blocks = raw.shape[1]
     if out_heads:  # a (layers, T, heads * D) fp32 view, by token
+        if rows % out_heads or out.dtype != torch.float32:
+            raise ValueError(f'by-token out: fp32, {rows} rows in groups of {out_heads} heads')
+        _shapes(out=(out, (None if layers is not None else (None, rows // out_heads), (None, t), out_heads * 64)))
+        _layer_map(layers, rows // out_heads)
         o, dt, m = _rows(out, out_heads, layers), F32, t
     else:  # the reference's 4-D out: (1, rows, T, D) bf16, or the identity phase's (W, L, N, D) slice
+        if out.dtype not in _DT:
+            raise ValueError('out: fp32 or bf16')
         m = out.shape[2]
-        o, dt = _blocked(out, rows, m, blocks), _DT[out.dtype]
-    rv = _blocked(raw, rows, m, blocks)
+        o, dt = _blocked(out, rows, m, blocks, t), _DT[out.dtype]
+    rv = _blocked(raw, rows, m, blocks, t)
+    _on_device(q, k, v, hub, raw, side, sq, steps, lse, hub_out, cos, sin, out, layers)
     if tc and t % 128 == 0:
         L = _lib.lib()
         nbytes = L.noise_moment_query_scores_workspace_bytes(rows, t)
@@ -223,11 +280,14 @@ def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, 
     views allow 16-byte stores (``tc=False``: the warp-MMA kernel, for comparison). Returns the workspace (its first
     int is the device status word) or None."""
     rows, t, d = q.shape
+    full = (rows, t, 64)
+    _shapes(q=(q, full), k=(k, full), v=(v, full), hub=(hub, full), side=(side, full), sq=(sq, (rows, t)),
+            steps=(steps, (rows, t)), lse=(lse, (rows, t)), hub_out=(hub_out, (rows, t)))
     q, k, v, hub = (_c(z, torch.bfloat16) for z in (q, k, v, hub))
     raw = _raw4(raw, rows, t)
     side = _c(side, torch.float32)
     sq, steps, lse, hub_out = (_c(z, torch.float32) for z in (sq, steps, lse, hub_out))
-    cos, sin = _rope(cos, sin)
+    cos, sin = _rope(cos, sin, t)
     if out.dim() == 3:
         out, values = out.unsqueeze(0), values.unsqueeze(0)
     if values.shape != out.shape or values.stride() != out.stride() or values.dtype != out.dtype:
@@ -235,7 +295,8 @@ def moment_key_scores_impl(q, k, v, hub, raw, sq, side, cos, sin, lse, hub_out, 
     if out.dtype not in _DT:
         raise ValueError('out / values: fp32 or bf16')
     blocks, m = raw.shape[1], out.shape[2]
-    rv, ro, rvals = _blocked(raw, rows, m, blocks), _blocked(out, rows, m, blocks), _blocked(values, rows, m, blocks)
+    rv, ro, rvals = (_blocked(z, rows, m, blocks, t) for z in (raw, out, values))
+    _on_device(q, k, v, hub, raw, side, sq, steps, lse, hub_out, cos, sin, out, values)
     if tc and t % 128 == 0:
         L = _lib.lib()
         nbytes = L.noise_moment_key_scores_workspace_bytes(rows, t)

@@ -311,3 +311,32 @@ def test_dust_wrappers_refuse_mismatched_operands():
         dust.head_error(h['raw'][..., :2048], h['y'], h['clean_loss'], h['draws'], 0.1, h['nrep'], h['noise'])
     with pytest.raises(ValueError):
         dust.head_error(h['raw'], h['y'], h['clean_loss'][:, :-1], h['draws'], 0.1, h['nrep'], h['noise'])
+
+
+def test_credit_wrappers_refuse_mismatched_operands():
+    """The credit ops check every operand against the rows x T x 64 the kernels address (per-row vectors [rows, T],
+    RoPE tables of T positions, blocked raw / out views large enough), before any pointer reaches the library."""
+    import sys
+    import torch
+    sys.path.insert(0, str(ROOT / 'tests' / 'golden'))
+    from credit_inputs import credit_inputs
+    from noise_b200 import moment_kernels as mk
+    x = credit_inputs()
+    q, k, v, hub = (z.bfloat16() for z in (x['qp'], x['kp'], x['values'], x['hub']))
+    rows, t, _ = q.shape
+    lse, sq = torch.zeros(rows, t), torch.ones(rows, t)
+    bad = [
+        lambda: mk.implicit_key_context_edges_impl(q, k[:, :-1], v, hub, 64),
+        lambda: mk.value_pass(q, k, lse[:, :-1], x['hub'], 64),
+        lambda: mk.key_scan(x['qp'], x['kp'], x['k_raw'], lse, x['values'], x['hub'], lse, x['cos'][:100],
+                            x['sin'][:100], 64, 0.003),
+        lambda: mk.key_scan(x['qp'], x['kp'], x['k_raw'], lse, x['values'][:1], x['hub'], lse, x['cos'], x['sin'], 64,
+                            0.003),
+        lambda: mk.moment_query_scores_impl(q, k, v, hub, x['q_raw'].unsqueeze(0), sq, x['kp'][..., :32], x['cos'],
+                                            x['sin'], lse, lse, sq, torch.empty(1, rows, t, 64, dtype=torch.bfloat16)),
+        lambda: mk.moment_query_scores_impl(q, k, v, hub, x['q_raw'].unsqueeze(0), sq, x['kp'], x['cos'], x['sin'],
+                                            lse, lse, sq, torch.empty(1, rows, t // 2, 64, dtype=torch.bfloat16)),
+    ]
+    for call in bad:
+        with pytest.raises(ValueError):
+            call()
