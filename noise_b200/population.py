@@ -58,7 +58,8 @@ class PackedGPT:
 
     def __init__(self, params, device=None, cos=None, sin=None):
         self.params = params
-        self.device = torch.device(device) if device is not None else params['lm_head.weight'].device
+        head = params.get('lm_head.weight')  # a missing one is reported by refresh's shape check
+        self.device = torch.device(device) if device is not None else (head.device if head is not None else None)
         self._key = None
         self._cos, self._sin = cos, sin
         self.refresh()
@@ -79,13 +80,23 @@ class PackedGPT:
 
     def refresh(self):
         """Re-pack if a source changed; ``packs`` = the pack kernels this call launched."""
+        p = self.params
+        for name, shape in PARAMS:  # each is packed into a slot of exactly this size
+            if name not in p or tuple(p[name].shape) != shape:
+                raise ValueError(f'{name}: expected shape {shape}, got '
+                                 f'{tuple(p[name].shape) if name in p else "nothing"}')
         key = self._source_key()
         self.packs = 0
         if key == self._key:
             return self
-        p, dev = self.params, self.device
+        dev = self.device
         for t in p.values():
             _lib.require_cuda(t)
+        if self._cos is not None:
+            for z in (self._cos, self._sin):
+                if z.dtype != torch.bfloat16 or z.dim() != 2 or z.shape[1] != HEAD_DIM // 2:
+                    raise ValueError(f'RoPE tables: bf16 [positions, {HEAD_DIM // 2}], got {z.dtype} {tuple(z.shape)}')
+            _lib.require_cuda(self._cos, self._sin)
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.wqkv, self.wproj, self.wfc, self.wmproj, self.wgate, self.ve = [], [], [], [], [], []
         for i in range(N_LAYER):
@@ -125,6 +136,11 @@ class PackedGPT:
         self._key = key
         return self
 
+    def check_length(self, length):
+        """The RoPE tables cover positions 0 .. length - 1 (the kernels read one row per position)."""
+        if self._cos.shape[0] < length or self._sin.shape[0] < length:
+            raise ValueError(f'the RoPE tables hold {self._cos.shape[0]} positions, the rows {length}')
+
 
 _packed = {}
 
@@ -159,6 +175,7 @@ def _run(packed, slices, keep, sign, idx, targets, reduction):
     dev = packed.device
     sign, idx, targets = _row_args(sign, idx, targets, reduction)
     m, length = sign.shape[0], idx.shape[0]
+    packed.check_length(length)
     L = _lib.lib()
     nbytes = L.noise_population_workspace_bytes(m, length)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
@@ -181,13 +198,17 @@ def population_loss(model, p, noise, sign, idx, targets, reduction='mean'):
     noise: name -> (a [m, out], b [m, in]) for matrices and embeddings, eps [m, numel] for the mixing scalars;
     sign [m] (+-sigma); idx, targets [T] int64 with T % 128 == 0."""
     packed = _packed_for(model, p)
+    m = sign.shape[0] if sign.dim() == 1 else -1
     slices, keep = [], []
-    for name in NAMES:
+    for name, shape in PARAMS:
         v = noise[name]
         if isinstance(v, (tuple, list)):
             a, b = (t.detach().float() for t in v)
             if a.stride(-1) != 1 or b.stride(-1) != 1:
                 a, b = a.contiguous(), b.contiguous()
+            if len(shape) != 2 or tuple(a.shape) != (m, shape[0]) or tuple(b.shape) != (m, shape[1]):
+                raise ValueError(f'{name}: a [m, out] and b [m, in] for m = {m} members of a {shape} parameter, got '
+                                 f'{tuple(a.shape)}, {tuple(b.shape)}')
             _lib.require_cuda(a, b)
             keep += [a, b]
             slices.append(_lib.Slice(a.data_ptr(), b.data_ptr(), None, a.stride(0), b.stride(0)))
@@ -195,6 +216,8 @@ def population_loss(model, p, noise, sign, idx, targets, reduction='mean'):
             e = v.detach().float()
             if e.stride(-1) != 1:
                 e = e.contiguous()
+            if len(shape) != 1 or tuple(e.shape) != (m, shape[0]):
+                raise ValueError(f'{name}: eps [m, {shape[0]}] for m = {m} members, got {tuple(e.shape)}')
             _lib.require_cuda(e)
             keep.append(e)
             slices.append(_lib.Slice(e.data_ptr(), e.data_ptr(), None, e.stride(0), e.stride(0)))
@@ -245,6 +268,7 @@ def population_loss_offsets_noalloc(packed, buffer, member_off, sign, idx, targe
     slices, member_off = _offset_slices(packed, buffer, member_off, sign.shape[0])
     sign, idx, targets = _row_args(sign, idx, targets, reduction)
     m, length = sign.shape[0], idx.shape[0]
+    packed.check_length(length)
     dev = packed.device
     losses = torch.empty((m, length) if reduction == 'none' else (m,), dtype=torch.float32, device=dev)
     arr = (_lib.Slice * len(NAMES))(*slices)
@@ -273,6 +297,9 @@ def gpt_loss(model, p, idx, targets, loss_reduction='mean'):
     if idx.dim() != 2 or targets.shape != idx.shape:
         raise ValueError('idx and targets must be [B, T] of the same shape')
     rows, length = idx.shape
+    packed.check_length(length)
+    if loss_reduction not in _lib.REDUCTION:
+        raise ValueError(f'loss_reduction must be one of {sorted(_lib.REDUCTION)}')
     L = _lib.lib()
     nbytes = L.noise_gpt_workspace_bytes(rows, length)
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
@@ -295,6 +322,8 @@ def head_loss(x, weight, targets, vocab=VOCAB):
     dev = x.device
     xs = x.detach().reshape(-1, N_EMBD).float().contiguous()
     w = weight.detach()[:VOCAB]
+    if tuple(w.shape) != (VOCAB, N_EMBD):
+        raise ValueError(f'weight: [>= {VOCAB}, {N_EMBD}], got {tuple(weight.shape)}')
     w = (w if w.dtype == torch.bfloat16 else w.bfloat16()).contiguous()
     tg = targets.detach().reshape(-1).long().contiguous()
     _lib.require_cuda(xs, w, tg)

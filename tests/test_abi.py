@@ -340,3 +340,21 @@ def test_credit_wrappers_refuse_mismatched_operands():
     for call in bad:
         with pytest.raises(ValueError):
             call()
+
+
+def test_population_wrappers_refuse_mismatched_operands():
+    """Every parameter is packed into a slot of its GPT shape, so a mismatched one is refused before any pack; the
+    head loss needs the LM head's 4096 rows."""
+    import torch
+    from noise_b200 import population
+    from oracle import gpt
+    w = gpt.init_weights(0, eggroll=True)
+    bad = dict(w)
+    bad['transformer.h.0.attn.c_q.weight'] = w['transformer.h.0.attn.c_q.weight'][:256]
+    with pytest.raises(ValueError):
+        population.PackedGPT(bad)
+    missing = {k: v for k, v in w.items() if k != 'lm_head.weight'}
+    with pytest.raises(ValueError):
+        population.PackedGPT(missing)
+    with pytest.raises(ValueError):
+        population.head_loss(torch.randn(2, 128, 512), torch.randn(2048, 512), torch.zeros(2, 128, dtype=torch.long))
