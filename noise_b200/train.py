@@ -64,9 +64,20 @@ def rebuild_update(buffer, offsets, weight, count, shard, grad_flat, fp):
     """Write into grad_flat (fp32, FlatParams layout) the update terms of the pairs shard = (start, stop):
     G_P = -(1 / count) sum_j w_j a_j b_j^T. offsets: int64 [60, pairs]; weight: fp32 [pairs].
     Returns (device status word, number of the library's kernels enqueued)."""
+    start, stop = shard
+    pairs = offsets.shape[1] if offsets.dim() == 2 else -1
+    if offsets.dtype != torch.int64 or tuple(offsets.shape) != (len(PARAMS), pairs) or tuple(weight.shape) != (pairs,):
+        raise ValueError(f'offsets int64 [{len(PARAMS)}, pairs] and weight [pairs]: got {offsets.dtype} '
+                         f'{tuple(offsets.shape)}, {tuple(weight.shape)}')
+    if not 0 <= start <= stop <= pairs:
+        raise ValueError(f'shard {shard} outside the {pairs} pairs')
+    if buffer.dtype != torch.float32 or buffer.dim() != 1:
+        raise ValueError('buffer: a 1-D fp32 tensor')
+    if grad_flat.dtype != torch.float32 or grad_flat.shape != fp.flat.shape or not grad_flat.is_contiguous():
+        raise ValueError(f'grad_flat: contiguous fp32 {tuple(fp.flat.shape)}')
+    _lib.require_cuda(buffer, offsets, weight, grad_flat)
     L = _lib.lib()
     stream = _lib.stream_handle(buffer.device)
-    start, stop = shard
     n = stop - start
     scale = -1.0 / count
     status = torch.zeros(_lib.STATUS_BYTES // 4, dtype=torch.int32, device=buffer.device)
@@ -109,6 +120,9 @@ class AdamW:
         self.t = 0
 
     def step(self, grad, lr=None):
+        if grad.dtype != torch.float32 or grad.shape != self.flat.shape or not grad.is_contiguous():
+            raise ValueError(f'grad: contiguous fp32 {tuple(self.flat.shape)}')
+        _lib.require_cuda(self.flat, grad)
         self.t += 1
         _lib.check(_lib.lib().noise_adam_step(self.flat.data_ptr(), self.exp_avg.data_ptr(),
                                               self.exp_avg_sq.data_ptr(), grad.data_ptr(), self.flat.numel(),
