@@ -105,67 +105,142 @@ SIGNATURES = [
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
       ctypes.c_void_p]),
     ('noise_pack_bf16', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
-    ('noise_rank1_operands', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_rank1_operands_f32', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_rank1_small', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_adam_step', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
-    ('noise_implicit_key_context', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_value_pass', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
-    ('noise_implicit_key_context_ws', ctypes.c_int, [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_rank1_operands', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_rank1_operands_f32', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_rank1_small', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_adam_step', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_float,
+      ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+    ('noise_implicit_key_context', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_value_pass', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows),
+      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    ('noise_implicit_key_context_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_value_pass_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
-    ('noise_value_pass_ws', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_value_pass_ws', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(Rows), ctypes.POINTER(Rows),
+      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_key_scan', ctypes.c_int,
-     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+      ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
     ('noise_moment_key_scores', ctypes.c_int,
-     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p]),
     ('noise_moment_query_scores', ctypes.c_int,
-     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_moment_key_scores_v', ctypes.c_int,
-     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int,
+      ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
     ('noise_key_scan_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
-    ('noise_key_scan_ws', ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_key_scan_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.POINTER(Rows),
+      ctypes.POINTER(Rows), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_moment_key_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_moment_key_scores_ws', ctypes.c_int,
-     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int,
+      ctypes.c_int, ctypes.POINTER(Rows), ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+      ctypes.c_void_p]),
     ('noise_moment_query_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_moment_query_scores_ws', ctypes.c_int,
-     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+      ctypes.c_void_p]),
     ('noise_moment_query_scores_v', ctypes.c_int,
-     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
-    ('noise_pack_heads', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_head_prep', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
+     [ctypes.c_void_p] * 4 + [ctypes.POINTER(Rows), ctypes.c_int] + [ctypes.c_void_p] * 7 + [ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, ctypes.POINTER(Rows), ctypes.c_int, ctypes.c_void_p]),
+    ('noise_pack_heads', ctypes.c_int,
+     [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_head_prep', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+      ctypes.c_float, ctypes.c_float, ctypes.POINTER(HeadPrep), ctypes.c_void_p]),
     ('noise_id_head_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
-    ('noise_id_head_scores', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_id_head_scores', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+      ctypes.c_float, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     ('noise_exchange_alloc', ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]),
     ('noise_exchange_open', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
     ('noise_exchange_close', ctypes.c_int, [ctypes.c_void_p]),
     ('noise_exchange_free', ctypes.c_int, [ctypes.c_void_p]),
-    ('noise_exchange_wait', ctypes.c_int, [ctypes.POINTER(Peers), ctypes.c_int, ctypes.c_uint32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_alltoall_peer', ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(Peers), ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
-    ('noise_pack_heads_peer', ctypes.c_int, [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Peers), ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
-    ('noise_hidden_credits', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_at_b_layers', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_square_credit_grads', ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_future_scores', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_key_response', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_exchange_wait', ctypes.c_int,
+     [ctypes.POINTER(Peers), ctypes.c_int, ctypes.c_uint32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_alltoall_peer', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_size_t, ctypes.POINTER(Peers), ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32,
+      ctypes.c_void_p]),
+    ('noise_pack_heads_peer', ctypes.c_int,
+     [ctypes.POINTER(HeadPieces), ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(Peers), ctypes.c_size_t,
+      ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
+    ('noise_hidden_credits', ctypes.c_int,
+     [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_at_b_layers', ctypes.c_int,
+     [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_square_credit_grads', ctypes.c_int,
+     [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_future_scores', ctypes.c_int,
+     [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_key_response', ctypes.c_int,
+     [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_future_scores_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 2),
     ('noise_key_response_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 2),
-    ('noise_future_scores_ws', ctypes.c_int, [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_key_response_ws', ctypes.c_int, [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_query_response', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_future_scores_ws', ctypes.c_int,
+     [ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+       ctypes.c_void_p]),
+    ('noise_key_response_ws', ctypes.c_int,
+     [ctypes.POINTER(View3), ctypes.c_void_p, ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+       ctypes.c_void_p]),
+    ('noise_query_response', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_expm1_f32', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]),
     ('noise_query_response_workspace_bytes', ctypes.c_size_t, [ctypes.c_int] * 4),
-    ('noise_query_response_ws', ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_routed_response', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_routed_response_ws', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_readout_stats', ctypes.c_int, [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]),
-    ('noise_readout_staged', ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p]),
-    ('noise_readout_staged_ws', ctypes.c_int, [ctypes.c_void_p] * 8 + [ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_readout_direct_ws', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
-    ('noise_readout_direct', ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ScorerTables), ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
+    ('noise_query_response_ws', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.POINTER(View3), ctypes.POINTER(View3), ctypes.POINTER(View3),
+      ctypes.POINTER(View3)] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+       ctypes.c_void_p]),
+    ('noise_routed_response', ctypes.c_int,
+     [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_routed_response_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_readout_stats', ctypes.c_int,
+     [ctypes.c_void_p] * 5 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]),
+    ('noise_readout_staged', ctypes.c_int,
+     [ctypes.c_void_p] * 8 + [ctypes.POINTER(ScorerTables), ctypes.c_void_p,
+      ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p]),
+    ('noise_readout_staged_ws', ctypes.c_int,
+     [ctypes.c_void_p] * 8 + [ctypes.POINTER(ScorerTables), ctypes.c_void_p,
+      ctypes.c_void_p] + [ctypes.c_int] * 6 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_readout_direct_ws', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+      ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ScorerTables), ctypes.c_void_p,
+      ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    ('noise_readout_direct', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+      ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ScorerTables), ctypes.c_void_p,
+      ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p]),
     ('noise_cycle_weights', ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] + [ctypes.c_void_p] * 7),
-    ('noise_cycle_finish', ctypes.c_int, [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
-    ('noise_coordinate_change', ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_cycle_finish', ctypes.c_int,
+     [ctypes.c_void_p] * 9 + [ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
+    ('noise_coordinate_change', ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p]),
     ('noise_block_workspace_bytes', ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
     ('noise_block_forward', ctypes.c_int,
      [ctypes.POINTER(GPT), ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Jitter), ctypes.c_int,
