@@ -601,8 +601,10 @@ int noise_population_loss(const noise_gpt_t* model, const noise_slice_t* noise, 
  * utils/model.py:24-31, has no counterpart): work item `item` of a launch over head_rows (member x head) rows of
  * `pairs` pairs of 128-query tiles, dealt round-robin to `grid` persistent CTAs, is pair *pair of head row *head_row.
  * order 0: heaviest pair first over the launch (the forward's default); order 1: blocks of `grid` head rows, each CTA
- * taking every pair of one row in turn so the row's keys and values are re-read from L2 (the forward uses it when
- * the environment variable NOISE_B200_ATTN_ORDER is "1"). */
+ * taking every pair of one row in turn so the row's keys and values are re-read from L2; order 2: head-major, a row's
+ * pairs heaviest first, which the kernel's CTAs claim from a launch-wide counter as they finish (grid unused). The
+ * forward uses order 1 or 2 when the environment variable NOISE_B200_ATTN_ORDER is "1" or "2"; order 2 keeps its
+ * counter in word 32 of the workspace's status block. */
 int noise_attention_item(int order, int item, int head_rows, int pairs, int grid, int* pair, int* head_row);
 
 /* Bytes of scratch noise_gpt_loss needs for `rows` rows of `tokens` tokens. */

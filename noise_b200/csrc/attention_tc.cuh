@@ -47,6 +47,7 @@ struct TAttnArgs {
   int* status;
   const float* jit;  // [M, 512] fp32 added to the attention output before c_proj, or NULL (Dust's o jitter site)
   int order;         // attention_item's order
+  int* next_item;    // order 2: the launch's next unclaimed work item (zeroed before the launch)
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -69,8 +70,16 @@ __device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
 //   order 1: blocks of `grid` head rows, each block heaviest pair first: CTA c takes every pair of head row
 //            blk grid + c in turn, so the row's keys and values come from HBM once and then from L2, while each round
 //            still takes one pair level. The rows past the last whole block are dealt heaviest first over all CTAs.
-// Both are bijections of [0, npairs bh) onto (pair, row).
+//   order 2: head-major, a row's pairs heaviest first; the CTAs claim items in this order from a launch-wide counter
+//            as they finish their previous one, so the CTAs working on a head row at once share its keys and values
+//            through L2 within a few items, and the unequal costs of the pair levels balance dynamically.
+// All are bijections of [0, npairs bh) onto (pair, row).
 __host__ __device__ inline void attention_item(int order, int w, int bh, int npairs, int grid, int& pi, int& row) {
+  if (order == 2) {  // head-major, heaviest pair first within a row; the items are claimed dynamically
+    pi = npairs - 1 - w % npairs;
+    row = w / npairs;
+    return;
+  }
   const int per = grid * npairs, full = order == 1 ? bh / grid : 0;
   if (w < full * per) {
     const int r = w % per;
@@ -94,7 +103,10 @@ __device__ __forceinline__ TileRange tile_range(int qt, int window) {
   return TileRange{edge ? (q0 - window) / TA_BK : 0, q0 / TA_BK, edge};
 }
 
-template <bool JIT>  // JIT: add TAttnArgs::jit to the attention output (Dust's o jitter site)
+// JIT: add TAttnArgs::jit to the attention output (Dust's o jitter site). DYN: take work items in order 2 from the
+// launch-wide counter p.next_item (the producer lane claims one, then hands its index to the MMA and softmax warps
+// through a 2-slot ring in shared memory); otherwise CTA c takes items c, c + grid, ...
+template <bool JIT, bool DYN>
 __global__ void __launch_bounds__(TA_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, TAttnArgs p) {
@@ -113,6 +125,9 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   uint64_t* o_empty = o_full + 2;            // per group: the group's warps read its O
   uint64_t* drain = o_empty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* item_full = bar + 22;                           // DYN: slot's item index written (2)
+  uint64_t* item_empty = bar + 24;                          // DYN: slot read by the MMA warp and 8 softmax warps (2)
+  volatile int* item_slot = reinterpret_cast<int*>(bar + 26);  // DYN: 2 item indices (-1: no more work)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = p.T / TA_BQ;
@@ -155,6 +170,12 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       mbar_init(&o_empty[b], 4);
     }
     mbar_init(drain, 1);
+    if constexpr (DYN) {
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&item_full[b], 1);
+        mbar_init(&item_empty[b], 9);
+      }
+    }
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -171,12 +192,42 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   const uint32_t sbase = smem_u32(smem);
+  // the CTA's n-th work item without DYN: c + n grid (-1 past the launch's items)
+  auto static_item = [&](int n) {
+    const int w = static_cast<int>(blockIdx.x) + n * static_cast<int>(gridDim.x);
+    return w < items ? w : -1;
+  };
+  // DYN, the producer lane: claim the launch's next item for the CTA's n-th and hand its index over in slot n % 2
+  // (-1 once the launch's items are gone; -2 if the slot's wait gave up)
+  auto claim_item = [&](int n) {
+    const int slot = n & 1;
+    if (!mbar_wait(&item_empty[slot], (static_cast<uint32_t>(n >> 1) & 1u) ^ 1u, p.status)) return -2;
+    int w = atomicAdd(p.next_item, 1);
+    if (w >= items) w = -1;
+    item_slot[slot] = w;
+    mbar_arrive(&item_full[slot]);
+    return w;
+  };
+  // DYN, the MMA and softmax warps: the CTA's n-th item index from slot n % 2, then the slot is released (one arrival
+  // per warp); the wait is warp-wide, so every lane of a warp gets the same index
+  auto take_item = [&](int n) {
+    const int slot = n & 1;
+    if (!mbar_wait_warp(&item_full[slot], static_cast<uint32_t>(n >> 1) & 1u, p.status)) return -2;
+    const int w = item_slot[slot];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&item_empty[slot]);
+    return w;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       int kv = 0, nitem = 0;  // K / V tiles issued, items started
       bool ok = true;
-      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+      auto next = [&](int n) {
+        if constexpr (DYN) return claim_item(n);
+        else return static_item(n);
+      };
+      for (int w = next(0); w >= 0 && ok; ++nitem, w = ok ? next(nitem) : -1) {
         const Item it = item(w);
         const int row0 = it.bh * p.T;
         if (!mbar_wait(q_empty, (static_cast<uint32_t>(nitem) & 1u) ^ 1u, p.status)) break;
@@ -206,7 +257,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       int kv = 0, nitem = 0;
       int s_count[2] = {0, 0}, pv_count[2] = {0, 0};
       bool ok = true;
-      for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+      auto next = [&](int n) {
+        if constexpr (DYN) return take_item(n);
+        else return static_item(n);
+      };
+      for (int w = next(0); w >= 0 && ok; ++nitem, w = ok ? next(nitem) : -1) {
         const Item it = item(w);
         const TileRange rg[2] = {it.ra, it.rb};
         auto sees = [&](int g, int kt) { return kt >= rg[g].lo && kt <= rg[g].hi; };
@@ -293,7 +348,11 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     constexpr float OFF = 8.f * 1.4426950408889634f;     // the fixed offset 8 in base 2
     int cnt = 0, nitem = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < items && ok; w += gridDim.x, ++nitem) {
+    auto next = [&](int n) {
+      if constexpr (DYN) return take_item(n);
+      else return static_item(n);
+    };
+    for (int w = next(0); w >= 0 && ok; ++nitem, w = ok ? next(nitem) : -1) {
       const Item it = item(w);
       const TileRange rg = g == 0 ? it.ra : it.rb;
       const int tq = (g == 0 ? it.qa : it.qb) * TA_BQ + r;

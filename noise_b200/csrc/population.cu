@@ -1021,12 +1021,12 @@ static int run_gemm_plain(const void* A, int M, int K, const void* B, int N, flo
   return cudaGetLastError() == cudaSuccess ? NOISE_OK : NOISE_ERR_CUDA;
 }
 
-// attention_item's order for every attention launch: 1 when NOISE_B200_ATTN_ORDER is "1" (head rows in per-CTA
-// blocks), else 0 (the launch-wide heaviest-first order)
+// attention_item's order for every attention launch: NOISE_B200_ATTN_ORDER "1" (head rows in per-CTA blocks) or "2"
+// (head-major, items claimed from a launch-wide counter), else 0 (the launch-wide heaviest-first order)
 static int attention_order() {
   static const int order = [] {
     const char* e = getenv("NOISE_B200_ATTN_ORDER");
-    return e && e[0] == '1' && e[1] == '\0' ? 1 : 0;
+    return e && (e[0] == '1' || e[0] == '2') && e[1] == '\0' ? e[0] - '0' : 0;
   }();
   return order;
 }
@@ -1039,15 +1039,21 @@ static int run_attention(const void* q, const void* k, const void* v, int M, int
   if ((rc = make_map(&mq, q, HD, rows, TA_BQ)) || (rc = make_map(&mk, k, HD, rows, TA_BK)) ||
       (rc = make_map(&mv, v, HD, rows, TA_BK)))
     return rc;
-  auto kern = args.jit ? attention_tc_kernel<true> : attention_tc_kernel<false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
-    return NOISE_ERR_CUDA;
-  launch_begin(s, K_ATTENTION);
-  const int sms = sm_count();
-  if (sms <= 0) return NOISE_ERR_CUDA;
   TAttnArgs a = args;
   a.bh = members * H;
   a.order = attention_order();
+  const bool dyn = a.order == 2;
+  auto kern = args.jit ? (dyn ? attention_tc_kernel<true, true> : attention_tc_kernel<true, false>)
+                       : (dyn ? attention_tc_kernel<false, true> : attention_tc_kernel<false, false>);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
+    return NOISE_ERR_CUDA;
+  const int sms = sm_count();
+  if (sms <= 0) return NOISE_ERR_CUDA;
+  if (dyn) {  // the work counter: word 32 of the workspace's 256-byte status block (word 0 is the status)
+    a.next_item = a.status + 32;
+    if (cudaMemsetAsync(a.next_item, 0, sizeof(int), s) != cudaSuccess) return NOISE_ERR_CUDA;
+  }
+  launch_begin(s, K_ATTENTION);
   const int items = (T / TA_BQ + 1) / 2 * a.bh;
   kern<<<items < sms ? items : sms, TA_THREADS, TA_SMEM, s>>>(mq, mk, mv, a);
   launch_end(s);
@@ -1126,7 +1132,7 @@ using namespace noise;
 extern "C" {
 
 int noise_attention_item(int order, int item, int head_rows, int pairs, int grid, int* pair, int* head_row) {
-  if (!pair || !head_row || order < 0 || order > 1) return NOISE_ERR_ARGUMENT;
+  if (!pair || !head_row || order < 0 || order > 2) return NOISE_ERR_ARGUMENT;
   const int64_t items = static_cast<int64_t>(head_rows) * pairs;
   if (head_rows < 1 || pairs < 1 || items > 0x7FFFFFFF || grid < 1 || grid > items || item < 0 || item >= items)
     return NOISE_ERR_SHAPE;

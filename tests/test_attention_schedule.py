@@ -2,7 +2,8 @@
 both orders are bijections of the launch's items onto (pair, head row); order 0 is the launch-wide heaviest-first
 order; order 1 gives each persistent CTA every pair of one head row in turn while every round of the grid still takes
 one pair level, so per-CTA work stays as balanced as order 0's at the bench's launch (512 members x 8 heads, T 2048,
-148 CTAs); and, in an LRU model of the L2, order 1 reads each head row's keys and values from HBM once."""
+148 CTAs); and, in an LRU model of the L2, order 1 reads each head row's keys and values from HBM once. Order 2 is
+head-major with items claimed dynamically: balanced by the claiming, and L2-local with a much smaller cache."""
 import ctypes
 
 import pytest
@@ -23,7 +24,8 @@ def item():
 
 
 def key_span(pi, tokens, window):
-    """(lo, hi) key tiles one item streams: the union of its two query tiles' ranges (tile_range in attention_tc.cuh)."""
+    """(lo, hi) key tiles one item streams: the union of its two query tiles' ranges (attention_tc.cuh's
+    tile_range)."""
     nq = tokens // TQ
 
     def lo_hi(qt):
@@ -47,7 +49,7 @@ def schedule(item, order, bh, npairs, grid):
 @pytest.mark.parametrize('bh,npairs,grid', [(3, 1, 3), (10, 8, 80), (148, 8, 148), (300, 8, 148), (4096, 8, 148),
                                             (37, 5, 100)])
 def test_orders_are_bijections(item, bh, npairs, grid):
-    for order in (0, 1):
+    for order in (0, 1, 2):
         got = schedule(item, order, bh, npairs, grid)
         assert sorted(got) == [(p, r) for p in range(npairs) for r in range(bh)], order
 
@@ -88,7 +90,7 @@ def test_rejects_bad_arguments():
     from noise_b200 import _lib
     L = _lib.lib()
     a, b = ctypes.c_int(), ctypes.c_int()
-    assert L.noise_attention_item(2, 0, 8, 8, 8, ctypes.byref(a), ctypes.byref(b)) == 4   # order
+    assert L.noise_attention_item(3, 0, 8, 8, 8, ctypes.byref(a), ctypes.byref(b)) == 4   # order
     assert L.noise_attention_item(1, 64, 8, 8, 8, ctypes.byref(a), ctypes.byref(b)) == 1  # item past the launch
     assert L.noise_attention_item(1, 0, 8, 8, 65, ctypes.byref(a), ctypes.byref(b)) == 1  # grid above the items
     assert L.noise_attention_item(1, 0, 8, 8, 8, None, ctypes.byref(b)) == 4
@@ -99,33 +101,74 @@ def dram_tiles_lru(item, order, bh, tokens, window, grid=148, l2_mb=126):
     to the algorithmic q, k, v, y once each: the grid's CTAs take their items round-robin (attention_item) and advance
     one tile access each in turn (every item loads Q_A, Q_B, then K and V of each key tile, and stores y_A, y_B). A
     model of the B200's L2 (126 MB, not exactly LRU, split over two dies), for the schedule's locality only."""
-    from collections import OrderedDict
     nq = tokens // TQ
     npairs = (nq + 1) // 2
     streams = [[] for _ in range(grid)]
     for w in range(bh * npairs):
-        pi, row = item(order, w, bh, npairs, grid)
-        lo, hi = key_span(pi, tokens, window)
-        acc = [('q', row, 2 * pi), ('q', row, 2 * pi + 1)]
-        for kt in range(lo, hi + 1):
-            acc += [('k', row, kt), ('v', row, kt)]
-        streams[w % grid] += acc + [('y', row, 2 * pi), ('y', row, 2 * pi + 1)]
-    cap, lru, moved = l2_mb * 64, OrderedDict(), 0
+        streams[w % grid] += item_tiles(*item(order, w, bh, npairs, grid), tokens, window)
+    cache = LruTiles(l2_mb)
     pos = [0] * grid
     while any(pos[c] < len(streams[c]) for c in range(grid)):
         for c in range(grid):
             if pos[c] < len(streams[c]):
-                key = streams[c][pos[c]]
+                cache.touch(streams[c][pos[c]])
                 pos[c] += 1
-                if key in lru and key[0] != 'y':
-                    lru.move_to_end(key)
-                else:
-                    moved += 1  # a miss read from HBM, or a store written back
-                    lru[key] = True
-                    lru.move_to_end(key)
-                    while len(lru) > cap:
-                        lru.popitem(last=False)
-    return moved / (bh * nq * 4)
+    return cache.moved / (bh * nq * 4)
+
+
+def item_tiles(pi, row, tokens, window):
+    """The 16 KB tiles one work item touches, in order: Q_A, Q_B, K and V of each key tile, y_A, y_B."""
+    lo, hi = key_span(pi, tokens, window)
+    acc = [('q', row, 2 * pi), ('q', row, 2 * pi + 1)]
+    for kt in range(lo, hi + 1):
+        acc += [('k', row, kt), ('v', row, kt)]
+    return acc + [('y', row, 2 * pi), ('y', row, 2 * pi + 1)]
+
+
+class LruTiles:
+    """An LRU cache of l2_mb in 16 KB tiles, counting the tiles moved to or from HBM (misses and stores)."""
+
+    def __init__(self, l2_mb):
+        from collections import OrderedDict
+        self.cap, self.lru, self.moved = l2_mb * 64, OrderedDict(), 0
+
+    def touch(self, key):
+        if key in self.lru and key[0] != 'y':
+            self.lru.move_to_end(key)
+            return
+        self.moved += 1  # a miss read from HBM, or a store written back
+        self.lru[key] = True
+        self.lru.move_to_end(key)
+        while len(self.lru) > self.cap:
+            self.lru.popitem(last=False)
+
+
+def dram_tiles_dynamic(item, bh, tokens, window, grid=148, l2_mb=126):
+    """Order 2 as the kernel runs it: each CTA claims the next item in order when it finishes its last, and every tile
+    access takes one time unit. Returns (the last CTA's finish / the evenly shared work, traffic relative to the
+    algorithmic q, k, v, y once each) under an LRU cache of l2_mb."""
+    import heapq
+    nq = tokens // TQ
+    npairs = (nq + 1) // 2
+    items = bh * npairs
+    claimed, work, events = 0, 0, []
+    for c in range(min(grid, items)):
+        s = item_tiles(*item(2, claimed, bh, npairs, grid), tokens, window)
+        claimed, work = claimed + 1, work + len(s)
+        heapq.heappush(events, (0, c, s, 0))
+    cache, finish = LruTiles(l2_mb), 0
+    while events:
+        t, c, s, pos = heapq.heappop(events)
+        cache.touch(s[pos])
+        if pos + 1 < len(s):
+            heapq.heappush(events, (t + 1, c, s, pos + 1))
+            continue
+        finish = max(finish, t + 1)
+        if claimed < items:
+            s = item_tiles(*item(2, claimed, bh, npairs, grid), tokens, window)
+            claimed, work = claimed + 1, work + len(s)
+            heapq.heappush(events, (t + 1, c, s, 0))
+    return finish / (work / min(grid, items)), cache.moved / (bh * nq * 4)
 
 
 @pytest.mark.parametrize('window', [1024, 2048])
@@ -136,3 +179,12 @@ def test_order_one_reads_keys_and_values_once(item, window):
     r0 = dram_tiles_lru(item, 0, 512, 2048, window)
     r1 = dram_tiles_lru(item, 1, 512, 2048, window)
     assert 2.0 < r0 < 2.8 and r1 < 1.05, (r0, r1)
+
+
+@pytest.mark.parametrize('window', [1024, 2048])
+def test_order_two_claims_balance_and_share_rows(item, window):
+    """Order 2, claimed dynamically, at the bench's launch (512 members x 8 heads): the last CTA finishes within 1% of
+    the evenly shared work, and each head row's keys and values come from HBM once even when only 16 MB of the L2
+    behaves like LRU (order 1 needs about 80-100 MB)."""
+    span, traffic = dram_tiles_dynamic(item, 4096, 2048, window, l2_mb=16)
+    assert span < 1.01 and traffic < 1.02, (span, traffic)
