@@ -86,8 +86,9 @@ WINDOWS = [1024, 1024, 1024, 2048, 1024, 1024, 1024, 2048]
 
 
 def attention_order():
-    """The attention kernel's work order this run uses (the library reads NOISE_B200_ATTN_ORDER: "1" or default 0)."""
-    return 1 if os.environ.get('NOISE_B200_ATTN_ORDER') == '1' else 0
+    """The attention kernel's work order this run uses (the library reads NOISE_B200_ATTN_ORDER: "1", "2" or default
+    0)."""
+    return {'1': 1, '2': 2}.get(os.environ.get('NOISE_B200_ATTN_ORDER'), 0)
 
 
 def kernel_work(kind, members, length):
