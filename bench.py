@@ -18,8 +18,9 @@ tokens, weak scaling, population forwards/s); --workload credit the credit-reado
 it (pack kernel, NCCL all_to_all_single) and fused over peer memory (HeadExchange), N ranks under torchrun;
 --workload epoch the first --updates updates of a one-epoch run with its projected wall time.
 
---impl reference times the reference's algorithm on the host CPU (the oracle restatement of eggroll.population_loss,
-fp32, all host threads) on a bounded sample of the same workload, rank 0 only, in the same unit.
+--impl reference times the reference on the host CPU (its own eggroll.population_loss from baseline/_ref when
+installed, else the oracle restatement of it; fp32, all host threads) on a bounded sample of the same workload, rank 0
+only, in the same unit.
 """
 import argparse
 import json
@@ -219,8 +220,9 @@ def cpu_reference_sample(threads):
 
 
 def run_reference(a):
-    """The reference arm: the reference's algorithm (the fp32 oracle port of eggroll.population_loss) on all the host
-    cores, rank 0 only, each step a bounded sample of the workload, reported in the unit of our arm's line."""
+    """The reference arm: the reference's own eggroll.population_loss (baseline/_ref; the fp32 oracle port of it when
+    the install is absent) on all the host cores, rank 0 only, each step a bounded sample of the workload, reported in
+    the unit of our arm's line."""
     rank = int(os.environ.get('RANK', 0))
     if rank != 0:
         return
